@@ -1,0 +1,305 @@
+/* CPU oracle for the quantized trunk forward — TEST INFRASTRUCTURE ONLY.
+ *
+ * This file is the checker, never the product: only tests/, the smoke check of
+ * __graft_entry__.py and bench.py's cpu_baseline / --impl reference legs load
+ * it.  It restates, in plain C, the reference's CPU arithmetic for the W8A8
+ * path (Rust_KataGo, crates/kata_nn), each function citing the lines it
+ * follows.  Parity is pinned by the reference's own known answers and
+ * closed-form test inputs (tests/test_oracle_golden.py).
+ *
+ * Build: gcc -O3 -fno-fast-math -ffp-contract=off -fopenmp -shared -fPIC
+ * (see oracle/build.py).  -ffp-contract=off matters: every multiply-add below
+ * is either two rounded operations or an explicit fmaf(), exactly as in the
+ * GPU kernels, so both sides round identically.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <float.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------ 16-bit codecs */
+
+/* IEEE binary16 round-to-nearest-even, restated from the reference's
+ * independent codec (crates/kata_nn/tests/test_mxfp8.rs:25-61). */
+uint16_t or_f16_encode(float value) {
+  uint32_t bits;
+  memcpy(&bits, &value, 4);
+  uint16_t sign = (uint16_t)((bits >> 16) & 0x8000u);
+  int32_t exponent = (int32_t)((bits >> 23) & 255u);
+  uint32_t mantissa = bits & 0x7fffffu;
+  if (exponent == 255) return (uint16_t)(sign | 0x7c00u | (mantissa ? 0x200u : 0u));
+  int32_t e = exponent - 127 + 15;
+  if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+  if (e <= 0) {
+    if (e < -10) return sign;
+    mantissa |= 0x800000u;
+    uint32_t shift = (uint32_t)(14 - e);
+    uint32_t rounded = mantissa >> shift;
+    uint32_t remainder = mantissa & ((1u << shift) - 1u);
+    uint32_t midpoint = 1u << (shift - 1);
+    if (remainder > midpoint || (remainder == midpoint && (rounded & 1u))) rounded += 1;
+    return (uint16_t)(sign | rounded);
+  }
+  uint32_t rounded = mantissa >> 13;
+  uint32_t remainder = mantissa & 0x1fffu;
+  if (remainder > 0x1000u || (remainder == 0x1000u && (rounded & 1u))) {
+    rounded += 1;
+    if (rounded == 0x400u) {
+      rounded = 0;
+      e += 1;
+      if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    }
+  }
+  return (uint16_t)(sign | ((uint32_t)e << 10) | rounded);
+}
+
+/* test_mxfp8.rs:8-23 */
+float or_f16_decode(uint16_t bits) {
+  uint32_t exponent = (bits >> 10) & 31u;
+  uint32_t mantissa = bits & 1023u;
+  double magnitude;
+  if (exponent == 0) magnitude = (double)mantissa * ldexp(1.0, -24);
+  else if (exponent == 31) magnitude = mantissa == 0 ? INFINITY : NAN;
+  else magnitude = (double)(1024 + mantissa) * ldexp(1.0, (int)exponent - 25);
+  float m = (float)magnitude;
+  return (bits & 0x8000u) ? -m : m;
+}
+
+/* bfloat16 round-to-nearest-even (the upper 16 bits of binary32). */
+uint16_t or_bf16_encode(float value) {
+  uint32_t bits;
+  memcpy(&bits, &value, 4);
+  if ((bits & 0x7fffffffu) > 0x7f800000u) return (uint16_t)(((bits >> 16) & 0x8000u) | 0x7fc0u);
+  uint32_t lsb = (bits >> 16) & 1u;
+  bits += 0x7fffu + lsb;
+  return (uint16_t)(bits >> 16);
+}
+
+float or_bf16_decode(uint16_t b) {
+  uint32_t bits = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+static float round16(float v, int f16) {
+  return f16 ? or_f16_decode(or_f16_encode(v)) : or_bf16_decode(or_bf16_encode(v));
+}
+
+void or_encode16(const float* x, size_t n, int f16, uint16_t* out) {
+  for (size_t i = 0; i < n; ++i) out[i] = f16 ? or_f16_encode(x[i]) : or_bf16_encode(x[i]);
+}
+
+void or_decode16(const uint16_t* x, size_t n, int f16, float* out) {
+  for (size_t i = 0; i < n; ++i) out[i] = f16 ? or_f16_decode(x[i]) : or_bf16_decode(x[i]);
+}
+
+/* ------------------------------------------------------------------ elementwise math */
+
+static float pow2i(int k) {
+  uint32_t bits = (uint32_t)(k + 127) << 23;
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+/* exp(x) by Cody-Waite reduction with the Cephes ln2 split and the degree-7
+ * Taylor polynomial; the same operation sequence as the GPU kernels. */
+float or_expf(float x) {
+  if (x != x) return x;
+  if (x > 0x1.62e42ep+6f) return INFINITY;
+  if (x < -0x1.9fe36ap+6f) return 0.0f;
+  const float n = rintf(x * 0x1.715476p+0f);
+  float r = fmaf(-n, 0x1.63p-1f, x);
+  r = fmaf(n, 0x1.bd0106p-13f, r);
+  float p = 0x1.a01a02p-13f;
+  p = fmaf(p, r, 0x1.6c16c2p-10f);
+  p = fmaf(p, r, 0x1.111112p-7f);
+  p = fmaf(p, r, 0x1.555556p-5f);
+  p = fmaf(p, r, 0x1.555556p-3f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int ni = (int)n;
+  const int n1 = ni / 2;
+  const int n2 = ni - n1;
+  return (p * pow2i(n1)) * pow2i(n2);
+}
+
+/* g / (1 + e^-g): the SiLU inside the reference's SwiGLU (int8_ops.cu:111-113). */
+float or_silu(float g) { return g / (1.0f + or_expf(-g)); }
+
+/* GELU erf form with Abramowitz & Stegun 7.1.26 for erf. */
+float or_gelu(float x) {
+  const float z = fabsf(x) * 0x1.6a09e6p-1f;
+  const float t = 1.0f / fmaf(0x1.4f740ap-2f, z, 1.0f);
+  float poly = fmaf(0x1.0fb844p+0f, t, -0x1.7401c6p+0f);
+  poly = fmaf(poly, t, 0x1.6be1c6p+0f);
+  poly = fmaf(poly, t, -0x1.23531cp-2f);
+  poly = fmaf(poly, t, 0x1.04f20cp-2f);
+  const float e = or_expf(-(z * z));
+  const float erf_abs = 1.0f + (-((poly * t) * e));
+  const float erf = x < 0.0f ? -erf_abs : erf_abs;
+  return (0.5f * x) * (1.0f + erf);
+}
+
+void or_act(const float* x, size_t n, int act, float* out) {
+  for (size_t i = 0; i < n; ++i)
+    out[i] = act == 1 ? or_gelu(x[i]) : (act == 2 ? or_silu(x[i]) : x[i]);
+}
+
+/* ------------------------------------------------------------------ INT8 quantisation */
+
+/* Per-output-channel weight quantisation: QuantizedWeights::new
+ * (crates/kata_nn/src/backends/int8.rs:171-211). q is [n, kp], kp = ceil(k/16)*16. */
+int or_int8_quantize_weights(const float* w, int n, int k, int8_t* q, float* scales) {
+  if (n <= 0 || k <= 0 || k > 8192 || n % 4 != 0) return 1;
+  for (size_t i = 0; i < (size_t)n * k; ++i)
+    if (!isfinite(w[i])) return 2;
+  const int kp = (k + 15) / 16 * 16;
+  for (int r = 0; r < n; ++r) {
+    const float* row = w + (size_t)r * k;
+    float amax = 0.0f;
+    for (int c = 0; c < k; ++c) amax = fmaxf(amax, fabsf(row[c]));
+    float s = amax == 0.0f ? 1.0f : fmaxf(amax / 127.0f, FLT_MIN);
+    scales[r] = s;
+    for (int c = 0; c < kp; ++c) {
+      float v = c < k ? rintf(row[c] / s) : 0.0f;
+      v = v < -127.0f ? -127.0f : (v > 127.0f ? 127.0f : v);
+      q[(size_t)r * kp + c] = (int8_t)v;
+    }
+  }
+  return 0;
+}
+
+/* Shared tail of every activation quantiser: scale = NaN for a row holding a
+ * non-finite value, 1 for an all-zero row, amax/127 otherwise; q = clamp(rne(v/s))
+ * (int8_ops.cu:36-46, :72-88; CPU form tests/int8_kernels.rs:277-283). */
+static void quantize_values(const float* v, int width, int kp, int8_t* q, float* scale_out) {
+  float amax = 0.0f;
+  int bad = 0;
+  for (int c = 0; c < width; ++c) {
+    amax = fmaxf(amax, fabsf(v[c]));
+    bad |= !isfinite(v[c]);
+  }
+  const float scale = bad ? NAN : (amax == 0.0f ? 1.0f : amax / 127.0f);
+  *scale_out = scale;
+  for (int c = 0; c < kp; ++c) {
+    int qi = 0;
+    if (c < width && !bad) {
+      float r = rintf(v[c] / scale);
+      r = r < -127.0f ? -127.0f : (r > 127.0f ? 127.0f : r);
+      qi = (int)r;
+    }
+    q[c] = (int8_t)qi;
+  }
+}
+
+/* Row quantiser on already-decoded values (x[rows, stride] floats that were
+ * 16-bit values): int8_quantize_rows_kernel (int8_ops.cu:62-89, :140-176). */
+void or_int8_quantize_rows(const float* x, int rows, int width, int stride, int kp, int8_t* q,
+                           float* scales) {
+  for (int r = 0; r < rows; ++r)
+    quantize_values(x + (size_t)r * stride, width, kp, q + (size_t)r * kp, scales + r);
+}
+
+/* Fused RMSNorm quantiser: int8_rms_quantize (int8_ops.cu:8-47) with its exact
+ * summation order — lane l accumulates fma(x, x, s) over columns l, l+32, ...,
+ * then the xor butterfly 16, 8, 4, 2, 1 — and rstd = 1/sqrt(sum/W + eps)
+ * correctly rounded (the reference calls CUDA's rsqrtf here).  The normalised
+ * value is (x*rstd)*gamma rounded to the 16-bit boundary (f16 or bf16). */
+void or_int8_rms_quantize(const float* x, int rows, int width, int stride, const float* gamma,
+                          float eps, int bound_f16, int kp, int8_t* q, float* scales,
+                          float* normed /* nullable [rows, width] */) {
+  float* v = (float*)malloc(sizeof(float) * (size_t)width);
+  for (int r = 0; r < rows; ++r) {
+    const float* row = x + (size_t)r * stride;
+    float lanes[32];
+    for (int l = 0; l < 32; ++l) {
+      float s = 0.0f;
+      for (int c = l; c < width; c += 32) s = fmaf(row[c], row[c], s);
+      lanes[l] = s;
+    }
+    for (int step = 16; step; step >>= 1) {
+      float next[32];
+      for (int l = 0; l < 32; ++l) next[l] = lanes[l] + lanes[l ^ step];
+      memcpy(lanes, next, sizeof(lanes));
+    }
+    const float rstd = 1.0f / sqrtf(lanes[0] / (float)width + eps);
+    for (int c = 0; c < width; ++c) v[c] = round16((row[c] * rstd) * gamma[c], bound_f16);
+    if (normed) memcpy(normed + (size_t)r * width, v, sizeof(float) * (size_t)width);
+    quantize_values(v, width, kp, q + (size_t)r * kp, scales + r);
+  }
+  free(v);
+}
+
+/* ------------------------------------------------------------------ integer GEMM */
+
+/* dots[m, n] = sum_k a[m, k] * w[n, k] in int32 (tests/int8_kernels.rs:287-291). */
+void or_igemm(const int8_t* a, const int8_t* w, int m, int n, int kp, int32_t* dots, int threads) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel for schedule(static) if (threads != 1)
+#endif
+  for (int i = 0; i < m; ++i) {
+    const int8_t* ar = a + (size_t)i * kp;
+    for (int j = 0; j < n; ++j) {
+      const int8_t* wr = w + (size_t)j * kp;
+      int32_t s = 0;
+      for (int k = 0; k < kp; ++k) s += (int32_t)ar[k] * (int32_t)wr[k];
+      dots[(size_t)i * n + j] = s;
+    }
+  }
+}
+
+/* value = (f32(dot) * sa[row]) * sw[col] with two rounded multiplies
+ * (int8_ops.cu:182; tests/int8_kernels.rs:296). */
+void or_dequant(const int32_t* dots, const float* sa, const float* sw, int m, int n, float* out) {
+  for (int i = 0; i < m; ++i)
+    for (int j = 0; j < n; ++j) out[(size_t)i * n + j] = ((float)dots[(size_t)i * n + j] * sa[i]) * sw[j];
+}
+
+/* The reference's complete CPU W8A8 projection (tests/int8_kernels.rs:273-301):
+ * quantise fp16 rows, integer dot, dequant, round to fp16.  Used as the timed
+ * CPU baseline.  x16: [m, k] fp16 bits; wq: [n, kp]; out16: [m, n]. */
+void or_w8a8_project_half(const uint16_t* x16, int m, int k, const int8_t* wq, const float* sw,
+                          int n, int threads, uint16_t* out16) {
+  const int kp = (k + 15) / 16 * 16;
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel if (threads != 1)
+#endif
+  {
+    float* v = (float*)malloc(sizeof(float) * (size_t)k);
+    int8_t* q = (int8_t*)malloc((size_t)kp);
+#ifdef _OPENMP
+#pragma omp for schedule(static)
+#endif
+    for (int i = 0; i < m; ++i) {
+      for (int c = 0; c < k; ++c) v[c] = or_f16_decode(x16[(size_t)i * k + c]);
+      float sa;
+      quantize_values(v, k, kp, q, &sa);
+      for (int j = 0; j < n; ++j) {
+        const int8_t* wr = wq + (size_t)j * kp;
+        int32_t s = 0;
+        for (int c = 0; c < kp; ++c) s += (int32_t)q[c] * (int32_t)wr[c];
+        out16[(size_t)i * n + j] = or_f16_encode(((float)s * sa) * sw[j]);
+      }
+    }
+    free(v);
+    free(q);
+  }
+}
+
+int or_max_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

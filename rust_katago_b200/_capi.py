@@ -1,0 +1,88 @@
+"""ctypes binding of ``libkatab200.so`` (the C ABI declared in include/katab200.h).
+
+Loading fails loudly when the library has not been built: there is no
+fallback implementation of any entry point.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libkatab200.so"
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+F = ctypes.c_float
+U = ctypes.c_uint64
+PP = ctypes.POINTER(ctypes.c_void_p)
+IP = ctypes.POINTER(ctypes.c_int)
+STREAM = ctypes.c_size_t  # uintptr_t
+
+# name -> (restype, argtypes); must list every function include/katab200.h declares.
+SIGNATURES: dict[str, tuple] = {
+    "kb_last_error": (ctypes.c_char_p, []),
+    "kb_version": (I, []),
+    "kb_device_check": (I, [I]),
+    "kb_int8_quantize_weights": (I, [P, I, I, P, P]),
+    "kb_int8_weight_upload": (I, [P, I, I, I, PP]),
+    "kb_int8_weight_info": (I, [P, IP, IP, IP, IP, PP, PP]),
+    "kb_int8_weight_destroy": (None, [P]),
+    "kb_int8_gemm_i32": (I, [P, P, P, I, I, I, STREAM]),
+    "kb_int8_linear": (I, [P, P, P, P, P, I, I, I, I, I, I, P, I, I, P, STREAM]),
+    "kb_int8_quantize_rows": (I, [P, I, I, I, I, I, P, P, STREAM]),
+    "kb_int8_rms_quantize": (I, [P, I, I, I, I, P, F, I, I, P, P, STREAM]),
+    "kb_int8_workspace_create": (I, [STREAM, I, I, I, PP]),
+    "kb_int8_workspace_destroy": (None, [P]),
+    "kb_int8_workspace_buffers": (I, [P, PP, PP, PP]),
+    "kb_int8_project_half": (I, [P, STREAM, P, I, P, P, I]),
+    "kb_int8_project_residual": (I, [P, STREAM, P, I, P, P, I]),
+    "kb_int8_ffn": (I, [P, STREAM, P, P, P, P, I]),
+    "kb_int8_ffn_rms": (I, [P, STREAM, P, F, P, P, P, I]),
+    "kb_int8_ffn_gelu_rms": (I, [P, STREAM, P, F, P, P, P, P, P, I]),
+    "kb_bf16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
+}
+
+# Constants mirrored from include/katab200.h.
+KB_OK, KB_E_INVALID, KB_E_CUDA, KB_E_STATE, KB_E_NONFINITE, KB_E_UNSUPPORTED = range(6)
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+EPI_I32, EPI_F16, EPI_RES_F32, EPI_16, EPI_RES16, EPI_SWIGLU16, EPI_F32 = range(7)
+ACT_NONE, ACT_GELU, ACT_SILU = 0, 1, 2
+LAYOUT_PLAIN, LAYOUT_SWIGLU_DUAL = 0, 1
+
+_lib: ctypes.CDLL | None = None
+
+
+class KbError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"katab200 error {code}: {message}")
+        self.code = code
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m rust_katago_b200.build` "
+                "(there is no CPU fallback)"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(code: int) -> None:
+    if code != KB_OK:
+        msg = load().kb_last_error().decode(errors="replace")
+        raise KbError(code, msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

@@ -1,0 +1,79 @@
+// Internal C++ interface between the kernels (*.cu) and the host runtime
+// (model, workspace and C-ABI layers).  Not part of the public ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "kb_status.h"
+
+namespace kb {
+
+// Thread-local last error, surfaced through kb_last_error().
+void set_error(const std::string& msg);
+const char* last_error();
+
+// Returns 0, or sets the thread-local error and returns a KB_E_* code.
+int check_cuda(cudaError_t e, const char* what);
+
+int num_sms(int device);
+
+// ------------------------------------------------------------------ GEMM
+// Epilogue variants of the tcgen05 GEMM.  `dot` below is the 32-bit TMEM
+// accumulator of one output element: an exact int32 for kind::i8, an fp32 sum
+// for kind::f16 (bf16 operands) and kind::mxf8f6f4.
+enum Epi : int {
+  kEpiI32 = 0,       // out_i32 = dot                                (LtPlan::run, int8.rs:542-599)
+  kEpiF16 = 1,       // out_f16 = half((f32(dot)*sa)*sw)             (int8_ops.cu:178-185)
+  kEpiResF32 = 2,    // res_f32 = res + (f32(dot)*sa)*sw             (int8_ops.cu:187-194)
+  kEpi16 = 3,        // out16 = T16(act(v + bias)), optional row amax
+  kEpiRes16 = 4,     // res16 = T16(f32(res16) + (v + bias))
+  kEpiSwiGLU16 = 5,  // dual tile [gate|up] -> T16(u*(g/(1+e^-g))), gate/up rounded to T16 first
+  kEpiF32 = 6,       // out_f32 = v + bias (+ res_f32 when residual != null)
+};
+
+struct GemmArgs {
+  int m = 0, n = 0, k = 0;   // k: padded K in elements of the operand type
+  void* out = nullptr;       // output base
+  long ldo = 0;              // output row stride in elements
+  const float* row_scale = nullptr;  // [m] activation scales (int8 only)
+  const float* col_scale = nullptr;  // [n] weight scales (int8 only)
+  const float* bias = nullptr;       // [n] or null
+  void* residual = nullptr;          // kEpiF32 optional residual input
+  long ldr = 0;
+  unsigned* row_amax = nullptr;      // [m] |v| bit maximum, or null
+  int act = 0;                       // Act
+  int out_f16 = 0;                   // 16-bit outputs: 1 = fp16, 0 = bf16
+  int n_out = 0;                     // SwiGLU: logical output columns (hidden)
+  unsigned* status = nullptr;        // sticky status word (timeouts)
+  unsigned layer = KB_NO_LAYER;
+  // MXFP8 only: block-scale factors, 1 byte per (row, 32-element K block),
+  // stored as [rows_padded/128][k/128][32 rows][4 row groups][4 K blocks].
+  const uint8_t* sfa = nullptr;
+  const uint8_t* sfb = nullptr;
+};
+
+enum GemmKind : int { kGemmI8 = 0, kGemmBF16 = 1, kGemmMXF8 = 2 };
+
+// Launch C[m,n] = A[m,k] * B[n,k]^T with the selected epilogue.  A and B are
+// row-major with K contiguous (K-major), row strides k elements.  Returns 0 or
+// a KB_E_* code with the error text set.
+int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs& args,
+                cudaStream_t stream, int bn_hint = 0);
+
+// Columns per N tile chosen for a given N (the SwiGLU dual-weight packing
+// depends on it).
+int gemm_pick_bn(int kind, int epi, int n);
+
+}  // namespace kb
+
+// Error codes returned by every C-ABI entry point (0 = success).
+#define KB_OK 0
+#define KB_E_INVALID 1
+#define KB_E_CUDA 2
+#define KB_E_STATE 3
+#define KB_E_NONFINITE 4
+#define KB_E_UNSUPPORTED 5
