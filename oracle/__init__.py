@@ -227,7 +227,7 @@ def swiglu_ffn_f16(x: np.ndarray, dual_w: np.ndarray, down_w: np.ndarray, residu
     return out.astype(np.float32), {"q": q, "sa": sa, "hidden": hidden, "q2": q2, "s2": s2}
 
 
-def gelu_ffn_bf16(residual_bf16: np.ndarray, gamma, eps, up_w, up_b, down_w, down_b):
+def gelu_ffn_bf16(residual_bf16: np.ndarray, gamma, eps, up_w, up_b, down_w, down_b, threads: int = 0):
     """BASELINE-topology FFN block on a bf16 residual: RMSNorm -> bf16 -> INT8 ->
     up GEMM (+bias) + GELU -> bf16 -> INT8 -> down GEMM (+bias) -> bf16 residual.
     residual_bf16: uint16 bits [rows, C].  Returns new residual bits and intermediates."""
@@ -235,12 +235,12 @@ def gelu_ffn_bf16(residual_bf16: np.ndarray, gamma, eps, up_w, up_b, down_w, dow
     uq, us = quantize_weights(up_w)
     dq, ds = quantize_weights(down_w)
     q, sa, normed = rms_quantize(x, gamma, eps, False, kp=uq.shape[1])
-    v = dequant(igemm(q, uq), sa, us)
+    v = dequant(igemm(q, uq, threads), sa, us)
     if up_b is not None:
         v = (v + up_b[None, :].astype(np.float32)).astype(np.float32)
     hidden = round16(act(v, 1), False)
     q2, s2 = quantize_rows(hidden, kp=dq.shape[1])
-    d = dequant(igemm(q2, dq), s2, ds)
+    d = dequant(igemm(q2, dq, threads), s2, ds)
     if down_b is not None:
         d = (d + down_b[None, :].astype(np.float32)).astype(np.float32)
     out = bf16_encode((x + d).astype(np.float32))

@@ -134,18 +134,21 @@ float or_expf(float x) {
 /* g / (1 + e^-g): the SiLU inside the reference's SwiGLU (int8_ops.cu:111-113). */
 float or_silu(float g) { return g / (1.0f + or_expf(-g)); }
 
-/* GELU erf form with Abramowitz & Stegun 7.1.26 for erf. */
+/* GELU(x) = x * Phi(x): Phi(x) = 0.5 + xc * P(xc^2/8 - 1) on |x| <= 4 with the
+ * degree-10 polynomial of rust_katago_b200/gelu_fit.py, 0 below -4, 1 above 4;
+ * the same fused multiply-add sequence as the kernels. */
 float or_gelu(float x) {
-  const float z = fabsf(x) * 0x1.6a09e6p-1f;
-  const float t = 1.0f / fmaf(0x1.4f740ap-2f, z, 1.0f);
-  float poly = fmaf(0x1.0fb844p+0f, t, -0x1.7401c6p+0f);
-  poly = fmaf(poly, t, 0x1.6be1c6p+0f);
-  poly = fmaf(poly, t, -0x1.23531cp-2f);
-  poly = fmaf(poly, t, 0x1.04f20cp-2f);
-  const float e = or_expf(-(z * z));
-  const float erf_abs = 1.0f + (-((poly * t) * e));
-  const float erf = x < 0.0f ? -erf_abs : erf_abs;
-  return (0.5f * x) * (1.0f + erf);
+  static const float c[11] = {0x1.68585ap-3f, -0x1.5961f4p-4f, 0x1.ca3788p-5f, -0x1.2df2f6p-5f,
+                              0x1.70d728p-6f, -0x1.9ab164p-7f, 0x1.9a7b1cp-8f, -0x1.5eeeecp-9f,
+                              0x1.229b08p-10f, -0x1.31c494p-11f, 0x1.a02d8ap-13f};
+  const float xc = fminf(fmaxf(x, -4.0f), 4.0f);
+  const float s = fmaf(xc * xc, 0.125f, -1.0f);
+  float p = c[10];
+  for (int i = 9; i >= 0; --i) p = fmaf(p, s, c[i]);
+  float phi = fmaf(xc, p, 0.5f);
+  if (x < -4.0f) phi = 0.0f;
+  if (x > 4.0f) phi = 1.0f;
+  return x * phi;
 }
 
 void or_act(const float* x, size_t n, int act, float* out) {
@@ -208,21 +211,29 @@ void or_int8_quantize_rows(const float* x, int rows, int width, int stride, int 
     quantize_values(x + (size_t)r * stride, width, kp, q + (size_t)r * kp, scales + r);
 }
 
-/* Fused RMSNorm quantiser: int8_rms_quantize (int8_ops.cu:8-47) with its exact
- * summation order — lane l accumulates fma(x, x, s) over columns l, l+32, ...,
- * then the xor butterfly 16, 8, 4, 2, 1 — and rstd = 1/sqrt(sum/W + eps)
- * correctly rounded (the reference calls CUDA's rsqrtf here).  The normalised
- * value is (x*rstd)*gamma rounded to the 16-bit boundary (f16 or bf16). */
+/* Fused RMSNorm quantiser: int8_rms_quantize (int8_ops.cu:8-47) — one warp per
+ * row, per-lane partial sums then the xor butterfly 16, 8, 4, 2, 1 — in the
+ * product's lane assignment: lane l owns the 8-column groups l, l+32, ... and
+ * accumulates fma(x, x, s) over them in order (the reference strides single
+ * columns over lanes instead; the butterfly is identical).  rstd =
+ * 1/sqrt(sum/W + eps) correctly rounded (the reference calls CUDA's rsqrtf).
+ * The normalised value is (x*rstd)*gamma rounded to the 16-bit boundary. */
 void or_int8_rms_quantize(const float* x, int rows, int width, int stride, const float* gamma,
                           float eps, int bound_f16, int kp, int8_t* q, float* scales,
                           float* normed /* nullable [rows, width] */) {
   float* v = (float*)malloc(sizeof(float) * (size_t)width);
+  const int groups = (width + 7) / 8;
   for (int r = 0; r < rows; ++r) {
     const float* row = x + (size_t)r * stride;
     float lanes[32];
     for (int l = 0; l < 32; ++l) {
       float s = 0.0f;
-      for (int c = l; c < width; c += 32) s = fmaf(row[c], row[c], s);
+      for (int g = l; g < groups; g += 32)
+        for (int t = 0; t < 8; ++t) {
+          const int c = 8 * g + t;
+          const float xv = c < width ? row[c] : 0.0f;
+          s = fmaf(xv, xv, s);
+        }
       lanes[l] = s;
     }
     for (int step = 16; step; step >>= 1) {

@@ -9,13 +9,17 @@
 //   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, 32 B of K
 //               per instruction) into one of two TMEM accumulators and commits
 //               ring slots / accumulators back through mbarriers;
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
-//               output row per thread), dequant / bias / activation / residual /
-//               row-amax, 16-byte global stores.
+//   warps 2-9   epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
+//               output row per thread; two warps per 32-lane quarter, each taking
+//               half of the tile's columns), dequant / bias / activation /
+//               residual / row-amax, then 16-bit results go through a swizzled
+//               2 KiB shared-memory staging tile per warp and a TMA store.
 // The double-buffered accumulator lets the epilogue of tile i overlap the MMAs
 // of tile i+1.  Every wait is bounded (kb_ptx.cuh); a timeout records
 // KB_STATUS_TIMEOUT in the status word and the kernel returns.
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <atomic>
 #include <mutex>
@@ -30,7 +34,10 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle row of K per stage
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageTile = 32 * 64;  // one 32x32 16-bit staging tile (2 KiB)
+constexpr int kStagingBytes = kEpiWarps * 2 * kStageTile;
 
 template <int BN>
 struct GemmCfg {
@@ -38,8 +45,9 @@ struct GemmCfg {
   static constexpr int kBBytes = BN * kBKBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (192 * 1024) / kStageBytes;
+  static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmemBytes = kRingBytes + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 template <int KIND>
@@ -73,141 +81,126 @@ __device__ __forceinline__ void load_vec32(const float* p, int col0, int n, floa
   }
 }
 
-__device__ __forceinline__ void store16x32(uint16_t* dst, const uint16_t (&h)[32], int valid,
+__device__ __forceinline__ uint4 pack8(const uint16_t* h) {
+  uint4 t;
+  t.x = h[0] | (uint32_t(h[1]) << 16);
+  t.y = h[2] | (uint32_t(h[3]) << 16);
+  t.z = h[4] | (uint32_t(h[5]) << 16);
+  t.w = h[6] | (uint32_t(h[7]) << 16);
+  return t;
+}
+
+// Round a pair to the 16-bit output type; element 0 in the low half.
+__device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
+  if (f16) {
+    const __half2 h = __floats2half2_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack16x2(uint32_t w, bool f16) {
+  if (f16) return make_float2(from_f16(static_cast<uint16_t>(w & 0xffffu)), from_f16(static_cast<uint16_t>(w >> 16)));
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// 32-bit float bits of the larger |half| held in a packed pair of |16-bit| values.
+__device__ __forceinline__ uint32_t amax16_to_f32bits(uint32_t m2, bool f16) {
+  const uint32_t m = max(m2 & 0xffffu, m2 >> 16);
+  return f16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m))) : (m << 16);
+}
+
+__device__ __forceinline__ void store16x32(uint16_t* dst, const uint32_t (&hw)[16], int valid,
                                            bool vec) {
   if (vec && valid == 32) {
     uint4* q = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint4 t;
-      t.x = h[8 * i] | (uint32_t(h[8 * i + 1]) << 16);
-      t.y = h[8 * i + 2] | (uint32_t(h[8 * i + 3]) << 16);
-      t.z = h[8 * i + 4] | (uint32_t(h[8 * i + 5]) << 16);
-      t.w = h[8 * i + 6] | (uint32_t(h[8 * i + 7]) << 16);
-      q[i] = t;
-    }
+    for (int i = 0; i < 4; ++i) q[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-      if (i < valid) dst[i] = h[i];
+      if (i < valid) dst[i] = static_cast<uint16_t>(i & 1 ? hw[i / 2] >> 16 : hw[i / 2] & 0xffffu);
   }
 }
 
-__device__ __forceinline__ void load16x32(const uint16_t* src, uint16_t (&h)[32], int valid,
+__device__ __forceinline__ void load16x32(const uint16_t* src, uint32_t (&hw)[16], int valid,
                                           bool vec) {
   if (vec && valid == 32) {
     const uint4* q = reinterpret_cast<const uint4*>(src);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint4 t = q[i];
-      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        h[8 * i + 2 * j] = static_cast<uint16_t>(w[j] & 0xffffu);
-        h[8 * i + 2 * j + 1] = static_cast<uint16_t>(w[j] >> 16);
-      }
+      hw[4 * i] = t.x;
+      hw[4 * i + 1] = t.y;
+      hw[4 * i + 2] = t.z;
+      hw[4 * i + 3] = t.w;
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) h[i] = i < valid ? src[i] : 0;
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t lo = 2 * i < valid ? src[2 * i] : 0u;
+      const uint32_t hi = 2 * i + 1 < valid ? src[2 * i + 1] : 0u;
+      hw[i] = lo | (hi << 16);
+    }
   }
 }
 
-// Epilogue of one 32-column chunk held by this thread (row `row`, columns
-// col0..col0+31).  `amax` accumulates |value| bits for the row-amax output.
-template <int KIND, int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t (&acc)[32], int row,
-                                               int col0, float sa, uint32_t& amax) {
-  const int valid = min(32, g.n - col0);
-  float sw[32], bias[32];
+// Per-warp output path for 32 rows x 32 columns of 16-bit results.  With a TMA
+// output map the thread's row goes into a 64-byte-swizzled staging tile (16-byte
+// chunk c of row r at c ^ ((r >> 1) & 3): conflict-free, and exactly the layout a
+// SWIZZLE_64B tensor store reads), then lane 0 issues one bulk tensor store.
+// Two staging tiles per warp alternate so a store overlaps the next chunk.
+struct Out16 {
+  const CUtensorMap* map;
+  uint8_t* stage;  // this warp's two staging tiles
+  int sb;          // staging tile to use next
+};
+
+__device__ __forceinline__ void emit16(Out16& o, const GemmArgs& g, const uint32_t (&hw)[16], int row,
+                                       int row0q, int col0, int lane, bool row_ok, int valid) {
+  if (o.map != nullptr) {
+    uint8_t* buf = o.stage + o.sb * kStageTile;
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
+          make_uint4(hw[4 * c], hw[4 * c + 1], hw[4 * c + 2], hw[4 * c + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(o.map, buf, col0, row0q);
+      bulk_commit();
+    }
+    o.sb ^= 1;
+  } else if (row_ok) {
+    uint16_t* dst = static_cast<uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
+    store16x32(dst, hw, valid, (reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+  }
+}
+
+// Dequantised pair (i, i+1) of a 32-column chunk: (f32(dot) * sa) * sw, or the
+// fp32 accumulator itself for the bf16 / MXFP8 kinds.
+template <int KIND>
+__device__ __forceinline__ float2 acc_pair(const uint32_t (&v)[32], int i, float sa, const float (&sw)[32]) {
   if constexpr (KIND == kGemmI8) {
-    load_vec32(g.col_scale, col0, g.n, sw);
-  }
-  if constexpr (EPI == kEpi16 || EPI == kEpiRes16 || EPI == kEpiF32) {
-    load_vec32(g.bias, col0, g.n, bias);
-  }
-  if constexpr (EPI == kEpiI32) {
-    int32_t* dst = static_cast<int32_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-    const bool vec = valid == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
-    if (vec) {
-      int4* q = reinterpret_cast<int4*>(dst);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        q[i] = make_int4(int(acc[4 * i]), int(acc[4 * i + 1]), int(acc[4 * i + 2]),
-                         int(acc[4 * i + 3]));
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < valid) dst[i] = static_cast<int32_t>(acc[i]);
-    }
-  } else if constexpr (EPI == kEpiF16 || EPI == kEpi16) {
-    uint16_t h[32];
-    const bool f16 = (EPI == kEpiF16) ? true : (g.out_f16 != 0);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float v = acc_value<KIND>(acc[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
-      if constexpr (EPI == kEpi16) {
-        if (g.bias) v = __fadd_rn(v, bias[i]);
-        v = apply_act(v, g.act);
-      }
-      h[i] = bits16(v, f16);
-      if (i < valid) amax = max(amax, abs_bits(from16(h[i], f16)));
-    }
-    uint16_t* dst = static_cast<uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-    store16x32(dst, h, valid, (reinterpret_cast<uintptr_t>(dst) & 15) == 0);
-  } else if constexpr (EPI == kEpiResF32) {
-    float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-    const bool vec = valid == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
-    if (vec) {
-      float4* q = reinterpret_cast<float4*>(dst);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float4 r = q[i];
-        r.x = __fadd_rn(r.x, acc_value<KIND>(acc[4 * i], sa, sw[4 * i]));
-        r.y = __fadd_rn(r.y, acc_value<KIND>(acc[4 * i + 1], sa, sw[4 * i + 1]));
-        r.z = __fadd_rn(r.z, acc_value<KIND>(acc[4 * i + 2], sa, sw[4 * i + 2]));
-        r.w = __fadd_rn(r.w, acc_value<KIND>(acc[4 * i + 3], sa, sw[4 * i + 3]));
-        q[i] = r;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < valid) dst[i] = __fadd_rn(dst[i], acc_value<KIND>(acc[i], sa, sw[i]));
-    }
-  } else if constexpr (EPI == kEpiRes16) {
-    const bool f16 = g.out_f16 != 0;
-    uint16_t* dst = static_cast<uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
-    uint16_t h[32];
-    load16x32(dst, h, valid, vec);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float v = acc_value<KIND>(acc[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
-      if (g.bias) v = __fadd_rn(v, bias[i]);
-      h[i] = bits16(__fadd_rn(from16(h[i], f16), v), f16);
-    }
-    store16x32(dst, h, valid, vec);
-  } else if constexpr (EPI == kEpiF32) {
-    float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-    const float* res = g.residual ? static_cast<const float*>(g.residual) +
-                                        static_cast<size_t>(row) * g.ldr + col0
-                                  : nullptr;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      if (i < valid) {
-        float v = acc_value<KIND>(acc[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
-        if (g.bias) v = __fadd_rn(v, bias[i]);
-        if (res) v = __fadd_rn(res[i], v);
-        dst[i] = v;
-      }
-    }
+    // Scalar rounded multiplies: a packed multiply followed by the bias add
+    // may be contracted into a fused multiply-add by the assembler, which
+    // would change the rounding.
+    return make_float2(
+        __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[2 * i])), sa), sw[2 * i]),
+        __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[2 * i + 1])), sa), sw[2 * i + 1]));
+  } else {
+    return make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
   }
 }
 
-template <int KIND, int BN, int EPI>
+template <int KIND, int BN, int EPI, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                const __grid_constant__ CUtensorMap tmap_b, const GemmArgs g) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g, const int use_tma_out) {
   using Cfg = GemmCfg<BN>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kElemBytes = (KIND == kGemmBF16) ? 2 : 1;
@@ -217,7 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* ring = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes);
+  uint8_t* staging = smem + Cfg::kRingBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kStagingBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -238,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -246,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (use_tma_out) tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -330,15 +325,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps (TMEM lane quarter = warp % 4)
-    const int quarter = warp & 3;
+    // ---------------- epilogue warps
+    const int e = warp - 2;          // 0..7
+    const int quarter = warp & 3;    // TMEM lanes this warp may access: 32*quarter..+31
+    const int half = e >> 2;         // which half of the tile's columns
+    Out16 o{use_tma_out ? &tmap_out : nullptr, staging + e * 2 * kStageTile, 0};
+    const bool f16 = (EPI == kEpiF16) ? true : (g.out_f16 != 0);
     int acc = 0;
     uint32_t aph = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag))) break;
       tc_fence_after();
       const int mb = tile / tiles_n, nb = tile % tiles_n;
-      const int row = mb * kBM + quarter * 32 + lane;
+      const int row0q = mb * kBM + quarter * 32;
+      const int row = row0q + lane;
       const bool row_ok = row < g.m;
       float sa = 1.0f;
       if constexpr (KIND == kGemmI8 && EPI != kEpiI32) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
@@ -348,51 +348,131 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == kEpiSwiGLU16) {
         // Tile columns [0, BN/2) are gate channels, [BN/2, BN) the matching up
         // channels (the dual weight is interleaved per tile at load).
-        const bool f16 = g.out_f16 != 0;
+        constexpr int kChunks = BN / 128;
 #pragma unroll 1
-        for (int j = 0; j < BN / 64; ++j) {
+        for (int jj = 0; jj < kChunks; ++jj) {
+          const int j = half * kChunks + jj;
           uint32_t vg[32], vu[32];
           tmem_ld32(taddr + j * 32, vg);
           tmem_ld32(taddr + BN / 2 + j * 32, vu);
           tmem_ld_wait();
           const int gcol0 = nb * BN + j * 32;
           const int ocol0 = nb * (BN / 2) + j * 32;
-          if (row_ok && ocol0 < g.n_out) {
+          if (ocol0 < g.n_out) {
             float swg[32], swu[32];
             if constexpr (KIND == kGemmI8) {
               load_vec32(g.col_scale, gcol0, g.n, swg);
               load_vec32(g.col_scale, gcol0 + BN / 2, g.n, swu);
             }
             const int valid = min(32, g.n_out - ocol0);
-            uint16_t h[32];
+            uint32_t hw[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float gv = from16(bits16(acc_value<KIND>(vg[i], sa, KIND == kGemmI8 ? swg[i] : 1.0f), f16), f16);
-              const float uv = from16(bits16(acc_value<KIND>(vu[i], sa, KIND == kGemmI8 ? swu[i] : 1.0f), f16), f16);
-              h[i] = bits16(__fmul_rn(uv, kb_silu(gv)), f16);
-              if (i < valid) amax = max(amax, abs_bits(from16(h[i], f16)));
+            for (int i = 0; i < 16; ++i) {
+              uint32_t pair = 0;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int c = 2 * i + h;
+                const float gv = from16(bits16(acc_value<KIND>(vg[c], sa, KIND == kGemmI8 ? swg[c] : 1.0f), f16), f16);
+                const float uv = from16(bits16(acc_value<KIND>(vu[c], sa, KIND == kGemmI8 ? swu[c] : 1.0f), f16), f16);
+                const uint16_t b = bits16(__fmul_rn(uv, kb_silu(gv)), f16);
+                if (c < valid) amax = max(amax, abs_bits(from16(b, f16)));
+                pair |= static_cast<uint32_t>(b) << (16 * h);
+              }
+              hw[i] = pair;
             }
-            uint16_t* dst = static_cast<uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + ocol0;
-            store16x32(dst, h, valid, (reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+            emit16(o, g, hw, row, row0q, ocol0, lane, row_ok, valid);
           }
         }
       } else {
+        constexpr int kChunks = BN / 64;
 #pragma unroll 1
-        for (int j = 0; j < BN / 32; ++j) {
+        for (int jj = 0; jj < kChunks; ++jj) {
+          const int j = half * kChunks + jj;
           uint32_t v[32];
           tmem_ld32(taddr + j * 32, v);
           tmem_ld_wait();
           const int col0 = nb * BN + j * 32;
-          if (row_ok && col0 < g.n) epilogue_chunk<KIND, EPI>(g, v, row, col0, sa, amax);
+          if (col0 >= g.n) continue;  // warp-uniform
+          const int valid = min(32, g.n - col0);
+          if constexpr (EPI == kEpiF16 || EPI == kEpi16 || EPI == kEpiRes16) {
+            float sw[32], bias[32];
+            if constexpr (KIND == kGemmI8) load_vec32(g.col_scale, col0, g.n, sw);
+            // A null bias loads as zeros; adding +0 is exact here because the
+            // dequantised value is never -0 for kind::i8 (dot 0 -> +0).
+            if constexpr (EPI != kEpiF16) load_vec32(g.bias, col0, g.n, bias);
+            uint32_t hw[16];
+            if constexpr (EPI == kEpiRes16) {
+              const uint16_t* src = static_cast<const uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
+              if (row_ok) load16x32(src, hw, valid, (reinterpret_cast<uintptr_t>(src) & 15) == 0);
+            }
+            uint32_t amax2 = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float2 x = acc_pair<KIND>(v, i, sa, sw);
+              if constexpr (EPI != kEpiF16) {
+                x.x = __fadd_rn(x.x, bias[2 * i]);
+                x.y = __fadd_rn(x.y, bias[2 * i + 1]);
+              }
+              if constexpr (EPI == kEpiRes16) {
+                const float2 r = unpack16x2(hw[i], f16);
+                hw[i] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
+              } else {
+                hw[i] = pack16x2(apply_act2<ACT>(x), f16);
+                const uint32_t mask = 2 * i + 1 < valid ? 0x7fff7fffu : (2 * i < valid ? 0x00007fffu : 0u);
+                amax2 = __vmaxu2(amax2, hw[i] & mask);
+              }
+            }
+            if constexpr (EPI != kEpiRes16) amax = max(amax, amax16_to_f32bits(amax2, f16));
+            emit16(o, g, hw, row, row0q, col0, lane, row_ok, valid);
+          } else if (row_ok) {
+            float sw[32], bias[32];
+            if constexpr (KIND == kGemmI8 && EPI != kEpiI32) load_vec32(g.col_scale, col0, g.n, sw);
+            if constexpr (EPI == kEpiF32) load_vec32(g.bias, col0, g.n, bias);
+            if constexpr (EPI == kEpiI32) {
+              int32_t* dst = static_cast<int32_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
+              if (valid == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                int4* q = reinterpret_cast<int4*>(dst);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  q[i] = make_int4(int(v[4 * i]), int(v[4 * i + 1]), int(v[4 * i + 2]), int(v[4 * i + 3]));
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < valid) dst[i] = static_cast<int32_t>(v[i]);
+              }
+            } else if constexpr (EPI == kEpiResF32) {
+              float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < valid) dst[i] = __fadd_rn(dst[i], acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f));
+            } else if constexpr (EPI == kEpiF32) {
+              float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
+              const float* res = g.residual ? static_cast<const float*>(g.residual) +
+                                                  static_cast<size_t>(row) * g.ldr + col0
+                                            : nullptr;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                if (i < valid) {
+                  float x = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
+                  if (g.bias) x = __fadd_rn(x, bias[i]);
+                  if (res) x = __fadd_rn(res[i], x);
+                  dst[i] = x;
+                }
+              }
+            }
+          }
         }
       }
-      if (g.row_amax != nullptr && row_ok) atomicMax(g.row_amax + row, amax);
+      // Accumulator fully read: hand it back to the MMA warp before the
+      // stores of this tile drain.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (g.row_amax != nullptr && row_ok) atomicMax(g.row_amax + row, amax);
       acc ^= 1;
       if (acc == 0) aph ^= 1;
     }
+    if (lane == 0 && use_tma_out) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -423,33 +503,23 @@ EncodeTiledFn encode_fn() {
 }
 
 // Row-major [rows, k] operand, box {128 bytes of K, box_rows}, 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* base, int kind, long rows, long k, int box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) {
-    set_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
-    return KB_E_CUDA;
-  }
+int make_operand_map(CUtensorMap* map, const void* base, int kind, long rows, long k, int box_rows) {
   const int elem = kind == kGemmBF16 ? 2 : 1;
   const CUtensorMapDataType dt =
       kind == kGemmBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * elem};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBKBytes / elem), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("cuTensorMapEncodeTiled failed (code " + std::to_string(int(r)) + ")");
-    return KB_E_CUDA;
-  }
-  return KB_OK;
+  return encode_2d(map, dt, base, k, rows, k * elem, kBKBytes / elem, box_rows,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int KIND, int BN, int EPI>
-int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, cudaStream_t stream) {
+bool epi_16bit(int epi) {
+  return epi == kEpiF16 || epi == kEpi16 || epi == kEpiRes16 || epi == kEpiSwiGLU16;
+}
+
+template <int KIND, int BN, int EPI, int ACT>
+int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int use_tma_out,
+               const GemmArgs& g, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
-  auto kern = gemm_kernel<KIND, BN, EPI>;
+  auto kern = gemm_kernel<KIND, BN, EPI, ACT>;
   int dev = 0;
   cudaGetDevice(&dev);
   // Function attributes live in each device's context: set once per device.
@@ -462,27 +532,51 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, 
   }
   const int tiles = ((g.m + kBM - 1) / kBM) * ((g.n + BN - 1) / BN);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, g);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, g, use_tma_out);
   return check_cuda(cudaGetLastError(), "gemm launch");
 }
 
 template <int KIND, int BN>
-int dispatch_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
-                 cudaStream_t s) {
+int dispatch_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int tma_out,
+                 const GemmArgs& g, cudaStream_t s) {
   switch (epi) {
-    case kEpiI32: return launch_one<KIND, BN, kEpiI32>(ma, mb, g, s);
-    case kEpiF16: return launch_one<KIND, BN, kEpiF16>(ma, mb, g, s);
-    case kEpiResF32: return launch_one<KIND, BN, kEpiResF32>(ma, mb, g, s);
-    case kEpi16: return launch_one<KIND, BN, kEpi16>(ma, mb, g, s);
-    case kEpiRes16: return launch_one<KIND, BN, kEpiRes16>(ma, mb, g, s);
-    case kEpiSwiGLU16: return launch_one<KIND, BN, kEpiSwiGLU16>(ma, mb, g, s);
-    case kEpiF32: return launch_one<KIND, BN, kEpiF32>(ma, mb, g, s);
+    case kEpiI32: return launch_one<KIND, BN, kEpiI32, kActNone>(ma, mb, mo, tma_out, g, s);
+    case kEpiF16: return launch_one<KIND, BN, kEpiF16, kActNone>(ma, mb, mo, tma_out, g, s);
+    case kEpiResF32: return launch_one<KIND, BN, kEpiResF32, kActNone>(ma, mb, mo, tma_out, g, s);
+    case kEpi16:
+      if (g.act == kActGelu) return launch_one<KIND, BN, kEpi16, kActGelu>(ma, mb, mo, tma_out, g, s);
+      if (g.act == kActSilu) return launch_one<KIND, BN, kEpi16, kActSilu>(ma, mb, mo, tma_out, g, s);
+      return launch_one<KIND, BN, kEpi16, kActNone>(ma, mb, mo, tma_out, g, s);
+    case kEpiRes16: return launch_one<KIND, BN, kEpiRes16, kActNone>(ma, mb, mo, tma_out, g, s);
+    case kEpiSwiGLU16: return launch_one<KIND, BN, kEpiSwiGLU16, kActNone>(ma, mb, mo, tma_out, g, s);
+    case kEpiF32: return launch_one<KIND, BN, kEpiF32, kActNone>(ma, mb, mo, tma_out, g, s);
   }
   set_error("unknown GEMM epilogue");
   return KB_E_INVALID;
 }
 
 }  // namespace
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long cols, long rows,
+              long row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+    return KB_E_CUDA;
+  }
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (code " + std::to_string(int(r)) + ")");
+    return KB_E_CUDA;
+  }
+  return KB_OK;
+}
 
 int gemm_pick_bn(int kind, int epi, int n) {
   (void)kind;
@@ -510,19 +604,40 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     set_error("INT8 dequant epilogue needs row and column scales");
     return KB_E_INVALID;
   }
+  if (g.act < kActNone || g.act > kActSilu) {
+    set_error("unknown activation");
+    return KB_E_INVALID;
+  }
   const int bn = bn_hint ? bn_hint : gemm_pick_bn(kind, epi, g.n);
-  CUtensorMap ma, mb;
-  int rc = make_map(&ma, a, kind, g.m, g.k, kBM);
+  CUtensorMap ma, mb, mo;
+  memset(&mo, 0, sizeof(mo));
+  int rc = make_operand_map(&ma, a, kind, g.m, g.k, kBM);
   if (rc) return rc;
-  rc = make_map(&mb, b, kind, g.n, g.k, bn);
+  rc = make_operand_map(&mb, b, kind, g.n, g.k, bn);
   if (rc) return rc;
+  // 16-bit outputs leave through TMA stores when the row stride allows it.
+  int tma_out = 0;
+  // Tactic switch (like the reference's KATAGO_CUDA_* keys): KB_GEMM_DIRECT_STORE=1
+  // writes 16-bit outputs with plain vector stores instead of TMA stores.
+  static const bool direct_store = [] {
+    const char* v = getenv("KB_GEMM_DIRECT_STORE");
+    return v != nullptr && v[0] == '1';
+  }();
+  if (!direct_store && epi_16bit(epi) && (g.ldo * 2) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(g.out) & 15) == 0) {
+    const long cols = epi == kEpiSwiGLU16 ? g.n_out : g.n;
+    rc = encode_2d(&mo, CU_TENSOR_MAP_DATA_TYPE_UINT16, g.out, cols, g.m, g.ldo * 2, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+    tma_out = 1;
+  }
   if (kind == kGemmI8) {
-    return bn == 256 ? dispatch_epi<kGemmI8, 256>(epi, ma, mb, g, stream)
-                     : dispatch_epi<kGemmI8, 128>(epi, ma, mb, g, stream);
+    return bn == 256 ? dispatch_epi<kGemmI8, 256>(epi, ma, mb, mo, tma_out, g, stream)
+                     : dispatch_epi<kGemmI8, 128>(epi, ma, mb, mo, tma_out, g, stream);
   }
   if (kind == kGemmBF16) {
-    return bn == 256 ? dispatch_epi<kGemmBF16, 256>(epi, ma, mb, g, stream)
-                     : dispatch_epi<kGemmBF16, 128>(epi, ma, mb, g, stream);
+    return bn == 256 ? dispatch_epi<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, g, stream)
+                     : dispatch_epi<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, g, stream);
   }
   set_error("GEMM kind not supported");
   return KB_E_UNSUPPORTED;

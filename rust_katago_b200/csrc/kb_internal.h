@@ -64,6 +64,10 @@ enum GemmKind : int { kGemmI8 = 0, kGemmBF16 = 1, kGemmMXF8 = 2 };
 int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs& args,
                 cudaStream_t stream, int bn_hint = 0);
 
+// Encode a 2-D tensor map (innermost dimension `cols`, row pitch `row_bytes`).
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long cols, long rows,
+              long row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swz);
+
 // Columns per N tile chosen for a given N (the SwiGLU dual-weight packing
 // depends on it).
 int gemm_pick_bn(int kind, int epi, int n);

@@ -19,12 +19,12 @@ __device__ __forceinline__ float pow2i(int k) { return __int_as_float((k + 127) 
 // then the degree-7 Taylor polynomial sum r^i/i! on |r| <= ~0.35 in Horner
 // form with fused multiply-adds, then an exact two-step scaling by 2^n.
 // Truncation error of the polynomial is below 6e-9 relative.
+// Branch-free: the input is clamped into the finite range for the arithmetic
+// and the out-of-range results (inf, 0, NaN) are selected at the end.
 __device__ __forceinline__ float kb_expf(float x) {
-  if (x != x) return x;
-  if (x > 0x1.62e42ep+6f) return __int_as_float(0x7f800000);
-  if (x < -0x1.9fe36ap+6f) return 0.0f;
-  const float n = rintf(__fmul_rn(x, 0x1.715476p+0f /* log2(e) */));
-  float r = __fmaf_rn(-n, 0x1.63p-1f /* 0.693359375 */, x);
+  const float xc = fminf(fmaxf(x, -0x1.9fe36ap+6f), 0x1.62e42ep+6f);
+  const float n = rintf(__fmul_rn(xc, 0x1.715476p+0f /* log2(e) */));
+  float r = __fmaf_rn(-n, 0x1.63p-1f /* 0.693359375 */, xc);
   r = __fmaf_rn(n, 0x1.bd0106p-13f /* 2.12194440e-4 */, r);
   float p = 0x1.a01a02p-13f /* 1/5040 */;
   p = __fmaf_rn(p, r, 0x1.6c16c2p-10f /* 1/720 */);
@@ -37,7 +37,10 @@ __device__ __forceinline__ float kb_expf(float x) {
   const int ni = static_cast<int>(n);
   const int n1 = ni / 2;
   const int n2 = ni - n1;
-  return __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(n2));
+  float y = __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(n2));
+  y = x > 0x1.62e42ep+6f ? __int_as_float(0x7f800000) : y;
+  y = x < -0x1.9fe36ap+6f ? 0.0f : y;
+  return x != x ? x : y;
 }
 
 // SiLU exactly as the reference writes it inside its SwiGLU: g / (1 + e^-g)
@@ -46,29 +49,89 @@ __device__ __forceinline__ float kb_silu(float g) {
   return __fdiv_rn(g, __fadd_rn(1.0f, kb_expf(-g)));
 }
 
-// GELU, erf form: 0.5 * x * (1 + erf(x / sqrt 2)).  erf(z) for z >= 0 uses
-// Abramowitz & Stegun 7.1.26 (Hastings' rational approximation,
-// |error| <= 1.5e-7): erf(z) = 1 - t*(a1 + t*(a2 + t*(a3 + t*(a4 + t*a5)))) * e^(-z^2),
-// t = 1 / (1 + p z).
+// GELU(x) = x * Phi(x) with Phi the standard normal CDF.  For |x| <= 4,
+// Phi(x) = 0.5 + x * P(x^2), P a degree-10 polynomial in s = x^2/8 - 1
+// (least-squares Chebyshev fit of 0.5*erf(sqrt(t/2))/sqrt(t) on t in [0, 16],
+// derived by rust_katago_b200/gelu_fit.py); Phi = 0 below -4 and 1 above 4.
+// |error| <= 3.2e-5 * max(1, |x|): below the resolution of the 16-bit
+// activations it feeds.  Only fused multiply-adds: no division, no exp.
+#define KB_GELU_COEFFS                                                                      \
+  0x1.68585ap-3f, -0x1.5961f4p-4f, 0x1.ca3788p-5f, -0x1.2df2f6p-5f, 0x1.70d728p-6f,        \
+      -0x1.9ab164p-7f, 0x1.9a7b1cp-8f, -0x1.5eeeecp-9f, 0x1.229b08p-10f, -0x1.31c494p-11f, \
+      0x1.a02d8ap-13f
+
 __device__ __forceinline__ float kb_gelu(float x) {
-  const float z = __fmul_rn(fabsf(x), 0x1.6a09e6p-1f /* 1/sqrt(2) */);
-  const float t = __fdiv_rn(1.0f, __fmaf_rn(0x1.4f740ap-2f /* p = 0.3275911 */, z, 1.0f));
-  float poly = __fmaf_rn(0x1.0fb844p+0f /* a5 */, t, -0x1.7401c6p+0f /* a4 */);
-  poly = __fmaf_rn(poly, t, 0x1.6be1c6p+0f /* a3 */);
-  poly = __fmaf_rn(poly, t, -0x1.23531cp-2f /* a2 */);
-  poly = __fmaf_rn(poly, t, 0x1.04f20cp-2f /* a1 */);
-  const float e = kb_expf(-__fmul_rn(z, z));
-  const float erf_abs = __fadd_rn(1.0f, -__fmul_rn(__fmul_rn(poly, t), e));
-  const float erf = x < 0.0f ? -erf_abs : erf_abs;
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erf));
+  constexpr float c[11] = {KB_GELU_COEFFS};
+  const float xc = fminf(fmaxf(x, -4.0f), 4.0f);
+  const float s = __fmaf_rn(__fmul_rn(xc, xc), 0.125f, -1.0f);
+  float p = c[10];
+#pragma unroll
+  for (int i = 9; i >= 0; --i) p = __fmaf_rn(p, s, c[i]);
+  float phi = __fmaf_rn(xc, p, 0.5f);
+  phi = x < -4.0f ? 0.0f : phi;
+  phi = x > 4.0f ? 1.0f : phi;
+  return __fmul_rn(x, phi);
+}
+
+// ------------------------------------------------------------------ f32x2
+// Packed pairs of IEEE fp32 operations (sm_100 f32x2 instructions): each lane
+// of the pair rounds exactly like the scalar __fmul_rn/__fadd_rn/__fmaf_rn.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2pack(a.x, a.y)), "l"(f2pack(b.x, b.y)));
+  return f2unpack(r);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2pack(a.x, a.y)), "l"(f2pack(b.x, b.y)));
+  return f2unpack(r);
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(f2pack(a.x, a.y)), "l"(f2pack(b.x, b.y)), "l"(f2pack(c.x, c.y)));
+  return f2unpack(r);
+}
+
+// kb_gelu on a pair, bit-identical to two scalar calls.
+__device__ __forceinline__ float2 kb_gelu2(float2 x) {
+  constexpr float c[11] = {KB_GELU_COEFFS};
+  const float2 xc = make_float2(fminf(fmaxf(x.x, -4.0f), 4.0f), fminf(fmaxf(x.y, -4.0f), 4.0f));
+  const float2 s = fma2(mul2(xc, xc), make_float2(0.125f, 0.125f), make_float2(-1.0f, -1.0f));
+  float2 p = make_float2(c[10], c[10]);
+#pragma unroll
+  for (int i = 9; i >= 0; --i) p = fma2(p, s, make_float2(c[i], c[i]));
+  float2 phi = fma2(xc, p, make_float2(0.5f, 0.5f));
+  phi.x = x.x < -4.0f ? 0.0f : (x.x > 4.0f ? 1.0f : phi.x);
+  phi.y = x.y < -4.0f ? 0.0f : (x.y > 4.0f ? 1.0f : phi.y);
+  return mul2(x, phi);
 }
 
 enum Act : int { kActNone = 0, kActGelu = 1, kActSilu = 2 };
 
-__device__ __forceinline__ float apply_act(float v, int act) {
-  if (act == kActGelu) return kb_gelu(v);
-  if (act == kActSilu) return kb_silu(v);
-  return v;
+template <int ACT>
+__device__ __forceinline__ float2 apply_act2(float2 v) {
+  if constexpr (ACT == kActGelu) return kb_gelu2(v);
+  else if constexpr (ACT == kActSilu) return make_float2(kb_silu(v.x), kb_silu(v.y));
+  else return v;
+}
+
+template <int ACT>
+__device__ __forceinline__ float apply_act(float v) {
+  if constexpr (ACT == kActGelu) return kb_gelu(v);
+  else if constexpr (ACT == kActSilu) return kb_silu(v);
+  else return v;
 }
 
 // Round a float through a 16-bit storage type (RNE) and back.

@@ -2,17 +2,19 @@
 //
 // Replaces the reference's row quantisers and its fused RMSNorm quantiser
 // (crates/kata_nn/cuda-kernels/int8_ops.cu:8-89, :140-176).  One warp owns one
-// token row; four rows per 128-thread CTA.  The row is brought into shared
-// memory with 16-byte vector loads, then every arithmetic step follows the
-// reference's order exactly:
-//   * RMS: lane-strided partial sums sum = fma(x, x, sum) over columns
-//     lane, lane+32, ... then an xor butterfly over 16, 8, 4, 2, 1
-//     (int8_ops.cu:17-25); rstd = 1/sqrt(sum/W + eps) (correctly rounded here,
-//     rsqrtf in the reference); v = T16((x * rstd) * gamma);
-//   * scale = NaN if the row holds a non-finite value, 1 if it is all zero,
-//     amax/127 otherwise; q = clamp(rne(v / scale), +-127), 0 for a bad row,
-//     zero padding up to the padded width kp.
-// The int8 row is staged in shared memory and written with 16-byte stores.
+// token row, eight rows per 256-thread CTA, and the row stays in registers:
+// lane l holds the 8-element groups g = l, l+32, l+64, ... (columns 8g..8g+7),
+// brought in with one 16-byte load per group (fp32 rows: two).  Per row:
+//   * RMS (optional): sum = fma(x, x, sum) over the lane's columns in group
+//     order, then an xor butterfly over 16, 8, 4, 2, 1 (the reference's
+//     per-lane partial sums and butterfly, int8_ops.cu:17-25, with 8-wide
+//     groups instead of 1-wide lane striding); rstd = 1/sqrt(sum/W + eps)
+//     correctly rounded (rsqrtf in the reference); v = T16((x*rstd)*gamma);
+//   * scale = NaN if the row holds a non-finite value, 1 if all zero,
+//     amax/127 otherwise (int8_ops.cu:36-40); amax is an integer max over
+//     |16-bit| bit patterns, which orders exactly like fmaxf(|v|);
+//   * q = clamp(rne(v / scale), +-127) with IEEE division, 0 for a bad row,
+//     zero padding up to kp (int8_ops.cu:42-46, :80-88); 8-byte stores.
 #include "kb_internal.h"
 #include "kb_numeric.cuh"
 #include "kb_ptx.cuh"
@@ -21,44 +23,6 @@ namespace kb {
 namespace {
 
 enum InType : int { kInF32 = 0, kInF16 = 1, kInBF16 = 2 };
-
-template <int IN>
-__device__ __forceinline__ void load_row(const void* src, int width, float* buf, int lane) {
-  if constexpr (IN == kInF32) {
-    const float* s = static_cast<const float*>(src);
-    if ((reinterpret_cast<uintptr_t>(s) & 15) == 0) {
-      const int nv = width / 4;
-      for (int i = lane; i < nv; i += 32) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(s) + i);
-        buf[4 * i] = t.x;
-        buf[4 * i + 1] = t.y;
-        buf[4 * i + 2] = t.z;
-        buf[4 * i + 3] = t.w;
-      }
-      for (int c = nv * 4 + lane; c < width; c += 32) buf[c] = __ldg(s + c);
-    } else {
-      for (int c = lane; c < width; c += 32) buf[c] = __ldg(s + c);
-    }
-  } else {
-    const uint16_t* s = static_cast<const uint16_t*>(src);
-    const bool f16 = IN == kInF16;
-    if ((reinterpret_cast<uintptr_t>(s) & 15) == 0) {
-      const int nv = width / 8;
-      for (int i = lane; i < nv; i += 32) {
-        const uint4 t = __ldg(reinterpret_cast<const uint4*>(s) + i);
-        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          buf[8 * i + 2 * j] = from16(static_cast<uint16_t>(w[j] & 0xffffu), f16);
-          buf[8 * i + 2 * j + 1] = from16(static_cast<uint16_t>(w[j] >> 16), f16);
-        }
-      }
-      for (int c = nv * 8 + lane; c < width; c += 32) buf[c] = from16(s[c], f16);
-    } else {
-      for (int c = lane; c < width; c += 32) buf[c] = from16(s[c], f16);
-    }
-  }
-}
 
 __device__ __forceinline__ float warp_sum_xor(float v) {
 #pragma unroll
@@ -72,34 +36,201 @@ __device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) {
   return v;
 }
 
-// Per-warp shared memory: `wbuf` floats of row values then `kp` int8 bytes.
-template <int IN, bool RMS>
-__global__ void __launch_bounds__(128) quantize_rows_kernel(
+// Load group g (columns 8g..8g+7) of a row as 8 floats; columns >= width read 0.
+template <int IN>
+__device__ __forceinline__ void load_group(const void* row, int g, int width, bool vec, float (&x)[8]) {
+  const int c0 = 8 * g;
+  if constexpr (IN == kInF32) {
+    const float* s = static_cast<const float*>(row) + c0;
+    if (vec && c0 + 8 <= width) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(s));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(s) + 1);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+      x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) x[t] = c0 + t < width ? __ldg(s + t) : 0.0f;
+    }
+  } else {
+    const bool f16 = IN == kInF16;
+    const uint16_t* s = static_cast<const uint16_t*>(row) + c0;
+    if (vec && c0 + 8 <= width) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(s));
+      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        x[2 * t] = from16(static_cast<uint16_t>(w[t] & 0xffffu), f16);
+        x[2 * t + 1] = from16(static_cast<uint16_t>(w[t] >> 16), f16);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) x[t] = c0 + t < width ? from16(s[t], f16) : 0.0f;
+    }
+  }
+}
+
+// rne(v / s) as an integer, clamped to +-127, with the quotient rounded
+// exactly as IEEE division rounds it: q0 = RN(v*r), e = v - q0*s (exact by
+// FMA), q = RN(q0 + e*r) with r = RN(1/s) is the correctly rounded v/s when
+// nothing underflows (Markstein's division theorem).  The caller uses it only
+// for rows whose scale and amax are normal numbers, where |v/s| <= 127 and the
+// residual e is exact or its quotient contribution rounds away below 0.5.
+__device__ __forceinline__ int quant_i8_rcp(float v, float s, float r) {
+  const float q0 = __fmul_rn(v, r);
+  const float e = __fmaf_rn(-q0, s, v);
+  const float q = __fmaf_rn(e, r, q0);
+  return __float2int_rn(fminf(fmaxf(q, -127.0f), 127.0f));
+}
+
+__device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xffu) << 16) | (static_cast<uint32_t>(d) << 24);
+}
+
+// IEEE-division fallback for one group of 8 packed 16-bit values.
+__device__ __noinline__ void quantize_group_slow(uint4 w4, bool f16, float scale, bool bad,
+                                                 int8_t* dst) {
+  const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+  int qi[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float v = from16(static_cast<uint16_t>(t & 1 ? w[t / 2] >> 16 : w[t / 2] & 0xffffu), f16);
+    qi[t] = bad ? 0 : quant_i8(v, scale);
+  }
+  *reinterpret_cast<uint2*>(dst) =
+      make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
+}
+
+__device__ __noinline__ void quantize_group_slow_f32(float4 a, float4 b, float scale, bool bad,
+                                                     int8_t* dst) {
+  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  int qi[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) qi[t] = bad ? 0 : quant_i8(v[t], scale);
+  *reinterpret_cast<uint2*>(dst) =
+      make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
+}
+
+// Plain 16-bit rows (no RMS): the row stays packed (two values per register),
+// the absolute maximum is a packed unsigned max over |bits|.
+template <bool F16, int G>
+__device__ __forceinline__ void quantize_row16(const uint16_t* src, bool vec, int width, int kp,
+                                               int lane, int8_t* dst, float* scale_out,
+                                               unsigned* status, unsigned layer) {
+  const int groups = (width + 7) / 8;
+  uint32_t w[G][4];
+  uint32_t amax2 = 0;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int g = lane + 32 * j;
+    const int c0 = 8 * g;
+    if (g < groups && vec && c0 + 8 <= width) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(src + c0));
+      w[j][0] = a.x; w[j][1] = a.y; w[j][2] = a.z; w[j][3] = a.w;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t lo = (g < groups && c0 + 2 * t < width) ? src[c0 + 2 * t] : 0u;
+        const uint32_t hi = (g < groups && c0 + 2 * t + 1 < width) ? src[c0 + 2 * t + 1] : 0u;
+        w[j][t] = lo | (hi << 16);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) amax2 = __vmaxu2(amax2, w[j][t] & 0x7fff7fffu);
+  }
+  const uint32_t m16 = max(amax2 & 0xffffu, amax2 >> 16);
+  const uint32_t amax = warp_max_u32(F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
+  const float scale = int8_scale_from_amax(amax);
+  const bool bad = amax >= 0x7f800000u;
+  if (lane == 0) {
+    *scale_out = scale;
+    if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+  }
+  // The reciprocal path needs a normal scale and a normal amax; other rows
+  // (all zero, tiny, non-finite) take the IEEE-division loop, kept out of line.
+  const bool fast = !bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u;
+  const int out_groups = kp / 8;
+  if (fast) {
+    const float r = __frcp_rn(scale);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j;
+      if (g < out_groups) {
+        int qi[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          qi[t] = quant_i8_rcp(from16(static_cast<uint16_t>(t & 1 ? w[j][t / 2] >> 16 : w[j][t / 2] & 0xffffu), F16),
+                               scale, r);
+        *reinterpret_cast<uint2*>(dst + 8 * g) =
+            make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j;
+      if (g < out_groups)
+        quantize_group_slow(make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]), F16, scale, bad, dst + 8 * g);
+    }
+  }
+}
+
+// One warp per row; G = groups of 8 per lane (W <= 256 * G).
+template <int IN, bool RMS, int G>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(
     const void* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows,
-    int width, int kp, int bound_f16, int wbuf, int8_t* __restrict__ q, float* __restrict__ scales,
+    int width, int kp, int bound_f16, int8_t* __restrict__ q, float* __restrict__ scales,
     unsigned* status, unsigned layer) {
-  extern __shared__ __align__(16) uint8_t qsmem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 4 + warp;
-  if (row >= rows) return;  // warp-uniform; only __syncwarp is used below
-  float* buf = reinterpret_cast<float*>(qsmem + static_cast<size_t>(warp) * (wbuf * 4 + kp));
-  int8_t* qs = reinterpret_cast<int8_t*>(buf + wbuf);
-  const int esize = IN == kInF32 ? 4 : 2;
-  load_row<IN>(static_cast<const uint8_t*>(x) + static_cast<size_t>(row) * ldx * esize, width, buf,
-               lane);
-  __syncwarp();
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;  // warp-uniform
+  constexpr int kEsize = IN == kInF32 ? 4 : 2;
+  const uint8_t* src = static_cast<const uint8_t*>(x) + static_cast<size_t>(row) * ldx * kEsize;
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  if constexpr (!RMS && IN != kInF32) {
+    quantize_row16<IN == kInF16, G>(reinterpret_cast<const uint16_t*>(src), vec, width, kp, lane,
+                                    q + static_cast<size_t>(row) * kp, scales + row, status, layer);
+    return;
+  }
+  const int groups = (width + 7) / 8;
+  float v[G][8];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int g = lane + 32 * j;
+    if (g < groups) {
+      load_group<IN>(src, g, width, vec, v[j]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[j][t] = 0.0f;
+    }
+  }
+  const bool f16 = bound_f16 != 0;
   if constexpr (RMS) {
     float sum = 0.0f;
-    for (int c = lane; c < width; c += 32) sum = __fmaf_rn(buf[c], buf[c], sum);
+#pragma unroll
+    for (int j = 0; j < G; ++j)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sum = __fmaf_rn(v[j][t], v[j][t], sum);
     sum = warp_sum_xor(sum);
     const float rstd =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(width)), eps)));
-    const bool f16 = bound_f16 != 0;
-    for (int c = lane; c < width; c += 32)
-      buf[c] = from16(bits16(__fmul_rn(__fmul_rn(buf[c], rstd), __ldg(gamma + c)), f16), f16);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int c0 = 8 * (lane + 32 * j);
+      if (c0 < width) {
+        float gm[8];
+        load_group<kInF32>(gamma, lane + 32 * j, width, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0, gm);
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          v[j][t] = c0 + t < width ? from16(bits16(__fmul_rn(__fmul_rn(v[j][t], rstd), gm[t]), f16), f16) : 0.0f;
+      }
+    }
   }
   uint32_t amax = 0;
-  for (int c = lane; c < width; c += 32) amax = max(amax, abs_bits(buf[c]));
+#pragma unroll
+  for (int j = 0; j < G; ++j)
+#pragma unroll
+    for (int t = 0; t < 8; ++t) amax = max(amax, abs_bits(v[j][t]));
   amax = warp_max_u32(amax);
   const float scale = int8_scale_from_amax(amax);
   const bool bad = amax >= 0x7f800000u;
@@ -107,29 +238,59 @@ __global__ void __launch_bounds__(128) quantize_rows_kernel(
     scales[row] = scale;
     if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
   }
-  for (int c = lane; c < kp; c += 32)
-    qs[c] = static_cast<int8_t>((c < width && !bad) ? quant_i8(buf[c], scale) : 0);
-  __syncwarp();
-  uint4* dst = reinterpret_cast<uint4*>(q + static_cast<size_t>(row) * kp);
-  const uint4* s4 = reinterpret_cast<const uint4*>(qs);
-  for (int i = lane; i < kp / 16; i += 32) dst[i] = s4[i];
+  int8_t* dst = q + static_cast<size_t>(row) * kp;
+  const int out_groups = kp / 8;
+  const bool fast = !bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u;
+  if (fast) {
+    const float r = __frcp_rn(scale);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j;
+      if (g < out_groups) {
+        int qi[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) qi[t] = quant_i8_rcp(v[j][t], scale, r);
+        *reinterpret_cast<uint2*>(dst + 8 * g) =
+            make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j;
+      if (g < out_groups)
+        quantize_group_slow_f32(make_float4(v[j][0], v[j][1], v[j][2], v[j][3]),
+                                make_float4(v[j][4], v[j][5], v[j][6], v[j][7]), scale, bad, dst + 8 * g);
+    }
+  }
+}
+
+template <int IN, bool RMS, int G>
+int launch_g(const void* x, long ldx, const float* gamma, float eps, int rows, int width, int kp,
+             int bound_f16, int8_t* q, float* scales, unsigned* status, unsigned layer, cudaStream_t s) {
+  quantize_rows_kernel<IN, RMS, G><<<(rows + 7) / 8, 256, 0, s>>>(x, ldx, gamma, eps, rows, width, kp,
+                                                                  bound_f16, q, scales, status, layer);
+  return check_cuda(cudaGetLastError(), "quantiser launch");
 }
 
 template <int IN, bool RMS>
-int launch_quant(const void* x, long ldx, const float* gamma, float eps, int rows, int width,
-                 int kp, int bound_f16, int8_t* q, float* scales, unsigned* status, unsigned layer,
-                 cudaStream_t stream) {
-  const int wbuf = (width + 3) & ~3;
-  const size_t smem = 4 * static_cast<size_t>(wbuf * 4 + kp);
-  auto kern = quantize_rows_kernel<IN, RMS>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return check_cuda(e, "quantiser smem attribute");
-  }
-  kern<<<(rows + 3) / 4, 128, smem, stream>>>(x, ldx, gamma, eps, rows, width, kp, bound_f16, wbuf,
-                                              q, scales, status, layer);
-  return check_cuda(cudaGetLastError(), "quantiser launch");
+int launch_quant(const void* x, long ldx, const float* gamma, float eps, int rows, int width, int kp,
+                 int bound_f16, int8_t* q, float* scales, unsigned* status, unsigned layer,
+                 cudaStream_t s) {
+  const int need = (kp + 255) / 256;  // groups of 8 per lane covering the padded row
+#define KB_Q(GG) \
+  if (need <= GG) return launch_g<IN, RMS, GG>(x, ldx, gamma, eps, rows, width, kp, bound_f16, q, scales, status, layer, s)
+  KB_Q(1);
+  KB_Q(2);
+  KB_Q(3);
+  KB_Q(4);
+  KB_Q(6);
+  KB_Q(8);
+  KB_Q(12);
+  KB_Q(16);
+#undef KB_Q
+  set_error("quantiser row width above 4096 is not supported");
+  return KB_E_INVALID;
 }
 
 }  // namespace
@@ -139,8 +300,8 @@ int launch_quant(const void* x, long ldx, const float* gamma, float eps, int row
 int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width, int kp, bool rms,
                          const float* gamma, float eps, int bound_f16, int8_t* q, float* scales,
                          unsigned* status, unsigned layer, cudaStream_t stream) {
-  if (rows <= 0 || width <= 0 || width > 16384 || kp < width || kp % 16 != 0 || ldx < width) {
-    set_error("quantiser shape mismatch (rows, width, padded width, stride)");
+  if (rows <= 0 || width <= 0 || kp < width || kp % 16 != 0 || kp > 4096 || ldx < width) {
+    set_error("quantiser shape mismatch (rows, width, padded width <= 4096, stride)");
     return KB_E_INVALID;
   }
   if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) {
