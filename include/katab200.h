@@ -174,6 +174,23 @@ KB_API int kb_int8_ffn_gelu_rms(kb_int8_workspace* ws, uintptr_t stream, const f
                          const kb_int8_weight* down, const float* down_bias, uint16_t* residual,
                          int rows);
 
+/* The same GELU FFN block as kb_int8_ffn_gelu_rms, for callers that cannot
+ * allocate device memory where they evaluate (a search thread evaluating a few
+ * positions mid-move, where cudaMalloc may synchronise the device; a host that
+ * owns all device memory under a fixed budget).  It takes no workspace and
+ * allocates nothing: its scratch is one static 8 MiB device array per device
+ * (reserved when the library is loaded, held until exit), so `rows` is limited
+ * to what fits (about 900 tokens, 2 positions, for C=768, F=3072); larger
+ * calls fail with KB_E_INVALID and say the limit.  The first call on each
+ * device looks the array's address up (cudaGetSymbolAddress) and should come
+ * before any stream capture.  All calls on a device share the array: calls
+ * that overlap on the GPU race; nothing in it needs clearing between calls.
+ * No counterpart in the reference. */
+KB_API int kb_int8_ffn_gelu_rms_noalloc(uintptr_t stream, const float* gamma, float eps,
+                                        const kb_int8_weight* up, const float* up_bias,
+                                        const kb_int8_weight* down, const float* down_bias,
+                                        uint16_t* residual, int rows);
+
 /* ------------------------------------------------------------------ bf16 GEMM */
 
 /* out = a[m,k] (bf16) * w[n,k]^T (bf16) with fp32 accumulation on tcgen05

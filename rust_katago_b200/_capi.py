@@ -40,6 +40,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_int8_ffn": (I, [P, STREAM, P, P, P, P, I]),
     "kb_int8_ffn_rms": (I, [P, STREAM, P, F, P, P, P, I]),
     "kb_int8_ffn_gelu_rms": (I, [P, STREAM, P, F, P, P, P, P, P, I]),
+    "kb_int8_ffn_gelu_rms_noalloc": (I, [STREAM, P, F, P, P, P, P, P, I]),
     "kb_bf16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
 }
 

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "../../include/katab200.h"
+#include "kb_handles.h"
 #include "kb_internal.h"
 
 namespace kb {
@@ -19,13 +20,6 @@ int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width
 }
 
 using namespace kb;
-
-struct kb_int8_weight {
-  int device = 0;
-  int n = 0, k = 0, kp = 0, n_stored = 0, layout = 0;
-  int8_t* q = nullptr;
-  float* scales = nullptr;
-};
 
 struct kb_int8_workspace {
   int device = 0;

@@ -132,6 +132,14 @@ class Int8Workspace:
              _ptr(gamma), eps, up.handle, _ptr(up_bias), down.handle, _ptr(down_bias), _ptr(residual_bf16), rows)
 
 
+def ffn_gelu_rms_noalloc(gamma, eps: float, up: Int8Weight, up_bias, down: Int8Weight, down_bias, residual_bf16,
+                         rows: int, stream=None):
+    """GELU FFN block without a workspace: scratch is a fixed static device
+    array (at most ~900 tokens for C=768, F=3072); calls overlapping on the GPU race."""
+    call("kb_int8_ffn_gelu_rms_noalloc", _stream(stream), _ptr(gamma), eps, up.handle, _ptr(up_bias), down.handle,
+         _ptr(down_bias), _ptr(residual_bf16), rows)
+
+
 # ------------------------------------------------------------------ kernel-level calls
 def gemm_i32(a, w, dots, m: int, n: int, kp: int, stream=None):
     call("kb_int8_gemm_i32", _ptr(a), _ptr(w), _ptr(dots), m, n, kp, _stream(stream))
