@@ -200,6 +200,105 @@ KB_API int kb_int8_ffn_gelu_rms_noalloc(uintptr_t stream, const float* gamma, fl
 KB_API int kb_bf16_linear(const uint16_t* a, const uint16_t* w, const float* bias, int m, int n, int k,
                    int epilogue, int act, int out_dtype, void* out, int ldo, uintptr_t stream);
 
+/* ------------------------------------------------------------------ attention */
+
+/* Multi-head attention over the 361 board tokens with RoPE on Q and K:
+ * qkv [batch*361, 3*heads*head_dim] ([Q | K | V], 16-bit, dtype KB_DT_BF16 or
+ * KB_DT_F16), rope_cos/rope_sin fp32 [361, heads, head_dim/2] (interleaved
+ * pairs), out [batch*361, heads*head_dim]; softmax(q.k * scale) over all keys.
+ * head_dim 32 or 64.  Replaces: attention_fa2_q64_kernel
+ * (cuda-kernels/attention_fa2_q64.cu:82-390) via cuda_exec.rs:3442. */
+KB_API int kb_attention(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
+                        int batch, int heads, int head_dim, float scale, int dtype, uintptr_t stream);
+
+/* ------------------------------------------------------------------ model and evaluator */
+
+#define KB_PREC_INT8 0 /* W8A8: every trunk linear INT8 x INT8 -> INT32 */
+
+/* Trunk shape (BASELINE b11c768: C=768, 11 blocks, 12 heads x 64, F=3072). */
+typedef struct kb_model_desc {
+  int trunk_channels; /* C; multiple of 64, <= 4096 */
+  int num_blocks;     /* 1..64 */
+  int num_heads;      /* heads * head_dim == C */
+  int head_dim;       /* 32 or 64 */
+  int ffn_channels;   /* F; multiple of 64, <= 4096 */
+  int precision;      /* KB_PREC_INT8 */
+} kb_model_desc;
+
+/* Weight blob: fp32, out-first [N, K] row-major matrices, in this order:
+ *   stem [C, 217]: 3x3 conv taps (ic*9 + ky*3 + kx, 22 input planes) then the
+ *                  19 global-input weights;
+ *   per block: rms1 [C], qkv [3C, C] ([Q; K; V]), out [C, C], rms2 [C],
+ *              up [F, C], up_bias [F], down [C, F], down_bias [C],
+ *              rope_freqs [heads, head_dim/2, 2] (x, y frequency per pair);
+ *   trunk tip: gamma [C], beta [C];
+ *   heads: p1 [96, C], g1 [96, C], g1_bias [96], v1 [192, C], v1_bias [192],
+ *          gpool_to_bias [96, 288], pass1 [96, 288], pass1_bias [96], pass2 [6, 96],
+ *          bias2 [96], conv2p [6, 96], v2 [192, 576], v2_bias [192], value [3, 192],
+ *          value_bias [3], misc [10, 192], misc_bias [10], moremisc [8, 192],
+ *          moremisc_bias [8], ownership [192].
+ * Same roles as the reference's LayerGraph layers (src/native_model.rs:21-165,
+ * tests/debug_exec_units.rs:101-380). */
+KB_API int kb_model_blob_floats(const kb_model_desc* desc, size_t* count);
+
+typedef struct kb_model kb_model;
+typedef struct kb_handle kb_handle;
+
+/* Quantise and upload a model to `device`.
+ * Replaces: CudaBackend::load_model_file + the deferred upload
+ * (src/backends/cuda.rs:2618-2680, cuda_exec.rs:674-815). */
+KB_API int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, int device,
+                         kb_model** out);
+KB_API void kb_model_destroy(kb_model* model);
+
+/* A compute handle: one stream, a workspace for max_batch positions, two
+ * pipeline slots with pinned staging.  Not thread-safe: one thread per handle.
+ * Replaces: CudaBackend::create_compute_handle (src/backends/cuda.rs:2926). */
+KB_API int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle** out);
+KB_API void kb_handle_destroy(kb_handle* handle);
+KB_API int kb_handle_stream(kb_handle* handle, uintptr_t* stream);
+
+/* Run forwards for each batch size once uncaptured and once captured into a
+ * CUDA graph.  Replaces: Backend::warmup_batches (backend.rs:206-410). */
+KB_API int kb_warmup(kb_handle* handle, const int* batches, int count);
+
+/* Asynchronous evaluation of n positions from host memory: spatial fp32
+ * [n, 22, 19, 19] (NCHW, or [n, 19, 19, 22] if the handle is NHWC), global
+ * fp32 [n, 19].  Returns a token.  Replaces: Backend::submit_output
+ * (cuda.rs:2196-2480). */
+KB_API int kb_submit(kb_handle* handle, int n, const float* spatial, const float* global,
+                     uint64_t* token);
+
+/* 1 if the token's outputs are ready, 0 if not, negative KB_E_* on error.
+ * Replaces: Backend::query_output_done. */
+KB_API int kb_query(kb_handle* handle, uint64_t token);
+
+/* Wait for a token and copy its raw outputs (no final activation, like the
+ * reference): policy [n, 6, 362], value [n, 3], misc [n, 10], moremisc [n, 8],
+ * ownership [n, 361] (any may be NULL).  status receives the sticky status word;
+ * if it holds any flag the outputs are withheld and KB_E_NONFINITE returned.
+ * Replaces: Backend::finish_output (cuda.rs:2510). */
+KB_API int kb_finish(kb_handle* handle, uint64_t token, float* policy, float* value, float* misc,
+                     float* moremisc, float* ownership, uint32_t status[2]);
+
+/* Device-resident forward on the handle's stream (inputs and the packed
+ * output [policy | value | misc | moremisc | ownership] in device memory),
+ * optionally through the per-batch-size CUDA graph.
+ * Replaces: CudaModel::apply (src/backends/cuda_exec.rs:913). */
+KB_API int kb_forward_device(kb_handle* handle, int n, const float* d_spatial, const float* d_global,
+                             float* d_out, int use_graph);
+
+/* kb_forward_device without a graph that also copies intermediates into
+ * d_trace, bf16 [(num_blocks + 2), n*361, C]: the stem output, each block's
+ * attention output, the final residual stream (for parity tests and debugging;
+ * plays the role of the reference's per-layer debug runs, tests/debug_exec_units.rs). */
+KB_API int kb_forward_trace(kb_handle* handle, int n, const float* d_spatial, const float* d_global,
+                            float* d_out, uint16_t* d_trace);
+
+/* Synchronise the handle's stream and read its status word [flags, first_layer].
+ * Replaces: mxfp8.rs validate_completed_status (:1181). */
+KB_API int kb_read_status(kb_handle* handle, uint32_t status[2]);
+
 #ifdef __cplusplus
 }
 #endif

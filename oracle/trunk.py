@@ -1,0 +1,190 @@
+"""CPU restatement of the full trunk forward — TEST INFRASTRUCTURE ONLY.
+
+Follows the reference's CPU restatement of every LayerGraph layer
+(Rust_KataGo crates/kata_nn/tests/debug_exec_units.rs:84-380) on the
+BASELINE b11c768 topology, with the INT8 linears through the C oracle
+(quantize_weights / rms_quantize / quantize_rows / igemm / dequant, bit-exact
+restatements of the reference's W8A8 arithmetic) and the same 16-bit rounding
+points as the product: bf16 residual stream, bf16 QKV / attention output /
+FFN hidden, bf16-rounded stem and head weights.
+
+What cannot be reproduced bit for bit, and is therefore compared with a
+tolerance: the fp32 accumulation order of the bf16 tensor-core GEMMs (stem,
+head linears) and of the attention kernel (which also rounds P to bf16 for
+the P.V product); the oracle accumulates those in float64.
+
+The weight blob is parsed here independently of the product's parser, from
+the layout documented in include/katab200.h (kb_model_blob_floats).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import bf16_encode, decode16, dequant, igemm, quantize_rows, quantize_weights, rms_quantize, round16
+
+SEQ, SIDE = 361, 19
+EPS = 1e-6
+
+
+def _sections(c, nb, nh, hd, f):
+    secs = [("stem", (c, 217))]
+    for i in range(nb):
+        secs += [(f"{i}.rms1", (c,)), (f"{i}.qkv", (3 * c, c)), (f"{i}.out", (c, c)), (f"{i}.rms2", (c,)),
+                 (f"{i}.up", (f, c)), (f"{i}.up_b", (f,)), (f"{i}.down", (c, f)), (f"{i}.down_b", (c,)),
+                 (f"{i}.rope", (nh, hd // 2, 2))]
+    secs += [("tip_g", (c,)), ("tip_b", (c,)), ("p1", (96, c)), ("g1", (96, c)), ("g1_b", (96,)),
+             ("v1", (192, c)), ("v1_b", (192,)), ("gm", (96, 288)), ("pass1", (96, 288)), ("pass1_b", (96,)),
+             ("pass2", (6, 96)), ("bias2", (96,)), ("conv2p", (6, 96)), ("v2", (192, 576)), ("v2_b", (192,)),
+             ("value", (3, 192)), ("value_b", (3,)), ("misc", (10, 192)), ("misc_b", (10,)),
+             ("moremisc", (8, 192)), ("moremisc_b", (8,)), ("own", (192,))]
+    return secs
+
+
+def parse(blob, c, nb, nh, hd, f):
+    w, off = {}, 0
+    for name, shape in _sections(c, nb, nh, hd, f):
+        k = int(np.prod(shape))
+        w[name] = np.asarray(blob[off:off + k], np.float32).reshape(shape)
+        off += k
+    if off != blob.size:
+        raise ValueError("blob size does not match the topology")
+    return w
+
+
+def bf(x):
+    """Round float32 values through bf16."""
+    return round16(np.asarray(x, np.float32), False)
+
+
+def silu64(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def stem_inputs(spatial, glob):
+    """[n*361, 217]: 3x3 taps (ic*9 + ky*3 + kx, zero padded) then 19 globals (debug_exec_units.rs:101-129)."""
+    n = spatial.shape[0]
+    pad = np.zeros((n, 22, SIDE + 2, SIDE + 2), np.float32)
+    pad[:, :, 1:-1, 1:-1] = spatial
+    taps = np.zeros((n, SIDE, SIDE, 22, 3, 3), np.float32)
+    for ky in range(3):
+        for kx in range(3):
+            taps[:, :, :, :, ky, kx] = pad[:, :, ky:ky + SIDE, kx:kx + SIDE].transpose(0, 2, 3, 1)
+    a = np.concatenate([taps.reshape(n, SEQ, 22 * 9), np.repeat(glob[:, None, :], SEQ, axis=1)], axis=2)
+    return a.reshape(n * SEQ, 217)
+
+
+def rope_tables(freqs):
+    """cos/sin [361, heads, pairs]: angle = x*f0 + y*f1 in float32 (native_model.rs:200-228)."""
+    nh, pairs, _ = freqs.shape
+    cs = np.zeros((SEQ, nh, pairs), np.float32)
+    sn = np.zeros_like(cs)
+    for y in range(SIDE):
+        for x in range(SIDE):
+            ang = (np.float32(x) * freqs[:, :, 0]).astype(np.float32) + (np.float32(y) * freqs[:, :, 1]).astype(np.float32)
+            ang = ang.astype(np.float32)
+            t = y * SIDE + x
+            cs[t] = np.cos(ang.astype(np.float64)).astype(np.float32)
+            sn[t] = np.sin(ang.astype(np.float64)).astype(np.float32)
+    return cs, sn
+
+
+def attention(qkv, cs, sn, n, nh, hd):
+    """Softmax attention per (position, head) with RoPE on Q and K
+    (debug_exec_units.rs:161-242; the kernel rounds rotated Q/K to bf16)."""
+    c = nh * hd
+    x = qkv.reshape(n, SEQ, 3, nh, hd)
+    q, k, v = x[:, :, 0], x[:, :, 1], x[:, :, 2]
+
+    def rot(t):
+        a, b = t[..., 0::2], t[..., 1::2]
+        ra = (a * cs[None]).astype(np.float32) - (b * sn[None]).astype(np.float32)
+        rb = (a * sn[None]).astype(np.float32) + (b * cs[None]).astype(np.float32)
+        out = np.empty_like(t)
+        out[..., 0::2] = ra
+        out[..., 1::2] = rb
+        return bf(out)
+
+    q, k = rot(q).astype(np.float64), rot(k).astype(np.float64)
+    v = v.astype(np.float64)
+    s = np.einsum("bqhd,bkhd->bhqk", q, k) / math.sqrt(hd)
+    s -= s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    o = np.einsum("bhqk,bkhd->bqhd", p, v)
+    return bf(o.reshape(n * SEQ, c).astype(np.float32))
+
+
+def forward(blob, topo, spatial, glob, teacher=None):
+    """Returns dict(policy [n,6,362], value [n,3], misc [n,10], moremisc [n,8],
+    ownership [n,361], residual [n*361, C]).
+
+    teacher: optional (stem [n*361, C], [attention [n*361, C] per block]) float
+    arrays that replace the oracle's own stem GEMM and attention results — the
+    two steps whose fp32 accumulation order cannot be reproduced on the CPU —
+    so that every other step can be compared bit for bit."""
+    c, nb, nh, hd, f = topo
+    w = parse(blob, c, nb, nh, hd, f)
+    n = spatial.shape[0]
+    if teacher is not None:
+        x = np.asarray(teacher[0], np.float32)
+    else:
+        a = bf(stem_inputs(spatial, glob)).astype(np.float64)
+        x = bf((a @ bf(w["stem"]).astype(np.float64).T).astype(np.float32))
+    for i in range(nb):
+        cs, sn = rope_tables(w[f"{i}.rope"])
+        qw, qs = quantize_weights(w[f"{i}.qkv"])
+        ow, os_ = quantize_weights(w[f"{i}.out"])
+        uw, us = quantize_weights(w[f"{i}.up"])
+        dw, ds = quantize_weights(w[f"{i}.down"])
+        q, sa, _ = rms_quantize(x, w[f"{i}.rms1"], EPS, False, kp=qw.shape[1])
+        qkv = bf(dequant(igemm(q, qw), sa, qs))
+        att = attention(qkv, cs, sn, n, nh, hd) if teacher is None else np.asarray(teacher[1][i], np.float32)
+        q2, s2 = quantize_rows(att, kp=ow.shape[1])
+        x = bf((x + dequant(igemm(q2, ow), s2, os_)).astype(np.float32))
+        q3, s3, _ = rms_quantize(x, w[f"{i}.rms2"], EPS, False, kp=uw.shape[1])
+        v = (dequant(igemm(q3, uw), s3, us) + w[f"{i}.up_b"][None, :]).astype(np.float32)
+        from . import act
+
+        hidden = bf(act(v, 1))
+        q4, s4 = quantize_rows(hidden, kp=dw.shape[1])
+        d = (dequant(igemm(q4, dw), s4, ds) + w[f"{i}.down_b"][None, :]).astype(np.float32)
+        x = bf((x + d).astype(np.float32))
+    # trunk tip: silu(x*gamma + beta) (debug_exec_units.rs:272-282)
+    from . import act
+
+    g = bf(act(((x * w["tip_g"][None, :]).astype(np.float32) + w["tip_b"][None, :]).astype(np.float32), 2))
+    g64 = g.astype(np.float64)
+    hp = np.concatenate([g64 @ bf(w["p1"]).astype(np.float64).T,
+                         g64 @ bf(w["g1"]).astype(np.float64).T + w["g1_b"],
+                         g64 @ bf(w["v1"]).astype(np.float64).T + w["v1_b"]], axis=1).reshape(n, SEQ, 384)
+    out = heads(hp, w, n)
+    out["residual"] = x
+    return out
+
+
+def heads(hp, w, n):
+    """PolicyHead / ValueHead (debug_exec_units.rs:283-380) in float64."""
+    p1, g1, v1 = hp[..., :96], hp[..., 96:192], hp[..., 192:]
+    ga = silu64(g1)
+    mean = ga.mean(axis=1)
+    pooled = np.concatenate([mean, mean * 0.5, ga.max(axis=1)], axis=1)  # [n, 288]
+    pass1 = silu64(pooled @ w["pass1"].T.astype(np.float64) + w["pass1_b"])
+    pass2 = pass1 @ w["pass2"].T.astype(np.float64)  # [n, 6]
+    gproj = pooled @ w["gm"].T.astype(np.float64) + w["bias2"]
+    pa = silu64(p1 + gproj[:, None, :])
+    moves = pa @ w["conv2p"].T.astype(np.float64)  # [n, 361, 6]
+    policy = np.zeros((n, 6, 362))
+    policy[:, :, :361] = moves.transpose(0, 2, 1)
+    policy[:, :, 361] = pass2
+    va = silu64(v1)
+    vm = va.mean(axis=1)
+    pooled_v = np.concatenate([vm, vm * 0.5, vm * 0.15], axis=1)  # [n, 576]
+    hid = silu64(pooled_v @ w["v2"].T.astype(np.float64) + w["v2_b"])
+    value = hid @ w["value"].T.astype(np.float64) + w["value_b"]
+    misc = hid @ w["misc"].T.astype(np.float64) + w["misc_b"]
+    more = hid @ w["moremisc"].T.astype(np.float64) + w["moremisc_b"]
+    own = va @ w["own"].astype(np.float64)
+    return {"policy": policy, "value": value, "misc": misc, "moremisc": more, "ownership": own}

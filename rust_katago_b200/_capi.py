@@ -42,7 +42,28 @@ SIGNATURES: dict[str, tuple] = {
     "kb_int8_ffn_gelu_rms": (I, [P, STREAM, P, F, P, P, P, P, P, I]),
     "kb_int8_ffn_gelu_rms_noalloc": (I, [STREAM, P, F, P, P, P, P, P, I]),
     "kb_bf16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
+    "kb_attention": (I, [P, P, P, P, I, I, I, F, I, STREAM]),
+    "kb_model_blob_floats": (I, [P, ctypes.POINTER(ctypes.c_size_t)]),
+    "kb_model_load": (I, [P, P, ctypes.c_size_t, I, PP]),
+    "kb_model_destroy": (None, [P]),
+    "kb_handle_create": (I, [P, I, I, PP]),
+    "kb_handle_destroy": (None, [P]),
+    "kb_handle_stream": (I, [P, ctypes.POINTER(ctypes.c_size_t)]),
+    "kb_warmup": (I, [P, ctypes.POINTER(ctypes.c_int), I]),
+    "kb_submit": (I, [P, I, P, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "kb_query": (I, [P, ctypes.c_uint64]),
+    "kb_finish": (I, [P, ctypes.c_uint64, P, P, P, P, P, ctypes.POINTER(ctypes.c_uint32)]),
+    "kb_forward_device": (I, [P, I, P, P, P, I]),
+    "kb_read_status": (I, [P, ctypes.POINTER(ctypes.c_uint32)]),
+    "kb_forward_trace": (I, [P, I, P, P, P, P]),
 }
+
+
+class ModelDesc(ctypes.Structure):
+    """kb_model_desc."""
+
+    _fields_ = [("trunk_channels", ctypes.c_int), ("num_blocks", ctypes.c_int), ("num_heads", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("ffn_channels", ctypes.c_int), ("precision", ctypes.c_int)]
 
 # Constants mirrored from include/katab200.h.
 KB_OK, KB_E_INVALID, KB_E_CUDA, KB_E_STATE, KB_E_NONFINITE, KB_E_UNSUPPORTED = range(6)

@@ -1,0 +1,785 @@
+// Model, compute handle and trunk sequencer behind the evaluator C ABI.
+//
+// Mirrors the reference's CUDA backend boundary (crates/kata_nn/src/backend.rs:
+// 206-410, implemented by CudaBackend in src/backends/cuda.rs:2610-3105):
+//   kb_model_load        ~ load_model_file + the deferred weight upload
+//                          (cuda.rs:2618-2680, cuda_exec.rs:674-815, int8.rs:222)
+//   kb_handle_create     ~ create_compute_handle (cuda.rs:2926): one stream,
+//                          one workspace per physical batch, two pipeline slots
+//   kb_submit / kb_query / kb_finish ~ submit_output / query_output_done /
+//                          finish_output (cuda.rs:2196-2510): pinned staging,
+//                          H2D, a CUDA graph per batch size, D2H, event wait,
+//                          sticky status check before outputs are published
+//   kb_forward_device    ~ CudaModel::apply (cuda_exec.rs:913) on device buffers
+//
+// The trunk (BASELINE b11c768 topology): stem (3x3 conv 22->C + global linear,
+// one bf16 GEMM) -> num_blocks x [RMSNorm -> INT8 QKV GEMM -> RoPE attention ->
+// INT8 out-proj + residual -> RMSNorm -> INT8 up GEMM + GELU -> INT8 down GEMM +
+// residual] on a bf16 residual stream -> trunk tip (BN affine + SiLU) -> one
+// bf16 GEMM for all per-token head linears -> policy/value heads.
+#include <math.h>
+#include <string.h>
+
+#include <map>
+#include <mutex>
+#include <new>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/katab200.h"
+#include "kb_handles.h"
+#include "kb_internal.h"
+
+namespace kb {
+int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width, int kp, bool rms,
+                         const float* gamma, float eps, int bound_f16, int8_t* q, float* scales,
+                         unsigned* status, unsigned layer, cudaStream_t stream);
+int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
+                     int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream);
+int stem_gather_launch(const float* spatial, const float* global, uint16_t* a, int batch, int nhwc,
+                       cudaStream_t s);
+int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, uint16_t* g, long rows, int c,
+                     cudaStream_t s);
+int heads_launch(const float* hp, const float* const* wts, float* policy, float* value, float* misc,
+                 float* moremisc, float* ownership, int batch, unsigned* status, cudaStream_t s);
+}  // namespace kb
+
+using namespace kb;
+
+namespace {
+
+constexpr int kSide = 19;
+constexpr int kSeq = 361;
+constexpr int kInC = 22, kInG = 19;
+constexpr int kStemK = 224, kStemKUsed = 217;
+constexpr int kHeadN = 384;  // p1 96 | g1 96 | v1 192
+constexpr float kRmsEps = 1e-6f;
+
+// Host-side view of the fp32 weight blob (layout documented in katab200.h).
+struct BlobCursor {
+  const float* p;
+  size_t left;
+  const float* take(size_t n) {
+    if (n > left) return nullptr;
+    const float* r = p;
+    p += n;
+    left -= n;
+    return r;
+  }
+};
+
+size_t blob_floats(const kb_model_desc& d) {
+  const size_t c = d.trunk_channels, f = d.ffn_channels, h = d.num_heads, hd = d.head_dim;
+  size_t n = c * kStemKUsed;
+  n += d.num_blocks * (c + 3 * c * c + c * c + c + f * c + f + c * f + c + h * (hd / 2) * 2);
+  n += 2 * c;
+  n += 96 * c + 96 * c + 96 + 192 * c + 192;
+  n += 96 * 288 + 96 * 288 + 96 + 6 * 96 + 96 + 6 * 96;
+  n += 192 * 576 + 192 + 3 * 192 + 3 + 10 * 192 + 10 + 8 * 192 + 8 + 192;
+  return n;
+}
+
+int validate_desc(const kb_model_desc* d) {
+  if (!d || d->trunk_channels <= 0 || d->trunk_channels % 64 != 0 || d->trunk_channels > 4096 ||
+      d->num_blocks <= 0 || d->num_blocks > 64 || d->num_heads <= 0 ||
+      (d->head_dim != 32 && d->head_dim != 64) || d->num_heads * d->head_dim != d->trunk_channels ||
+      d->ffn_channels <= 0 || d->ffn_channels % 64 != 0 || d->ffn_channels > 4096 ||
+      d->precision != KB_PREC_INT8) {
+    set_error("model descriptor: need C % 64 == 0 (<= 4096), heads*head_dim == C, head_dim 32|64, "
+              "F % 64 == 0 (<= 4096), 1..64 blocks, precision KB_PREC_INT8");
+    return KB_E_INVALID;
+  }
+  return KB_OK;
+}
+
+template <typename T>
+int dev_alloc(T** p, size_t count, const char* what) {
+  return check_cuda(cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16), what);
+}
+
+template <typename T>
+int upload(T** dst, const T* src, size_t count, const char* what) {
+  int rc = dev_alloc(dst, count, what);
+  if (rc) return rc;
+  return check_cuda(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice), what);
+}
+
+uint16_t bf16_bits(float v) {
+  uint32_t b;
+  memcpy(&b, &v, 4);
+  if ((b & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>(((b >> 16) & 0x8000u) | 0x7fc0u);
+  b += 0x7fffu + ((b >> 16) & 1u);
+  return static_cast<uint16_t>(b >> 16);
+}
+
+struct Block {
+  float* rms1 = nullptr;
+  float* rms2 = nullptr;
+  kb_int8_weight* qkv = nullptr;
+  kb_int8_weight* out = nullptr;
+  kb_int8_weight* up = nullptr;
+  kb_int8_weight* down = nullptr;
+  float* up_b = nullptr;
+  float* down_b = nullptr;
+  float* rope_cos = nullptr;  // [361, heads, head_dim/2]
+  float* rope_sin = nullptr;
+};
+
+}  // namespace
+
+struct kb_model {
+  kb_model_desc desc{};
+  int device = 0;
+  uint16_t* stem_w = nullptr;  // bf16 [C, 224]
+  std::vector<Block> blocks;
+  float* tip_gamma = nullptr;
+  float* tip_beta = nullptr;
+  uint16_t* head_w = nullptr;  // bf16 [384, C]
+  float* head_b = nullptr;     // [384]
+  float* small = nullptr;      // all small head weights, one allocation
+  const float* head_ptrs[15] = {};
+};
+
+namespace {
+
+struct Slot {
+  float* h_spatial = nullptr;  // pinned
+  float* h_global = nullptr;
+  float* h_out = nullptr;      // pinned [policy | value | misc | moremisc | ownership]
+  float* d_spatial = nullptr;
+  float* d_global = nullptr;
+  float* d_out = nullptr;
+  unsigned* h_status = nullptr;  // pinned copy of the status word
+  cudaEvent_t done = nullptr;
+  int n = 0;
+  bool busy = false;
+  uint64_t token = 0;
+};
+
+constexpr int kOutPerPos = 6 * 362 + 3 + 10 + 8 + 361;
+
+}  // namespace
+
+struct kb_handle {
+  kb_model* model = nullptr;
+  int device = 0;
+  int max_batch = 0;
+  int nhwc = 0;
+  cudaStream_t stream = nullptr;
+  // workspace
+  uint16_t* stem_a = nullptr;   // [M, 224] bf16
+  uint16_t* x = nullptr;        // [M, C] residual
+  uint16_t* qkv = nullptr;      // [M, 3C]
+  uint16_t* att = nullptr;      // [M, C] (also the trunk-tip output)
+  uint16_t* hidden = nullptr;   // [M, F]
+  int8_t* q = nullptr;          // [M, max kp]
+  float* scales = nullptr;      // [M]
+  float* hp = nullptr;          // [M, 384] fp32
+  unsigned* status = nullptr;   // [2]
+  Slot slots[2];
+  uint64_t next_token = 1;
+  // Graphs bake in buffer addresses: one per (batch size, input and output buffers).
+  using GraphKey = std::tuple<int, const void*, const void*, const void*>;
+  std::map<GraphKey, cudaGraphExec_t> graphs;
+  std::map<GraphKey, int> warmed;
+  std::mutex mu;
+};
+
+namespace {
+
+void destroy_model(kb_model* m) {
+  if (!m) return;
+  cudaFree(m->stem_w);
+  for (auto& b : m->blocks) {
+    cudaFree(b.rms1);
+    cudaFree(b.rms2);
+    kb_int8_weight_destroy(b.qkv);
+    kb_int8_weight_destroy(b.out);
+    kb_int8_weight_destroy(b.up);
+    kb_int8_weight_destroy(b.down);
+    cudaFree(b.up_b);
+    cudaFree(b.down_b);
+    cudaFree(b.rope_cos);
+    cudaFree(b.rope_sin);
+  }
+  cudaFree(m->tip_gamma);
+  cudaFree(m->tip_beta);
+  cudaFree(m->head_w);
+  cudaFree(m->head_b);
+  cudaFree(m->small);
+  delete m;
+}
+
+// One forward pass of n positions on device buffers, enqueued on `s`.  When
+// `trace` is non-null it receives bf16 [(num_blocks + 2), n*361, C]: the stem
+// output, each block's attention output, and the final residual stream.
+int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, float* d_out,
+            uint16_t* trace = nullptr) {
+  kb_model* m = h->model;
+  const kb_model_desc& d = m->desc;
+  const int c = d.trunk_channels, f = d.ffn_channels, M = n * kSeq;
+  cudaStream_t s = h->stream;
+  int rc = check_cuda(cudaMemsetAsync(h->status, 0, sizeof(unsigned), s), "status reset");
+  if (!rc) rc = check_cuda(cudaMemsetAsync(h->status + 1, 0xff, sizeof(unsigned), s), "status reset");
+  if (rc) return rc;
+  rc = stem_gather_launch(d_spatial, d_global, h->stem_a, n, h->nhwc, s);
+  if (rc) return rc;
+  {
+    GemmArgs g;
+    g.m = M;
+    g.n = c;
+    g.k = kStemK;
+    g.out = h->x;
+    g.ldo = c;
+    g.out_f16 = 0;
+    rc = gemm_launch(kGemmBF16, kEpi16, h->stem_a, m->stem_w, g, s);
+    if (rc) return rc;
+  }
+  const size_t plane = static_cast<size_t>(M) * c;
+  if (trace) {
+    rc = check_cuda(cudaMemcpyAsync(trace, h->x, plane * 2, cudaMemcpyDeviceToDevice, s), "trace copy");
+    if (rc) return rc;
+  }
+  const float scale = 1.0f / sqrtf(static_cast<float>(d.head_dim));
+  for (int bi = 0; bi < d.num_blocks; ++bi) {
+    const Block& b = m->blocks[bi];
+    const unsigned layer = static_cast<unsigned>(bi);
+    // attention
+    rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.qkv->kp, true, b.rms1, kRmsEps, 0, h->q, h->scales,
+                              h->status, layer, s);
+    if (rc) return rc;
+    GemmArgs g;
+    g.m = M;
+    g.n = 3 * c;
+    g.k = b.qkv->kp;
+    g.out = h->qkv;
+    g.ldo = 3 * c;
+    g.row_scale = h->scales;
+    g.col_scale = b.qkv->scales;
+    g.out_f16 = 0;
+    g.status = h->status;
+    g.layer = layer;
+    rc = gemm_launch(kGemmI8, kEpi16, h->q, b.qkv->q, g, s);
+    if (rc) return rc;
+    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s);
+    if (rc) return rc;
+    if (trace) {
+      rc = check_cuda(cudaMemcpyAsync(trace + (1 + bi) * plane, h->att, plane * 2, cudaMemcpyDeviceToDevice, s),
+                      "trace copy");
+      if (rc) return rc;
+    }
+    rc = quantize_rows_launch(h->att, KB_DT_BF16, c, M, c, b.out->kp, false, nullptr, 0.0f, 0, h->q, h->scales,
+                              h->status, layer, s);
+    if (rc) return rc;
+    GemmArgs o;
+    o.m = M;
+    o.n = c;
+    o.k = b.out->kp;
+    o.out = h->x;
+    o.ldo = c;
+    o.row_scale = h->scales;
+    o.col_scale = b.out->scales;
+    o.out_f16 = 0;
+    o.status = h->status;
+    o.layer = layer;
+    rc = gemm_launch(kGemmI8, kEpiRes16, h->q, b.out->q, o, s);
+    if (rc) return rc;
+    // FFN
+    rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.up->kp, true, b.rms2, kRmsEps, 0, h->q, h->scales,
+                              h->status, layer, s);
+    if (rc) return rc;
+    GemmArgs u;
+    u.m = M;
+    u.n = f;
+    u.k = b.up->kp;
+    u.out = h->hidden;
+    u.ldo = f;
+    u.row_scale = h->scales;
+    u.col_scale = b.up->scales;
+    u.bias = b.up_b;
+    u.act = 1;
+    u.out_f16 = 0;
+    u.status = h->status;
+    u.layer = layer;
+    rc = gemm_launch(kGemmI8, kEpi16, h->q, b.up->q, u, s);
+    if (rc) return rc;
+    rc = quantize_rows_launch(h->hidden, KB_DT_BF16, f, M, f, b.down->kp, false, nullptr, 0.0f, 0, h->q,
+                              h->scales, h->status, layer, s);
+    if (rc) return rc;
+    GemmArgs dn;
+    dn.m = M;
+    dn.n = c;
+    dn.k = b.down->kp;
+    dn.out = h->x;
+    dn.ldo = c;
+    dn.row_scale = h->scales;
+    dn.col_scale = b.down->scales;
+    dn.bias = b.down_b;
+    dn.out_f16 = 0;
+    dn.status = h->status;
+    dn.layer = layer;
+    rc = gemm_launch(kGemmI8, kEpiRes16, h->q, b.down->q, dn, s);
+    if (rc) return rc;
+  }
+  if (trace) {
+    rc = check_cuda(cudaMemcpyAsync(trace + (1 + d.num_blocks) * plane, h->x, plane * 2, cudaMemcpyDeviceToDevice, s),
+                    "trace copy");
+    if (rc) return rc;
+  }
+  rc = trunk_tip_launch(h->x, m->tip_gamma, m->tip_beta, h->att, M, c, s);
+  if (rc) return rc;
+  {
+    GemmArgs g;
+    g.m = M;
+    g.n = kHeadN;
+    g.k = c;
+    g.out = h->hp;
+    g.ldo = kHeadN;
+    g.bias = m->head_b;
+    rc = gemm_launch(kGemmBF16, kEpiF32, h->att, m->head_w, g, s);
+    if (rc) return rc;
+  }
+  float* pol = d_out;
+  float* val = pol + static_cast<size_t>(n) * 6 * 362;
+  float* misc = val + static_cast<size_t>(n) * 3;
+  float* more = misc + static_cast<size_t>(n) * 10;
+  float* own = more + static_cast<size_t>(n) * 8;
+  return heads_launch(h->hp, m->head_ptrs, pol, val, misc, more, own, n, h->status, s);
+}
+
+// Forward through a CUDA graph per batch size: the first call for a size runs
+// directly (so lazy module loading and function attributes happen outside
+// capture), the second captures and instantiates, later calls replay.
+int run_forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, float* d_out, bool use_graph) {
+  if (!use_graph) return forward(h, n, d_spatial, d_global, d_out);
+  const kb_handle::GraphKey key{n, d_spatial, d_global, d_out};
+  auto it = h->graphs.find(key);
+  if (it != h->graphs.end()) return check_cuda(cudaGraphLaunch(it->second, h->stream), "graph launch");
+  if (!h->warmed[key]) {
+    h->warmed[key] = 1;
+    return forward(h, n, d_spatial, d_global, d_out);
+  }
+  cudaGraph_t graph = nullptr;
+  int rc = check_cuda(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+  if (rc) return rc;
+  const int frc = forward(h, n, d_spatial, d_global, d_out);
+  rc = check_cuda(cudaStreamEndCapture(h->stream, &graph), "end capture");
+  if (frc) {
+    if (graph) cudaGraphDestroy(graph);
+    return frc;
+  }
+  if (rc) return rc;
+  cudaGraphExec_t exec = nullptr;
+  rc = check_cuda(cudaGraphInstantiate(&exec, graph, 0), "graph instantiate");
+  cudaGraphDestroy(graph);
+  if (rc) return rc;
+  h->graphs[key] = exec;
+  return check_cuda(cudaGraphLaunch(exec, h->stream), "graph launch");
+}
+
+void destroy_handle(kb_handle* h) {
+  if (!h) return;
+  for (auto& kv : h->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& sl : h->slots) {
+    cudaFreeHost(sl.h_spatial);
+    cudaFreeHost(sl.h_global);
+    cudaFreeHost(sl.h_out);
+    cudaFreeHost(sl.h_status);
+    cudaFree(sl.d_spatial);
+    cudaFree(sl.d_global);
+    cudaFree(sl.d_out);
+    if (sl.done) cudaEventDestroy(sl.done);
+  }
+  cudaFree(h->stem_a);
+  cudaFree(h->x);
+  cudaFree(h->qkv);
+  cudaFree(h->att);
+  cudaFree(h->hidden);
+  cudaFree(h->q);
+  cudaFree(h->scales);
+  cudaFree(h->hp);
+  cudaFree(h->status);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  delete h;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kb_model_blob_floats(const kb_model_desc* desc, size_t* count) {
+  int rc = validate_desc(desc);
+  if (rc) return rc;
+  if (!count) {
+    set_error("null count");
+    return KB_E_INVALID;
+  }
+  *count = blob_floats(*desc);
+  return KB_OK;
+}
+
+int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, int device, kb_model** out) {
+  if (!out) {
+    set_error("null output handle");
+    return KB_E_INVALID;
+  }
+  *out = nullptr;
+  int rc = validate_desc(desc);
+  if (rc) return rc;
+  if (!blob || count != blob_floats(*desc)) {
+    set_error("weight blob size mismatch (see kb_model_blob_floats)");
+    return KB_E_INVALID;
+  }
+  for (size_t i = 0; i < count; ++i) {
+    if (!std::isfinite(blob[i])) {
+      set_error("model weights contain NaN or infinity");
+      return KB_E_INVALID;
+    }
+  }
+  rc = check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  if (rc) return rc;
+  rc = kb_device_check(device);
+  if (rc) return rc;
+  kb_model* m = new (std::nothrow) kb_model;
+  if (!m) {
+    set_error("out of host memory");
+    return KB_E_INVALID;
+  }
+  m->desc = *desc;
+  m->device = device;
+  const kb_model_desc& d = *desc;
+  const int c = d.trunk_channels, f = d.ffn_channels, nh = d.num_heads, hd = d.head_dim;
+  BlobCursor cur{blob, count};
+  // stem [C, 217] -> bf16 [C, 224]
+  {
+    const float* w = cur.take(static_cast<size_t>(c) * kStemKUsed);
+    std::vector<uint16_t> wb(static_cast<size_t>(c) * kStemK, 0);
+    for (int r = 0; r < c; ++r)
+      for (int k = 0; k < kStemKUsed; ++k) wb[static_cast<size_t>(r) * kStemK + k] = bf16_bits(w[r * kStemKUsed + k]);
+    rc = upload(&m->stem_w, wb.data(), wb.size(), "upload stem");
+  }
+  m->blocks.resize(d.num_blocks);
+  for (int bi = 0; bi < d.num_blocks && !rc; ++bi) {
+    Block& b = m->blocks[bi];
+    const float* rms1 = cur.take(c);
+    const float* qkv = cur.take(3ull * c * c);
+    const float* ow = cur.take(1ull * c * c);
+    const float* rms2 = cur.take(c);
+    const float* up = cur.take(1ull * f * c);
+    const float* up_b = cur.take(f);
+    const float* dn = cur.take(1ull * c * f);
+    const float* dn_b = cur.take(c);
+    const float* freqs = cur.take(static_cast<size_t>(nh) * (hd / 2) * 2);
+    rc = upload(&b.rms1, rms1, c, "upload rms");
+    if (!rc) rc = upload(&b.rms2, rms2, c, "upload rms");
+    if (!rc) rc = kb_int8_weight_upload(qkv, 3 * c, c, KB_LAYOUT_PLAIN, &b.qkv);
+    if (!rc) rc = kb_int8_weight_upload(ow, c, c, KB_LAYOUT_PLAIN, &b.out);
+    if (!rc) rc = kb_int8_weight_upload(up, f, c, KB_LAYOUT_PLAIN, &b.up);
+    if (!rc) rc = kb_int8_weight_upload(dn, c, f, KB_LAYOUT_PLAIN, &b.down);
+    if (!rc) rc = upload(&b.up_b, up_b, f, "upload bias");
+    if (!rc) rc = upload(&b.down_b, dn_b, c, "upload bias");
+    if (!rc) {
+      // Learned 2-D RoPE tables: angle = x*f0 + y*f1 in fp32, cosf/sinf
+      // (native_model.rs:200-228), laid out [token, head, pair].
+      const int pairs = hd / 2;
+      std::vector<float> cs(static_cast<size_t>(kSeq) * nh * pairs), sn(cs.size());
+      for (int y = 0; y < kSide; ++y)
+        for (int x = 0; x < kSide; ++x)
+          for (int hh = 0; hh < nh; ++hh)
+            for (int p = 0; p < pairs; ++p) {
+              const int fi = (hh * pairs + p) * 2;
+              const float angle = static_cast<float>(x) * freqs[fi] + static_cast<float>(y) * freqs[fi + 1];
+              const size_t idx = ((static_cast<size_t>(y) * kSide + x) * nh + hh) * pairs + p;
+              cs[idx] = cosf(angle);
+              sn[idx] = sinf(angle);
+            }
+      rc = upload(&b.rope_cos, cs.data(), cs.size(), "upload rope");
+      if (!rc) rc = upload(&b.rope_sin, sn.data(), sn.size(), "upload rope");
+    }
+  }
+  if (!rc) {
+    const float* tg = cur.take(c);
+    const float* tb = cur.take(c);
+    rc = upload(&m->tip_gamma, tg, c, "upload tip");
+    if (!rc) rc = upload(&m->tip_beta, tb, c, "upload tip");
+  }
+  if (!rc) {
+    const float* p1 = cur.take(96ull * c);
+    const float* g1 = cur.take(96ull * c);
+    const float* g1b = cur.take(96);
+    const float* v1 = cur.take(192ull * c);
+    const float* v1b = cur.take(192);
+    std::vector<uint16_t> hw(static_cast<size_t>(kHeadN) * c);
+    std::vector<float> hb(kHeadN, 0.0f);
+    for (size_t i = 0; i < 96ull * c; ++i) {
+      hw[i] = bf16_bits(p1[i]);
+      hw[96ull * c + i] = bf16_bits(g1[i]);
+    }
+    for (size_t i = 0; i < 192ull * c; ++i) hw[192ull * c + i] = bf16_bits(v1[i]);
+    for (int i = 0; i < 96; ++i) hb[96 + i] = g1b[i];
+    for (int i = 0; i < 192; ++i) hb[192 + i] = v1b[i];
+    rc = upload(&m->head_w, hw.data(), hw.size(), "upload head linears");
+    if (!rc) rc = upload(&m->head_b, hb.data(), hb.size(), "upload head bias");
+    // small head weights, order = HeadWeights
+    static const size_t sizes[15] = {96 * 288, 96 * 288, 96, 6 * 96, 96, 6 * 96, 192 * 576, 192,
+                                     3 * 192,  3,        10 * 192, 10, 8 * 192, 8, 192};
+    // blob order: g_matmul, pass1_w, pass1_b, pass2_w, bias2, conv2p_w, v2_w, v2_b,
+    //             value_w, value_b, misc_w, misc_b, moremisc_w, moremisc_b, own_w
+    size_t total = 0;
+    for (size_t s : sizes) total += (s + 3) & ~static_cast<size_t>(3);
+    std::vector<float> small(total, 0.0f);
+    size_t off = 0;
+    size_t offs[15];
+    for (int i = 0; i < 15; ++i) {
+      const float* src = cur.take(sizes[i]);
+      memcpy(small.data() + off, src, sizes[i] * sizeof(float));
+      offs[i] = off;
+      off += (sizes[i] + 3) & ~static_cast<size_t>(3);
+    }
+    if (!rc) rc = upload(&m->small, small.data(), small.size(), "upload head weights");
+    if (!rc)
+      for (int i = 0; i < 15; ++i) m->head_ptrs[i] = m->small + offs[i];
+  }
+  if (!rc && cur.left != 0) {
+    set_error("internal: weight blob not fully consumed");
+    rc = KB_E_STATE;
+  }
+  if (rc) {
+    destroy_model(m);
+    return rc;
+  }
+  *out = m;
+  return KB_OK;
+}
+
+void kb_model_destroy(kb_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  destroy_model(m);
+}
+
+int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle** out) {
+  if (!out || !model || max_batch <= 0 || max_batch > 4096) {
+    set_error("kb_handle_create: need a model and 1 <= max_batch <= 4096");
+    return KB_E_INVALID;
+  }
+  *out = nullptr;
+  int rc = check_cuda(cudaSetDevice(model->device), "cudaSetDevice");
+  if (rc) return rc;
+  kb_handle* h = new (std::nothrow) kb_handle;
+  if (!h) {
+    set_error("out of host memory");
+    return KB_E_INVALID;
+  }
+  h->model = model;
+  h->device = model->device;
+  h->max_batch = max_batch;
+  h->nhwc = inputs_nhwc ? 1 : 0;
+  const kb_model_desc& d = model->desc;
+  const size_t M = static_cast<size_t>(max_batch) * kSeq, c = d.trunk_channels, f = d.ffn_channels;
+  size_t kq = c > f ? c : f;
+  kq = (kq + 15) / 16 * 16;
+  rc = check_cuda(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking), "stream create");
+  if (!rc) rc = dev_alloc(&h->stem_a, M * kStemK, "workspace");
+  if (!rc) rc = dev_alloc(&h->x, M * c, "workspace");
+  if (!rc) rc = dev_alloc(&h->qkv, M * 3 * c, "workspace");
+  if (!rc) rc = dev_alloc(&h->att, M * c, "workspace");
+  if (!rc) rc = dev_alloc(&h->hidden, M * f, "workspace");
+  if (!rc) rc = dev_alloc(&h->q, M * kq, "workspace");
+  if (!rc) rc = dev_alloc(&h->scales, M, "workspace");
+  if (!rc) rc = dev_alloc(&h->hp, M * kHeadN, "workspace");
+  if (!rc) rc = dev_alloc(&h->status, 2, "status word");
+  for (auto& sl : h->slots) {
+    const size_t ns = static_cast<size_t>(max_batch) * kInC * kSeq, ng = static_cast<size_t>(max_batch) * kInG,
+                 no = static_cast<size_t>(max_batch) * kOutPerPos;
+    if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_spatial, ns * sizeof(float)), "pinned input");
+    if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_global, ng * sizeof(float)), "pinned input");
+    if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_out, no * sizeof(float)), "pinned output");
+    if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_status, 2 * sizeof(unsigned)), "pinned status");
+    if (!rc) rc = dev_alloc(&sl.d_spatial, ns, "device input");
+    if (!rc) rc = dev_alloc(&sl.d_global, ng, "device input");
+    if (!rc) rc = dev_alloc(&sl.d_out, no, "device output");
+    if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming), "event");
+  }
+  if (rc) {
+    destroy_handle(h);
+    return rc;
+  }
+  *out = h;
+  return KB_OK;
+}
+
+void kb_handle_destroy(kb_handle* h) {
+  if (!h) return;
+  cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->stream);
+  destroy_handle(h);
+}
+
+int kb_handle_stream(kb_handle* h, uintptr_t* stream) {
+  if (!h || !stream) {
+    set_error("null handle");
+    return KB_E_INVALID;
+  }
+  *stream = reinterpret_cast<uintptr_t>(h->stream);
+  return KB_OK;
+}
+
+int kb_forward_device(kb_handle* h, int n, const float* d_spatial, const float* d_global, float* d_out,
+                      int use_graph) {
+  if (!h || !d_spatial || !d_global || !d_out || n <= 0 || n > h->max_batch) {
+    set_error("kb_forward_device: need 1 <= n <= max_batch and device buffers");
+    return KB_E_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
+  if (rc) return rc;
+  return run_forward(h, n, d_spatial, d_global, d_out, use_graph != 0);
+}
+
+int kb_forward_trace(kb_handle* h, int n, const float* d_spatial, const float* d_global, float* d_out,
+                     uint16_t* d_trace) {
+  if (!h || !d_spatial || !d_global || !d_out || !d_trace || n <= 0 || n > h->max_batch) {
+    set_error("kb_forward_trace: need 1 <= n <= max_batch and device buffers");
+    return KB_E_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
+  if (rc) return rc;
+  return forward(h, n, d_spatial, d_global, d_out, d_trace);
+}
+
+int kb_read_status(kb_handle* h, uint32_t status[2]) {
+  if (!h || !status) {
+    set_error("null handle");
+    return KB_E_INVALID;
+  }
+  int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
+  if (!rc) rc = check_cuda(cudaStreamSynchronize(h->stream), "stream sync");
+  if (!rc) rc = check_cuda(cudaMemcpy(status, h->status, 2 * sizeof(unsigned), cudaMemcpyDeviceToHost), "status");
+  return rc;
+}
+
+int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, uint64_t* token) {
+  if (!h || !spatial || !global || !token || n <= 0 || n > h->max_batch) {
+    set_error("kb_submit: need 1 <= n <= max_batch, host inputs and a token");
+    return KB_E_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
+  if (rc) return rc;
+  Slot* sl = nullptr;
+  for (auto& cand : h->slots)
+    if (!cand.busy) {
+      sl = &cand;
+      break;
+    }
+  if (!sl) {
+    set_error("both pipeline slots are in flight: finish one before submitting again");
+    return KB_E_STATE;
+  }
+  const size_t ns = static_cast<size_t>(n) * kInC * kSeq, ng = static_cast<size_t>(n) * kInG;
+  memcpy(sl->h_spatial, spatial, ns * sizeof(float));
+  memcpy(sl->h_global, global, ng * sizeof(float));
+  cudaStream_t s = h->stream;
+  rc = check_cuda(cudaMemcpyAsync(sl->d_spatial, sl->h_spatial, ns * sizeof(float), cudaMemcpyHostToDevice, s), "H2D");
+  if (!rc) rc = check_cuda(cudaMemcpyAsync(sl->d_global, sl->h_global, ng * sizeof(float), cudaMemcpyHostToDevice, s), "H2D");
+  if (!rc) rc = run_forward(h, n, sl->d_spatial, sl->d_global, sl->d_out, true);
+  if (!rc)
+    rc = check_cuda(cudaMemcpyAsync(sl->h_out, sl->d_out, static_cast<size_t>(n) * kOutPerPos * sizeof(float),
+                                    cudaMemcpyDeviceToHost, s), "D2H");
+  if (!rc)
+    rc = check_cuda(cudaMemcpyAsync(sl->h_status, h->status, 2 * sizeof(unsigned), cudaMemcpyDeviceToHost, s), "D2H");
+  if (!rc) rc = check_cuda(cudaEventRecord(sl->done, s), "event record");
+  if (rc) return rc;
+  sl->busy = true;
+  sl->n = n;
+  sl->token = h->next_token++;
+  *token = sl->token;
+  return KB_OK;
+}
+
+int kb_query(kb_handle* h, uint64_t token) {
+  if (!h) {
+    set_error("null handle");
+    return -KB_E_INVALID;
+  }
+  for (auto& sl : h->slots) {
+    if (sl.busy && sl.token == token) {
+      const cudaError_t e = cudaEventQuery(sl.done);
+      if (e == cudaSuccess) return 1;
+      if (e == cudaErrorNotReady) return 0;
+      return -check_cuda(e, "event query");
+    }
+  }
+  set_error("unknown or already finished token");
+  return -KB_E_STATE;
+}
+
+int kb_finish(kb_handle* h, uint64_t token, float* policy, float* value, float* misc, float* moremisc,
+              float* ownership, uint32_t status[2]) {
+  if (!h) {
+    set_error("null handle");
+    return KB_E_INVALID;
+  }
+  Slot* sl = nullptr;
+  for (auto& cand : h->slots)
+    if (cand.busy && cand.token == token) sl = &cand;
+  if (!sl) {
+    set_error("unknown or already finished token");
+    return KB_E_STATE;
+  }
+  int rc = check_cuda(cudaEventSynchronize(sl->done), "event wait");
+  sl->busy = false;
+  if (rc) return rc;
+  const int n = sl->n;
+  if (status) {
+    status[0] = sl->h_status[0];
+    status[1] = sl->h_status[1];
+  }
+  if (sl->h_status[0] != 0) {
+    set_error("forward reported status flags " + std::to_string(sl->h_status[0]) + " at layer " +
+              std::to_string(static_cast<int>(sl->h_status[1])) + "; outputs withheld");
+    return KB_E_NONFINITE;
+  }
+  const float* src = sl->h_out;
+  const size_t np = static_cast<size_t>(n) * 6 * 362;
+  if (policy) memcpy(policy, src, np * sizeof(float));
+  src += np;
+  if (value) memcpy(value, src, static_cast<size_t>(n) * 3 * sizeof(float));
+  src += static_cast<size_t>(n) * 3;
+  if (misc) memcpy(misc, src, static_cast<size_t>(n) * 10 * sizeof(float));
+  src += static_cast<size_t>(n) * 10;
+  if (moremisc) memcpy(moremisc, src, static_cast<size_t>(n) * 8 * sizeof(float));
+  src += static_cast<size_t>(n) * 8;
+  if (ownership) memcpy(ownership, src, static_cast<size_t>(n) * kSeq * sizeof(float));
+  return KB_OK;
+}
+
+int kb_warmup(kb_handle* h, const int* batches, int count) {
+  if (!h || (!batches && count > 0) || count < 0) {
+    set_error("kb_warmup: invalid arguments");
+    return KB_E_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
+  for (int i = 0; i < count && !rc; ++i) {
+    const int n = batches[i];
+    if (n <= 0 || n > h->max_batch) {
+      set_error("kb_warmup: batch size out of range");
+      return KB_E_INVALID;
+    }
+    // Zero inputs (a fresh handle's device memory is not meaningful), then for
+    // each pipeline slot one direct run and one captured run.
+    for (auto& sl : h->slots) {
+      if (!rc) rc = check_cuda(cudaMemsetAsync(sl.d_spatial, 0, static_cast<size_t>(n) * kInC * kSeq * sizeof(float), h->stream), "memset");
+      if (!rc) rc = check_cuda(cudaMemsetAsync(sl.d_global, 0, static_cast<size_t>(n) * kInG * sizeof(float), h->stream), "memset");
+      for (int k = 0; k < 2 && !rc; ++k) rc = run_forward(h, n, sl.d_spatial, sl.d_global, sl.d_out, true);
+    }
+  }
+  if (!rc) rc = check_cuda(cudaStreamSynchronize(h->stream), "warmup sync");
+  return rc;
+}
+
+}  // extern "C"
