@@ -118,6 +118,16 @@ KB_API int kb_int8_linear(const int8_t* a, const float* sa, const int8_t* w, con
 KB_API int kb_int8_quantize_rows(const void* x, int dtype, int rows, int width, int stride, int kp,
                           int8_t* q, float* scales, uintptr_t stream);
 
+/* Streaming variant for 16-bit rows whose |value| bit maximum is already known
+ * (row_amax [rows], uint32 = max of (bits & 0x7fffffff) of the fp32 values,
+ * as written by a GEMM epilogue's row_amax): same scales and integers as
+ * kb_int8_quantize_rows, one pass, no row reduction.  Row starts must be
+ * 16-byte aligned (stride % 8 == 0).  No single reference counterpart: it
+ * splits int8_swiglu_quantize's row reduction (int8_ops.cu:93-138) into the
+ * producing GEMM. */
+KB_API int kb_int8_quantize_rows_amax(const void* x, int dtype, int rows, int width, int stride, int kp,
+                                      const uint32_t* row_amax, int8_t* q, float* scales, uintptr_t stream);
+
 /* Fused RMSNorm -> 16-bit boundary (boundary_dtype KB_DT_F16 or KB_DT_BF16)
  * -> per-token INT8 quantisation.
  * Replaces: int8_rms_quantize{384,512}_kernel (int8_ops.cu:8-57) and

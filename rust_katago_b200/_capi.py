@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_int8_gemm_i32": (I, [P, P, P, I, I, I, STREAM]),
     "kb_int8_linear": (I, [P, P, P, P, P, I, I, I, I, I, I, P, I, I, P, STREAM]),
     "kb_int8_quantize_rows": (I, [P, I, I, I, I, I, P, P, STREAM]),
+    "kb_int8_quantize_rows_amax": (I, [P, I, I, I, I, I, P, P, P, STREAM]),
     "kb_int8_rms_quantize": (I, [P, I, I, I, I, P, F, I, I, P, P, STREAM]),
     "kb_int8_workspace_create": (I, [STREAM, I, I, I, PP]),
     "kb_int8_workspace_destroy": (None, [P]),

@@ -82,7 +82,7 @@ __device__ __forceinline__ uint32_t rope_pair(uint32_t w, float c, float s, bool
 template <int D, bool F16>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const uint16_t* __restrict__ qkv, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
-    uint16_t* __restrict__ out, int seq, int heads, float scale_log2) {
+    uint16_t* __restrict__ out, int seq, int heads, float scale_log2, uint32_t* __restrict__ row_amax) {
   constexpr int kStride = D + 8;  // bf16 elements per smem row (16 B pad: conflict-free ldmatrix)
   constexpr int kKSteps = D / 16;
   constexpr int kDTiles = D / 8;
@@ -232,18 +232,32 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
       }
     }
     const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+    uint32_t am0 = 0, am1 = 0;  // packed |16-bit| maxima of this thread's values in rows r0, r1
 #pragma unroll
     for (int n = 0; n < kDTiles; ++n) {
       const int d = n * 8 + q4 * 2;
-      if (r0 < seq) {
-        uint16_t* dst = out + (static_cast<size_t>(b) * seq + r0) * c + h * D + d;
-        *reinterpret_cast<uint32_t*>(dst) =
-            F16 ? pack_f16x2(o[n][0] * inv0, o[n][1] * inv0) : pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
-      }
-      if (r1 < seq) {
-        uint16_t* dst = out + (static_cast<size_t>(b) * seq + r1) * c + h * D + d;
-        *reinterpret_cast<uint32_t*>(dst) =
-            F16 ? pack_f16x2(o[n][2] * inv1, o[n][3] * inv1) : pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
+      const uint32_t w0 =
+          F16 ? pack_f16x2(o[n][0] * inv0, o[n][1] * inv0) : pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
+      const uint32_t w1 =
+          F16 ? pack_f16x2(o[n][2] * inv1, o[n][3] * inv1) : pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
+      am0 = __vmaxu2(am0, w0 & 0x7fff7fffu);
+      am1 = __vmaxu2(am1, w1 & 0x7fff7fffu);
+      if (r0 < seq) *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * seq + r0) * c + h * D + d) = w0;
+      if (r1 < seq) *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * seq + r1) * c + h * D + d) = w1;
+    }
+    if (row_amax != nullptr) {
+      // Row maxima for the following streaming quantiser: reduce over the 4
+      // threads that share a row, one atomic per (row, head).
+      uint32_t m0 = max(am0 & 0xffffu, am0 >> 16), m1 = max(am1 & 0xffffu, am1 >> 16);
+      m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+      m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+      m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+      m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+      if (q4 == 0) {
+        const uint32_t f0 = F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m0))) : (m0 << 16);
+        const uint32_t f1 = F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m1))) : (m1 << 16);
+        if (r0 < seq) atomicMax(row_amax + static_cast<size_t>(b) * seq + r0, f0);
+        if (r1 < seq) atomicMax(row_amax + static_cast<size_t>(b) * seq + r1, f1);
       }
     }
   }
@@ -251,7 +265,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 
 template <int D, bool F16>
 int launch_attention(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint16_t* out, int batch,
-                     int seq, int heads, float scale, cudaStream_t stream) {
+                     int seq, int heads, float scale, uint32_t* row_amax, cudaStream_t stream) {
   const size_t smem = 2 * static_cast<size_t>(kMaxSeq) * (D + 8) * sizeof(uint16_t);
   auto kern = attention_kernel<D, F16>;
   int dev = 0;
@@ -264,7 +278,7 @@ int launch_attention(const uint16_t* qkv, const float* cos_t, const float* sin_t
     configured.fetch_or(bit);
   }
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<batch * heads, kAttnThreads, smem, stream>>>(qkv, cos_t, sin_t, out, seq, heads, scale_log2);
+  kern<<<batch * heads, kAttnThreads, smem, stream>>>(qkv, cos_t, sin_t, out, seq, heads, scale_log2, row_amax);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 
@@ -273,7 +287,8 @@ int launch_attention(const uint16_t* qkv, const float* cos_t, const float* sin_t
 // qkv: [batch*seq, 3*heads*D] 16-bit; cos/sin: [seq, heads, D/2] fp32;
 // out: [batch*seq, heads*D] 16-bit.  scale multiplies q.k before the softmax.
 int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
-                     int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream) {
+                     int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
+                     uint32_t* row_amax) {
   if (!qkv || !rope_cos || !rope_sin || !out || batch <= 0 || seq <= 0 || seq > kMaxSeq || heads <= 0 ||
       !(scale > 0.0f)) {
     set_error("attention: invalid arguments (seq must be 1..384)");
@@ -285,11 +300,11 @@ int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* ro
     return KB_E_INVALID;
   }
   if (head_dim == 64)
-    return f16 ? launch_attention<64, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, stream)
-               : launch_attention<64, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, stream);
+    return f16 ? launch_attention<64, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream)
+               : launch_attention<64, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream);
   if (head_dim == 32)
-    return f16 ? launch_attention<32, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, stream)
-               : launch_attention<32, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, stream);
+    return f16 ? launch_attention<32, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream)
+               : launch_attention<32, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream);
   set_error("attention: head_dim must be 32 or 64");
   return KB_E_UNSUPPORTED;
 }

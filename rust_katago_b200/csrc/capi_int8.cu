@@ -255,6 +255,16 @@ int kb_int8_quantize_rows(const void* x, int dtype, int rows, int width, int str
                               nullptr, KB_NO_LAYER, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int kb_int8_quantize_rows_amax(const void* x, int dtype, int rows, int width, int stride, int kp,
+                               const uint32_t* row_amax, int8_t* q, float* scales, uintptr_t stream) {
+  if (!x || !q || !scales || !row_amax) {
+    set_error("kb_int8_quantize_rows_amax: null pointer");
+    return KB_E_INVALID;
+  }
+  return quantize_rows_amax_launch(x, dtype, stride, row_amax, rows, width, kp, q, scales, nullptr, KB_NO_LAYER,
+                                   reinterpret_cast<cudaStream_t>(stream));
+}
+
 int kb_int8_rms_quantize(const void* x, int dtype, int rows, int width, int stride,
                          const float* gamma, float eps, int boundary_dtype, int kp, int8_t* q,
                          float* scales, uintptr_t stream) {

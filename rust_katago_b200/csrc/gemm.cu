@@ -37,17 +37,23 @@ constexpr int kBKBytes = 128;  // one 128-byte swizzle row of K per stage
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStageTile = 32 * 64;  // one 32x32 16-bit staging tile (2 KiB)
-constexpr int kStagingBytes = kEpiWarps * 2 * kStageTile;
+constexpr int kSmemLimit = 227 * 1024;
 
-template <int BN>
+// SB = staging tiles per epilogue warp (stores in flight per warp).  Short-K
+// GEMMs are bound by how fast the epilogue can drain results, so they trade
+// one ring stage for four staging tiles per warp; long-K GEMMs keep the deeper
+// ring and two staging tiles.
+template <int BN, int SB>
 struct GemmCfg {
   static constexpr int kABytes = kBM * kBKBytes;
   static constexpr int kBBytes = BN * kBKBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (192 * 1024) / kStageBytes;
+  static constexpr int kStagingBytes = kEpiWarps * SB * kStageTile;
+  static constexpr int kStages = (kSmemLimit - kStagingBytes - 1024 - 256) / kStageBytes;
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kSmemBytes = kRingBytes + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(kStages >= 3, "ring too shallow");
 };
 
 template <int KIND>
@@ -153,15 +159,16 @@ __device__ __forceinline__ void load16x32(const uint16_t* src, uint32_t (&hw)[16
 // Two staging tiles per warp alternate so a store overlaps the next chunk.
 struct Out16 {
   const CUtensorMap* map;
-  uint8_t* stage;  // this warp's two staging tiles
+  uint8_t* stage;  // this warp's SB staging tiles
   int sb;          // staging tile to use next
 };
 
+template <int SB>
 __device__ __forceinline__ void emit16(Out16& o, const GemmArgs& g, const uint32_t (&hw)[16], int row,
                                        int row0q, int col0, int lane, bool row_ok, int valid) {
   if (o.map != nullptr) {
     uint8_t* buf = o.stage + o.sb * kStageTile;
-    if (lane == 0) bulk_wait_read<1>();
+    if (lane == 0) bulk_wait_read<SB - 1>();
     __syncwarp();
     const int sw = (lane >> 1) & 3;
 #pragma unroll
@@ -174,7 +181,7 @@ __device__ __forceinline__ void emit16(Out16& o, const GemmArgs& g, const uint32
       tma_store_2d(o.map, buf, col0, row0q);
       bulk_commit();
     }
-    o.sb ^= 1;
+    o.sb = o.sb + 1 == SB ? 0 : o.sb + 1;
   } else if (row_ok) {
     uint16_t* dst = static_cast<uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
     store16x32(dst, hw, valid, (reinterpret_cast<uintptr_t>(dst) & 15) == 0);
@@ -197,11 +204,11 @@ __device__ __forceinline__ float2 acc_pair(const uint32_t (&v)[32], int i, float
   }
 }
 
-template <int KIND, int BN, int EPI, int ACT>
+template <int KIND, int BN, int EPI, int ACT, int SB>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g, const int use_tma_out) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, SB>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kElemBytes = (KIND == kGemmBF16) ? 2 : 1;
   constexpr int kBKElems = kBKBytes / kElemBytes;
@@ -211,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* ring = smem;
   uint8_t* staging = smem + Cfg::kRingBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kStagingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::kStagingBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -329,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int e = warp - 2;          // 0..7
     const int quarter = warp & 3;    // TMEM lanes this warp may access: 32*quarter..+31
     const int half = e >> 2;         // which half of the tile's columns
-    Out16 o{use_tma_out ? &tmap_out : nullptr, staging + e * 2 * kStageTile, 0};
+    Out16 o{use_tma_out ? &tmap_out : nullptr, staging + e * SB * kStageTile, 0};
     const bool f16 = (EPI == kEpiF16) ? true : (g.out_f16 != 0);
     int acc = 0;
     uint32_t aph = 0;
@@ -380,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               hw[i] = pair;
             }
-            emit16(o, g, hw, row, row0q, ocol0, lane, row_ok, valid);
+            emit16<SB>(o, g, hw, row, row0q, ocol0, lane, row_ok, valid);
           }
         }
       } else {
@@ -423,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             if constexpr (EPI != kEpiRes16) amax = max(amax, amax16_to_f32bits(amax2, f16));
-            emit16(o, g, hw, row, row0q, col0, lane, row_ok, valid);
+            emit16<SB>(o, g, hw, row, row0q, col0, lane, row_ok, valid);
           } else if (row_ok) {
             float sw[32], bias[32];
             if constexpr (KIND == kGemmI8 && EPI != kEpiI32) load_vec32(g.col_scale, col0, g.n, sw);
@@ -515,11 +522,11 @@ bool epi_16bit(int epi) {
   return epi == kEpiF16 || epi == kEpi16 || epi == kEpiRes16 || epi == kEpiSwiGLU16;
 }
 
-template <int KIND, int BN, int EPI, int ACT>
+template <int KIND, int BN, int EPI, int ACT, int SB>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int use_tma_out,
                const GemmArgs& g, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
-  auto kern = gemm_kernel<KIND, BN, EPI, ACT>;
+  using Cfg = GemmCfg<BN, SB>;
+  auto kern = gemm_kernel<KIND, BN, EPI, ACT, SB>;
   int dev = 0;
   cudaGetDevice(&dev);
   // Function attributes live in each device's context: set once per device.
@@ -536,23 +543,32 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   return check_cuda(cudaGetLastError(), "gemm launch");
 }
 
-template <int KIND, int BN>
+template <int KIND, int BN, int SB>
 int dispatch_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int tma_out,
                  const GemmArgs& g, cudaStream_t s) {
   switch (epi) {
-    case kEpiI32: return launch_one<KIND, BN, kEpiI32, kActNone>(ma, mb, mo, tma_out, g, s);
-    case kEpiF16: return launch_one<KIND, BN, kEpiF16, kActNone>(ma, mb, mo, tma_out, g, s);
-    case kEpiResF32: return launch_one<KIND, BN, kEpiResF32, kActNone>(ma, mb, mo, tma_out, g, s);
+    case kEpiI32: return launch_one<KIND, BN, kEpiI32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiF16: return launch_one<KIND, BN, kEpiF16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiResF32: return launch_one<KIND, BN, kEpiResF32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
     case kEpi16:
-      if (g.act == kActGelu) return launch_one<KIND, BN, kEpi16, kActGelu>(ma, mb, mo, tma_out, g, s);
-      if (g.act == kActSilu) return launch_one<KIND, BN, kEpi16, kActSilu>(ma, mb, mo, tma_out, g, s);
-      return launch_one<KIND, BN, kEpi16, kActNone>(ma, mb, mo, tma_out, g, s);
-    case kEpiRes16: return launch_one<KIND, BN, kEpiRes16, kActNone>(ma, mb, mo, tma_out, g, s);
-    case kEpiSwiGLU16: return launch_one<KIND, BN, kEpiSwiGLU16, kActNone>(ma, mb, mo, tma_out, g, s);
-    case kEpiF32: return launch_one<KIND, BN, kEpiF32, kActNone>(ma, mb, mo, tma_out, g, s);
+      if (g.act == kActGelu) return launch_one<KIND, BN, kEpi16, kActGelu, SB>(ma, mb, mo, tma_out, g, s);
+      if (g.act == kActSilu) return launch_one<KIND, BN, kEpi16, kActSilu, SB>(ma, mb, mo, tma_out, g, s);
+      return launch_one<KIND, BN, kEpi16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiRes16: return launch_one<KIND, BN, kEpiRes16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiSwiGLU16: return launch_one<KIND, BN, kEpiSwiGLU16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiF32: return launch_one<KIND, BN, kEpiF32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
   }
   set_error("unknown GEMM epilogue");
   return KB_E_INVALID;
+}
+
+template <int KIND, int BN>
+int dispatch_sb(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int tma_out,
+                const GemmArgs& g, cudaStream_t s) {
+  // Deep staging when the epilogue, not the K loop, bounds the tile time.
+  const int k_bytes = g.k * (KIND == kGemmBF16 ? 2 : 1);
+  if (tma_out && k_bytes <= 1024) return dispatch_epi<KIND, BN, 4>(epi, ma, mb, mo, tma_out, g, s);
+  return dispatch_epi<KIND, BN, 2>(epi, ma, mb, mo, tma_out, g, s);
 }
 
 }  // namespace
@@ -632,12 +648,12 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     tma_out = 1;
   }
   if (kind == kGemmI8) {
-    return bn == 256 ? dispatch_epi<kGemmI8, 256>(epi, ma, mb, mo, tma_out, g, stream)
-                     : dispatch_epi<kGemmI8, 128>(epi, ma, mb, mo, tma_out, g, stream);
+    return bn == 256 ? dispatch_sb<kGemmI8, 256>(epi, ma, mb, mo, tma_out, g, stream)
+                     : dispatch_sb<kGemmI8, 128>(epi, ma, mb, mo, tma_out, g, stream);
   }
   if (kind == kGemmBF16) {
-    return bn == 256 ? dispatch_epi<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, g, stream)
-                     : dispatch_epi<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, g, stream);
+    return bn == 256 ? dispatch_sb<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, g, stream)
+                     : dispatch_sb<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, g, stream);
   }
   set_error("GEMM kind not supported");
   return KB_E_UNSUPPORTED;

@@ -64,6 +64,14 @@ enum GemmKind : int { kGemmI8 = 0, kGemmBF16 = 1, kGemmMXF8 = 2 };
 int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs& args,
                 cudaStream_t stream, int bn_hint = 0);
 
+// Activation quantisers (quant.cu).
+int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width, int kp, bool rms,
+                         const float* gamma, float eps, int bound_f16, int8_t* q, float* scales,
+                         unsigned* status, unsigned layer, cudaStream_t stream);
+int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t* row_amax, int rows, int width,
+                              int kp, int8_t* q, float* scales, unsigned* status, unsigned layer,
+                              cudaStream_t stream);
+
 // Encode a 2-D tensor map (innermost dimension `cols`, row pitch `row_bytes`).
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long cols, long rows,
               long row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swz);

@@ -32,11 +32,9 @@
 #include "kb_internal.h"
 
 namespace kb {
-int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width, int kp, bool rms,
-                         const float* gamma, float eps, int bound_f16, int8_t* q, float* scales,
-                         unsigned* status, unsigned layer, cudaStream_t stream);
 int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
-                     int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream);
+                     int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
+                     uint32_t* row_amax = nullptr);
 int stem_gather_launch(const float* spatial, const float* global, uint16_t* a, int batch, int nhwc,
                        cudaStream_t s);
 int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, uint16_t* g, long rows, int c,
@@ -175,6 +173,7 @@ struct kb_handle {
   uint16_t* hidden = nullptr;   // [M, F]
   int8_t* q = nullptr;          // [M, max kp]
   float* scales = nullptr;      // [M]
+  uint32_t* row_amax = nullptr; // [M] |bits| maximum of the FFN hidden rows
   float* hp = nullptr;          // [M, 384] fp32
   unsigned* status = nullptr;   // [2]
   Slot slots[2];
@@ -262,15 +261,18 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
     g.layer = layer;
     rc = gemm_launch(kGemmI8, kEpi16, h->q, b.qkv->q, g, s);
     if (rc) return rc;
-    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s);
+    rc = check_cuda(cudaMemsetAsync(h->row_amax, 0, static_cast<size_t>(M) * sizeof(uint32_t), s), "amax reset");
+    if (rc) return rc;
+    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s,
+                          h->row_amax);
     if (rc) return rc;
     if (trace) {
       rc = check_cuda(cudaMemcpyAsync(trace + (1 + bi) * plane, h->att, plane * 2, cudaMemcpyDeviceToDevice, s),
                       "trace copy");
       if (rc) return rc;
     }
-    rc = quantize_rows_launch(h->att, KB_DT_BF16, c, M, c, b.out->kp, false, nullptr, 0.0f, 0, h->q, h->scales,
-                              h->status, layer, s);
+    rc = quantize_rows_amax_launch(h->att, KB_DT_BF16, c, h->row_amax, M, c, b.out->kp, h->q, h->scales,
+                                   h->status, layer, s);
     if (rc) return rc;
     GemmArgs o;
     o.m = M;
@@ -289,7 +291,10 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
     rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.up->kp, true, b.rms2, kRmsEps, 0, h->q, h->scales,
                               h->status, layer, s);
     if (rc) return rc;
+    rc = check_cuda(cudaMemsetAsync(h->row_amax, 0, static_cast<size_t>(M) * sizeof(uint32_t), s), "amax reset");
+    if (rc) return rc;
     GemmArgs u;
+    u.row_amax = h->row_amax;
     u.m = M;
     u.n = f;
     u.k = b.up->kp;
@@ -304,8 +309,8 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
     u.layer = layer;
     rc = gemm_launch(kGemmI8, kEpi16, h->q, b.up->q, u, s);
     if (rc) return rc;
-    rc = quantize_rows_launch(h->hidden, KB_DT_BF16, f, M, f, b.down->kp, false, nullptr, 0.0f, 0, h->q,
-                              h->scales, h->status, layer, s);
+    rc = quantize_rows_amax_launch(h->hidden, KB_DT_BF16, f, h->row_amax, M, f, b.down->kp, h->q, h->scales,
+                                   h->status, layer, s);
     if (rc) return rc;
     GemmArgs dn;
     dn.m = M;
@@ -398,6 +403,7 @@ void destroy_handle(kb_handle* h) {
   cudaFree(h->hidden);
   cudaFree(h->q);
   cudaFree(h->scales);
+  cudaFree(h->row_amax);
   cudaFree(h->hp);
   cudaFree(h->status);
   if (h->stream) cudaStreamDestroy(h->stream);
@@ -588,6 +594,7 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
   if (!rc) rc = dev_alloc(&h->hidden, M * f, "workspace");
   if (!rc) rc = dev_alloc(&h->q, M * kq, "workspace");
   if (!rc) rc = dev_alloc(&h->scales, M, "workspace");
+  if (!rc) rc = dev_alloc(&h->row_amax, M, "workspace");
   if (!rc) rc = dev_alloc(&h->hp, M * kHeadN, "workspace");
   if (!rc) rc = dev_alloc(&h->status, 2, "status word");
   for (auto& sl : h->slots) {

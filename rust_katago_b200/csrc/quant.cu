@@ -111,6 +111,69 @@ __device__ __noinline__ void quantize_group_slow_f32(float4 a, float4 b, float s
       make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
 }
 
+template <bool F16>
+__device__ __forceinline__ uint2 quant_group_fast(const uint32_t (&w)[4], float scale, float r) {
+  int qi[8];
+#pragma unroll
+  for (int t = 0; t < 8; t += 2) {
+    // Pair of values through packed fp32: q0 = v*r, e = v - q0*s, q = q0 + e*r
+    // (a packed multiply feeding only multiplicands cannot be contracted).
+    const uint32_t pw = w[t / 2];
+    const float2 v = make_float2(from16(static_cast<uint16_t>(pw & 0xffffu), F16), from16(static_cast<uint16_t>(pw >> 16), F16));
+    const float2 q0 = mul2(v, make_float2(r, r));
+    const float2 e = fma2(make_float2(-q0.x, -q0.y), make_float2(scale, scale), v);
+    const float2 q = fma2(e, make_float2(r, r), q0);
+    // |v/scale| <= 127 for a normal scale = amax/127, so no clamp is needed.
+    qi[t] = __float2int_rn(q.x);
+    qi[t + 1] = __float2int_rn(q.y);
+  }
+  return make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
+}
+
+__device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
+  if (f16) {
+    const __half2 h = __floats2half2_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Quantise a warp-held row of packed 16-bit values (lane l holds groups
+// l, l+32, ...; amax2 = this lane's packed |bits| maximum).
+template <bool F16, int G>
+__device__ __forceinline__ void quantize_packed_row(const uint32_t (&w)[G][4], uint32_t amax2, int kp, int lane,
+                                                    int8_t* dst, float* scale_out, unsigned* status,
+                                                    unsigned layer) {
+  const uint32_t m16 = max(amax2 & 0xffffu, amax2 >> 16);
+  const uint32_t amax = warp_max_u32(F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
+  const float scale = int8_scale_from_amax(amax);
+  const bool bad = amax >= 0x7f800000u;
+  if (lane == 0) {
+    *scale_out = scale;
+    if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+  }
+  // The reciprocal path needs a normal scale and a normal amax; other rows
+  // (all zero, tiny, non-finite) take the IEEE-division loop, kept out of line.
+  const bool fast = !bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u;
+  const int out_groups = kp / 8;
+  if (fast) {
+    const float r = __frcp_rn(scale);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j;
+      if (g < out_groups) *reinterpret_cast<uint2*>(dst + 8 * g) = quant_group_fast<F16>(w[j], scale, r);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j;
+      if (g < out_groups)
+        quantize_group_slow(make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]), F16, scale, bad, dst + 8 * g);
+    }
+  }
+}
+
 // Plain 16-bit rows (no RMS): the row stays packed (two values per register),
 // the absolute maximum is a packed unsigned max over |bits|.
 template <bool F16, int G>
@@ -138,41 +201,7 @@ __device__ __forceinline__ void quantize_row16(const uint16_t* src, bool vec, in
 #pragma unroll
     for (int t = 0; t < 4; ++t) amax2 = __vmaxu2(amax2, w[j][t] & 0x7fff7fffu);
   }
-  const uint32_t m16 = max(amax2 & 0xffffu, amax2 >> 16);
-  const uint32_t amax = warp_max_u32(F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
-  const float scale = int8_scale_from_amax(amax);
-  const bool bad = amax >= 0x7f800000u;
-  if (lane == 0) {
-    *scale_out = scale;
-    if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
-  }
-  // The reciprocal path needs a normal scale and a normal amax; other rows
-  // (all zero, tiny, non-finite) take the IEEE-division loop, kept out of line.
-  const bool fast = !bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u;
-  const int out_groups = kp / 8;
-  if (fast) {
-    const float r = __frcp_rn(scale);
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int g = lane + 32 * j;
-      if (g < out_groups) {
-        int qi[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-          qi[t] = quant_i8_rcp(from16(static_cast<uint16_t>(t & 1 ? w[j][t / 2] >> 16 : w[j][t / 2] & 0xffffu), F16),
-                               scale, r);
-        *reinterpret_cast<uint2*>(dst + 8 * g) =
-            make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
-      }
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int g = lane + 32 * j;
-      if (g < out_groups)
-        quantize_group_slow(make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]), F16, scale, bad, dst + 8 * g);
-    }
-  }
+  quantize_packed_row<F16, G>(w, amax2, kp, lane, dst, scale_out, status, layer);
 }
 
 // One warp per row; G = groups of 8 per lane (W <= 256 * G).
@@ -214,17 +243,29 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
     sum = warp_sum_xor(sum);
     const float rstd =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(width)), eps)));
+    // v = T16((x * rstd) * gamma), kept packed; columns past `width` are 0.
+    uint32_t nw[G][4];
+    uint32_t amax2 = 0;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       const int c0 = 8 * (lane + 32 * j);
-      if (c0 < width) {
-        float gm[8];
+      float gm[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (c0 < width)
         load_group<kInF32>(gamma, lane + 32 * j, width, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0, gm);
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
-          v[j][t] = c0 + t < width ? from16(bits16(__fmul_rn(__fmul_rn(v[j][t], rstd), gm[t]), f16), f16) : 0.0f;
+      for (int t = 0; t < 4; ++t) {
+        const float2 n2 = mul2(mul2(make_float2(v[j][2 * t], v[j][2 * t + 1]), make_float2(rstd, rstd)),
+                               make_float2(gm[2 * t], gm[2 * t + 1]));
+        nw[j][t] = pack16x2(n2, bound_f16 != 0);
+        amax2 = __vmaxu2(amax2, nw[j][t] & 0x7fff7fffu);
       }
     }
+    int8_t* dst = q + static_cast<size_t>(row) * kp;
+    if (bound_f16)
+      quantize_packed_row<true, G>(nw, amax2, kp, lane, dst, scales + row, status, layer);
+    else
+      quantize_packed_row<false, G>(nw, amax2, kp, lane, dst, scales + row, status, layer);
+    return;
   }
   uint32_t amax = 0;
 #pragma unroll
@@ -293,7 +334,90 @@ int launch_quant(const void* x, long ldx, const float* gamma, float eps, int row
   return KB_E_INVALID;
 }
 
+// Streaming quantiser for rows whose absolute maximum was already produced by
+// the kernel that wrote them (the GEMM / attention epilogue's row_amax): no row
+// reduction.  A thread owns four 8-column groups, strided by the block size so
+// each of its four 16-byte loads is coalesced across the warp and all four are
+// in flight together; results leave as 8-byte stores.  Same scale and
+// rounding as quantize_row16 (bit-identical results).
+constexpr int kStreamGroups = 4;
+
+template <bool F16>
+__global__ void __launch_bounds__(256) quantize_rows_amax_kernel(
+    const uint16_t* __restrict__ x, long ldx, const uint32_t* __restrict__ row_amax, int rows, int width,
+    int kp, int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
+  const int out_groups = kp / 8;
+  const long total = static_cast<long>(rows) * out_groups;
+  const long step = static_cast<long>(gridDim.x) * blockDim.x * kStreamGroups;
+  for (long base = static_cast<long>(blockIdx.x) * blockDim.x * kStreamGroups + threadIdx.x; base < total;
+       base += step) {
+    uint32_t w[kStreamGroups][4];
+    int row[kStreamGroups], c0[kStreamGroups];
+#pragma unroll
+    for (int j = 0; j < kStreamGroups; ++j) {
+      const long idx = base + static_cast<long>(j) * blockDim.x;
+      w[j][0] = w[j][1] = w[j][2] = w[j][3] = 0;
+      row[j] = -1;
+      if (idx < total) {
+        row[j] = static_cast<int>(idx / out_groups);
+        c0[j] = 8 * static_cast<int>(idx % out_groups);
+        const uint16_t* src = x + static_cast<size_t>(row[j]) * ldx + c0[j];
+        if (c0[j] + 8 <= width) {
+          const uint4 a = __ldg(reinterpret_cast<const uint4*>(src));
+          w[j][0] = a.x; w[j][1] = a.y; w[j][2] = a.z; w[j][3] = a.w;
+        } else {
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            if (c0[j] + t < width) w[j][t / 2] |= static_cast<uint32_t>(src[t]) << (16 * (t & 1));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kStreamGroups; ++j) {
+      if (row[j] < 0) continue;
+      const uint32_t amax = __ldg(row_amax + row[j]);
+      const float scale = int8_scale_from_amax(amax);
+      const bool bad = amax >= 0x7f800000u;
+      if (c0[j] == 0) {
+        scales[row[j]] = scale;
+        if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+      }
+      int8_t* dst = q + static_cast<size_t>(row[j]) * kp + c0[j];
+      if (!bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u)
+        *reinterpret_cast<uint2*>(dst) = quant_group_fast<F16>(w[j], scale, __frcp_rn(scale));
+      else
+        quantize_group_slow(make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]), F16, scale, bad, dst);
+    }
+  }
+}
+
 }  // namespace
+
+// Quantise 16-bit rows given their |value| bit maximum (row_amax, [rows]).
+// Row starts must be 16-byte aligned (ldx % 8 == 0).
+int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t* row_amax, int rows, int width,
+                              int kp, int8_t* q, float* scales, unsigned* status, unsigned layer,
+                              cudaStream_t stream) {
+  if (rows <= 0 || width <= 0 || kp < width || kp % 16 != 0 || ldx < width || ldx % 8 != 0 ||
+      (dtype != kInF16 && dtype != kInBF16) || row_amax == nullptr ||
+      (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 15)) {
+    set_error("amax quantiser: need 16-bit rows with 16-byte aligned starts, kp % 16 == 0, and row_amax");
+    return KB_E_INVALID;
+  }
+  const long total = static_cast<long>(rows) * (kp / 8);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long max_blocks = static_cast<long>(num_sms(dev)) * 8;
+  const long need = (total + 256 * kStreamGroups - 1) / (256 * kStreamGroups);
+  const long blocks = need < max_blocks ? need : max_blocks;
+  if (dtype == kInF16)
+    quantize_rows_amax_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, q, scales, status, layer);
+  else
+    quantize_rows_amax_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, q, scales, status, layer);
+  return check_cuda(cudaGetLastError(), "amax quantiser launch");
+}
 
 // dtype: 0 = f32, 1 = f16, 2 = bf16.  rms: apply RMSNorm with gamma/eps and a
 // 16-bit boundary (bound_f16: 1 = fp16, 0 = bf16) before quantising.

@@ -155,6 +155,11 @@ def quantize_rows(x, dtype, rows, width, stride, kp, q, scales, stream=None):
     call("kb_int8_quantize_rows", _ptr(x), dtype, rows, width, stride, kp, _ptr(q), _ptr(scales), _stream(stream))
 
 
+def quantize_rows_amax(x, dtype, rows, width, stride, kp, row_amax, q, scales, stream=None):
+    call("kb_int8_quantize_rows_amax", _ptr(x), dtype, rows, width, stride, kp, _ptr(row_amax), _ptr(q),
+         _ptr(scales), _stream(stream))
+
+
 def rms_quantize(x, dtype, rows, width, stride, gamma, eps, boundary_dtype, kp, q, scales, stream=None):
     call("kb_int8_rms_quantize", _ptr(x), dtype, rows, width, stride, _ptr(gamma), eps, boundary_dtype, kp,
          _ptr(q), _ptr(scales), _stream(stream))

@@ -158,6 +158,31 @@ def test_quantize_rows_bit_exact(cuda, oracle, dtype, rows, width, stride):
     assert same_f32(host(s), os_)
 
 
+@pytest.mark.parametrize("rows,width", [(1, 8), (361, 3072), (1000, 472), (92416, 3072)])
+def test_gemm_row_amax_and_streaming_quantiser(cuda, oracle, rows, width):
+    """GEMM epilogue row_amax + streaming quantiser == full-row quantiser (bitwise)."""
+    torch = cuda
+    rng = np.random.default_rng(rows + width)
+    kp = 768
+    a = torch.from_numpy(rng.integers(-127, 128, (rows, kp), dtype=np.int8)).cuda()
+    w = torch.from_numpy(rng.integers(-127, 128, (width, kp), dtype=np.int8)).cuda()
+    sa = torch.from_numpy(rng.uniform(1e-4, 1e-2, rows).astype(np.float32)).cuda()
+    sw = torch.from_numpy(rng.uniform(1e-4, 1e-2, width).astype(np.float32)).cuda()
+    bias = torch.from_numpy((0.02 * rng.standard_normal(width)).astype(np.float32)).cuda()
+    out = torch.zeros((rows, width), dtype=torch.int16, device="cuda")
+    amax = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    int8.linear(a, sa, w, sw, bias, rows, width, kp, _capi.EPI_16, out, width, act=_capi.ACT_GELU, row_amax=amax)
+    kpo = (width + 15) // 16 * 16
+    q = torch.full((rows, kpo), 9, dtype=torch.int8, device="cuda")
+    s = torch.zeros(rows, device="cuda")
+    int8.quantize_rows_amax(out, _capi.DT_BF16, rows, width, width, kpo, amax, q, s)
+    torch.cuda.synchronize()
+    hid = oracle.decode16(out.cpu().numpy().view(np.uint16), False)
+    oq, os_ = oracle.quantize_rows(hid, kp=kpo)
+    assert (q.cpu().numpy() == oq).all()
+    assert same_f32(s.cpu().numpy(), os_)
+
+
 # ------------------------------------------------------------------ FFN blocks
 def ref_weights(n):
     # crates/kata_nn/tests/int8_kernels.rs:352-357
