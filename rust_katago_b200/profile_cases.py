@@ -1,0 +1,82 @@
+"""Kernel cases for profiling the library under Nsight Compute.
+
+    python -m rust_katago_b200.profile_cases <case> [batch]
+
+Each case runs one kernel family at the b11c768 trunk's batch-256 shapes (or
+one whole forward) twice, so `ncu -s 1 -c 1` captures a warm launch:
+
+  trunk   two forwards without a graph (104 kernels each)
+  up      INT8 GEMM 92416x3072x768 + bias + GELU (the FFN up projection)
+  down    INT8 GEMM 92416x768x3072 + bias + bf16 residual
+  qkv     INT8 GEMM 92416x2304x768
+  attn    RoPE attention, 256 positions x 12 heads x 64
+  quant   streaming quantiser of the 92416x3072 bf16 FFN hidden
+  rms     fused RMSNorm -> bf16 -> INT8 quantiser, 92416x768
+"""
+
+from __future__ import annotations
+
+import sys
+
+
+def main(argv):
+    import torch
+
+    from . import _capi, backend, int8, synthetic
+
+    case = argv[1] if len(argv) > 1 else "trunk"
+    batch = int(argv[2]) if len(argv) > 2 else 256
+    m = batch * 361
+    torch.cuda.set_device(0)
+    if case == "trunk":
+        topo = synthetic.B11C768
+        model = backend.CudaBackend.load_model(topo, synthetic.make_blob(topo, 1234))
+        h = backend.CudaBackend.create_compute_handle(model, batch)
+        sp, gl = synthetic.make_positions(batch, 5)
+        dsp, dgl = torch.from_numpy(sp).cuda(), torch.from_numpy(gl).cuda()
+        dout = torch.zeros(batch * backend.OUT_PER_POS, device="cuda")
+        for _ in range(2):
+            h.forward_device(batch, dsp, dgl, dout, use_graph=False)
+    elif case in ("up", "down", "qkv"):
+        n, k, epi, act = {"up": (3072, 768, _capi.EPI_16, _capi.ACT_GELU),
+                          "down": (768, 3072, _capi.EPI_RES16, 0),
+                          "qkv": (2304, 768, _capi.EPI_16, 0)}[case]
+        a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda")
+        w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda")
+        sa = torch.rand(m, device="cuda") * 0.01
+        sw = torch.rand(n, device="cuda") * 0.01
+        b = torch.rand(n, device="cuda")
+        out = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+        for _ in range(2):
+            int8.linear(a, sa, w, sw, b, m, n, k, epi, out, n, act=act)
+    elif case == "attn":
+        heads, d = 12, 64
+        qkv = torch.randn(m, 3 * heads * d, device="cuda").to(torch.bfloat16)
+        cs = torch.ones(361, heads, d // 2, device="cuda")
+        sn = torch.zeros_like(cs)
+        out = torch.empty(m, heads * d, dtype=torch.bfloat16, device="cuda")
+        for _ in range(2):
+            _capi.call("kb_attention", qkv.data_ptr(), cs.data_ptr(), sn.data_ptr(), out.data_ptr(), batch, heads,
+                       d, 0.125, _capi.DT_BF16, int(torch.cuda.current_stream().cuda_stream))
+    elif case == "quant":
+        x = torch.randn(m, 3072, device="cuda").to(torch.bfloat16).view(torch.int16)
+        amax = torch.full((m,), 0x41000000, dtype=torch.int32, device="cuda")  # |x| <= 8.0 as f32 bits
+        q = torch.empty(m, 3072, dtype=torch.int8, device="cuda")
+        s = torch.empty(m, device="cuda")
+        for _ in range(2):
+            int8.quantize_rows_amax(x, _capi.DT_BF16, m, 3072, 3072, 3072, amax, q, s)
+    elif case == "rms":
+        x = torch.randn(m, 768, device="cuda").to(torch.bfloat16).view(torch.int16)
+        g = torch.ones(768, device="cuda")
+        q = torch.empty(m, 768, dtype=torch.int8, device="cuda")
+        s = torch.empty(m, device="cuda")
+        for _ in range(2):
+            int8.rms_quantize(x, _capi.DT_BF16, m, 768, 768, g, 1e-6, _capi.DT_BF16, 768, q, s)
+    else:
+        raise SystemExit(f"unknown case {case!r}; see the module docstring")
+    torch.cuda.synchronize()
+    print("ok", case, batch)
+
+
+if __name__ == "__main__":
+    main(sys.argv)
