@@ -221,6 +221,87 @@ KB_API int kb_bf16_linear(const uint16_t* a, const uint16_t* w, const float* bia
 KB_API int kb_attention(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
                         int batch, int heads, int head_dim, float scale, int dtype, uintptr_t stream);
 
+/* ------------------------------------------------------------------ MXFP8 (block-scaled E4M3) */
+
+/* Status word [flags, first_layer]: flags OR-ed, first_layer = first layer
+ * that reported (0xffffffff = none); same protocol as mxfp8.rs:22-30. */
+#define KB_STATUS_NAN 1u               /* NaN input to a quantiser */
+#define KB_STATUS_INF 2u               /* infinite input to a quantiser */
+#define KB_STATUS_OUTPUT_NONFINITE 4u  /* a non-finite value reached an output */
+#define KB_STATUS_WEIGHT_OVERFLOW 8u   /* an MXFP8 weight decodes to a non-finite value */
+#define KB_STATUS_UNSUPPORTED_ARCH 16u /* kernel ran on a device other than sm_100 */
+#define KB_STATUS_TIMEOUT 32u          /* a bounded device wait gave up (no hang, no trap) */
+
+/* MXFP8 projection outputs (Mxfp8Output, src/backends/mxfp8.rs:382-400, plus bf16). */
+#define KB_MX_OUT_HALF 0           /* out f16 [rows, n] = half(acc) */
+#define KB_MX_OUT_FLOAT 1          /* out f32 = acc */
+#define KB_MX_OUT_FLOAT_RESIDUAL 2 /* out f32 = out + acc (beta = 1) */
+#define KB_MX_OUT_BF16 3           /* out bf16 = bf16(act(acc + bias)) */
+
+/* Reset a status word to [0, 0xffffffff] on `stream`.
+ * Replaces: mxfp8_begin_forward_kernel (cuda-kernels/mxfp8.cu:91-96) via
+ * Mxfp8Workspace::begin_forward (src/backends/mxfp8.rs:977). */
+KB_API int kb_status_reset(uint32_t* status, uintptr_t stream);
+
+/* kp = ceil(k/32)*32; blocks4 = ceil(kp/128)*4; data bytes = rows*kp; scale bytes
+ * = ceil(rows/128)*128*blocks4.  Rejects rows <= 0, k outside 1..8192 and sizes
+ * beyond 32-bit indexing.  Replaces: dimensions (src/backends/mxfp8.rs:56-76). */
+KB_API int kb_mxfp8_dimensions(int rows, int k, int* kp, int* blocks4, size_t* data_bytes, size_t* scale_bytes);
+
+/* Block-32 quantiser: x [rows, stride] (dtype KB_DT_F32/F16/BF16) -> q E4M3
+ * [rows, kp] and scales (UE8M0, packed 512-byte tiles of 128 rows x 4 blocks:
+ * byte ((row/128)*(blocks4/4) + block/4)*512 + (row%32)*16 + (row%128/32)*4 +
+ * block%4).  Scale bytes of padding rows/blocks and of [scale bytes,
+ * scale_capacity) are zeroed.  NaN/Inf inputs set KB_STATUS_NAN/INF with `layer`
+ * and give their block scale 127 and zero bytes.
+ * Replaces: mxfp8_quantize_{half,float}_kernel + mxfp8_clear_scales_kernel
+ * (cuda-kernels/mxfp8.cu:36-149) via Mxfp8Kernels::quantize (mxfp8.rs:209-270). */
+KB_API int kb_mxfp8_quantize(const void* x, int dtype, int rows, int k, int stride, uint8_t* q, uint8_t* scales,
+                             size_t scale_capacity, uint32_t* status, uint32_t layer, uintptr_t stream);
+
+/* Fused RMSNorm -> 16-bit boundary (boundary_dtype KB_DT_F16 or KB_DT_BF16) ->
+ * MXFP8: v = T16((x * rstd) * gamma) with the same rstd and rounding as
+ * kb_int8_rms_quantize, then the block-32 quantiser of kb_mxfp8_quantize on v.
+ * width <= 4096.  The whole scale buffer (scale_capacity bytes) is cleared first.
+ * Replaces: rms_norm_f32_w4_kernel (cuda-kernels/executor.cu:478-519) followed by
+ * mxfp8_quantize_half_kernel (cuda-kernels/mxfp8.cu:103-108). */
+KB_API int kb_mxfp8_rms_quantize(const void* x, int dtype, int rows, int width, int stride, const float* gamma,
+                                 float eps, int boundary_dtype, uint8_t* q, uint8_t* scales, size_t scale_capacity,
+                                 uint32_t* status, uint32_t layer, uintptr_t stream);
+
+typedef struct kb_mxfp8_weight kb_mxfp8_weight;
+
+/* Quantise an original fp32 weight [n, stride] (first k columns used) on the
+ * current device and keep it resident (immutable).  Rejects NaN/Inf (host
+ * scan) and weights whose decoded value overflows fp32 (device check).
+ * Replaces: Mxfp8Weight::upload_from_f32 (src/backends/mxfp8.rs:290-350). */
+KB_API int kb_mxfp8_weight_upload(const float* w, int n, int k, int stride, kb_mxfp8_weight** out);
+
+KB_API int kb_mxfp8_weight_info(const kb_mxfp8_weight* w, int* n, int* k, int* kp, const uint8_t** q,
+                                const uint8_t** scales, size_t* scale_bytes);
+
+KB_API void kb_mxfp8_weight_destroy(kb_mxfp8_weight* w);
+
+/* Block-scaled GEMM on quantised activations: out[rows, n] from a_q [rows, kp]
+ * and a_scales (packed, as produced by kb_mxfp8_quantize for this kp) against
+ * the weight, fp32 accumulation on tcgen05 (kind::mxf8f6f4.block_scale,
+ * UE8M0 x 32).  out_kind KB_MX_OUT_*; bias (n fp32, or NULL) and act
+ * (KB_ACT_*) apply to KB_MX_OUT_BF16 only.  A non-finite output sets
+ * KB_STATUS_OUTPUT_NONFINITE with `layer`.  ldo: output row stride in elements.
+ * Replaces: LtPlan::run (src/backends/mxfp8.rs:683-720) + mxfp8_check_*_output_kernel
+ * (cuda-kernels/mxfp8.cu:151-159). */
+KB_API int kb_mxfp8_gemm(const uint8_t* a_q, const uint8_t* a_scales, int rows, const kb_mxfp8_weight* w,
+                         const float* bias, int act, int out_kind, void* out, long ldo, uint32_t* status,
+                         uint32_t layer, uintptr_t stream);
+
+/* One MXFP8 projection: quantise x [rows, stride] (16-bit, dtype KB_DT_F16 or
+ * KB_DT_BF16) into the caller's scratch (q: rows*kp bytes, scales: at least the
+ * scale bytes of (rows, kp), cleared beyond), then kb_mxfp8_gemm.
+ * Replaces: Mxfp8Workspace::project{,_half,_f32} (src/backends/mxfp8.rs:1055-1159). */
+KB_API int kb_mxfp8_project(const kb_mxfp8_weight* w, const void* x, int dtype, int rows, int stride,
+                            uint8_t* q_scratch, uint8_t* scale_scratch, size_t scale_capacity, int out_kind,
+                            void* out, long ldo, uint32_t* status, uint32_t layer, uintptr_t stream);
+
 /* ------------------------------------------------------------------ model and evaluator */
 
 #define KB_PREC_INT8 0 /* W8A8: every trunk linear INT8 x INT8 -> INT32 */

@@ -44,6 +44,15 @@ SIGNATURES: dict[str, tuple] = {
     "kb_int8_ffn_gelu_rms_noalloc": (I, [STREAM, P, F, P, P, P, P, P, I]),
     "kb_bf16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
     "kb_attention": (I, [P, P, P, P, I, I, I, F, I, STREAM]),
+    "kb_status_reset": (I, [P, STREAM]),
+    "kb_mxfp8_dimensions": (I, [I, I, IP, IP, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
+    "kb_mxfp8_quantize": (I, [P, I, I, I, I, P, P, ctypes.c_size_t, P, ctypes.c_uint32, STREAM]),
+    "kb_mxfp8_rms_quantize": (I, [P, I, I, I, I, P, F, I, P, P, ctypes.c_size_t, P, ctypes.c_uint32, STREAM]),
+    "kb_mxfp8_weight_upload": (I, [P, I, I, I, PP]),
+    "kb_mxfp8_weight_info": (I, [P, IP, IP, IP, PP, PP, ctypes.POINTER(ctypes.c_size_t)]),
+    "kb_mxfp8_weight_destroy": (None, [P]),
+    "kb_mxfp8_gemm": (I, [P, P, I, P, P, I, I, P, ctypes.c_long, P, ctypes.c_uint32, STREAM]),
+    "kb_mxfp8_project": (I, [P, P, I, I, I, P, P, ctypes.c_size_t, I, P, ctypes.c_long, P, ctypes.c_uint32, STREAM]),
     "kb_model_blob_floats": (I, [P, ctypes.POINTER(ctypes.c_size_t)]),
     "kb_model_load": (I, [P, P, ctypes.c_size_t, I, PP]),
     "kb_model_destroy": (None, [P]),
@@ -72,6 +81,10 @@ DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 EPI_I32, EPI_F16, EPI_RES_F32, EPI_16, EPI_RES16, EPI_SWIGLU16, EPI_F32 = range(7)
 ACT_NONE, ACT_GELU, ACT_SILU = 0, 1, 2
 LAYOUT_PLAIN, LAYOUT_SWIGLU_DUAL = 0, 1
+MX_OUT_HALF, MX_OUT_FLOAT, MX_OUT_FLOAT_RESIDUAL, MX_OUT_BF16 = range(4)
+STATUS_NAN, STATUS_INF, STATUS_OUTPUT_NONFINITE, STATUS_WEIGHT_OVERFLOW = 1, 2, 4, 8
+STATUS_UNSUPPORTED_ARCH, STATUS_TIMEOUT = 16, 32
+NO_LAYER = 0xFFFFFFFF
 
 _lib: ctypes.CDLL | None = None
 

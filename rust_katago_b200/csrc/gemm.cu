@@ -43,18 +43,34 @@ constexpr int kSmemLimit = 227 * 1024;
 // GEMMs are bound by how fast the epilogue can drain results, so they trade
 // one ring stage for four staging tiles per warp; long-K GEMMs keep the deeper
 // ring and two staging tiles.
-template <int BN, int SB>
+constexpr uint32_t pow2_cols(uint32_t c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
+
+template <int KIND, int BN, int SB>
 struct GemmCfg {
   static constexpr int kABytes = kBM * kBKBytes;
   static constexpr int kBBytes = BN * kBKBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  // MXFP8: one 512-byte scale tile of A (128 rows x 4 K blocks) and BN/128 of B
+  // per stage, each copied to 4 TMEM columns by tcgen05.cp.
+  static constexpr int kSfBytes = KIND == kGemmMXF8 ? 512 + 512 * (BN / 128) : 0;
+  static constexpr int kSfCols = KIND == kGemmMXF8 ? 4 + 4 * (BN / 128) : 0;
   static constexpr int kStagingBytes = kEpiWarps * SB * kStageTile;
-  static constexpr int kStages = (kSmemLimit - kStagingBytes - 1024 - 256) / kStageBytes;
+  static constexpr int kStages = (kSmemLimit - kStagingBytes - 1024 - 256) / (kStageBytes + kSfBytes);
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kSmemBytes = kRingBytes + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSfRingBytes = kStages * kSfBytes;
+  static constexpr uint32_t kTmemCols = pow2_cols(2 * BN + kStages * kSfCols);
+  static constexpr int kSmemBytes =
+      kRingBytes + kStagingBytes + kSfRingBytes + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(kStages >= 3, "ring too shallow");
+  static_assert(2 * BN + kStages * kSfCols <= 512, "TMEM columns exceeded");
 };
+
+// Shared-memory descriptor of one 512-byte scale tile for tcgen05.cp
+// .32x128b: 32 rows of 16 bytes, no swizzle, 8-row core groups 128 bytes apart.
+__device__ __forceinline__ uint64_t sf_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(128 >> 4) << 32) |
+         (1ull << 46);
+}
 
 template <int KIND>
 __device__ __forceinline__ float acc_value(uint32_t bits, float sa, float sw) {
@@ -188,6 +204,18 @@ __device__ __forceinline__ void emit16(Out16& o, const GemmArgs& g, const uint32
   }
 }
 
+// True when any of the first `valid` 16-bit values is Inf or NaN.
+__device__ __forceinline__ bool nonfinite16(const uint32_t (&hw)[16], int valid, bool f16) {
+  const uint32_t m = f16 ? 0x7c00u : 0x7f80u;
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    bad |= (2 * i < valid) && ((hw[i] & m) == m);
+    bad |= (2 * i + 1 < valid) && (((hw[i] >> 16) & m) == m);
+  }
+  return bad;
+}
+
 // Dequantised pair (i, i+1) of a 32-column chunk: (f32(dot) * sa) * sw, or the
 // fp32 accumulator itself for the bf16 / MXFP8 kinds.
 template <int KIND>
@@ -208,7 +236,7 @@ template <int KIND, int BN, int EPI, int ACT, int SB>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g, const int use_tma_out) {
-  using Cfg = GemmCfg<BN, SB>;
+  using Cfg = GemmCfg<KIND, BN, SB>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kElemBytes = (KIND == kGemmBF16) ? 2 : 1;
   constexpr int kBKElems = kBKBytes / kElemBytes;
@@ -218,7 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* ring = smem;
   uint8_t* staging = smem + Cfg::kRingBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::kStagingBytes);
+  uint8_t* sf_ring = staging + Cfg::kStagingBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sf_ring + Cfg::kSfRingBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -273,9 +302,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* sa = ring + s * Cfg::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes + Cfg::kSfBytes);
           tma_load_2d(sa, &tmap_a, &full[s], kb * kBKElems, mb * kBM);
           tma_load_2d(sa + Cfg::kABytes, &tmap_b, &full[s], kb * kBKElems, nb * BN);
+          if constexpr (KIND == kGemmMXF8) {
+            // Scale tiles: tile (row/128, kblock) of the packed layout is 512
+            // contiguous bytes; k_blocks tiles per 128-row band.
+            uint8_t* sf = sf_ring + s * Cfg::kSfBytes;
+            bulk_load(sf, g.sfa + (static_cast<size_t>(mb) * k_blocks + kb) * 512u, 512u, &full[s]);
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              bulk_load(sf + 512 * (j + 1),
+                        g.sfb + (static_cast<size_t>(nb * (BN / 128) + j) * k_blocks + kb) * 512u, 512u, &full[s]);
+          }
           issued |= 1u << s;
           issued_par = (issued_par & ~(1u << s)) | (ph << s);
           if (++s == kStages) {
@@ -314,10 +353,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(ring + s * Cfg::kStageBytes);
           const uint64_t adesc = sw128_desc(a_addr);
           const uint64_t bdesc = sw128_desc(a_addr + Cfg::kABytes);
+          if constexpr (KIND == kGemmMXF8) {
+            // Scale tiles -> TMEM (4 columns each, replicated to all four lane
+            // quarters); tcgen05.cp and tcgen05.mma from this thread execute in
+            // issue order.  Column c, byte b of lane l then holds the scale of
+            // row 32c + l%32, K block b: the MMA of K block kk selects byte kk.
+            const uint32_t tsf = tmem_base + static_cast<uint32_t>(2 * BN + s * Cfg::kSfCols);
+            const uint32_t sf_addr = smem_u32(sf_ring + s * Cfg::kSfBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBKBytes / 32; ++kk) {
-            // +32 bytes along K inside the swizzle atom = +2 in the address field.
-            mma_issue<KIND>(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0, 0, 0);
+            for (int j = 0; j < 1 + BN / 128; ++j) tmem_cp_32x128_warpx4(tsf + 4 * j, sf_desc(sf_addr + 512 * j));
+#pragma unroll
+            for (int kk = 0; kk < kBKBytes / 32; ++kk) {
+              const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 29) | (static_cast<uint32_t>(kk) << 4);
+              mma_issue<KIND>(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, id, (kb | kk) != 0, tsf, tsf + 4);
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < kBKBytes / 32; ++kk) {
+              // +32 bytes along K inside the swizzle atom = +2 in the address field.
+              mma_issue<KIND>(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0, 0, 0);
+            }
           }
           tc_commit(&empty[s]);
           if (++s == kStages) {
@@ -352,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
       uint32_t amax = 0;
+      bool nonfinite = false;  // MXFP8: output finite check (mxfp8.cu:81-88 in the reference)
       if constexpr (EPI == kEpiSwiGLU16) {
         // Tile columns [0, BN/2) are gate channels, [BN/2, BN) the matching up
         // channels (the dual weight is interleaved per tile at load).
@@ -430,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             if constexpr (EPI != kEpiRes16) amax = max(amax, amax16_to_f32bits(amax2, f16));
+            if constexpr (KIND == kGemmMXF8) nonfinite |= row_ok && nonfinite16(hw, valid, f16);
             emit16<SB>(o, g, hw, row, row0q, col0, lane, row_ok, valid);
           } else if (row_ok) {
             float sw[32], bias[32];
@@ -451,7 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
 #pragma unroll
               for (int i = 0; i < 32; ++i)
-                if (i < valid) dst[i] = __fadd_rn(dst[i], acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f));
+                if (i < valid) {
+                  const float x = __fadd_rn(dst[i], acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f));
+                  dst[i] = x;
+                  if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(x);
+                }
             } else if constexpr (EPI == kEpiF32) {
               float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
               const float* res = g.residual ? static_cast<const float*>(g.residual) +
@@ -464,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   if (g.bias) x = __fadd_rn(x, bias[i]);
                   if (res) x = __fadd_rn(res[i], x);
                   dst[i] = x;
+                  if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(x);
                 }
               }
             }
@@ -476,6 +538,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (g.row_amax != nullptr && row_ok) atomicMax(g.row_amax + row, amax);
+      if constexpr (KIND == kGemmMXF8) {
+        if (__any_sync(0xffffffffu, nonfinite) && lane == 0)
+          record_status(g.status, KB_STATUS_OUTPUT_NONFINITE, g.layer);
+      }
       acc ^= 1;
       if (acc == 0) aph ^= 1;
     }
@@ -525,7 +591,7 @@ bool epi_16bit(int epi) {
 template <int KIND, int BN, int EPI, int ACT, int SB>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int use_tma_out,
                const GemmArgs& g, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN, SB>;
+  using Cfg = GemmCfg<KIND, BN, SB>;
   auto kern = gemm_kernel<KIND, BN, EPI, ACT, SB>;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -547,7 +613,9 @@ template <int KIND, int BN, int SB>
 int dispatch_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int tma_out,
                  const GemmArgs& g, cudaStream_t s) {
   switch (epi) {
-    case kEpiI32: return launch_one<KIND, BN, kEpiI32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiI32:
+      if constexpr (KIND != kGemmMXF8) return launch_one<KIND, BN, kEpiI32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+      break;
     case kEpiF16: return launch_one<KIND, BN, kEpiF16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
     case kEpiResF32: return launch_one<KIND, BN, kEpiResF32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
     case kEpi16:
@@ -555,7 +623,9 @@ int dispatch_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CU
       if (g.act == kActSilu) return launch_one<KIND, BN, kEpi16, kActSilu, SB>(ma, mb, mo, tma_out, g, s);
       return launch_one<KIND, BN, kEpi16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
     case kEpiRes16: return launch_one<KIND, BN, kEpiRes16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
-    case kEpiSwiGLU16: return launch_one<KIND, BN, kEpiSwiGLU16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiSwiGLU16:
+      if constexpr (KIND != kGemmMXF8) return launch_one<KIND, BN, kEpiSwiGLU16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+      break;
     case kEpiF32: return launch_one<KIND, BN, kEpiF32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
   }
   set_error("unknown GEMM epilogue");
@@ -616,6 +686,21 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     set_error("GEMM operands must be 16-byte aligned");
     return KB_E_INVALID;
   }
+  if (kind == kGemmMXF8) {
+    if (epi == kEpiI32 || epi == kEpiSwiGLU16) {
+      set_error("MXFP8 GEMM supports the f16 / 16-bit / residual / f32 epilogues");
+      return KB_E_INVALID;
+    }
+    if (g.sfa == nullptr || g.sfb == nullptr || (reinterpret_cast<uintptr_t>(g.sfa) & 15) ||
+        (reinterpret_cast<uintptr_t>(g.sfb) & 15)) {
+      set_error("MXFP8 GEMM needs 16-byte aligned scale-factor tiles for A and B");
+      return KB_E_INVALID;
+    }
+    if (g.k % 32 != 0) {
+      set_error("MXFP8 GEMM K must be padded to a multiple of 32");
+      return KB_E_INVALID;
+    }
+  }
   if (kind == kGemmI8 && epi != kEpiI32 && (g.row_scale == nullptr || g.col_scale == nullptr)) {
     set_error("INT8 dequant epilogue needs row and column scales");
     return KB_E_INVALID;
@@ -624,7 +709,9 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     set_error("unknown activation");
     return KB_E_INVALID;
   }
-  const int bn = bn_hint ? bn_hint : gemm_pick_bn(kind, epi, g.n);
+  // MXFP8 keeps BN = 128: two 128-column accumulators plus the per-stage
+  // scale-factor columns fill the 512 TMEM columns.
+  const int bn = kind == kGemmMXF8 ? 128 : bn_hint ? bn_hint : gemm_pick_bn(kind, epi, g.n);
   CUtensorMap ma, mb, mo;
   memset(&mo, 0, sizeof(mo));
   int rc = make_operand_map(&ma, a, kind, g.m, g.k, kBM);
@@ -655,6 +742,7 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     return bn == 256 ? dispatch_sb<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, g, stream)
                      : dispatch_sb<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, g, stream);
   }
+  if (kind == kGemmMXF8) return dispatch_sb<kGemmMXF8, 128>(epi, ma, mb, mo, tma_out, g, stream);
   set_error("GEMM kind not supported");
   return KB_E_UNSUPPORTED;
 }

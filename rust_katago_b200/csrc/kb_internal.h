@@ -72,6 +72,22 @@ int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t
                               int kp, int8_t* q, float* scales, unsigned* status, unsigned layer,
                               cudaStream_t stream);
 
+// MXFP8 (mxfp8.cu).  Largest K the block-scaled path accepts (the reference's
+// MAX_K, crates/kata_nn/src/backends/mxfp8.rs:31).
+constexpr int kMxfp8MaxK = 8192;
+// kp = ceil(K/32)*32, blocks4 = ceil(kp/32/4)*4, data = rows*kp bytes,
+// scales = ceil(rows/128)*128*blocks4 bytes (mxfp8.rs:56-76).
+int mxfp8_dims(long rows, long k, int* kp, int* blocks4, size_t* data_bytes, size_t* scale_bytes);
+// Block-32 quantiser of fp32/fp16/bf16 rows (dtype KB_DT_*) into E4M3 [rows, kp]
+// and packed UE8M0 scales; clears scale bytes in [scale_bytes, scale_capacity).
+int mxfp8_quantize_launch(const void* x, int dtype, long ld, int rows, int k, uint8_t* q, uint8_t* scales,
+                          size_t scale_capacity, bool check_weight, unsigned* status, unsigned layer,
+                          cudaStream_t stream);
+// Fused RMSNorm -> 16-bit boundary -> MXFP8 (quant.cu); row width <= 4096.
+int rms_mxfp8_launch(const void* x, int dtype, long ldx, int rows, int width, const float* gamma, float eps,
+                     int bound_f16, uint8_t* q, uint8_t* scales, unsigned* status, unsigned layer,
+                     cudaStream_t stream);
+
 // Encode a 2-D tensor map (innermost dimension `cols`, row pitch `row_bytes`).
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long cols, long rows,
               long row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swz);

@@ -16,6 +16,7 @@
 //   * q = clamp(rne(v / scale), +-127) with IEEE division, 0 for a bad row,
 //     zero padding up to kp (int8_ops.cu:42-46, :80-88); 8-byte stores.
 #include "kb_internal.h"
+#include "kb_mxfp8.cuh"
 #include "kb_numeric.cuh"
 #include "kb_ptx.cuh"
 
@@ -204,6 +205,125 @@ __device__ __forceinline__ void quantize_row16(const uint16_t* src, bool vec, in
   quantize_packed_row<F16, G>(w, amax2, kp, lane, dst, scale_out, status, layer);
 }
 
+// RMSNorm of a warp-held row (lane l holds groups l, l+32, ...):
+// sum = fma(x, x, sum) over the lane's columns in group order, xor butterfly,
+// rstd = 1/sqrt(sum/W + eps) correctly rounded, v = T16((x*rstd)*gamma) packed;
+// columns past `width` are 0.  amax2: the lane's packed |16-bit| maximum.
+template <int G>
+__device__ __forceinline__ void rms_normalize(const float (&v)[G][8], const float* __restrict__ gamma, float eps,
+                                              int width, int lane, bool f16, uint32_t (&nw)[G][4],
+                                              uint32_t& amax2) {
+  float sum = 0.0f;
+#pragma unroll
+  for (int j = 0; j < G; ++j)
+#pragma unroll
+    for (int t = 0; t < 8; ++t) sum = __fmaf_rn(v[j][t], v[j][t], sum);
+  sum = warp_sum_xor(sum);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(width)), eps)));
+  amax2 = 0;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int c0 = 8 * (lane + 32 * j);
+    float gm[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c0 < width)
+      load_group<kInF32>(gamma, lane + 32 * j, width, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0, gm);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 n2 = mul2(mul2(make_float2(v[j][2 * t], v[j][2 * t + 1]), make_float2(rstd, rstd)),
+                             make_float2(gm[2 * t], gm[2 * t + 1]));
+      nw[j][t] = pack16x2(n2, f16);
+      amax2 = __vmaxu2(amax2, nw[j][t] & 0x7fff7fffu);
+    }
+  }
+}
+
+// MXFP8 block-32 quantisation of a warp-held packed 16-bit row: the four lanes
+// 4q..4q+3 of group index j hold one 32-column block, whose amax is a quad
+// reduction.  Same scale / rounding / non-finite rules as mxfp8.cu.
+template <bool F16, int G>
+__device__ __forceinline__ void mx_quantize_packed_row(const uint32_t (&w)[G][4], int row, int kp, int blocks4,
+                                                       int lane, uint8_t* __restrict__ dst,
+                                                       uint8_t* __restrict__ scales, unsigned* status,
+                                                       unsigned layer) {
+  const uint32_t inf16 = F16 ? 0x7c00u : 0x7f80u;
+  const int nblocks = kp >> 5;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int g = lane + 32 * j;
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) m2 = __vmaxu2(m2, w[j][t] & 0x7fff7fffu);
+    const uint32_t m16 = max(m2 & 0xffffu, m2 >> 16);
+    unsigned bad = 0;
+    if (m16 >= inf16) {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t h = ((t & 1) ? w[j][t / 2] >> 16 : w[j][t / 2]) & 0x7fffu;
+        if (h > inf16) bad |= KB_STATUS_NAN;
+        else if (h == inf16) bad |= KB_STATUS_INF;
+      }
+      record_status(status, bad, layer);
+    }
+    // Finite |v| bits of the block (non-finite lanes contribute 0, the block is zeroed).
+    uint32_t a = bad ? 0u : (F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
+    unsigned any_bad = bad;
+    a = max(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = max(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    any_bad |= __shfl_xor_sync(0xffffffffu, any_bad, 1);
+    any_bad |= __shfl_xor_sync(0xffffffffu, any_bad, 2);
+    const int blk = g >> 2;
+    if (blk >= nblocks) continue;  // quad-uniform
+    const bool zero = a == 0u || any_bad != 0;
+    const uint32_t scale = zero ? 127u : ue8m0_ceil(__fdiv_rn(__uint_as_float(a), 448.0f));
+    const float rcp = ue8m0_reciprocal(scale);
+    uint32_t out[2] = {0u, 0u};
+    if (!zero) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float lo = from16(static_cast<uint16_t>(w[j][t] & 0xffffu), F16);
+        const float hi = from16(static_cast<uint16_t>(w[j][t] >> 16), F16);
+        out[t >> 1] |= e4m3x2(__fmul_rn(lo, rcp), __fmul_rn(hi, rcp)) << (16 * (t & 1));
+      }
+    }
+    *reinterpret_cast<uint2*>(dst + 8 * g) = make_uint2(out[0], out[1]);
+    if ((lane & 3) == 0) scales[mx_scale_offset(row, blk, blocks4)] = static_cast<uint8_t>(scale);
+  }
+}
+
+// Fused RMSNorm -> 16-bit boundary -> MXFP8 (E4M3 + UE8M0 per 32 columns).
+template <int IN, int G>
+__global__ void __launch_bounds__(256) rms_mxfp8_kernel(
+    const void* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows, int width, int kp,
+    int blocks4, int bound_f16, uint8_t* __restrict__ q, uint8_t* __restrict__ scales, unsigned* status,
+    unsigned layer) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;  // warp-uniform
+  constexpr int kEsize = IN == kInF32 ? 4 : 2;
+  const uint8_t* src = static_cast<const uint8_t*>(x) + static_cast<size_t>(row) * ldx * kEsize;
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  const int groups = (width + 7) / 8;
+  float v[G][8];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int g = lane + 32 * j;
+    if (g < groups) {
+      load_group<IN>(src, g, width, vec, v[j]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[j][t] = 0.0f;
+    }
+  }
+  uint32_t nw[G][4];
+  uint32_t amax2;
+  rms_normalize<G>(v, gamma, eps, width, lane, bound_f16 != 0, nw, amax2);
+  uint8_t* dst = q + static_cast<size_t>(row) * kp;
+  if (bound_f16)
+    mx_quantize_packed_row<true, G>(nw, row, kp, blocks4, lane, dst, scales, status, layer);
+  else
+    mx_quantize_packed_row<false, G>(nw, row, kp, blocks4, lane, dst, scales, status, layer);
+}
+
 // One warp per row; G = groups of 8 per lane (W <= 256 * G).
 template <int IN, bool RMS, int G>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(
@@ -233,33 +353,10 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
       for (int t = 0; t < 8; ++t) v[j][t] = 0.0f;
     }
   }
-  const bool f16 = bound_f16 != 0;
   if constexpr (RMS) {
-    float sum = 0.0f;
-#pragma unroll
-    for (int j = 0; j < G; ++j)
-#pragma unroll
-      for (int t = 0; t < 8; ++t) sum = __fmaf_rn(v[j][t], v[j][t], sum);
-    sum = warp_sum_xor(sum);
-    const float rstd =
-        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(width)), eps)));
-    // v = T16((x * rstd) * gamma), kept packed; columns past `width` are 0.
     uint32_t nw[G][4];
     uint32_t amax2 = 0;
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int c0 = 8 * (lane + 32 * j);
-      float gm[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (c0 < width)
-        load_group<kInF32>(gamma, lane + 32 * j, width, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0, gm);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 n2 = mul2(mul2(make_float2(v[j][2 * t], v[j][2 * t + 1]), make_float2(rstd, rstd)),
-                               make_float2(gm[2 * t], gm[2 * t + 1]));
-        nw[j][t] = pack16x2(n2, bound_f16 != 0);
-        amax2 = __vmaxu2(amax2, nw[j][t] & 0x7fff7fffu);
-      }
-    }
+    rms_normalize<G>(v, gamma, eps, width, lane, bound_f16 != 0, nw, amax2);
     int8_t* dst = q + static_cast<size_t>(row) * kp;
     if (bound_f16)
       quantize_packed_row<true, G>(nw, amax2, kp, lane, dst, scales + row, status, layer);
@@ -392,6 +489,40 @@ __global__ void __launch_bounds__(256) quantize_rows_amax_kernel(
 }
 
 }  // namespace
+
+// Fused RMSNorm -> 16-bit -> MXFP8 over rows of `width` (<= 4096) columns.
+int rms_mxfp8_launch(const void* x, int dtype, long ldx, int rows, int width, const float* gamma, float eps,
+                     int bound_f16, uint8_t* q, uint8_t* scales, unsigned* status, unsigned layer,
+                     cudaStream_t stream) {
+  int kp = 0, blocks4 = 0;
+  int rc = mxfp8_dims(rows, width, &kp, &blocks4, nullptr, nullptr);
+  if (rc) return rc;
+  if (width > 4096 || ldx < width || gamma == nullptr || !(eps > 0.0f) ||
+      (reinterpret_cast<uintptr_t>(q) & 15) != 0) {
+    set_error("RMS MXFP8 quantiser: width <= 4096, stride >= width, gamma, eps > 0, 16-byte aligned output");
+    return KB_E_INVALID;
+  }
+  const int need = (kp + 255) / 256;
+  const int grid = (rows + 7) / 8;
+#define KB_MXQ(IN, GG)                                                                                         \
+  if (need <= GG) {                                                                                            \
+    rms_mxfp8_kernel<IN, GG><<<grid, 256, 0, stream>>>(x, ldx, gamma, eps, rows, width, kp, blocks4, bound_f16, \
+                                                        q, scales, status, layer);                             \
+    return check_cuda(cudaGetLastError(), "rms mxfp8 launch");                                                  \
+  }
+#define KB_MXQ_ALL(IN) \
+  KB_MXQ(IN, 1) KB_MXQ(IN, 2) KB_MXQ(IN, 3) KB_MXQ(IN, 4) KB_MXQ(IN, 6) KB_MXQ(IN, 8) KB_MXQ(IN, 12) KB_MXQ(IN, 16)
+  switch (dtype) {
+    case kInF32: KB_MXQ_ALL(kInF32) break;
+    case kInF16: KB_MXQ_ALL(kInF16) break;
+    case kInBF16: KB_MXQ_ALL(kInBF16) break;
+    default: set_error("unknown activation dtype"); return KB_E_INVALID;
+  }
+#undef KB_MXQ_ALL
+#undef KB_MXQ
+  set_error("RMS MXFP8 quantiser width above 4096 is not supported");
+  return KB_E_INVALID;
+}
 
 // Quantise 16-bit rows given their |value| bit maximum (row_amax, [rows]).
 // Row starts must be 16-byte aligned (ldx % 8 == 0).

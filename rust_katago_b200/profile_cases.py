@@ -12,6 +12,8 @@ one whole forward) twice, so `ncu -s 1 -c 1` captures a warm launch:
   attn    RoPE attention, 256 positions x 12 heads x 64
   quant   streaming quantiser of the 92416x3072 bf16 FFN hidden
   rms     fused RMSNorm -> bf16 -> INT8 quantiser, 92416x768
+  mxup    MXFP8 block-scaled GEMM 92416x3072x768 -> bf16 (the up projection)
+  mxquant MXFP8 block-32 quantiser of a 92416x768 bf16 activation
 """
 
 from __future__ import annotations
@@ -72,6 +74,27 @@ def main(argv):
         s = torch.empty(m, device="cuda")
         for _ in range(2):
             int8.rms_quantize(x, _capi.DT_BF16, m, 768, 768, g, 1e-6, _capi.DT_BF16, 768, q, s)
+    elif case in ("mxup", "mxquant"):
+        import numpy as np
+
+        from . import mxfp8
+
+        k, n = 768, 3072
+        x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        _, _, data, scale = mxfp8.dimensions(m, k)
+        q = torch.empty(data, dtype=torch.uint8, device="cuda")
+        sc = torch.empty(scale, dtype=torch.uint8, device="cuda")
+        st = torch.zeros(2, dtype=torch.int32, device="cuda")
+        mxfp8.reset_status(st)
+        if case == "mxquant":
+            for _ in range(2):
+                mxfp8.quantize(x, _capi.DT_BF16, m, k, k, q, sc, st)
+        else:
+            w = mxfp8.Mxfp8Weight(np.random.default_rng(0).standard_normal((n, k), np.float32) * 0.02, n, k, k)
+            mxfp8.quantize(x, _capi.DT_BF16, m, k, k, q, sc, st)
+            out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+            for _ in range(2):
+                mxfp8.gemm(q, sc, m, w, out, n, mxfp8.OUT_BF16, st)
     else:
         raise SystemExit(f"unknown case {case!r}; see the module docstring")
     torch.cuda.synchronize()
