@@ -25,6 +25,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -39,6 +40,25 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "positions/sec b11c768 W8A8 fwd @1/2/4/8 B200; INT8 GEMM % tensor peak"
 L2_FLUSH_BYTES = 256 << 20
+
+
+# ncu summaries (profiles/*.md) of the GEMMs that can dominate the step.
+PROFILE_OF_GEMM = {"up 768->3072 + GELU": "gemm_i8_up_gelu_b256.md"}
+
+
+def profile_traffic(gemm_label):
+    """DRAM bytes (read + write) per launch recorded in the committed ncu summary, or None."""
+    name = PROFILE_OF_GEMM.get(gemm_label)
+    path = Path(__file__).resolve().parent / "profiles" / name if name else None
+    if path is None or not path.exists():
+        return None
+    total = 0.0
+    for key in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+        m = re.search(re.escape(key) + r"\s*\|\s*([0-9.]+)\s*MB", path.read_text())
+        if not m:
+            return None
+        total += float(m.group(1)) * 1e6
+    return total
 
 
 def load_peaks():
@@ -398,8 +418,11 @@ def main():
     dom = max(gemm_rows, key=lambda r: r["ms"] * r["per_step"])
     tot_ops = sum(2.0 * r["m"] * r["n"] * r["k"] * r["per_step"] for r in gemm_rows)
     tot_ms = sum(r["ms"] * r["per_step"] for r in gemm_rows)
+    traffic = profile_traffic(dom["gemm"])
     roofline = {"bound": "tensor", "achieved": dom["tops"], "peak": int8_peak, "unit": "TFLOP/s",
-                "frac": dom["tops"] / int8_peak, "traffic": None,
+                "frac": dom["tops"] / int8_peak, "traffic": traffic,
+                "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM, "
+                                "from the ncu capture summarised in profiles/ (same shape, warm launch)",
                 "kernel": f"gemm_kernel<i8,256> {dom['gemm']} (m={dom['m']}, n={dom['n']}, k={dom['k']})",
                 "kernel_ms": dom["ms"],
                 "peak_note": f"INT8 dense peak = 2 x the {peaks['source']} cuBLAS bf16 burst "
