@@ -227,13 +227,21 @@ class TrunkWorkload:
     N(0,1)); one CUDA graph per forward."""
 
     name = "config3: full b11c768 W8A8 trunk forward (11 blocks, 12x64 attention, FFN 768->3072->768, heads)"
+    dtype = "int8"
+    kernel = "gemm_kernel<i8,256>"
+    precision = "int8"
+
+    def topology(self):
+        from rust_katago_b200 import synthetic
+
+        return synthetic.B11C768
 
     def __init__(self, batch: int, torch, seed: int = 1234, build_device: bool = True):
         from rust_katago_b200 import backend, synthetic
 
         self.torch = torch
         self.batch = batch
-        self.topo = synthetic.B11C768
+        self.topo = self.topology()
         self.blob = synthetic.make_blob(self.topo, seed)
         self.spatial, self.glob = synthetic.make_positions(max(batch, 4), seed + 1)
         if not build_device:
@@ -280,11 +288,53 @@ class TrunkWorkload:
         t = self.topo
         t0 = time.perf_counter()
         ot.forward(self.blob, (t.trunk_channels, t.num_blocks, t.num_heads, t.head_dim, t.ffn_channels),
-                   self.spatial[:positions], self.glob[:positions])
+                   self.spatial[:positions], self.glob[:positions], precision=self.precision)
         return time.perf_counter() - t0
 
+    def gemm_launcher(self, m, n, k, epi, act):
+        return gemm_launcher(self.torch, m, n, k, epi, act)
 
-WORKLOADS = {"ffn": FfnWorkload, "trunk": TrunkWorkload}
+
+class TrunkMxfp8Workload(TrunkWorkload):
+    """the same trunk with every projection MXFP8 (E4M3
+    operands, UE8M0 scale per 32 K, fp32 accumulation on tcgen05
+    kind::mxf8f6f4.block_scale); same seeds, weights quantised from fp32."""
+
+    name = "config4: full b11c768 MXFP8 trunk forward (11 blocks, 12x64 attention, FFN 768->3072->768, heads)"
+    dtype = "e4m3"
+    kernel = "gemm_kernel<mxf8f6f4.block_scale,128>"
+    precision = "mxfp8"
+
+    def topology(self):
+        from rust_katago_b200 import synthetic
+
+        return synthetic.B11C768_MXFP8
+
+    def gemm_launcher(self, m, n, k, epi, act):
+        """A launch of the MXFP8 GEMM on quantised random operands of the given shape."""
+        from rust_katago_b200 import _capi, mxfp8
+
+        torch = self.torch
+        x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        _, _, data, scale = mxfp8.dimensions(m, k)
+        q = torch.empty(data, dtype=torch.uint8, device="cuda")
+        sc = torch.zeros(scale, dtype=torch.uint8, device="cuda")
+        st = torch.zeros(2, dtype=torch.int32, device="cuda")
+        mxfp8.reset_status(st)
+        mxfp8.quantize(x, _capi.DT_BF16, m, k, k, q, sc, st)
+        w = mxfp8.Mxfp8Weight(np.random.default_rng(n + k).standard_normal((n, k), np.float32) * 0.02, n, k, k)
+        bias = torch.rand(n, device="cuda") * 0.01
+        out = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+        kind = mxfp8.OUT_BF16_RESIDUAL if epi == _capi.EPI_RES16 else mxfp8.OUT_BF16
+
+        def launch():
+            mxfp8.gemm(q, sc, m, w, out, n, kind, st, bias=bias, act=act)
+
+        launch.keep = (x, q, sc, st, w, bias, out)
+        return launch
+
+
+WORKLOADS = {"ffn": FfnWorkload, "trunk": TrunkWorkload, "trunk_mxfp8": TrunkMxfp8Workload}
 
 
 # ------------------------------------------------------------------ runners
@@ -340,12 +390,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="trunk")
-    ap.add_argument("--batch", type=int, default=None, help="positions per GPU (trunk 256, ffn 64)")
+    ap.add_argument("--batch", type=int, default=None, help="positions per GPU (trunk / trunk_mxfp8 256, ffn 64)")
     ap.add_argument("--ref-positions", type=int, default=1, help="positions per CPU reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.batch is None:
-        args.batch = 256 if args.workload == "trunk" else 64
+        args.batch = 64 if args.workload == "ffn" else 256
     if args.impl == "reference":
         return run_reference(args)
 
@@ -409,7 +459,7 @@ def main():
     int8_peak = 2.0 * peaks["bf16_tflops"]
     gemm_rows = []
     for label, m, n, k, epi, act, per_step in wl.gemms():
-        fn = gemm_launcher(torch, m, n, k, epi, act)
+        fn = wl.gemm_launcher(m, n, k, epi, act) if hasattr(wl, "gemm_launcher") else gemm_launcher(torch, m, n, k, epi, act)
         for _ in range(3):
             fn()
         ms = statistics.mean(time_launches(torch, torch.cuda.current_stream(), fn, flush, 10))
@@ -423,9 +473,11 @@ def main():
                 "frac": dom["tops"] / int8_peak, "traffic": traffic,
                 "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM, "
                                 "from the ncu capture summarised in profiles/ (same shape, warm launch)",
-                "kernel": f"gemm_kernel<i8,256> {dom['gemm']} (m={dom['m']}, n={dom['n']}, k={dom['k']})",
+                "kernel": f"{getattr(wl, 'kernel', 'gemm_kernel<i8,256>')} {dom['gemm']} "
+                          f"(m={dom['m']}, n={dom['n']}, k={dom['k']})",
                 "kernel_ms": dom["ms"],
-                "peak_note": f"INT8 dense peak = 2 x the {peaks['source']} cuBLAS bf16 burst "
+                "peak_note": f"{'FP8' if getattr(wl, 'dtype', 'int8') == 'e4m3' else 'INT8'} dense peak = "
+                             f"2 x the {peaks['source']} cuBLAS bf16 burst "
                              f"({peaks['bf16_tflops']} TFLOP/s): tcgen05 kind::i8 issues at twice kind::f16",
                 "int8_gemms": gemm_rows,
                 "int8_gemm_frac_of_peak": tot_ops / (tot_ms / 1e3) / 1e12 / int8_peak,
@@ -447,7 +499,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8",
+            "vs_baseline": None, "dtype": getattr(wl, "dtype", "int8"),
             "data": "synthetic (seeded: weights N(0,0.02), positions 22 binary planes p=0.3 + 19 N(0,1) globals)",
             "config": {"workload": wl.name, "batch_per_gpu": args.batch, "tokens_per_gpu": args.batch * 361,
                        "parallelism": f"batch-sharded x{world}, weights replicated, no collective",

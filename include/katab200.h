@@ -237,6 +237,7 @@ KB_API int kb_attention(const uint16_t* qkv, const float* rope_cos, const float*
 #define KB_MX_OUT_FLOAT 1          /* out f32 = acc */
 #define KB_MX_OUT_FLOAT_RESIDUAL 2 /* out f32 = out + acc (beta = 1) */
 #define KB_MX_OUT_BF16 3           /* out bf16 = bf16(act(acc + bias)) */
+#define KB_MX_OUT_BF16_RESIDUAL 4  /* out bf16 = bf16(f32(out) + (acc + bias)) */
 
 /* Reset a status word to [0, 0xffffffff] on `stream`.
  * Replaces: mxfp8_begin_forward_kernel (cuda-kernels/mxfp8.cu:91-96) via
@@ -286,7 +287,7 @@ KB_API void kb_mxfp8_weight_destroy(kb_mxfp8_weight* w);
  * and a_scales (packed, as produced by kb_mxfp8_quantize for this kp) against
  * the weight, fp32 accumulation on tcgen05 (kind::mxf8f6f4.block_scale,
  * UE8M0 x 32).  out_kind KB_MX_OUT_*; bias (n fp32, or NULL) and act
- * (KB_ACT_*) apply to KB_MX_OUT_BF16 only.  A non-finite output sets
+ * (KB_ACT_*) apply to KB_MX_OUT_BF16 / KB_MX_OUT_BF16_RESIDUAL only (act: BF16).  A non-finite output sets
  * KB_STATUS_OUTPUT_NONFINITE with `layer`.  ldo: output row stride in elements.
  * Replaces: LtPlan::run (src/backends/mxfp8.rs:683-720) + mxfp8_check_*_output_kernel
  * (cuda-kernels/mxfp8.cu:151-159). */
@@ -304,7 +305,8 @@ KB_API int kb_mxfp8_project(const kb_mxfp8_weight* w, const void* x, int dtype, 
 
 /* ------------------------------------------------------------------ model and evaluator */
 
-#define KB_PREC_INT8 0 /* W8A8: every trunk linear INT8 x INT8 -> INT32 */
+#define KB_PREC_INT8 0  /* W8A8: every trunk linear INT8 x INT8 -> INT32 */
+#define KB_PREC_MXFP8 1 /* every trunk linear E4M3 x E4M3 with UE8M0 scales per 32 K, fp32 accumulate */
 
 /* Trunk shape (BASELINE b11c768: C=768, 11 blocks, 12 heads x 64, F=3072). */
 typedef struct kb_model_desc {
@@ -313,7 +315,7 @@ typedef struct kb_model_desc {
   int num_heads;      /* heads * head_dim == C */
   int head_dim;       /* 32 or 64 */
   int ffn_channels;   /* F; multiple of 64, <= 4096 */
-  int precision;      /* KB_PREC_INT8 */
+  int precision;      /* KB_PREC_INT8 or KB_PREC_MXFP8 */
 } kb_model_desc;
 
 /* Weight blob: fp32, out-first [N, K] row-major matrices, in this order:

@@ -120,8 +120,11 @@ def quantize(source, rows: int, k: int, stride: int, check_weight: bool = False)
     src = np.asarray(source, np.float32).ravel()
     p = Packed(rows, k)
     x = np.zeros((rows, p.kp), np.float32)
-    for r in range(rows):
-        x[r, :k] = src[r * stride:r * stride + k]
+    if stride == k:
+        x[:, :k] = src[:rows * k].reshape(rows, k)
+    else:
+        for r in range(rows):
+            x[r, :k] = src[r * stride:r * stride + k]
     nan, inf = np.isnan(x), np.isinf(x)
     if nan.any():
         p.status |= STATUS_NAN

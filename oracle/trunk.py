@@ -117,9 +117,32 @@ def attention(qkv, cs, sn, n, nh, hd):
     return bf(o.reshape(n * SEQ, c).astype(np.float32))
 
 
-def forward(blob, topo, spatial, glob, teacher=None):
+def _mx_weight(w):
+    """Decoded float64 [n, k] of an MXFP8 weight quantised from the original fp32."""
+    from . import mxfp8 as mx
+
+    n, k = w.shape
+    return mx.quantize(w, n, k, k, check_weight=True).decoded()
+
+
+def _mx_linear(xv, wdec):
+    """fp32 accumulator of an MXFP8 projection: the activation's 16-bit values
+    quantised block-32 (mxfp8.cu:36-79), the product of decoded operands summed
+    exactly in float64, rounded once to fp32 (the tensor core accumulates in
+    fp32 in an order not reproduced here)."""
+    from . import mxfp8 as mx
+
+    rows, k = xv.shape
+    xdec = mx.quantize(np.ascontiguousarray(xv, np.float32), rows, k, k).decoded()
+    return (xdec @ wdec.T).astype(np.float32)
+
+
+def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
     """Returns dict(policy [n,6,362], value [n,3], misc [n,10], moremisc [n,8],
     ownership [n,361], residual [n*361, C]).
+
+    precision "mxfp8" runs every trunk projection as the MXFP8 path does
+    (block-32 E4M3 activations and weights, UE8M0 scales, fp32 accumulation).
 
     teacher: optional (stem [n*361, C], [attention [n*361, C] per block]) float
     arrays that replace the oracle's own stem GEMM and attention results — the
@@ -133,8 +156,22 @@ def forward(blob, topo, spatial, glob, teacher=None):
     else:
         a = bf(stem_inputs(spatial, glob)).astype(np.float64)
         x = bf((a @ bf(w["stem"]).astype(np.float64).T).astype(np.float32))
+    from . import act
+
     for i in range(nb):
         cs, sn = rope_tables(w[f"{i}.rope"])
+        if precision == "mxfp8":
+            wq, wo, wu, wd = (_mx_weight(w[f"{i}.{nm}"]) for nm in ("qkv", "out", "up", "down"))
+            _, _, normed = rms_quantize(x, w[f"{i}.rms1"], EPS, False)
+            qkv = bf(_mx_linear(normed, wq))
+            att = attention(qkv, cs, sn, n, nh, hd) if teacher is None else np.asarray(teacher[1][i], np.float32)
+            x = bf((x + _mx_linear(att, wo)).astype(np.float32))
+            _, _, normed = rms_quantize(x, w[f"{i}.rms2"], EPS, False)
+            v = (_mx_linear(normed, wu) + w[f"{i}.up_b"][None, :]).astype(np.float32)
+            hidden = bf(act(v, 1))
+            d = (_mx_linear(hidden, wd) + w[f"{i}.down_b"][None, :]).astype(np.float32)
+            x = bf((x + d).astype(np.float32))
+            continue
         qw, qs = quantize_weights(w[f"{i}.qkv"])
         ow, os_ = quantize_weights(w[f"{i}.out"])
         uw, us = quantize_weights(w[f"{i}.up"])
@@ -146,15 +183,11 @@ def forward(blob, topo, spatial, glob, teacher=None):
         x = bf((x + dequant(igemm(q2, ow), s2, os_)).astype(np.float32))
         q3, s3, _ = rms_quantize(x, w[f"{i}.rms2"], EPS, False, kp=uw.shape[1])
         v = (dequant(igemm(q3, uw), s3, us) + w[f"{i}.up_b"][None, :]).astype(np.float32)
-        from . import act
-
         hidden = bf(act(v, 1))
         q4, s4 = quantize_rows(hidden, kp=dw.shape[1])
         d = (dequant(igemm(q4, dw), s4, ds) + w[f"{i}.down_b"][None, :]).astype(np.float32)
         x = bf((x + d).astype(np.float32))
     # trunk tip: silu(x*gamma + beta) (debug_exec_units.rs:272-282)
-    from . import act
-
     g = bf(act(((x * w["tip_g"][None, :]).astype(np.float32) + w["tip_b"][None, :]).astype(np.float32), 2))
     g64 = g.astype(np.float64)
     hp = np.concatenate([g64 @ bf(w["p1"]).astype(np.float64).T,

@@ -81,7 +81,8 @@ DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 EPI_I32, EPI_F16, EPI_RES_F32, EPI_16, EPI_RES16, EPI_SWIGLU16, EPI_F32 = range(7)
 ACT_NONE, ACT_GELU, ACT_SILU = 0, 1, 2
 LAYOUT_PLAIN, LAYOUT_SWIGLU_DUAL = 0, 1
-MX_OUT_HALF, MX_OUT_FLOAT, MX_OUT_FLOAT_RESIDUAL, MX_OUT_BF16 = range(4)
+PREC_INT8, PREC_MXFP8 = 0, 1
+MX_OUT_HALF, MX_OUT_FLOAT, MX_OUT_FLOAT_RESIDUAL, MX_OUT_BF16, MX_OUT_BF16_RESIDUAL = range(5)
 STATUS_NAN, STATUS_INF, STATUS_OUTPUT_NONFINITE, STATUS_WEIGHT_OVERFLOW = 1, 2, 4, 8
 STATUS_UNSUPPORTED_ARCH, STATUS_TIMEOUT = 16, 32
 NO_LAYER = 0xFFFFFFFF

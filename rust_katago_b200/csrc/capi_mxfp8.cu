@@ -30,6 +30,7 @@ int out_epilogue(int out_kind, int* epi, int* out_f16, int* elem) {
     case KB_MX_OUT_FLOAT: *epi = kEpiF32, *out_f16 = 0, *elem = 4; return KB_OK;
     case KB_MX_OUT_FLOAT_RESIDUAL: *epi = kEpiResF32, *out_f16 = 0, *elem = 4; return KB_OK;
     case KB_MX_OUT_BF16: *epi = kEpi16, *out_f16 = 0, *elem = 2; return KB_OK;
+    case KB_MX_OUT_BF16_RESIDUAL: *epi = kEpiRes16, *out_f16 = 0, *elem = 2; return KB_OK;
   }
   set_error("unknown MXFP8 output kind");
   return KB_E_INVALID;
@@ -192,8 +193,9 @@ int kb_mxfp8_gemm(const uint8_t* a_q, const uint8_t* a_scales, int rows, const k
     set_error("MXFP8 output must be 16-byte aligned with a row stride of at least N");
     return KB_E_INVALID;
   }
-  if (out_kind != KB_MX_OUT_BF16 && (bias != nullptr || act != KB_ACT_NONE)) {
-    set_error("bias and activation apply to KB_MX_OUT_BF16 only");
+  if ((out_kind != KB_MX_OUT_BF16 && bias != nullptr && out_kind != KB_MX_OUT_BF16_RESIDUAL) ||
+      (out_kind != KB_MX_OUT_BF16 && act != KB_ACT_NONE)) {
+    set_error("bias applies to the bf16 outputs only, the activation to KB_MX_OUT_BF16 only");
     return KB_E_INVALID;
   }
   GemmArgs g;

@@ -83,9 +83,9 @@ int validate_desc(const kb_model_desc* d) {
       d->num_blocks <= 0 || d->num_blocks > 64 || d->num_heads <= 0 ||
       (d->head_dim != 32 && d->head_dim != 64) || d->num_heads * d->head_dim != d->trunk_channels ||
       d->ffn_channels <= 0 || d->ffn_channels % 64 != 0 || d->ffn_channels > 4096 ||
-      d->precision != KB_PREC_INT8) {
+      (d->precision != KB_PREC_INT8 && d->precision != KB_PREC_MXFP8)) {
     set_error("model descriptor: need C % 64 == 0 (<= 4096), heads*head_dim == C, head_dim 32|64, "
-              "F % 64 == 0 (<= 4096), 1..64 blocks, precision KB_PREC_INT8");
+              "F % 64 == 0 (<= 4096), 1..64 blocks, precision KB_PREC_INT8 or KB_PREC_MXFP8");
     return KB_E_INVALID;
   }
   return KB_OK;
@@ -118,6 +118,11 @@ struct Block {
   kb_int8_weight* out = nullptr;
   kb_int8_weight* up = nullptr;
   kb_int8_weight* down = nullptr;
+  // KB_PREC_MXFP8: the same four projections as block-scaled E4M3 weights.
+  kb_mxfp8_weight* mqkv = nullptr;
+  kb_mxfp8_weight* mout = nullptr;
+  kb_mxfp8_weight* mup = nullptr;
+  kb_mxfp8_weight* mdown = nullptr;
   float* up_b = nullptr;
   float* down_b = nullptr;
   float* rope_cos = nullptr;  // [361, heads, head_dim/2]
@@ -171,8 +176,10 @@ struct kb_handle {
   uint16_t* qkv = nullptr;      // [M, 3C]
   uint16_t* att = nullptr;      // [M, C] (also the trunk-tip output)
   uint16_t* hidden = nullptr;   // [M, F]
-  int8_t* q = nullptr;          // [M, max kp]
+  int8_t* q = nullptr;          // [M, max kp] int8 or E4M3 bytes
   float* scales = nullptr;      // [M]
+  uint8_t* mx_scales = nullptr; // MXFP8 packed UE8M0 scales for [M, max kp]
+  size_t mx_scale_bytes = 0;
   uint32_t* row_amax = nullptr; // [M] |bits| maximum of the FFN hidden rows
   float* hp = nullptr;          // [M, 384] fp32
   unsigned* status = nullptr;   // [2]
@@ -197,6 +204,10 @@ void destroy_model(kb_model* m) {
     kb_int8_weight_destroy(b.out);
     kb_int8_weight_destroy(b.up);
     kb_int8_weight_destroy(b.down);
+    kb_mxfp8_weight_destroy(b.mqkv);
+    kb_mxfp8_weight_destroy(b.mout);
+    kb_mxfp8_weight_destroy(b.mup);
+    kb_mxfp8_weight_destroy(b.mdown);
     cudaFree(b.up_b);
     cudaFree(b.down_b);
     cudaFree(b.rope_cos);
@@ -208,6 +219,60 @@ void destroy_model(kb_model* m) {
   cudaFree(m->head_b);
   cudaFree(m->small);
   delete m;
+}
+
+// GemmArgs of one MXFP8 projection of the trunk (bf16 output or residual).
+GemmArgs mx_args(kb_handle* h, const kb_mxfp8_weight* w, int M, void* out, const float* bias, int act,
+                 unsigned layer) {
+  GemmArgs g;
+  g.m = M;
+  g.n = w->n;
+  g.k = w->kp;
+  g.out = out;
+  g.ldo = w->n;
+  g.bias = bias;
+  g.act = act;
+  g.out_f16 = 0;
+  g.status = h->status;
+  g.layer = layer;
+  g.sfa = h->mx_scales;
+  g.sfb = w->scales;
+  return g;
+}
+
+// One transformer block with MXFP8 projections (KB_PREC_MXFP8):
+// RMSNorm -> MXFP8 -> QKV GEMM (bf16) -> RoPE attention -> MXFP8 -> out-proj +
+// residual -> RMSNorm -> MXFP8 -> up GEMM + bias + GELU (bf16) -> MXFP8 ->
+// down GEMM + bias + residual.  Every activation quantiser is the block-32
+// E4M3/UE8M0 quantiser of the reference's MXFP8 path (mxfp8.cu:36-79) applied
+// to the 16-bit boundary, as Mxfp8Workspace::project does (mxfp8.rs:1055-1121).
+int mxfp8_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale, uint16_t* trace_att) {
+  const kb_model_desc& d = h->model->desc;
+  const int c = d.trunk_channels, f = d.ffn_channels, M = n * kSeq;
+  cudaStream_t s = h->stream;
+  uint8_t* q = reinterpret_cast<uint8_t*>(h->q);
+  int rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms1, kRmsEps, 0, q, h->mx_scales, h->status, layer, s);
+  if (!rc) rc = gemm_launch(kGemmMXF8, kEpi16, q, b.mqkv->q, mx_args(h, b.mqkv, M, h->qkv, nullptr, 0, layer), s);
+  if (!rc)
+    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s);
+  if (!rc && trace_att)
+    rc = check_cuda(cudaMemcpyAsync(trace_att, h->att, static_cast<size_t>(M) * c * 2, cudaMemcpyDeviceToDevice, s),
+                    "trace copy");
+  // Quantiser scale capacity = this shape's bytes: no tail clear inside the forward.
+  size_t sb_c = 0, sb_f = 0;
+  if (!rc) rc = mxfp8_dims(M, c, nullptr, nullptr, nullptr, &sb_c);
+  if (!rc) rc = mxfp8_dims(M, f, nullptr, nullptr, nullptr, &sb_f);
+  if (!rc)
+    rc = mxfp8_quantize_launch(h->att, KB_DT_BF16, c, M, c, q, h->mx_scales, sb_c, false, h->status, layer, s);
+  if (!rc) rc = gemm_launch(kGemmMXF8, kEpiRes16, q, b.mout->q, mx_args(h, b.mout, M, h->x, nullptr, 0, layer), s);
+  if (!rc) rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms2, kRmsEps, 0, q, h->mx_scales, h->status, layer, s);
+  if (!rc)
+    rc = gemm_launch(kGemmMXF8, kEpi16, q, b.mup->q, mx_args(h, b.mup, M, h->hidden, b.up_b, KB_ACT_GELU, layer), s);
+  if (!rc)
+    rc = mxfp8_quantize_launch(h->hidden, KB_DT_BF16, f, M, f, q, h->mx_scales, sb_f, false, h->status, layer, s);
+  if (!rc)
+    rc = gemm_launch(kGemmMXF8, kEpiRes16, q, b.mdown->q, mx_args(h, b.mdown, M, h->x, b.down_b, 0, layer), s);
+  return rc;
 }
 
 // One forward pass of n positions on device buffers, enqueued on `s`.  When
@@ -244,6 +309,11 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
   for (int bi = 0; bi < d.num_blocks; ++bi) {
     const Block& b = m->blocks[bi];
     const unsigned layer = static_cast<unsigned>(bi);
+    if (d.precision == KB_PREC_MXFP8) {
+      rc = mxfp8_block(h, b, layer, n, scale, trace ? trace + (1 + bi) * plane : nullptr);
+      if (rc) return rc;
+      continue;
+    }
     // attention
     rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.qkv->kp, true, b.rms1, kRmsEps, 0, h->q, h->scales,
                               h->status, layer, s);
@@ -403,6 +473,7 @@ void destroy_handle(kb_handle* h) {
   cudaFree(h->hidden);
   cudaFree(h->q);
   cudaFree(h->scales);
+  cudaFree(h->mx_scales);
   cudaFree(h->row_amax);
   cudaFree(h->hp);
   cudaFree(h->status);
@@ -479,10 +550,17 @@ int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, in
     const float* freqs = cur.take(static_cast<size_t>(nh) * (hd / 2) * 2);
     rc = upload(&b.rms1, rms1, c, "upload rms");
     if (!rc) rc = upload(&b.rms2, rms2, c, "upload rms");
-    if (!rc) rc = kb_int8_weight_upload(qkv, 3 * c, c, KB_LAYOUT_PLAIN, &b.qkv);
-    if (!rc) rc = kb_int8_weight_upload(ow, c, c, KB_LAYOUT_PLAIN, &b.out);
-    if (!rc) rc = kb_int8_weight_upload(up, f, c, KB_LAYOUT_PLAIN, &b.up);
-    if (!rc) rc = kb_int8_weight_upload(dn, c, f, KB_LAYOUT_PLAIN, &b.down);
+    if (d.precision == KB_PREC_MXFP8) {
+      if (!rc) rc = kb_mxfp8_weight_upload(qkv, 3 * c, c, c, &b.mqkv);
+      if (!rc) rc = kb_mxfp8_weight_upload(ow, c, c, c, &b.mout);
+      if (!rc) rc = kb_mxfp8_weight_upload(up, f, c, c, &b.mup);
+      if (!rc) rc = kb_mxfp8_weight_upload(dn, c, f, f, &b.mdown);
+    } else {
+      if (!rc) rc = kb_int8_weight_upload(qkv, 3 * c, c, KB_LAYOUT_PLAIN, &b.qkv);
+      if (!rc) rc = kb_int8_weight_upload(ow, c, c, KB_LAYOUT_PLAIN, &b.out);
+      if (!rc) rc = kb_int8_weight_upload(up, f, c, KB_LAYOUT_PLAIN, &b.up);
+      if (!rc) rc = kb_int8_weight_upload(dn, c, f, KB_LAYOUT_PLAIN, &b.down);
+    }
     if (!rc) rc = upload(&b.up_b, up_b, f, "upload bias");
     if (!rc) rc = upload(&b.down_b, dn_b, c, "upload bias");
     if (!rc) {
@@ -594,6 +672,14 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
   if (!rc) rc = dev_alloc(&h->hidden, M * f, "workspace");
   if (!rc) rc = dev_alloc(&h->q, M * kq, "workspace");
   if (!rc) rc = dev_alloc(&h->scales, M, "workspace");
+  if (!rc && d.precision == KB_PREC_MXFP8) {
+    rc = mxfp8_dims(static_cast<long>(M), static_cast<long>(c > f ? c : f), nullptr, nullptr, nullptr,
+                    &h->mx_scale_bytes);
+    if (!rc) rc = dev_alloc(&h->mx_scales, h->mx_scale_bytes, "workspace");
+    // Scale bytes of padding rows are never written by the quantisers: keep
+    // them finite (zero) so they only ever scale zero-filled operand rows.
+    if (!rc) rc = check_cuda(cudaMemset(h->mx_scales, 0, h->mx_scale_bytes), "workspace clear");
+  }
   if (!rc) rc = dev_alloc(&h->row_amax, M, "workspace");
   if (!rc) rc = dev_alloc(&h->hp, M * kHeadN, "workspace");
   if (!rc) rc = dev_alloc(&h->status, 2, "status word");

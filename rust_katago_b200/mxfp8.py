@@ -26,8 +26,8 @@ from . import _capi
 from ._capi import call, load
 from .int8 import _ptr, _stream
 
-OUT_HALF, OUT_FLOAT, OUT_FLOAT_RESIDUAL, OUT_BF16 = (_capi.MX_OUT_HALF, _capi.MX_OUT_FLOAT,
-                                                     _capi.MX_OUT_FLOAT_RESIDUAL, _capi.MX_OUT_BF16)
+OUT_HALF, OUT_FLOAT, OUT_FLOAT_RESIDUAL, OUT_BF16, OUT_BF16_RESIDUAL = (
+    _capi.MX_OUT_HALF, _capi.MX_OUT_FLOAT, _capi.MX_OUT_FLOAT_RESIDUAL, _capi.MX_OUT_BF16, _capi.MX_OUT_BF16_RESIDUAL)
 
 
 def dimensions(rows: int, k: int):

@@ -27,14 +27,17 @@ class Topology:
     num_heads: int = 12
     head_dim: int = 64
     ffn_channels: int = 3072
+    precision: int = 0  # KB_PREC_INT8 (0) or KB_PREC_MXFP8 (1)
 
     def desc(self):
         from ._capi import ModelDesc
 
-        return ModelDesc(self.trunk_channels, self.num_blocks, self.num_heads, self.head_dim, self.ffn_channels, 0)
+        return ModelDesc(self.trunk_channels, self.num_blocks, self.num_heads, self.head_dim, self.ffn_channels,
+                         self.precision)
 
 
 B11C768 = Topology()
+B11C768_MXFP8 = Topology(precision=1)
 
 
 def blob_sections(t: Topology):

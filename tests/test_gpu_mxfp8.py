@@ -291,3 +291,69 @@ def test_sticky_status_first_layer_and_overflow(kb):
     # Host misuse is rejected before any launch.
     with pytest.raises(_capi.KbError):
         ws.project(w, d_good, _capi.DT_F16, k - 1, out, m.OUT_FLOAT, 1)
+
+
+@pytest.mark.parametrize("boundary", ["bf16", "f16"])
+def test_rms_mxfp8_matches_oracle(kb, oracle, boundary):
+    """Fused RMSNorm -> 16-bit -> MXFP8 equals the oracle's RMSNorm (same
+    summation order, rstd and rounding as the INT8 RMS quantiser) followed by
+    the block-32 quantiser, byte for byte; includes a NaN row."""
+    _capi, m = kb
+    rows, width = 723, 768
+    rng = np.random.default_rng(5)
+    x = oracle.decode16(oracle.bf16_encode((rng.standard_normal((rows, width)) * 3).astype(np.float32)), False)
+    x[5, 17] = np.nan
+    gamma = (1 + 0.02 * rng.standard_normal(width)).astype(np.float32)
+    f16 = boundary == "f16"
+    _, _, normed = oracle.rms_quantize(x, gamma, 1e-6, f16)
+    expected = mx.quantize(normed, rows, width, width)
+    _, _, data, scale = m.dimensions(rows, width)
+    q = torch.zeros(data, dtype=torch.uint8, device="cuda")
+    s = torch.full((scale,), 0xEE, dtype=torch.uint8, device="cuda")
+    st = torch.zeros(2, dtype=torch.int32, device="cuda")
+    m.reset_status(st)
+    dx = torch.from_numpy(oracle.bf16_encode(x).view(np.int16)).cuda()
+    dg = torch.from_numpy(gamma).cuda()
+    m.rms_quantize(dx, _capi.DT_BF16, rows, width, width, dg, 1e-6, _capi.DT_F16 if f16 else _capi.DT_BF16, q, s, st,
+                   layer=9)
+    check_pack(q, s, expected)
+    torch.cuda.synchronize()
+    flags, layer = (int(v) & 0xFFFFFFFF for v in st.cpu().tolist())
+    assert flags == _capi.STATUS_NAN and layer == 9
+
+
+@pytest.mark.parametrize("residual", [False, True])
+def test_bf16_epilogues_bias_gelu_residual(kb, oracle, residual):
+    """bf16 outputs of the trunk: bf16(gelu(acc + bias)) and bf16(r + (acc + bias)),
+    acc within the fp32 accumulation bound of the exact decoded product."""
+    _capi, m = kb
+    rows, n, k = 777, 384, 768
+    rng = np.random.default_rng(7)
+    wf = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    xf = oracle.decode16(oracle.bf16_encode(rng.standard_normal((rows, k)).astype(np.float32)), False)
+    bias = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    w = m.Mxfp8Weight(wf, n, k, k)
+    _, _, data, scale = m.dimensions(rows, k)
+    q = torch.zeros(data, dtype=torch.uint8, device="cuda")
+    s = torch.zeros(scale, dtype=torch.uint8, device="cuda")
+    st = torch.zeros(2, dtype=torch.int32, device="cuda")
+    m.reset_status(st)
+    m.quantize(torch.from_numpy(oracle.bf16_encode(xf).view(np.int16)).cuda(), _capi.DT_BF16, rows, k, k, q, s, st)
+    r = oracle.decode16(oracle.bf16_encode(rng.standard_normal((rows, n)).astype(np.float32)), False)
+    out = torch.from_numpy(oracle.bf16_encode(r).view(np.int16)).cuda() if residual else \
+        torch.zeros((rows, n), dtype=torch.int16, device="cuda")
+    if residual:
+        m.gemm(q, s, rows, w, out, n, m.OUT_BF16_RESIDUAL, st, bias=torch.from_numpy(bias).cuda())
+    else:
+        m.gemm(q, s, rows, w, out, n, m.OUT_BF16, st, bias=torch.from_numpy(bias).cuda(), act=_capi.ACT_GELU)
+    torch.cuda.synchronize()
+    got = oracle.decode16(out.cpu().numpy().view(np.uint16), False)
+    exact, _ = mx.reference(mx.quantize(wf, n, k, k), mx.quantize(xf, rows, k, k))
+    v = (exact.astype(np.float32) + bias[None, :]).astype(np.float32)
+    ref = oracle.decode16(oracle.bf16_encode((r + v).astype(np.float32) if residual else oracle.act(v, 1)), False)
+    diff = np.abs(got.astype(np.float64) - ref)
+    # one bf16 step of the larger magnitude at most, on a small fraction of outputs
+    ulp = np.maximum(np.abs(ref), 1e-30) * 2.0 ** -7
+    assert np.all(diff <= ulp + 1e-6)
+    assert np.mean(diff > 0) < 0.02
+    m.validate_status([int(v) & 0xFFFFFFFF for v in st.cpu().tolist()])
