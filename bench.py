@@ -236,14 +236,15 @@ class TrunkWorkload:
 
         return synthetic.B11C768
 
-    def __init__(self, batch: int, torch, seed: int = 1234, build_device: bool = True):
+    def __init__(self, batch: int, torch, seed: int = 1234, build_device: bool = True, rank: int = 0):
         from rust_katago_b200 import backend, synthetic
 
         self.torch = torch
         self.batch = batch
         self.topo = self.topology()
-        self.blob = synthetic.make_blob(self.topo, seed)
-        self.spatial, self.glob = synthetic.make_positions(max(batch, 4), seed + 1)
+        self.blob = synthetic.make_blob(self.topo, seed)  # replicated weights: same seed on every rank
+        # each rank evaluates its own shard of distinct positions
+        self.spatial, self.glob = synthetic.make_positions(max(batch, 4), seed + 1 + 7919 * rank)
         if not build_device:
             return
         self.spatial, self.glob = self.spatial[:batch], self.glob[:batch]
@@ -413,7 +414,7 @@ def main():
     from rust_katago_b200 import _capi
 
     _capi.call("kb_device_check", local)
-    wl = WORKLOADS[args.workload](args.batch, torch, seed=1234)
+    wl = WORKLOADS[args.workload](args.batch, torch, seed=1234, **({"rank": rank} if args.workload != "ffn" else {}))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     stream = wl.stream
 
