@@ -134,20 +134,20 @@ float or_expf(float x) {
 /* g / (1 + e^-g): the SiLU inside the reference's SwiGLU (int8_ops.cu:111-113). */
 float or_silu(float g) { return g / (1.0f + or_expf(-g)); }
 
-/* GELU(x) = x * Phi(x): Phi(x) = 0.5 + xc * P(xc^2/8 - 1) on |x| <= 4 with the
- * degree-10 polynomial of rust_katago_b200/gelu_fit.py, 0 below -4, 1 above 4;
- * the same fused multiply-add sequence as the kernels. */
+/* GELU(x) = x * Phi(x): s = min(RN(x*x)*0.125 - 1 (fused), 1), P = the degree-10
+ * polynomial of rust_katago_b200/gelu_fit.py in s (Horner, fused),
+ * Phi = saturate(fma(x, P, 0.5)) to [0, 1] with NaN -> 0 (the PTX .sat rule);
+ * the same operation sequence as kb_gelu in the kernels. */
 float or_gelu(float x) {
   static const float c[11] = {0x1.68585ap-3f, -0x1.5961f4p-4f, 0x1.ca3788p-5f, -0x1.2df2f6p-5f,
                               0x1.70d728p-6f, -0x1.9ab164p-7f, 0x1.9a7b1cp-8f, -0x1.5eeeecp-9f,
                               0x1.229b08p-10f, -0x1.31c494p-11f, 0x1.a02d8ap-13f};
-  const float xc = fminf(fmaxf(x, -4.0f), 4.0f);
-  const float s = fmaf(xc * xc, 0.125f, -1.0f);
+  const float s = fminf(fmaf(x * x, 0.125f, -1.0f), 1.0f);
   float p = c[10];
   for (int i = 9; i >= 0; --i) p = fmaf(p, s, c[i]);
-  float phi = fmaf(xc, p, 0.5f);
-  if (x < -4.0f) phi = 0.0f;
-  if (x > 4.0f) phi = 1.0f;
+  float phi = fmaf(x, p, 0.5f);
+  if (!(phi > 0.0f)) phi = 0.0f; /* negative, zero or NaN */
+  if (phi > 1.0f) phi = 1.0f;
   return x * phi;
 }
 

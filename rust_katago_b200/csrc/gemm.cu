@@ -24,6 +24,7 @@
 #include <atomic>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "kb_internal.h"
 #include "kb_numeric.cuh"
@@ -101,15 +102,6 @@ __device__ __forceinline__ void load_vec32(const float* p, int col0, int n, floa
 #pragma unroll
     for (int i = 0; i < 32; ++i) dst[i] = col0 + i < n ? __ldg(p + col0 + i) : 0.0f;
   }
-}
-
-__device__ __forceinline__ uint4 pack8(const uint16_t* h) {
-  uint4 t;
-  t.x = h[0] | (uint32_t(h[1]) << 16);
-  t.y = h[2] | (uint32_t(h[3]) << 16);
-  t.z = h[4] | (uint32_t(h[5]) << 16);
-  t.w = h[6] | (uint32_t(h[7]) << 16);
-  return t;
 }
 
 // Round a pair to the 16-bit output type; element 0 in the low half.
@@ -202,18 +194,6 @@ __device__ __forceinline__ void emit16(Out16& o, const GemmArgs& g, const uint32
     uint16_t* dst = static_cast<uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
     store16x32(dst, hw, valid, (reinterpret_cast<uintptr_t>(dst) & 15) == 0);
   }
-}
-
-// True when any of the first `valid` 16-bit values is Inf or NaN.
-__device__ __forceinline__ bool nonfinite16(const uint32_t (&hw)[16], int valid, bool f16) {
-  const uint32_t m = f16 ? 0x7c00u : 0x7f80u;
-  bool bad = false;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    bad |= (2 * i < valid) && ((hw[i] & m) == m);
-    bad |= (2 * i + 1 < valid) && (((hw[i] >> 16) & m) == m);
-  }
-  return bad;
 }
 
 // Dequantised pair (i, i+1) of a 32-column chunk: (f32(dot) * sa) * sw, or the
@@ -458,35 +438,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (col0 >= g.n) continue;  // warp-uniform
           const int valid = min(32, g.n - col0);
           if constexpr (EPI == kEpiF16 || EPI == kEpi16 || EPI == kEpiRes16) {
-            float sw[32], bias[32];
+            float sw[32];
             if constexpr (KIND == kGemmI8) load_vec32(g.col_scale, col0, g.n, sw);
-            // A null bias loads as zeros; adding +0 is exact here because the
-            // dequantised value is never -0 for kind::i8 (dot 0 -> +0).
-            if constexpr (EPI != kEpiF16) load_vec32(g.bias, col0, g.n, bias);
             uint32_t hw[16];
             if constexpr (EPI == kEpiRes16) {
               const uint16_t* src = static_cast<const uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
               if (row_ok) load16x32(src, hw, valid, (reinterpret_cast<uintptr_t>(src) & 15) == 0);
             }
-            uint32_t amax2 = 0;
+            // Separate unrolled bodies with and without bias (warp-uniform
+            // choice), so a bias-free projection issues no adds.
+            auto finish = [&](auto with_bias) {
+              constexpr bool kBias = decltype(with_bias)::value;
+              float bias[32];
+              if constexpr (kBias) load_vec32(g.bias, col0, g.n, bias);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float2 x = acc_pair<KIND>(v, i, sa, sw);
-              if constexpr (EPI != kEpiF16) {
-                x.x = __fadd_rn(x.x, bias[2 * i]);
-                x.y = __fadd_rn(x.y, bias[2 * i + 1]);
+              for (int i = 0; i < 16; ++i) {
+                float2 x = acc_pair<KIND>(v, i, sa, sw);
+                if constexpr (kBias) {
+                  x.x = __fadd_rn(x.x, bias[2 * i]);
+                  x.y = __fadd_rn(x.y, bias[2 * i + 1]);
+                }
+                if constexpr (EPI == kEpiRes16) {
+                  const float2 r = unpack16x2(hw[i], f16);
+                  hw[i] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
+                } else {
+                  hw[i] = pack16x2(apply_act2<ACT>(x), f16);
+                }
               }
-              if constexpr (EPI == kEpiRes16) {
-                const float2 r = unpack16x2(hw[i], f16);
-                hw[i] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
+            };
+            if (EPI != kEpiF16 && g.bias != nullptr)
+              finish(std::true_type{});
+            else
+              finish(std::false_type{});
+            // |16-bit| maximum of the stored values: the next quantiser's row
+            // amax, and the MXFP8 output finite check (Inf/NaN sort highest).
+            if (KIND == kGemmMXF8 || (EPI != kEpiRes16 && g.row_amax != nullptr)) {
+              uint32_t amax2 = 0;
+              if (valid == 32) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) amax2 = __vmaxu2(amax2, hw[i] & 0x7fff7fffu);
               } else {
-                hw[i] = pack16x2(apply_act2<ACT>(x), f16);
-                const uint32_t mask = 2 * i + 1 < valid ? 0x7fff7fffu : (2 * i < valid ? 0x00007fffu : 0u);
-                amax2 = __vmaxu2(amax2, hw[i] & mask);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const uint32_t mask = 2 * i + 1 < valid ? 0x7fff7fffu : (2 * i < valid ? 0x00007fffu : 0u);
+                  amax2 = __vmaxu2(amax2, hw[i] & mask);
+                }
               }
+              if constexpr (EPI != kEpiRes16) amax = max(amax, amax16_to_f32bits(amax2, f16));
+              if constexpr (KIND == kGemmMXF8)
+                nonfinite |= row_ok && max(amax2 & 0xffffu, amax2 >> 16) >= (f16 ? 0x7c00u : 0x7f80u);
             }
-            if constexpr (EPI != kEpiRes16) amax = max(amax, amax16_to_f32bits(amax2, f16));
-            if constexpr (KIND == kGemmMXF8) nonfinite |= row_ok && nonfinite16(hw, valid, f16);
             emit16<SB>(o, g, hw, row, row0q, col0, lane, row_ok, valid);
           } else if (row_ok) {
             float sw[32], bias[32];

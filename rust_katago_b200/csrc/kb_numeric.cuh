@@ -49,28 +49,34 @@ __device__ __forceinline__ float kb_silu(float g) {
   return __fdiv_rn(g, __fadd_rn(1.0f, kb_expf(-g)));
 }
 
-// GELU(x) = x * Phi(x) with Phi the standard normal CDF.  For |x| <= 4,
-// Phi(x) = 0.5 + x * P(x^2), P a degree-10 polynomial in s = x^2/8 - 1
-// (least-squares Chebyshev fit of 0.5*erf(sqrt(t/2))/sqrt(t) on t in [0, 16],
-// derived by rust_katago_b200/gelu_fit.py); Phi = 0 below -4 and 1 above 4.
-// |error| <= 3.2e-5 * max(1, |x|): below the resolution of the 16-bit
-// activations it feeds.  Only fused multiply-adds: no division, no exp.
+// GELU(x) = x * Phi(x) with Phi the standard normal CDF:
+//   s   = min(x^2/8 - 1, 1)                      (rounded: RN(RN(x*x)*0.125 - 1))
+//   P   = degree-10 polynomial in s (Horner, fused multiply-adds)
+//   Phi = saturate(fma(x, P, 0.5)) to [0, 1]
+// P is the least-squares Chebyshev fit of 0.5*erf(sqrt(t/2))/sqrt(t) on
+// t = x^2 in [0, 16] (rust_katago_b200/gelu_fit.py).  For |x| <= 4 this is
+// 0.5 + x*P(x^2); beyond, s stays at 1 and the saturation pins Phi to 0 or 1
+// (exactly, once |x| exceeds 4 by 2e-4).  |error| <= 3.2e-5 * max(1, |x|).
+// NaN propagates (Phi = 0, x * 0 = NaN).  Only fused multiply-adds, one min
+// and a saturating FMA: no division, no exp, no compare-and-select.
 #define KB_GELU_COEFFS                                                                      \
   0x1.68585ap-3f, -0x1.5961f4p-4f, 0x1.ca3788p-5f, -0x1.2df2f6p-5f, 0x1.70d728p-6f,        \
       -0x1.9ab164p-7f, 0x1.9a7b1cp-8f, -0x1.5eeeecp-9f, 0x1.229b08p-10f, -0x1.31c494p-11f, \
       0x1.a02d8ap-13f
 
+__device__ __forceinline__ float fma_sat(float a, float b, float c) {
+  float r;
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float kb_gelu(float x) {
   constexpr float c[11] = {KB_GELU_COEFFS};
-  const float xc = fminf(fmaxf(x, -4.0f), 4.0f);
-  const float s = __fmaf_rn(__fmul_rn(xc, xc), 0.125f, -1.0f);
+  const float s = fminf(__fmaf_rn(__fmul_rn(x, x), 0.125f, -1.0f), 1.0f);
   float p = c[10];
 #pragma unroll
   for (int i = 9; i >= 0; --i) p = __fmaf_rn(p, s, c[i]);
-  float phi = __fmaf_rn(xc, p, 0.5f);
-  phi = x < -4.0f ? 0.0f : phi;
-  phi = x > 4.0f ? 1.0f : phi;
-  return __fmul_rn(x, phi);
+  return __fmul_rn(x, fma_sat(x, p, 0.5f));
 }
 
 // ------------------------------------------------------------------ f32x2
@@ -107,15 +113,14 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 // kb_gelu on a pair, bit-identical to two scalar calls.
 __device__ __forceinline__ float2 kb_gelu2(float2 x) {
   constexpr float c[11] = {KB_GELU_COEFFS};
-  const float2 xc = make_float2(fminf(fmaxf(x.x, -4.0f), 4.0f), fminf(fmaxf(x.y, -4.0f), 4.0f));
-  const float2 s = fma2(mul2(xc, xc), make_float2(0.125f, 0.125f), make_float2(-1.0f, -1.0f));
+  float2 s = fma2(mul2(x, x), make_float2(0.125f, 0.125f), make_float2(-1.0f, -1.0f));
+  s.x = fminf(s.x, 1.0f);
+  s.y = fminf(s.y, 1.0f);
   float2 p = make_float2(c[10], c[10]);
 #pragma unroll
   for (int i = 9; i >= 0; --i) p = fma2(p, s, make_float2(c[i], c[i]));
-  float2 phi = fma2(xc, p, make_float2(0.5f, 0.5f));
-  phi.x = x.x < -4.0f ? 0.0f : (x.x > 4.0f ? 1.0f : phi.x);
-  phi.y = x.y < -4.0f ? 0.0f : (x.y > 4.0f ? 1.0f : phi.y);
-  return mul2(x, phi);
+  // (the packed FMA has no saturating form: two scalar saturating FMAs)
+  return mul2(x, make_float2(fma_sat(x.x, p.x, 0.5f), fma_sat(x.y, p.y, 0.5f)));
 }
 
 enum Act : int { kActNone = 0, kActGelu = 1, kActSilu = 2 };

@@ -5,7 +5,8 @@ GELU(x) = x * Phi(x), Phi the standard normal CDF.  For |x| <= 4,
 Phi(x) = 0.5 + x * P(t) with t = x^2, and P(t) = 0.5 * erf(sqrt(t/2)) / sqrt(t)
 is approximated by a degree-10 polynomial in s = t/8 - 1 (s in [-1, 1]):
 a least-squares Chebyshev fit on 40001 points, converted to the monomial
-basis and rounded to float32.  Outside |x| <= 4, Phi is taken as 0 or 1
+basis and rounded to float32.  The kernels evaluate P at s = min(x^2/8 - 1, 1)
+and saturate Phi to [0, 1], so beyond |x| = 4 Phi reaches exactly 0 or 1
 (|Phi - {0,1}| < 3.2e-5 there).  Max |GELU error| / max(1, |x|) < 3.2e-5,
 far below the bf16/fp16 resolution of the stored activations.
 
