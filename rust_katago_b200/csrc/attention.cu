@@ -15,6 +15,7 @@
 // accumulation): S = Q K^T, P = exp2((S - m) * scale * log2 e), O += P V.
 // Scores and probabilities never leave registers.
 #include <stdint.h>
+#include <stdlib.h>
 
 #include <atomic>
 
@@ -23,6 +24,12 @@
 #include "kb_ptx.cuh"
 
 namespace kb {
+
+bool attention_tc_supported(int seq, int head_dim);
+int attention_tc_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out, int batch,
+                        int seq, int heads, float scale, int f16, cudaStream_t stream, uint32_t* row_amax,
+                        unsigned* status);
+
 namespace {
 
 constexpr int kAttnWarps = 8;
@@ -288,7 +295,7 @@ int launch_attention(const uint16_t* qkv, const float* cos_t, const float* sin_t
 // out: [batch*seq, heads*D] 16-bit.  scale multiplies q.k before the softmax.
 int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
                      int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
-                     uint32_t* row_amax) {
+                     uint32_t* row_amax, unsigned* status) {
   if (!qkv || !rope_cos || !rope_sin || !out || batch <= 0 || seq <= 0 || seq > kMaxSeq || heads <= 0 ||
       !(scale > 0.0f)) {
     set_error("attention: invalid arguments (seq must be 1..384)");
@@ -299,6 +306,15 @@ int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* ro
     set_error("attention: qkv/tables must be 16-byte aligned");
     return KB_E_INVALID;
   }
+  // The board (seq 361, head_dim 64) runs on the tcgen05 kernel; other shapes
+  // (head_dim 32, short sequences) on the mma.sync kernel above.  Tactic
+  // switch KB_ATTENTION_MMA_SYNC=1 forces the latter (for A/B timing).
+  static const bool force_sync = [] {
+    const char* v = getenv("KB_ATTENTION_MMA_SYNC");
+    return v != nullptr && v[0] == '1';
+  }();
+  if (!force_sync && attention_tc_supported(seq, head_dim))
+    return attention_tc_launch(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, f16, stream, row_amax, status);
   if (head_dim == 64)
     return f16 ? launch_attention<64, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream)
                : launch_attention<64, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream);

@@ -6,7 +6,7 @@
 namespace kb {
 int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
                      int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
-                     uint32_t* row_amax = nullptr);
+                     uint32_t* row_amax = nullptr, unsigned* status = nullptr);
 }
 
 extern "C" int kb_attention(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,

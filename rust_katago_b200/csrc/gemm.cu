@@ -428,6 +428,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         constexpr int kChunks = BN / 64;
+        // Residual epilogue: the 16-bit residual of the next chunk is loaded
+        // while the current one is computed (one chunk of prefetch).
+        uint32_t res_next[16];
+        auto load_res = [&](int jj2) {
+          const int c = nb * BN + (half * kChunks + jj2) * 32;
+          if (row_ok && c < g.n) {
+            const uint16_t* src = static_cast<const uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + c;
+            load16x32(src, res_next, min(32, g.n - c), (reinterpret_cast<uintptr_t>(src) & 15) == 0);
+          }
+        };
+        if constexpr (EPI == kEpiRes16) load_res(0);
 #pragma unroll 1
         for (int jj = 0; jj < kChunks; ++jj) {
           const int j = half * kChunks + jj;
@@ -442,8 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (KIND == kGemmI8) load_vec32(g.col_scale, col0, g.n, sw);
             uint32_t hw[16];
             if constexpr (EPI == kEpiRes16) {
-              const uint16_t* src = static_cast<const uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-              if (row_ok) load16x32(src, hw, valid, (reinterpret_cast<uintptr_t>(src) & 15) == 0);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) hw[i] = res_next[i];
+              if (jj + 1 < kChunks) load_res(jj + 1);
             }
             // Separate unrolled bodies with and without bias (warp-uniform
             // choice), so a bias-free projection issues no adds.

@@ -34,7 +34,7 @@
 namespace kb {
 int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
                      int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
-                     uint32_t* row_amax = nullptr);
+                     uint32_t* row_amax = nullptr, unsigned* status = nullptr);
 int stem_gather_launch(const float* spatial, const float* global, uint16_t* a, int batch, int nhwc,
                        cudaStream_t s);
 int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, uint16_t* g, long rows, int c,
@@ -254,7 +254,8 @@ int mxfp8_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale
   int rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms1, kRmsEps, 0, q, h->mx_scales, h->status, layer, s);
   if (!rc) rc = gemm_launch(kGemmMXF8, kEpi16, q, b.mqkv->q, mx_args(h, b.mqkv, M, h->qkv, nullptr, 0, layer), s);
   if (!rc)
-    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s);
+    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s,
+                          nullptr, h->status);
   if (!rc && trace_att)
     rc = check_cuda(cudaMemcpyAsync(trace_att, h->att, static_cast<size_t>(M) * c * 2, cudaMemcpyDeviceToDevice, s),
                     "trace copy");
@@ -334,7 +335,7 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
     rc = check_cuda(cudaMemsetAsync(h->row_amax, 0, static_cast<size_t>(M) * sizeof(uint32_t), s), "amax reset");
     if (rc) return rc;
     rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s,
-                          h->row_amax);
+                          h->row_amax, h->status);
     if (rc) return rc;
     if (trace) {
       rc = check_cuda(cudaMemcpyAsync(trace + (1 + bi) * plane, h->att, plane * 2, cudaMemcpyDeviceToDevice, s),

@@ -112,23 +112,39 @@ __device__ __noinline__ void quantize_group_slow_f32(float4 a, float4 b, float s
       make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
 }
 
+// Round-to-nearest-even to an integer by adding 1.5 * 2^23: for |q| < 2^22 the
+// sum is exactly representable only at integers, so the add rounds q as rint
+// does, and the low byte of the sum's bits is the two's-complement int8 of
+// the result (the constant's low 22 bits are zero).  One FMA-pipe add per value
+// instead of a float-to-int conversion.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+// Low bytes of four such sums -> one packed int8x4 word (two byte permutes).
+__device__ __forceinline__ uint32_t pack4_magic(float a, float b, float c, float d) {
+  const uint32_t ab = __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x0040);
+  const uint32_t cd = __byte_perm(__float_as_uint(c), __float_as_uint(d), 0x0040);
+  return __byte_perm(ab, cd, 0x5410);
+}
+
 template <bool F16>
 __device__ __forceinline__ uint2 quant_group_fast(const uint32_t (&w)[4], float scale, float r) {
-  int qi[8];
+  float m[8];
 #pragma unroll
   for (int t = 0; t < 8; t += 2) {
     // Pair of values through packed fp32: q0 = v*r, e = v - q0*s, q = q0 + e*r
-    // (a packed multiply feeding only multiplicands cannot be contracted).
+    // (correctly rounded v/s), then rint(q) by the magic add.  A packed
+    // multiply feeding only multiplicands or an FMA cannot be contracted.
+    // |v/scale| <= 127 for a normal scale = amax/127, so no clamp is needed.
     const uint32_t pw = w[t / 2];
     const float2 v = make_float2(from16(static_cast<uint16_t>(pw & 0xffffu), F16), from16(static_cast<uint16_t>(pw >> 16), F16));
     const float2 q0 = mul2(v, make_float2(r, r));
     const float2 e = fma2(make_float2(-q0.x, -q0.y), make_float2(scale, scale), v);
     const float2 q = fma2(e, make_float2(r, r), q0);
-    // |v/scale| <= 127 for a normal scale = amax/127, so no clamp is needed.
-    qi[t] = __float2int_rn(q.x);
-    qi[t + 1] = __float2int_rn(q.y);
+    const float2 mq = add2(q, make_float2(kRoundMagic, kRoundMagic));
+    m[t] = mq.x;
+    m[t + 1] = mq.y;
   }
-  return make_uint2(pack4_i8(qi[0], qi[1], qi[2], qi[3]), pack4_i8(qi[4], qi[5], qi[6], qi[7]));
+  return make_uint2(pack4_magic(m[0], m[1], m[2], m[3]), pack4_magic(m[4], m[5], m[6], m[7]));
 }
 
 __device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
@@ -203,6 +219,43 @@ __device__ __forceinline__ void quantize_row16(const uint16_t* src, bool vec, in
     for (int t = 0; t < 4; ++t) amax2 = __vmaxu2(amax2, w[j][t] & 0x7fff7fffu);
   }
   quantize_packed_row<F16, G>(w, amax2, kp, lane, dst, scale_out, status, layer);
+}
+
+// Raw 16-bit groups (lane l: groups l, l+32, ...) of one row, zero past
+// `width`; loaded one row ahead of use by the RMS quantisers.
+template <int G>
+__device__ __forceinline__ void load_raw16(const uint16_t* __restrict__ src, int width, int lane, uint4 (&raw)[G]) {
+  const int groups = (width + 7) / 8;
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int g = lane + 32 * j;
+    const int c0 = 8 * g;
+    if (g < groups && vec && c0 + 8 <= width) {
+      raw[j] = __ldg(reinterpret_cast<const uint4*>(src + c0));
+    } else {
+      uint32_t w[4] = {0, 0, 0, 0};
+      if (g < groups) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          if (c0 + t < width) w[t / 2] |= static_cast<uint32_t>(__ldg(src + c0 + t)) << (16 * (t & 1));
+      }
+      raw[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+template <bool F16, int G>
+__device__ __forceinline__ void raw16_to_float(const uint4 (&raw)[G], float (&v)[G][8]) {
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      v[j][2 * t] = from16(static_cast<uint16_t>(w[t] & 0xffffu), F16);
+      v[j][2 * t + 1] = from16(static_cast<uint16_t>(w[t] >> 16), F16);
+    }
+  }
 }
 
 // RMSNorm of a warp-held row (lane l holds groups l, l+32, ...):
@@ -324,6 +377,69 @@ __global__ void __launch_bounds__(256) rms_mxfp8_kernel(
     mx_quantize_packed_row<false, G>(nw, row, kp, blocks4, lane, dst, scales, status, layer);
 }
 
+// Fused RMSNorm quantisers for 16-bit rows, persistent over rows: each warp
+// walks rows warp_id, warp_id + stride, ... and loads the next row while it
+// normalises and quantises the current one (the single-row form is bound by
+// the load latency of its one row).  MX = false: INT8 per-token output
+// (q int8 [rows, kp] + fp32 scales); MX = true: MXFP8 (q E4M3 + packed scales).
+template <bool F16IN, bool MX, int G>
+__global__ void __launch_bounds__(256) rms_rows16_kernel(
+    const uint16_t* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows, int width,
+    int kp, int blocks4, int bound_f16, void* __restrict__ q, void* __restrict__ scales, unsigned* status,
+    unsigned layer) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int step = gridDim.x * 8;
+  int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;  // warp-uniform
+  uint4 raw[G];
+  load_raw16<G>(x + static_cast<size_t>(row) * ldx, width, lane, raw);
+  for (; row < rows; row += step) {
+    float v[G][8];
+    raw16_to_float<F16IN, G>(raw, v);
+    if (row + step < rows) load_raw16<G>(x + static_cast<size_t>(row + step) * ldx, width, lane, raw);
+    uint32_t nw[G][4];
+    uint32_t amax2;
+    rms_normalize<G>(v, gamma, eps, width, lane, bound_f16 != 0, nw, amax2);
+    if constexpr (MX) {
+      uint8_t* dst = static_cast<uint8_t*>(q) + static_cast<size_t>(row) * kp;
+      if (bound_f16)
+        mx_quantize_packed_row<true, G>(nw, row, kp, blocks4, lane, dst, static_cast<uint8_t*>(scales), status, layer);
+      else
+        mx_quantize_packed_row<false, G>(nw, row, kp, blocks4, lane, dst, static_cast<uint8_t*>(scales), status, layer);
+    } else {
+      int8_t* dst = static_cast<int8_t*>(q) + static_cast<size_t>(row) * kp;
+      float* sc = static_cast<float*>(scales) + row;
+      if (bound_f16)
+        quantize_packed_row<true, G>(nw, amax2, kp, lane, dst, sc, status, layer);
+      else
+        quantize_packed_row<false, G>(nw, amax2, kp, lane, dst, sc, status, layer);
+    }
+  }
+}
+
+template <bool MX, int G>
+int launch_rms16(int dtype, const void* x, long ldx, const float* gamma, float eps, int rows, int width, int kp,
+                 int blocks4, int bound_f16, void* q, void* scales, unsigned* status, unsigned layer, cudaStream_t s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  // Persistent: as many CTAs as stay resident together, no second wave.
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &per_sm, dtype == kInF16 ? rms_rows16_kernel<true, MX, G> : rms_rows16_kernel<false, MX, G>, 256, 0);
+  if (e != cudaSuccess || per_sm < 1) per_sm = 1;
+  const int want = (rows + 7) / 8;
+  const int cap = per_sm * num_sms(dev);
+  const int grid = want < cap ? want : cap;
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  if (dtype == kInF16)
+    rms_rows16_kernel<true, MX, G><<<grid, 256, 0, s>>>(xs, ldx, gamma, eps, rows, width, kp, blocks4, bound_f16, q,
+                                                        scales, status, layer);
+  else
+    rms_rows16_kernel<false, MX, G><<<grid, 256, 0, s>>>(xs, ldx, gamma, eps, rows, width, kp, blocks4, bound_f16, q,
+                                                         scales, status, layer);
+  return check_cuda(cudaGetLastError(), "rms quantiser launch");
+}
+
 // One warp per row; G = groups of 8 per lane (W <= 256 * G).
 template <int IN, bool RMS, int G>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(
@@ -406,6 +522,8 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
 template <int IN, bool RMS, int G>
 int launch_g(const void* x, long ldx, const float* gamma, float eps, int rows, int width, int kp,
              int bound_f16, int8_t* q, float* scales, unsigned* status, unsigned layer, cudaStream_t s) {
+  if constexpr (RMS && IN != kInF32)
+    return launch_rms16<false, G>(IN, x, ldx, gamma, eps, rows, width, kp, 0, bound_f16, q, scales, status, layer, s);
   quantize_rows_kernel<IN, RMS, G><<<(rows + 7) / 8, 256, 0, s>>>(x, ldx, gamma, eps, rows, width, kp,
                                                                   bound_f16, q, scales, status, layer);
   return check_cuda(cudaGetLastError(), "quantiser launch");
@@ -506,6 +624,9 @@ int rms_mxfp8_launch(const void* x, int dtype, long ldx, int rows, int width, co
   const int grid = (rows + 7) / 8;
 #define KB_MXQ(IN, GG)                                                                                         \
   if (need <= GG) {                                                                                            \
+    if (IN != kInF32)                                                                                          \
+      return launch_rms16<true, GG>(IN, x, ldx, gamma, eps, rows, width, kp, blocks4, bound_f16, q, scales,     \
+                                    status, layer, stream);                                                    \
     rms_mxfp8_kernel<IN, GG><<<grid, 256, 0, stream>>>(x, ldx, gamma, eps, rows, width, kp, blocks4, bound_f16, \
                                                         q, scales, status, layer);                             \
     return check_cuda(cudaGetLastError(), "rms mxfp8 launch");                                                  \
