@@ -78,29 +78,46 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 }
 
 // Rows [r0, r0 + nrows) of Q or K (part = 0 / 1) or V (part = 2) of head h of
-// one position into a swizzled tile; rows at or past `seq` are zero.
+// one position into a swizzled tile; rows at or past `seq` are zero.  Each
+// thread handles kBatch 16-byte chunks per step with all their global loads
+// issued before any is used, so the copy is not bound by one load's latency.
+constexpr int kBatch = 4;
+
 template <bool F16>
 __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, size_t row_stride, int part, int h,
                                            int heads, const float* cos_t, const float* sin_t, int r0, int nrows,
                                            int seq, int tid, int nthreads) {
   const int c = heads * kD;
-  for (int t = tid; t < nrows * 8; t += nthreads) {
-    const int r = t >> 3, ch = t & 7;
-    const int tok = r0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (tok < seq) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(base + tok * row_stride + part * c + h * kD + ch * 8));
-      if (part == 2) {
-        v = raw;
-      } else {
-        const size_t ro = (static_cast<size_t>(tok) * heads + h) * (kD / 2) + ch * 4;
-        const float4 co = __ldg(reinterpret_cast<const float4*>(cos_t + ro));
-        const float4 si = __ldg(reinterpret_cast<const float4*>(sin_t + ro));
-        v = make_uint4(rope2(raw.x, co.x, si.x, F16), rope2(raw.y, co.y, si.y, F16), rope2(raw.z, co.z, si.z, F16),
-                       rope2(raw.w, co.w, si.w, F16));
+  const int total = nrows * 8;
+  for (int t0 = tid; t0 < total; t0 += kBatch * nthreads) {
+    uint4 raw[kBatch];
+    float4 co[kBatch], si[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int t = t0 + u * nthreads;
+      const int r = t >> 3, ch = t & 7;
+      const int tok = r0 + r;
+      raw[u] = make_uint4(0, 0, 0, 0);
+      if (t < total && tok < seq) {
+        raw[u] = __ldg(reinterpret_cast<const uint4*>(base + tok * row_stride + part * c + h * kD + ch * 8));
+        if (part != 2) {
+          const size_t ro = (static_cast<size_t>(tok) * heads + h) * (kD / 2) + ch * 4;
+          co[u] = __ldg(reinterpret_cast<const float4*>(cos_t + ro));
+          si[u] = __ldg(reinterpret_cast<const float4*>(sin_t + ro));
+        }
       }
     }
-    *reinterpret_cast<uint4*>(dst + sw128(r, ch)) = v;
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int t = t0 + u * nthreads;
+      if (t >= total) break;
+      const int r = t >> 3, ch = t & 7;
+      uint4 v = raw[u];
+      if (part != 2 && r0 + r < seq)
+        v = make_uint4(rope2(raw[u].x, co[u].x, si[u].x, F16), rope2(raw[u].y, co[u].y, si[u].y, F16),
+                       rope2(raw[u].z, co[u].z, si[u].z, F16), rope2(raw[u].w, co[u].w, si[u].w, F16));
+      *reinterpret_cast<uint4*>(dst + sw128(r, ch)) = v;
+    }
   }
 }
 

@@ -139,6 +139,21 @@ __device__ __forceinline__ float apply_act(float v) {
   else return v;
 }
 
+// Division of 32-bit dividends n < 2^31 by a runtime-invariant divisor d >= 1
+// without a division instruction (the round-up multiplier method of Granlund &
+// Montgomery, "Division by invariant integers using multiplication", 1994):
+// with s = ceil(log2 d) and m = floor(2^32 * (2^s - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> s.
+struct FastDiv {
+  uint32_t d = 1, m = 0, s = 0;
+  FastDiv() = default;
+  __host__ explicit FastDiv(uint32_t div) : d(div) {
+    while ((1ull << s) < d) ++s;
+    m = static_cast<uint32_t>((((1ull << s) - d) << 32) / d + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> s; }
+};
+
 // Round a float through a 16-bit storage type (RNE) and back.
 __device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 __device__ __forceinline__ float round_bf16(float v) {

@@ -560,22 +560,23 @@ constexpr int kStreamGroups = 4;
 template <bool F16>
 __global__ void __launch_bounds__(256) quantize_rows_amax_kernel(
     const uint16_t* __restrict__ x, long ldx, const uint32_t* __restrict__ row_amax, int rows, int width,
-    int kp, int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
+    int kp, FastDiv groups_div, int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status,
+    unsigned layer) {
   const int out_groups = kp / 8;
-  const long total = static_cast<long>(rows) * out_groups;
-  const long step = static_cast<long>(gridDim.x) * blockDim.x * kStreamGroups;
-  for (long base = static_cast<long>(blockIdx.x) * blockDim.x * kStreamGroups + threadIdx.x; base < total;
-       base += step) {
+  // total < 2^31 is checked by the launcher: 32-bit indices, no division instruction.
+  const int total = rows * out_groups;
+  const int step = gridDim.x * blockDim.x * kStreamGroups;
+  for (int base = blockIdx.x * blockDim.x * kStreamGroups + threadIdx.x; base < total; base += step) {
     uint32_t w[kStreamGroups][4];
     int row[kStreamGroups], c0[kStreamGroups];
 #pragma unroll
     for (int j = 0; j < kStreamGroups; ++j) {
-      const long idx = base + static_cast<long>(j) * blockDim.x;
+      const int idx = base + j * blockDim.x;
       w[j][0] = w[j][1] = w[j][2] = w[j][3] = 0;
       row[j] = -1;
       if (idx < total) {
-        row[j] = static_cast<int>(idx / out_groups);
-        c0[j] = 8 * static_cast<int>(idx % out_groups);
+        row[j] = static_cast<int>(groups_div.div(static_cast<uint32_t>(idx)));
+        c0[j] = 8 * (idx - row[j] * out_groups);
         const uint16_t* src = x + static_cast<size_t>(row[j]) * ldx + c0[j];
         if (c0[j] + 8 <= width) {
           const uint4 a = __ldg(reinterpret_cast<const uint4*>(src));
@@ -657,17 +658,22 @@ int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t
     return KB_E_INVALID;
   }
   const long total = static_cast<long>(rows) * (kp / 8);
+  if (total + 256L * kStreamGroups * 8 * 1024 > 0x7fffffffL) {
+    set_error("amax quantiser: rows * kp / 8 must stay below 2^31");
+    return KB_E_INVALID;
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   const long max_blocks = static_cast<long>(num_sms(dev)) * 8;
   const long need = (total + 256 * kStreamGroups - 1) / (256 * kStreamGroups);
   const long blocks = need < max_blocks ? need : max_blocks;
+  const FastDiv gdiv(static_cast<uint32_t>(kp / 8));
   if (dtype == kInF16)
     quantize_rows_amax_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, q, scales, status, layer);
+        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, gdiv, q, scales, status, layer);
   else
     quantize_rows_amax_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, q, scales, status, layer);
+        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, gdiv, q, scales, status, layer);
   return check_cuda(cudaGetLastError(), "amax quantiser launch");
 }
 
