@@ -8,24 +8,23 @@
 // to the 16-bit type, softmax of (q.k) * scale over all keys in fp32, P rounded
 // to the 16-bit type for the P.V product, output [tokens, C] heads merged.
 //
-// One CTA per (position, head); two CTAs share an SM (112 KB shared memory and
-// 256 TMEM columns each).  All 361 keys fit on chip, so there is no streaming:
-//   shared memory  K and V of the board, 368 rows x 128 B (keys padded to a
-//                  multiple of 16), and one 128-query Q tile, all in the UMMA
-//                  128-byte-swizzled layout (written by the CTA's threads,
-//                  with RoPE applied on the way in);
-//   TMEM           S (128 lanes x 192 fp32 columns) and O (64 columns).
-// Per 128-query tile, keys in two halves A = [0, 192) and B = [192, 368):
-//   MMA  S = Q K_A^T          softmax warps: row max, P_A = exp2((S - m) c) in
-//                             place over S as packed 16-bit (A operand), sum
-//   MMA  O = P_A V_A          (A from TMEM, V as an MN-major B operand)
-//   MMA  S = Q K_B^T          softmax: m' = max(m, max S_B), P_B, rescale O by
-//                             exp2((m - m') c) when the maximum moved
-//   MMA  O += P_B V_B         epilogue: O / sum -> 16-bit, row |max| for the
-//                             next quantiser.
-// Warps 0-3 (one TMEM lane quarter each, thread = query row) load, run the
-// softmax and the epilogue; warp 4 issues the MMAs.  Every wait is bounded;
-// the softmax warps leave together (warp-collective TMEM accesses follow).
+// Persistent: one CTA per SM walks (position, head) pairs.  All 361 keys fit
+// on chip, so nothing streams inside a pair:
+//   shared memory  K and V of two pairs (double buffer, 368 keys x 128 B each,
+//                  keys padded to a multiple of 16) and two 128-query Q tiles,
+//                  all in the UMMA 128-byte-swizzled layout, written by four
+//                  loader warps with RoPE applied on the way in;
+//   TMEM (512 col) S_A = Q K[0:192]^T (192 columns), S_B = Q K[192:368]^T (176),
+//                  O_A = P_A V[0:192] and O_B = P_B V[192:368] (64 each).
+// Per 128-query tile the two key halves are independent: softmax warp group A
+// (warps 0-3) and group B (warps 4-7), thread = query row, each take the row
+// max and sum of their half and write P = exp2((S - m) c) in place over S as
+// packed 16-bit values (the A operand of the P.V MMA, read from TMEM).  The
+// epilogue combines the halves: O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) /
+// (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), group A writing dims 0-31 and group
+// B dims 32-63, plus the row |max| for the next quantiser.  Warp 8 issues the
+// MMAs; the S MMAs of the next tile overlap this tile's epilogue, and the
+// loaders stage the next pair while this one computes.  Every wait is bounded.
 #include <stdint.h>
 
 #include <atomic>
@@ -43,12 +42,18 @@ constexpr int kHalfA = 192, kHalfB = kKeysPad - kHalfA;  // 176
 constexpr int kTileQ = 128;
 constexpr int kRowBytes = kD * 2;         // 128 B: one swizzle row
 constexpr int kKBytes = kKeysPad * kRowBytes;
+constexpr int kKVBytes = 2 * kKBytes;     // K then V of one pair
 constexpr int kQBytes = kTileQ * kRowBytes;
-constexpr int kSoftThreads = 128;
-constexpr int kTcThreads = kSoftThreads + 32;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kOCol = 192;
-constexpr int kSmemBytes = 2 * kKBytes + kQBytes + 128 /*barriers*/ + 1024 /*alignment*/;
+constexpr int kSoftWarps = 8, kLoadWarps = 4;
+constexpr int kMmaWarp = kSoftWarps;
+constexpr int kFaThreads = 32 * (kSoftWarps + 1 + kLoadWarps);  // 416
+constexpr int kLoadThreads = 32 * kLoadWarps;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSB = kHalfA, kOA = kHalfA + kHalfB, kOB = kOA + kD;  // TMEM columns
+constexpr int kBarBytes = 256;
+// (m, l) of each row and key half, double-buffered by tile parity.
+constexpr int kMlBytes = 2 * 2 * kTileQ * 8;
+constexpr int kSmemBytes = 2 * kKVBytes + 2 * kQBytes + kBarBytes + kMlBytes + 1024 /*alignment*/;
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
   if (f16) {
@@ -122,225 +127,249 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
 }
 
 template <bool F16>
-__global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(
+__global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
     const uint16_t* __restrict__ qkv, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
-    uint16_t* __restrict__ out, int seq, int heads, float scale_log2, uint32_t* __restrict__ row_amax,
+    uint16_t* __restrict__ out, int pairs, int seq, int heads, float scale_log2, uint32_t* __restrict__ row_amax,
     unsigned* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ks = smem;
-  uint8_t* vs = smem + kKBytes;
-  uint8_t* qs = smem + 2 * kKBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(qs + kQBytes);
-  uint64_t* s_full = bars + 0;  // S ready (tcgen05.commit), twice per tile
-  uint64_t* p_full = bars + 1;  // P in TMEM (128 softmax threads), twice per tile
-  uint64_t* o_full = bars + 2;  // P.V done (tcgen05.commit), twice per tile
-  uint64_t* q_full = bars + 3;  // next Q tile staged (128 threads)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  uint8_t* kv_buf = smem;                    // [2][K | V]
+  uint8_t* q_buf = smem + 2 * kKVBytes;      // [2][Q tile]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(q_buf + 2 * kQBytes);
+  uint64_t* kv_full = bars + 0;   // [2] loaders staged K/V           (128 arrivals)
+  uint64_t* kv_empty = bars + 2;  // [2] MMAs done with K/V            (commit)
+  uint64_t* q_full = bars + 4;    // [2] loaders staged a Q tile       (128 arrivals)
+  uint64_t* q_empty = bars + 6;   // [2] S MMAs done with a Q tile     (commit)
+  uint64_t* sa_full = bars + 8;   // S_A ready                         (commit)
+  uint64_t* sb_full = bars + 9;   // S_B ready                         (commit)
+  uint64_t* pa_full = bars + 10;  // P_A written, O read back          (128 arrivals)
+  uint64_t* pb_full = bars + 11;  // P_B written, O read back          (128 arrivals)
+  uint64_t* o_full = bars + 12;   // O_A and O_B ready                 (commit)
+  uint64_t* ml_full = bars + 13;  // both halves' (m, l) of a tile     (256 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float2* ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][2][128]
 
-  const int b = blockIdx.x / heads;
-  const int h = blockIdx.x % heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = heads * kD;
   const size_t row_stride = 3 * static_cast<size_t>(c);
-  const uint16_t* base = qkv + static_cast<size_t>(b) * seq * row_stride;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = (seq + kTileQ - 1) / kTileQ;
 
   if (threadIdx.x == 0) {
-    mbar_init(s_full, 1);
-    mbar_init(p_full, kSoftThreads);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], kLoadThreads);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&q_full[i], kLoadThreads);
+      mbar_init(&q_empty[i], 1);
+    }
+    mbar_init(sa_full, 1);
+    mbar_init(sb_full, 1);
+    mbar_init(pa_full, 128);
+    mbar_init(pb_full, 128);
     mbar_init(o_full, 1);
-    mbar_init(q_full, kSoftThreads);
+    mbar_init(ml_full, 256);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
-  // Stage K (rotated), V and the first Q tile with every thread of the CTA.
-  stage_rows<F16>(ks, base, row_stride, 1, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, threadIdx.x, kTcThreads);
-  stage_rows<F16>(vs, base, row_stride, 2, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, threadIdx.x, kTcThreads);
-  stage_rows<F16>(qs, base, row_stride, 0, h, heads, rope_cos, rope_sin, 0, kTileQ, seq, threadIdx.x, kTcThreads);
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
-    // ---------------------------------------------------------------- MMA issuer
+  if (warp > kMmaWarp) {
+    // ------------------------------------------------------------ loaders
+    const int tid = threadIdx.x - 32 * (kMmaWarp + 1);
+    int g = 0;  // global Q tile counter
+    for (int it = 0, p = blockIdx.x; p < pairs; ++it, p += gridDim.x) {
+      const int kb = it & 1;
+      const int b = p / heads, h = p % heads;
+      const uint16_t* base = qkv + static_cast<size_t>(b) * seq * row_stride;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
+      uint8_t* ks = kv_buf + kb * kKVBytes;
+      stage_rows<F16>(ks, base, row_stride, 1, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid, kLoadThreads);
+      stage_rows<F16>(ks + kKBytes, base, row_stride, 2, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid,
+                      kLoadThreads);
+      fence_proxy_async_smem();
+      mbar_arrive(&kv_full[kb]);
+      bool ok = true;
+      for (int t = 0; t < tiles; ++t, ++g) {
+        const int qb = g & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&q_empty[qb], ((g >> 1) & 1) ^ 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        stage_rows<F16>(q_buf + qb * kQBytes, base, row_stride, 0, h, heads, rope_cos, rope_sin, t * kTileQ, kTileQ,
+                        seq, tid, kLoadThreads);
+        fence_proxy_async_smem();
+        mbar_arrive(&q_full[qb]);
+      }
+      if (!ok) break;
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kFmt = F16 ? 0u : 1u;
       const uint32_t id_common = (1u << 4) | (kFmt << 7) | (kFmt << 10) | (static_cast<uint32_t>(128 >> 4) << 24);
       const uint32_t id_sa = id_common | (static_cast<uint32_t>(kHalfA >> 3) << 17);
       const uint32_t id_sb = id_common | (static_cast<uint32_t>(kHalfB >> 3) << 17);
       const uint32_t id_pv = id_common | (1u << 16) /* B MN-major */ | (static_cast<uint32_t>(kD >> 3) << 17);
-      const uint64_t qdesc = sw128_desc(smem_u32(qs));
-      const uint64_t kdesc = sw128_desc(smem_u32(ks));
-      const uint64_t vdesc = sw128_desc(smem_u32(vs));
-      // Half B starts 192 rows (192 * 128 B, >> 4 in the address field) further.
-      constexpr uint64_t kHalfBOff = (kHalfA * kRowBytes) >> 4;
-      constexpr uint64_t kKStep16 = (16 * kRowBytes) >> 4;  // 16 keys of V along K
-      for (int t = 0; t < tiles; ++t) {
-        if (t > 0 && !mbar_wait(q_full, (t - 1) & 1, abort_flag)) break;
-        tc_fence_after();
+      constexpr uint64_t kHalfOff = (kHalfA * kRowBytes) >> 4;  // 192 rows, descriptor units
+      constexpr uint64_t kStep16 = (16 * kRowBytes) >> 4;       // 16 keys of V along K
+      int g = 0;
+      bool ok = true;
+      for (int it = 0, p = blockIdx.x; p < pairs && ok; ++it, p += gridDim.x) {
+        const int kb = it & 1;
+        if (!mbar_wait(&kv_full[kb], (it >> 1) & 1, abort_flag)) break;
+        const uint64_t kdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes));
+        const uint64_t vdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes + kKBytes));
+        for (int t = 0; t < tiles; ++t, ++g) {
+          const int qb = g & 1;
+          if (!mbar_wait(&q_full[qb], (g >> 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t qdesc = sw128_desc(smem_u32(q_buf + qb * kQBytes));
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)  // 16 elements = 32 bytes of K per MMA
-          mma_issue<kKindBF16>(tmem, qdesc + 2 * kk, kdesc + 2 * kk, id_sa, kk != 0, 0, 0);
-        tc_commit(s_full);
-        if (!mbar_wait(p_full, 0, abort_flag)) break;
-        tc_fence_after();
-        for (int i = 0; i < kHalfA / 16; ++i)
-          mma_f16_ts(tmem + kOCol, tmem + 8 * i, vdesc + kKStep16 * i, id_pv, i != 0);
-        tc_commit(o_full);
-        if (!mbar_wait(o_full, 0, abort_flag)) break;  // P_A consumed before S is overwritten
-        tc_fence_after();
+          for (int kk = 0; kk < kD / 16; ++kk)
+            mma_issue<kKindBF16>(tmem, qdesc + 2 * kk, kdesc + 2 * kk, id_sa, kk != 0, 0, 0);
+          tc_commit(sa_full);
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_issue<kKindBF16>(tmem, qdesc + 2 * kk, kdesc + kHalfBOff + 2 * kk, id_sb, kk != 0, 0, 0);
-        tc_commit(s_full);
-        if (!mbar_wait(p_full, 1, abort_flag)) break;
-        tc_fence_after();
-        for (int i = 0; i < kHalfB / 16; ++i)
-          mma_f16_ts(tmem + kOCol, tmem + 8 * i, vdesc + kHalfBOff + kKStep16 * i, id_pv, 1);
-        tc_commit(o_full);
-        if (!mbar_wait(o_full, 1, abort_flag)) break;  // P_B consumed before the next tile's S
+          for (int kk = 0; kk < kD / 16; ++kk)
+            mma_issue<kKindBF16>(tmem + kSB, qdesc + 2 * kk, kdesc + kHalfOff + 2 * kk, id_sb, kk != 0, 0, 0);
+          tc_commit(sb_full);
+          tc_commit(&q_empty[qb]);
+          // P_A and P_B written (and the previous tile's O read back) by both groups.
+          if (!mbar_wait(pa_full, g & 1, abort_flag) || !mbar_wait(pb_full, g & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int i = 0; i < kHalfA / 16; ++i)
+            mma_f16_ts(tmem + kOA, tmem + 8 * i, vdesc + kStep16 * i, id_pv, i != 0);
+          for (int i = 0; i < kHalfB / 16; ++i)
+            mma_f16_ts(tmem + kOB, tmem + kSB + 8 * i, vdesc + kHalfOff + kStep16 * i, id_pv, i != 0);
+          tc_commit(o_full);
+          if (t + 1 == tiles) tc_commit(&kv_empty[kb]);
+          // P consumed before the next tile's S MMAs overwrite it.
+          if (!mbar_wait(o_full, g & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+        }
       }
     }
   } else {
-    // ---------------------------------------------------------------- softmax + epilogue
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const int row = warp * 32 + lane;
-    for (int t = 0; t < tiles; ++t) {
-      const int query = t * kTileQ + row;
-      // -- half A: keys [0, 192), all valid (seq > 192 is required by the launcher)
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, 0, abort_flag))) break;
-      tc_fence_after();
-      float m = __int_as_float(0xff800000);
-      for (int ch = 0; ch < kHalfA / 32; ++ch) {
-        uint32_t v[32];
-        tmem_ld32(lane_base + ch * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) m = fmaxf(m, __uint_as_float(v[i]));
-      }
-      float mc = m * scale_log2;
-      float l = 0.0f;
-      for (int ch = 0; ch < kHalfA / 32; ++ch) {
-        uint32_t v[32], pk[16];
-        tmem_ld32(lane_base + ch * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc));
-          const float p1 = ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc));
-          l += p0 + p1;
-          pk[i] = pack2(p0, p1, F16);
+    // ------------------------------------------------------------ softmax + epilogue
+    const int grp = warp >> 2;  // 0: keys [0, 192), 1: keys [192, 368)
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_col = grp ? kSB : 0u;
+    const int valid = grp ? seq - kHalfA : kHalfA;   // keys of this half below seq
+    constexpr int kChunks = (kHalfA + 31) / 32;      // 6 (half B's last chunk is partial)
+    uint64_t* s_bar = grp ? sb_full : sa_full;
+    uint64_t* p_bar = grp ? pb_full : pa_full;
+    int g = 0;
+    bool ok = true;
+    for (int p = blockIdx.x; p < pairs && ok; p += gridDim.x) {
+      const int b = p / heads, h = p % heads;
+      for (int t = 0; t < tiles; ++t, ++g) {
+        if (!__all_sync(0xffffffffu, mbar_wait(s_bar, g & 1, abort_flag))) {
+          ok = false;
+          break;
         }
-        tmem_st16(lane_base + ch * 16, pk);  // P over the S columns already read
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full);
-      // -- half B: keys [192, 368), valid below seq
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, 1, abort_flag))) break;
-      tc_fence_after();
-      const int valid_b = seq - kHalfA;
-      float mb = __int_as_float(0xff800000);
-      for (int ch = 0; ch < (kHalfB + 31) / 32; ++ch) {
-        uint32_t v[32];
-        tmem_ld32(lane_base + ch * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (ch * 32 + i < valid_b) mb = fmaxf(mb, __uint_as_float(v[i]));
-      }
-      const float mn = fmaxf(m, mb);
-      const float alpha = mn == m ? 1.0f : ex2(__fmul_rn(__fsub_rn(m, mn), scale_log2));
-      mc = mn * scale_log2;
-      float lb = 0.0f;
-      for (int ch = 0; ch < (kHalfB + 31) / 32; ++ch) {
-        uint32_t v[32], pk[16];
-        tmem_ld32(lane_base + ch * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k0 = ch * 32 + 2 * i;
-          const float p0 = k0 < valid_b ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
-          const float p1 = k0 + 1 < valid_b ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
-          lb += p0 + p1;
-          pk[i] = pack2(p0, p1, F16);
-        }
-        tmem_st16(lane_base + ch * 16, pk);
-      }
-      l = l * alpha + lb;
-      // O holds P_A.V_A scaled to the old maximum: rescale where it moved.
-      if (!__all_sync(0xffffffffu, mbar_wait(o_full, 0, abort_flag))) break;
-      tc_fence_after();
-      if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        tc_fence_after();
+        float m = __int_as_float(0xff800000);
+#pragma unroll 1
+        for (int ch = 0; ch < kChunks; ++ch) {
           uint32_t v[32];
-          tmem_ld32(lane_base + kOCol + half * 32, v);
+          tmem_ld32(lane_base + s_col + ch * 32, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          tmem_st32(lane_base + kOCol + half * 32, v);
+          for (int i = 0; i < 32; ++i)
+            if (ch * 32 + i < valid) m = fmaxf(m, __uint_as_float(v[i]));
         }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full);
-      // -- the next Q tile: S_B has consumed this one
-      if (t + 1 < tiles) {
-        stage_rows<F16>(qs, base, row_stride, 0, h, heads, rope_cos, rope_sin, (t + 1) * kTileQ, kTileQ, seq,
-                        threadIdx.x, kSoftThreads);
-        fence_proxy_async_smem();
-        mbar_arrive(q_full);
-      }
-      // -- epilogue: O / l -> 16-bit output row, row |max|
-      if (!__all_sync(0xffffffffu, mbar_wait(o_full, 1, abort_flag))) break;
-      tc_fence_after();
-      const float inv = 1.0f / l;
-      uint32_t am = 0;
-      uint16_t* dst = out + (static_cast<size_t>(b) * seq + query) * c + h * kD;
+        const float mc = m * scale_log2;
+        float l = 0.0f;
+#pragma unroll 1
+        for (int ch = 0; ch < kChunks; ++ch) {
+          uint32_t v[32], pk[16];
+          tmem_ld32(lane_base + s_col + ch * 32, v);
+          tmem_ld_wait();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t v[32], w[16];
-        tmem_ld32(lane_base + kOCol + half * 32, v);
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = ch * 32 + 2 * i;
+            const float p0 = k0 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
+            const float p1 = k0 + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
+            l += p0 + p1;
+            pk[i] = pack2(p0, p1, F16);
+          }
+          tmem_st16(lane_base + s_col + ch * 16, pk);  // P over S columns already read
+        }
+        ml[((g & 1) * 2 + grp) * kTileQ + row] = make_float2(m, l);
+        mbar_arrive(ml_full);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_bar);
+        if (!__all_sync(0xffffffffu, mbar_wait(o_full, g & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // both halves' (m, l) of this tile are in shared memory
+        if (!__all_sync(0xffffffffu, mbar_wait(ml_full, g & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const float2 a = ml[((g & 1) * 2 + 0) * kTileQ + row];
+        const float2 bb = ml[((g & 1) * 2 + 1) * kTileQ + row];
+        const float mx = fmaxf(a.x, bb.x);
+        const float fa = a.x == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(a.x, mx), scale_log2));
+        const float fb = bb.x == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(bb.x, mx), scale_log2));
+        const float inv = 1.0f / (a.y * fa + bb.y * fb);
+        const float wa = fa * inv, wb = fb * inv;
+        uint32_t oa[32], ob[32], w[16];
+        tmem_ld32(lane_base + kOA + grp * 32, oa);
+        tmem_ld32(lane_base + kOB + grp * 32, ob);
         tmem_ld_wait();
+        tc_fence_before();
+        uint32_t am = 0;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          w[i] = pack2(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv, F16);
+          const float x0 = __uint_as_float(oa[2 * i]) * wa + __uint_as_float(ob[2 * i]) * wb;
+          const float x1 = __uint_as_float(oa[2 * i + 1]) * wa + __uint_as_float(ob[2 * i + 1]) * wb;
+          w[i] = pack2(x0, x1, F16);
           am = __vmaxu2(am, w[i] & 0x7fff7fffu);
         }
+        const int query = t * kTileQ + row;
         if (query < seq) {
+          uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(b) * seq + query) * c + h * kD + grp * 32);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            reinterpret_cast<uint4*>(dst + half * 32)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          if (row_amax != nullptr) {
+            const uint32_t m16 = max(am & 0xffffu, am >> 16);
+            atomicMax(row_amax + static_cast<size_t>(b) * seq + query,
+                      F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
+          }
         }
       }
-      if (row_amax != nullptr && query < seq) {
-        const uint32_t m16 = max(am & 0xffffu, am >> 16);
-        atomicMax(row_amax + static_cast<size_t>(b) * seq + query,
-                  F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
-      }
-      tc_fence_before();
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (threadIdx.x == 0 && *abort_flag) record_status(status, KB_STATUS_TIMEOUT, KB_NO_LAYER);
-  if (warp == 4) tmem_dealloc(tmem, kTmemCols);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
 template <bool F16>
 int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint16_t* out, int batch, int seq,
               int heads, float scale, uint32_t* row_amax, unsigned* status, cudaStream_t stream) {
-  auto kern = attention_tc_kernel<F16>;
+  auto kern = attention_fa_kernel<F16>;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> configured{0};
@@ -351,8 +380,10 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
     configured.fetch_or(bit);
   }
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<batch * heads, kTcThreads, kSmemBytes, stream>>>(qkv, cos_t, sin_t, out, seq, heads, scale_log2, row_amax,
-                                                          status);
+  const int pairs = batch * heads;
+  const int grid = pairs < num_sms(dev) ? pairs : num_sms(dev);
+  kern<<<grid, kFaThreads, kSmemBytes, stream>>>(qkv, cos_t, sin_t, out, pairs, seq, heads, scale_log2, row_amax,
+                                                 status);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 
