@@ -216,6 +216,8 @@ KB_API int kb_bf16_linear(const uint16_t* a, const uint16_t* w, const float* bia
  * qkv [batch*361, 3*heads*head_dim] ([Q | K | V], 16-bit, dtype KB_DT_BF16 or
  * KB_DT_F16), rope_cos/rope_sin fp32 [361, heads, head_dim/2] (interleaved
  * pairs), out [batch*361, heads*head_dim]; softmax(q.k * scale) over all keys.
+ * rope_cos and rope_sin may both be NULL when Q and K are already rotated (the
+ * trunk rotates them in the QKV projection's epilogue).
  * head_dim 32 or 64.  Replaces: attention_fa2_q64_kernel
  * (cuda-kernels/attention_fa2_q64.cu:82-390) via cuda_exec.rs:3442. */
 KB_API int kb_attention(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,

@@ -91,23 +91,39 @@ def rope_tables(freqs):
     return cs, sn
 
 
-def attention(qkv, cs, sn, n, nh, hd):
-    """Softmax attention per (position, head) with RoPE on Q and K
-    (debug_exec_units.rs:161-242; the kernel rounds rotated Q/K to bf16)."""
+def rot(t, cs, sn):
+    """RoPE of interleaved pairs (2p, 2p+1) in float32 with each product and sum
+    rounded: (x c - y s, x s + y c); t [n, 361, heads, hd], tables [361, heads, hd/2]."""
+    t = np.asarray(t, np.float32)
+    a, b = t[..., 0::2], t[..., 1::2]
+    ra = (a * cs[None]).astype(np.float32) - (b * sn[None]).astype(np.float32)
+    rb = (a * sn[None]).astype(np.float32) + (b * cs[None]).astype(np.float32)
+    out = np.empty_like(t)
+    out[..., 0::2] = ra
+    out[..., 1::2] = rb
+    return out
+
+
+def rope_qkv(qkv32, cs, sn, n, nh, hd):
+    """The QKV projection's epilogue: Q and K rotated on the fp32 projection,
+    then everything rounded to bf16 (rotary tables native_model.rs:200-228)."""
+    c = nh * hd
+    x = np.asarray(qkv32, np.float32).reshape(n, SEQ, 3, nh, hd).copy()
+    x[:, :, 0] = rot(x[:, :, 0], cs, sn)
+    x[:, :, 1] = rot(x[:, :, 1], cs, sn)
+    return bf(x.reshape(n * SEQ, 3 * c))
+
+
+def attention(qkv, cs, sn, n, nh, hd, rotate=True):
+    """Softmax attention per (position, head) (debug_exec_units.rs:161-242).
+    rotate: apply RoPE to the 16-bit Q and K here and round to bf16 (the
+    attention kernel's own rotation); False when Q and K arrive rotated."""
     c = nh * hd
     x = qkv.reshape(n, SEQ, 3, nh, hd)
     q, k, v = x[:, :, 0], x[:, :, 1], x[:, :, 2]
-
-    def rot(t):
-        a, b = t[..., 0::2], t[..., 1::2]
-        ra = (a * cs[None]).astype(np.float32) - (b * sn[None]).astype(np.float32)
-        rb = (a * sn[None]).astype(np.float32) + (b * cs[None]).astype(np.float32)
-        out = np.empty_like(t)
-        out[..., 0::2] = ra
-        out[..., 1::2] = rb
-        return bf(out)
-
-    q, k = rot(q).astype(np.float64), rot(k).astype(np.float64)
+    if rotate:
+        q, k = bf(rot(q, cs, sn)), bf(rot(k, cs, sn))
+    q, k = q.astype(np.float64), k.astype(np.float64)
     v = v.astype(np.float64)
     s = np.einsum("bqhd,bkhd->bhqk", q, k) / math.sqrt(hd)
     s -= s.max(axis=-1, keepdims=True)
@@ -163,8 +179,9 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
         if precision == "mxfp8":
             wq, wo, wu, wd = (_mx_weight(w[f"{i}.{nm}"]) for nm in ("qkv", "out", "up", "down"))
             _, _, normed = rms_quantize(x, w[f"{i}.rms1"], EPS, False)
-            qkv = bf(_mx_linear(normed, wq))
-            att = attention(qkv, cs, sn, n, nh, hd) if teacher is None else np.asarray(teacher[1][i], np.float32)
+            qkv = rope_qkv(_mx_linear(normed, wq), cs, sn, n, nh, hd)
+            att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None
+                   else np.asarray(teacher[1][i], np.float32))
             x = bf((x + _mx_linear(att, wo)).astype(np.float32))
             _, _, normed = rms_quantize(x, w[f"{i}.rms2"], EPS, False)
             v = (_mx_linear(normed, wu) + w[f"{i}.up_b"][None, :]).astype(np.float32)
@@ -177,8 +194,9 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
         uw, us = quantize_weights(w[f"{i}.up"])
         dw, ds = quantize_weights(w[f"{i}.down"])
         q, sa, _ = rms_quantize(x, w[f"{i}.rms1"], EPS, False, kp=qw.shape[1])
-        qkv = bf(dequant(igemm(q, qw), sa, qs))
-        att = attention(qkv, cs, sn, n, nh, hd) if teacher is None else np.asarray(teacher[1][i], np.float32)
+        qkv = rope_qkv(dequant(igemm(q, qw), sa, qs), cs, sn, n, nh, hd)
+        att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None
+               else np.asarray(teacher[1][i], np.float32))
         q2, s2 = quantize_rows(att, kp=ow.shape[1])
         x = bf((x + dequant(igemm(q2, ow), s2, os_)).astype(np.float32))
         q3, s3, _ = rms_quantize(x, w[f"{i}.rms2"], EPS, False, kp=uw.shape[1])

@@ -116,13 +116,17 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
       const uint16_t* vr = base + key * row_stride + 2 * c + h * D + d0;
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(kr));
       vv = __ldg(reinterpret_cast<const uint4*>(vr));
-      const size_t ro = (static_cast<size_t>(key) * heads + h) * pairs_per_head + d0 / 2;
-      const float4 co = __ldg(reinterpret_cast<const float4*>(rope_cos + ro));
-      const float4 si = __ldg(reinterpret_cast<const float4*>(rope_sin + ro));
-      kv.x = rope_pair(raw.x, co.x, si.x, F16);
-      kv.y = rope_pair(raw.y, co.y, si.y, F16);
-      kv.z = rope_pair(raw.z, co.z, si.z, F16);
-      kv.w = rope_pair(raw.w, co.w, si.w, F16);
+      if (rope_cos != nullptr) {
+        const size_t ro = (static_cast<size_t>(key) * heads + h) * pairs_per_head + d0 / 2;
+        const float4 co = __ldg(reinterpret_cast<const float4*>(rope_cos + ro));
+        const float4 si = __ldg(reinterpret_cast<const float4*>(rope_sin + ro));
+        kv.x = rope_pair(raw.x, co.x, si.x, F16);
+        kv.y = rope_pair(raw.y, co.y, si.y, F16);
+        kv.z = rope_pair(raw.z, co.z, si.z, F16);
+        kv.w = rope_pair(raw.w, co.w, si.w, F16);
+      } else {
+        kv = raw;
+      }
     }
     *reinterpret_cast<uint4*>(ks + key * kStride + d0) = kv;
     *reinterpret_cast<uint4*>(vs + key * kStride + d0) = vv;
@@ -145,8 +149,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
         uint32_t w = 0;
         if (r < seq) {
           const uint32_t raw = *reinterpret_cast<const uint32_t*>(base + r * row_stride + h * D + d);
-          const size_t ro = (static_cast<size_t>(r) * heads + h) * pairs_per_head + d / 2;
-          w = rope_pair(raw, __ldg(rope_cos + ro), __ldg(rope_sin + ro), F16);
+          if (rope_cos != nullptr) {
+            const size_t ro = (static_cast<size_t>(r) * heads + h) * pairs_per_head + d / 2;
+            w = rope_pair(raw, __ldg(rope_cos + ro), __ldg(rope_sin + ro), F16);
+          } else {
+            w = raw;
+          }
         }
         qa[kk][part] = w;
       }
@@ -291,13 +299,14 @@ int launch_attention(const uint16_t* qkv, const float* cos_t, const float* sin_t
 
 }  // namespace
 
-// qkv: [batch*seq, 3*heads*D] 16-bit; cos/sin: [seq, heads, D/2] fp32;
-// out: [batch*seq, heads*D] 16-bit.  scale multiplies q.k before the softmax.
+// qkv: [batch*seq, 3*heads*D] 16-bit; cos/sin: [seq, heads, D/2] fp32, or both
+// null when Q and K are already rotated; out: [batch*seq, heads*D] 16-bit.
+// scale multiplies q.k before the softmax.
 int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
                      int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
                      uint32_t* row_amax, unsigned* status) {
-  if (!qkv || !rope_cos || !rope_sin || !out || batch <= 0 || seq <= 0 || seq > kMaxSeq || heads <= 0 ||
-      !(scale > 0.0f)) {
+  if (!qkv || (rope_cos == nullptr) != (rope_sin == nullptr) || !out || batch <= 0 || seq <= 0 ||
+      seq > kMaxSeq || heads <= 0 || !(scale > 0.0f)) {
     set_error("attention: invalid arguments (seq must be 1..384)");
     return KB_E_INVALID;
   }

@@ -16,16 +16,19 @@
 //                  loader warps with RoPE applied on the way in;
 //   TMEM (512 col) S_A = Q K[0:192]^T (192 columns), S_B = Q K[192:368]^T (176),
 //                  O_A = P_A V[0:192] and O_B = P_B V[192:368] (64 each).
-// Per 128-query tile the two key halves are independent: softmax warp group A
-// (warps 0-3) and group B (warps 4-7), thread = query row, each take the row
-// max and sum of their half and write P = exp2((S - m) c) in place over S as
-// packed 16-bit values (the A operand of the P.V MMA, read from TMEM).  The
-// epilogue combines the halves: O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) /
-// (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), group A writing dims 0-31 and group
-// B dims 32-63, plus the row |max| for the next quantiser.  Warp 8 issues the
-// MMAs; the S MMAs of the next tile overlap this tile's epilogue, and the
-// loaders stage the next pair while this one computes.  Every wait is bounded.
+// Per 128-query tile the two key halves are independent: softmax warps 0-7
+// take half A and warps 8-15 half B, four warps per TMEM lane quarter, each
+// thread one query row and 96 keys; the two warps of a half exchange their
+// partial maxima through shared memory, then write P = exp2((S - m) c) as
+// packed 16-bit values over the first 48 of their own 96 S columns (the A
+// operand of the P.V MMA, read from TMEM).  The epilogue combines the halves:
+// O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) / (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)),
+// each warp writing 16 of the 64 dims, plus the row |max| for the next
+// quantiser.  Warp 16 issues the MMAs; the S MMAs of the next tile overlap
+// this tile's epilogue, and warps 17-19 stage the next pair while this one
+// computes.  Every wait is bounded.
 #include <stdint.h>
+#include <string.h>
 
 #include <atomic>
 
@@ -44,15 +47,21 @@ constexpr int kRowBytes = kD * 2;         // 128 B: one swizzle row
 constexpr int kKBytes = kKeysPad * kRowBytes;
 constexpr int kKVBytes = 2 * kKBytes;     // K then V of one pair
 constexpr int kQBytes = kTileQ * kRowBytes;
-constexpr int kSoftWarps = 8, kLoadWarps = 4;
+constexpr int kSoftWarps = 16;
 constexpr int kMmaWarp = kSoftWarps;
-constexpr int kFaThreads = 32 * (kSoftWarps + 1 + kLoadWarps);  // 416
-constexpr int kLoadThreads = 32 * kLoadWarps;
+// Loader warps: one issuing TMA copies (Q and K arrive rotated), or three
+// staging and rotating with the CTA's threads (the table-driven RoPE path).
+template <bool ROPE>
+constexpr int load_warps() { return ROPE ? 3 : 1; }
+template <bool ROPE>
+constexpr int fa_threads() { return 32 * (kSoftWarps + 1 + load_warps<ROPE>()); }  // 640 / 576
+constexpr int kKvBox = 184;               // rows per K/V TMA box (2 boxes = 368 rows)
+constexpr int kSubKeys = 96;              // keys per softmax warp (4 warps per TMEM lane quarter)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSB = kHalfA, kOA = kHalfA + kHalfB, kOB = kOA + kD;  // TMEM columns
 constexpr int kBarBytes = 256;
-// (m, l) of each row and key half, double-buffered by tile parity.
-constexpr int kMlBytes = 2 * 2 * kTileQ * 8;
+// Per row and 96-key quarter (m, l), double-buffered by tile parity.
+constexpr int kMlBytes = 2 * 4 * kTileQ * 8;
 constexpr int kSmemBytes = 2 * kKVBytes + 2 * kQBytes + kBarBytes + kMlBytes + 1024 /*alignment*/;
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
@@ -82,16 +91,16 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
   return static_cast<uint32_t>(r * kRowBytes + ((c ^ (r & 7)) << 4));
 }
 
-// Rows [r0, r0 + nrows) of Q or K (part = 0 / 1) or V (part = 2) of head h of
-// one position into a swizzled tile; rows at or past `seq` are zero.  Each
+// Rows [r0, r0 + nrows) of Q, K or V (part = 0, 1, 2) of head h of one position
+// into a swizzled tile, rotated when `rotate`; rows at or past `seq` are zero.  Each
 // thread handles kBatch 16-byte chunks per step with all their global loads
 // issued before any is used, so the copy is not bound by one load's latency.
-constexpr int kBatch = 4;
+constexpr int kBatch = 3;
 
 template <bool F16>
 __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, size_t row_stride, int part, int h,
                                            int heads, const float* cos_t, const float* sin_t, int r0, int nrows,
-                                           int seq, int tid, int nthreads) {
+                                           int seq, int tid, int nthreads, bool rotate) {
   const int c = heads * kD;
   const int total = nrows * 8;
   for (int t0 = tid; t0 < total; t0 += kBatch * nthreads) {
@@ -105,7 +114,7 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
       raw[u] = make_uint4(0, 0, 0, 0);
       if (t < total && tok < seq) {
         raw[u] = __ldg(reinterpret_cast<const uint4*>(base + tok * row_stride + part * c + h * kD + ch * 8));
-        if (part != 2) {
+        if (rotate) {
           const size_t ro = (static_cast<size_t>(tok) * heads + h) * (kD / 2) + ch * 4;
           co[u] = __ldg(reinterpret_cast<const float4*>(cos_t + ro));
           si[u] = __ldg(reinterpret_cast<const float4*>(sin_t + ro));
@@ -118,7 +127,7 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
       if (t >= total) break;
       const int r = t >> 3, ch = t & 7;
       uint4 v = raw[u];
-      if (part != 2 && r0 + r < seq)
+      if (rotate && r0 + r < seq)
         v = make_uint4(rope2(raw[u].x, co[u].x, si[u].x, F16), rope2(raw[u].y, co[u].y, si[u].y, F16),
                        rope2(raw[u].z, co[u].z, si[u].z, F16), rope2(raw[u].w, co[u].w, si[u].w, F16));
       *reinterpret_cast<uint4*>(dst + sw128(r, ch)) = v;
@@ -126,11 +135,13 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
   }
 }
 
-template <bool F16>
-__global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
+template <bool F16, bool ROPE>
+__global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
+    const __grid_constant__ CUtensorMap map_kv, const __grid_constant__ CUtensorMap map_q,
     const uint16_t* __restrict__ qkv, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
     uint16_t* __restrict__ out, int pairs, int seq, int heads, float scale_log2, uint32_t* __restrict__ row_amax,
     unsigned* status) {
+  constexpr int kLoadThreads = 32 * load_warps<ROPE>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kv_buf = smem;                    // [2][K | V]
@@ -145,10 +156,12 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
   uint64_t* pa_full = bars + 10;  // P_A written, O read back          (128 arrivals)
   uint64_t* pb_full = bars + 11;  // P_B written, O read back          (128 arrivals)
   uint64_t* o_full = bars + 12;   // O_A and O_B ready                 (commit)
-  uint64_t* ml_full = bars + 13;  // both halves' (m, l) of a tile     (256 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* ml_full = bars + 13;  // all quarters' (m, l) of a tile    (512 arrivals)
+  uint64_t* mx_full = bars + 14;  // [2] both quarter maxima of a half (256 arrivals)
+  uint64_t* kv_tma = bars + 16;   // [2] K/V TMA copies landed         (tx bytes)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float2* ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][2][128]
+  float2* ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][4][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = heads * kD;
@@ -159,15 +172,18 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], kLoadThreads);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&q_full[i], kLoadThreads);
+      mbar_init(&q_full[i], ROPE ? kLoadThreads : 1);
       mbar_init(&q_empty[i], 1);
+      mbar_init(&kv_tma[i], 1);
     }
     mbar_init(sa_full, 1);
     mbar_init(sb_full, 1);
-    mbar_init(pa_full, 128);
-    mbar_init(pb_full, 128);
+    mbar_init(pa_full, 256);
+    mbar_init(pb_full, 256);
     mbar_init(o_full, 1);
-    mbar_init(ml_full, 256);
+    mbar_init(ml_full, 512);
+    mbar_init(&mx_full[0], 256);
+    mbar_init(&mx_full[1], 256);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -180,8 +196,50 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp > kMmaWarp) {
-    // ------------------------------------------------------------ loaders
+  if (warp > kMmaWarp && !ROPE) {
+    // ------------------------------------------------------------ TMA loader
+    // Q and K arrive rotated: K and V of a pair are two 184-row boxes each and
+    // a Q tile one 128-row box, landing in the UMMA 128-byte-swizzled layout.
+    if (lane == 0) {
+      tma_prefetch_desc(&map_kv);
+      tma_prefetch_desc(&map_q);
+    }
+    int g = 0;  // global Q tile counter
+    for (int it = 0, p = blockIdx.x; p < pairs; ++it, p += gridDim.x) {
+      const int kb = it & 1;
+      const int b = p / heads, h = p % heads;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
+      uint8_t* ks = kv_buf + kb * kKVBytes;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&kv_tma[kb], 2 * kKBytes);
+        tma_load_2d(ks, &map_kv, &kv_tma[kb], c + h * kD, b * seq);
+        tma_load_2d(ks + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], c + h * kD, b * seq + kKvBox);
+        tma_load_2d(ks + kKBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD, b * seq);
+        tma_load_2d(ks + kKBytes + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD, b * seq + kKvBox);
+      }
+      // V rows [seq, 368) hold the next position's values (or TMA zeros):
+      // clear them, their P is zero but 0 * Inf would not be.
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_tma[kb], (it >> 1) & 1, abort_flag))) break;
+      for (int i = lane; i < (kKeysPad - seq) * 8; i += 32)
+        *reinterpret_cast<uint4*>(ks + kKBytes + sw128(seq + (i >> 3), i & 7)) = make_uint4(0, 0, 0, 0);
+      fence_proxy_async_smem();
+      mbar_arrive(&kv_full[kb]);
+      bool ok = true;
+      for (int t = 0; t < tiles; ++t, ++g) {
+        const int qb = g & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&q_empty[qb], ((g >> 1) & 1) ^ 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&q_full[qb], kQBytes);
+          tma_load_2d(q_buf + qb * kQBytes, &map_q, &q_full[qb], h * kD, b * seq + t * kTileQ);
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp > kMmaWarp) {
+    // ------------------------------------------------------------ staging loaders (RoPE here)
     const int tid = threadIdx.x - 32 * (kMmaWarp + 1);
     int g = 0;  // global Q tile counter
     for (int it = 0, p = blockIdx.x; p < pairs; ++it, p += gridDim.x) {
@@ -190,9 +248,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
       const uint16_t* base = qkv + static_cast<size_t>(b) * seq * row_stride;
       if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
       uint8_t* ks = kv_buf + kb * kKVBytes;
-      stage_rows<F16>(ks, base, row_stride, 1, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid, kLoadThreads);
+      stage_rows<F16>(ks, base, row_stride, 1, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid, kLoadThreads,
+                      true);
       stage_rows<F16>(ks + kKBytes, base, row_stride, 2, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid,
-                      kLoadThreads);
+                      kLoadThreads, false);
       fence_proxy_async_smem();
       mbar_arrive(&kv_full[kb]);
       bool ok = true;
@@ -203,7 +262,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
           break;
         }
         stage_rows<F16>(q_buf + qb * kQBytes, base, row_stride, 0, h, heads, rope_cos, rope_sin, t * kTileQ, kTileQ,
-                        seq, tid, kLoadThreads);
+                        seq, tid, kLoadThreads, true);
         fence_proxy_async_smem();
         mbar_arrive(&q_full[qb]);
       }
@@ -249,10 +308,13 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
             break;
           }
           tc_fence_after();
+          // P of keys 16i..16i+15 of a half: column 8i of the half, plus 48 for
+          // the second 96 keys (written over that softmax warp's own S columns).
           for (int i = 0; i < kHalfA / 16; ++i)
-            mma_f16_ts(tmem + kOA, tmem + 8 * i, vdesc + kStep16 * i, id_pv, i != 0);
+            mma_f16_ts(tmem + kOA, tmem + 8 * i + (i >= 6 ? 48 : 0), vdesc + kStep16 * i, id_pv, i != 0);
           for (int i = 0; i < kHalfB / 16; ++i)
-            mma_f16_ts(tmem + kOB, tmem + kSB + 8 * i, vdesc + kHalfOff + kStep16 * i, id_pv, i != 0);
+            mma_f16_ts(tmem + kOB, tmem + kSB + 8 * i + (i >= 6 ? 48 : 0), vdesc + kHalfOff + kStep16 * i, id_pv,
+                       i != 0);
           tc_commit(o_full);
           if (t + 1 == tiles) tc_commit(&kv_empty[kb]);
           // P consumed before the next tile's S MMAs overwrite it.
@@ -265,14 +327,20 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int grp = warp >> 2;  // 0: keys [0, 192), 1: keys [192, 368)
-    const int row = (warp & 3) * 32 + lane;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t s_col = grp ? kSB : 0u;
-    const int valid = grp ? seq - kHalfA : kHalfA;   // keys of this half below seq
-    constexpr int kChunks = (kHalfA + 31) / 32;      // 6 (half B's last chunk is partial)
-    uint64_t* s_bar = grp ? sb_full : sa_full;
-    uint64_t* p_bar = grp ? pb_full : pa_full;
+    const int half = warp >> 3;               // 0: keys [0, 192), 1: keys [192, 368)
+    const int sub = (warp >> 2) & 1;          // which 96 keys of the half
+    const int quarter = warp & 3;             // TMEM lanes 32*quarter..
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t s_col = (half ? kSB : 0u) + sub * kSubKeys;          // first S column of this warp
+    // P (2 keys per column) goes over this warp's own, already read S columns:
+    // keys 96s..96s+95 of a half at columns 96s..96s+47 of that half.
+    const uint32_t p_col = s_col;
+    // keys of this warp below seq (only half B's second quarter is partial)
+    const int valid = min(kSubKeys, seq - (half * kHalfA + sub * kSubKeys));
+    uint64_t* s_bar = half ? sb_full : sa_full;
+    uint64_t* p_bar = half ? pb_full : pa_full;
+    const int q_slot = half * 2 + sub;        // (m, l) slot of this warp
     int g = 0;
     bool ok = true;
     for (int p = blockIdx.x; p < pairs && ok; p += gridDim.x) {
@@ -283,34 +351,59 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
           break;
         }
         tc_fence_after();
+        float2* mlg = ml + (g & 1) * 4 * kTileQ;
         float m = __int_as_float(0xff800000);
-#pragma unroll 1
-        for (int ch = 0; ch < kChunks; ++ch) {
+#pragma unroll
+        for (int ch = 0; ch < kSubKeys / 32; ++ch) {
           uint32_t v[32];
           tmem_ld32(lane_base + s_col + ch * 32, v);
           tmem_ld_wait();
+          if (valid == kSubKeys || (ch + 1) * 32 <= valid) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (ch * 32 + i < valid) m = fmaxf(m, __uint_as_float(v[i]));
+            for (int i = 0; i < 32; ++i) m = fmaxf(m, __uint_as_float(v[i]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (ch * 32 + i < valid) m = fmaxf(m, __uint_as_float(v[i]));
+          }
         }
+        // the half's maximum: this warp's and its partner's (other 96 keys)
+        mlg[q_slot * kTileQ + row].x = m;
+        mbar_arrive(&mx_full[half]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&mx_full[half], g & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        m = fmaxf(m, mlg[(half * 2 + (sub ^ 1)) * kTileQ + row].x);
         const float mc = m * scale_log2;
         float l = 0.0f;
-#pragma unroll 1
-        for (int ch = 0; ch < kChunks; ++ch) {
+#pragma unroll
+        for (int ch = 0; ch < kSubKeys / 32; ++ch) {
           uint32_t v[32], pk[16];
           tmem_ld32(lane_base + s_col + ch * 32, v);
           tmem_ld_wait();
+          if (valid == kSubKeys || (ch + 1) * 32 <= valid) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int k0 = ch * 32 + 2 * i;
-            const float p0 = k0 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
-            const float p1 = k0 + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
-            l += p0 + p1;
-            pk[i] = pack2(p0, p1, F16);
+            for (int i = 0; i < 16; ++i) {
+              const float p0 = ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc));
+              const float p1 = ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc));
+              l += p0 + p1;
+              pk[i] = pack2(p0, p1, F16);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int k0 = ch * 32 + 2 * i;
+              const float p0 = k0 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
+              const float p1 = k0 + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
+              l += p0 + p1;
+              pk[i] = pack2(p0, p1, F16);
+            }
           }
-          tmem_st16(lane_base + s_col + ch * 16, pk);  // P over S columns already read
+          // P over S columns this thread has already read (its own 96 keys)
+          tmem_st16(lane_base + p_col + ch * 16, pk);
         }
-        ml[((g & 1) * 2 + grp) * kTileQ + row] = make_float2(m, l);
+        mlg[q_slot * kTileQ + row] = make_float2(m, l);
         mbar_arrive(ml_full);
         tmem_st_wait();
         tc_fence_before();
@@ -320,26 +413,28 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
           break;
         }
         tc_fence_after();
-        // both halves' (m, l) of this tile are in shared memory
+        // every quarter's (m, l) of this tile is in shared memory
         if (!__all_sync(0xffffffffu, mbar_wait(ml_full, g & 1, abort_flag))) {
           ok = false;
           break;
         }
-        const float2 a = ml[((g & 1) * 2 + 0) * kTileQ + row];
-        const float2 bb = ml[((g & 1) * 2 + 1) * kTileQ + row];
-        const float mx = fmaxf(a.x, bb.x);
-        const float fa = a.x == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(a.x, mx), scale_log2));
-        const float fb = bb.x == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(bb.x, mx), scale_log2));
-        const float inv = 1.0f / (a.y * fa + bb.y * fb);
+        const float2 a0 = mlg[0 * kTileQ + row], a1 = mlg[1 * kTileQ + row];
+        const float2 b0 = mlg[2 * kTileQ + row], b1 = mlg[3 * kTileQ + row];
+        const float ma = a0.x, mb = b0.x;  // both quarters of a half share its maximum
+        const float mx = fmaxf(ma, mb);
+        const float fa = ma == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(ma, mx), scale_log2));
+        const float fb = mb == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(mb, mx), scale_log2));
+        const float inv = 1.0f / ((a0.y + a1.y) * fa + (b0.y + b1.y) * fb);
         const float wa = fa * inv, wb = fb * inv;
-        uint32_t oa[32], ob[32], w[16];
-        tmem_ld32(lane_base + kOA + grp * 32, oa);
-        tmem_ld32(lane_base + kOB + grp * 32, ob);
+        const int dim0 = (warp >> 2) * 16;    // this warp's 16 output dims
+        uint32_t oa[16], ob[16], w[8];
+        tmem_ld16(lane_base + kOA + dim0, oa);
+        tmem_ld16(lane_base + kOB + dim0, ob);
         tmem_ld_wait();
         tc_fence_before();
         uint32_t am = 0;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 8; ++i) {
           const float x0 = __uint_as_float(oa[2 * i]) * wa + __uint_as_float(ob[2 * i]) * wb;
           const float x1 = __uint_as_float(oa[2 * i + 1]) * wa + __uint_as_float(ob[2 * i + 1]) * wb;
           w[i] = pack2(x0, x1, F16);
@@ -347,9 +442,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
         }
         const int query = t * kTileQ + row;
         if (query < seq) {
-          uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(b) * seq + query) * c + h * kD + grp * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(b) * seq + query) * c + h * kD + dim0);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
           if (row_amax != nullptr) {
             const uint32_t m16 = max(am & 0xffffu, am >> 16);
             atomicMax(row_amax + static_cast<size_t>(b) * seq + query,
@@ -366,10 +461,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) attention_fa_kernel(
   if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
-template <bool F16>
+template <bool F16, bool ROPE>
 int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint16_t* out, int batch, int seq,
               int heads, float scale, uint32_t* row_amax, unsigned* status, cudaStream_t stream) {
-  auto kern = attention_fa_kernel<F16>;
+  auto kern = attention_fa_kernel<F16, ROPE>;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> configured{0};
@@ -379,11 +474,23 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
     if (e != cudaSuccess) return check_cuda(e, "attention smem attribute");
     configured.fetch_or(bit);
   }
+  CUtensorMap map_kv, map_q;
+  memset(&map_kv, 0, sizeof(map_kv));
+  memset(&map_q, 0, sizeof(map_q));
+  if (!ROPE) {
+    // [batch * seq rows, 3C columns] 16-bit; boxes of 64 columns (one head) x rows
+    const long cols = 3L * heads * kD, rows = static_cast<long>(batch) * seq;
+    int rc = encode_2d(&map_kv, CU_TENSOR_MAP_DATA_TYPE_UINT16, qkv, cols, rows, cols * 2, kD, kKvBox,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc) rc = encode_2d(&map_q, CU_TENSOR_MAP_DATA_TYPE_UINT16, qkv, cols, rows, cols * 2, kD, kTileQ,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
   const float scale_log2 = scale * 1.4426950408889634f;
   const int pairs = batch * heads;
   const int grid = pairs < num_sms(dev) ? pairs : num_sms(dev);
-  kern<<<grid, kFaThreads, kSmemBytes, stream>>>(qkv, cos_t, sin_t, out, pairs, seq, heads, scale_log2, row_amax,
-                                                 status);
+  kern<<<grid, fa_threads<ROPE>(), kSmemBytes, stream>>>(map_kv, map_q, qkv, cos_t, sin_t, out, pairs, seq, heads,
+                                                        scale_log2, row_amax, status);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 
@@ -395,8 +502,12 @@ bool attention_tc_supported(int seq, int head_dim) { return head_dim == kD && se
 int attention_tc_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out, int batch,
                         int seq, int heads, float scale, int f16, cudaStream_t stream, uint32_t* row_amax,
                         unsigned* status) {
-  return f16 ? launch_tc<true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream)
-             : launch_tc<false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream);
+  // Null tables: Q and K arrive already rotated (by the QKV projection's epilogue).
+  if (rope_cos == nullptr)
+    return f16 ? launch_tc<true, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream)
+               : launch_tc<false, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream);
+  return f16 ? launch_tc<true, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream)
+             : launch_tc<false, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream);
 }
 
 }  // namespace kb

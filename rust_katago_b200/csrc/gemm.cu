@@ -382,6 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0q = mb * kBM + quarter * 32;
       const int row = row0q + lane;
       const bool row_ok = row < g.m;
+      int token = 0;
+      if constexpr (EPI == kEpiRope16) token = row_ok ? row % g.rope_seq : 0;
       float sa = 1.0f;
       if constexpr (KIND == kGemmI8 && EPI != kEpiI32) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -448,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col0 = nb * BN + j * 32;
           if (col0 >= g.n) continue;  // warp-uniform
           const int valid = min(32, g.n - col0);
-          if constexpr (EPI == kEpiF16 || EPI == kEpi16 || EPI == kEpiRes16) {
+          if constexpr (EPI == kEpiF16 || EPI == kEpi16 || EPI == kEpiRes16 || EPI == kEpiRope16) {
             float sw[32];
             if constexpr (KIND == kGemmI8) load_vec32(g.col_scale, col0, g.n, sw);
             uint32_t hw[16];
@@ -456,6 +458,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) hw[i] = res_next[i];
               if (jj + 1 < kChunks) load_res(jj + 1);
+            }
+            // Rotary tables of this chunk's 16 pairs (kEpiRope16, Q and K columns).
+            float rc[16], rs[16];
+            bool rope = false;
+            if constexpr (EPI == kEpiRope16) {
+              rope = col0 < g.rope_cols;  // warp-uniform
+              if (rope && row_ok) {
+                const int half_cols = g.rope_cols / 2;
+                const int cc = col0 < half_cols ? col0 : col0 - half_cols;
+                const size_t off = (static_cast<size_t>(token) * g.rope_heads + cc / g.rope_hd) * (g.rope_hd / 2) +
+                                   (cc % g.rope_hd) / 2;
+                const float4* pc = reinterpret_cast<const float4*>(g.rope_cos + off);
+                const float4* ps = reinterpret_cast<const float4*>(g.rope_sin + off);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float4 a = __ldg(pc + i), b2 = __ldg(ps + i);
+                  rc[4 * i] = a.x, rc[4 * i + 1] = a.y, rc[4 * i + 2] = a.z, rc[4 * i + 3] = a.w;
+                  rs[4 * i] = b2.x, rs[4 * i + 1] = b2.y, rs[4 * i + 2] = b2.z, rs[4 * i + 3] = b2.w;
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) rc[i] = 1.0f, rs[i] = 0.0f;
+              }
             }
             // Separate unrolled bodies with and without bias (warp-uniform
             // choice), so a bias-free projection issues no adds.
@@ -473,6 +498,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (EPI == kEpiRes16) {
                   const float2 r = unpack16x2(hw[i], f16);
                   hw[i] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
+                } else if constexpr (EPI == kEpiRope16) {
+                  if (rope) {
+                    // (x, y) -> (x c - y s, x s + y c), each product and sum rounded
+                    const float c = rc[i], sn = rs[i];
+                    x = make_float2(__fsub_rn(__fmul_rn(x.x, c), __fmul_rn(x.y, sn)),
+                                    __fadd_rn(__fmul_rn(x.x, sn), __fmul_rn(x.y, c)));
+                  }
+                  hw[i] = pack16x2(x, f16);
                 } else {
                   hw[i] = pack16x2(apply_act2<ACT>(x), f16);
                 }
@@ -598,7 +631,7 @@ int make_operand_map(CUtensorMap* map, const void* base, int kind, long rows, lo
 }
 
 bool epi_16bit(int epi) {
-  return epi == kEpiF16 || epi == kEpi16 || epi == kEpiRes16 || epi == kEpiSwiGLU16;
+  return epi == kEpiF16 || epi == kEpi16 || epi == kEpiRes16 || epi == kEpiSwiGLU16 || epi == kEpiRope16;
 }
 
 template <int KIND, int BN, int EPI, int ACT, int SB>
@@ -636,6 +669,7 @@ int dispatch_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CU
       if (g.act == kActSilu) return launch_one<KIND, BN, kEpi16, kActSilu, SB>(ma, mb, mo, tma_out, g, s);
       return launch_one<KIND, BN, kEpi16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
     case kEpiRes16: return launch_one<KIND, BN, kEpiRes16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiRope16: return launch_one<KIND, BN, kEpiRope16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
     case kEpiSwiGLU16:
       if constexpr (KIND != kGemmMXF8) return launch_one<KIND, BN, kEpiSwiGLU16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
       break;
@@ -716,6 +750,13 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
   }
   if (kind == kGemmI8 && epi != kEpiI32 && (g.row_scale == nullptr || g.col_scale == nullptr)) {
     set_error("INT8 dequant epilogue needs row and column scales");
+    return KB_E_INVALID;
+  }
+  if (epi == kEpiRope16 &&
+      (g.rope_cos == nullptr || g.rope_sin == nullptr || g.rope_seq <= 0 || g.rope_heads <= 0 ||
+       (g.rope_hd != 32 && g.rope_hd != 64) || g.rope_cols != 2 * g.rope_heads * g.rope_hd || g.rope_cols > g.n ||
+       (reinterpret_cast<uintptr_t>(g.rope_cos) & 15) || (reinterpret_cast<uintptr_t>(g.rope_sin) & 15))) {
+    set_error("rotary epilogue: needs 16-byte aligned tables, head_dim 32 or 64, rope_cols = 2 * heads * head_dim <= N");
     return KB_E_INVALID;
   }
   if (g.act < kActNone || g.act > kActSilu) {

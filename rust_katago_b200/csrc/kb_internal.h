@@ -33,6 +33,7 @@ enum Epi : int {
   kEpiRes16 = 4,     // res16 = T16(f32(res16) + (v + bias))
   kEpiSwiGLU16 = 5,  // dual tile [gate|up] -> T16(u*(g/(1+e^-g))), gate/up rounded to T16 first
   kEpiF32 = 6,       // out_f32 = v + bias (+ res_f32 when residual != null)
+  kEpiRope16 = 7,    // QKV projection: out16 = T16(rot(v)) on columns < rope_cols (Q and K), T16(v) after
 };
 
 struct GemmArgs {
@@ -54,6 +55,12 @@ struct GemmArgs {
   // stored as [rows_padded/128][k/128][32 rows][4 row groups][4 K blocks].
   const uint8_t* sfa = nullptr;
   const uint8_t* sfb = nullptr;
+  // kEpiRope16: rotary tables [rope_seq, rope_heads, rope_hd / 2] (cos, sin of
+  // each pair (2p, 2p+1) of a head); the row's token is row % rope_seq, columns
+  // [0, rope_cols) hold Q then K, rope_cols / 2 = rope_heads * rope_hd wide each.
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int rope_cols = 0, rope_heads = 0, rope_seq = 0, rope_hd = 0;
 };
 
 enum GemmKind : int { kGemmI8 = 0, kGemmBF16 = 1, kGemmMXF8 = 2 };

@@ -221,6 +221,18 @@ void destroy_model(kb_model* m) {
   delete m;
 }
 
+// The QKV projection rotates Q and K in its epilogue (learned 2-D RoPE tables
+// [token, head, pair], native_model.rs:200-228): the rotation is applied to the
+// fp32 projection before the bf16 rounding, and attention reads rotated Q/K.
+void set_rope(GemmArgs& g, const Block& b, const kb_model_desc& d) {
+  g.rope_cos = b.rope_cos;
+  g.rope_sin = b.rope_sin;
+  g.rope_cols = 2 * d.trunk_channels;
+  g.rope_heads = d.num_heads;
+  g.rope_hd = d.head_dim;
+  g.rope_seq = kSeq;
+}
+
 // GemmArgs of one MXFP8 projection of the trunk (bf16 output or residual).
 GemmArgs mx_args(kb_handle* h, const kb_mxfp8_weight* w, int M, void* out, const float* bias, int act,
                  unsigned layer) {
@@ -252,10 +264,14 @@ int mxfp8_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale
   cudaStream_t s = h->stream;
   uint8_t* q = reinterpret_cast<uint8_t*>(h->q);
   int rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms1, kRmsEps, 0, q, h->mx_scales, h->status, layer, s);
-  if (!rc) rc = gemm_launch(kGemmMXF8, kEpi16, q, b.mqkv->q, mx_args(h, b.mqkv, M, h->qkv, nullptr, 0, layer), s);
+  if (!rc) {
+    GemmArgs gq = mx_args(h, b.mqkv, M, h->qkv, nullptr, 0, layer);
+    set_rope(gq, b, d);
+    rc = gemm_launch(kGemmMXF8, kEpiRope16, q, b.mqkv->q, gq, s);
+  }
   if (!rc)
-    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s,
-                          nullptr, h->status);
+    rc = attention_launch(h->qkv, nullptr, nullptr, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s, nullptr,
+                          h->status);
   if (!rc && trace_att)
     rc = check_cuda(cudaMemcpyAsync(trace_att, h->att, static_cast<size_t>(M) * c * 2, cudaMemcpyDeviceToDevice, s),
                     "trace copy");
@@ -330,11 +346,13 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
     g.out_f16 = 0;
     g.status = h->status;
     g.layer = layer;
-    rc = gemm_launch(kGemmI8, kEpi16, h->q, b.qkv->q, g, s);
+    set_rope(g, b, d);
+    rc = gemm_launch(kGemmI8, kEpiRope16, h->q, b.qkv->q, g, s);
     if (rc) return rc;
     rc = check_cuda(cudaMemsetAsync(h->row_amax, 0, static_cast<size_t>(M) * sizeof(uint32_t), s), "amax reset");
     if (rc) return rc;
-    rc = attention_launch(h->qkv, b.rope_cos, b.rope_sin, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s,
+    // Q and K were rotated by the QKV projection's epilogue: no tables here.
+    rc = attention_launch(h->qkv, nullptr, nullptr, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s,
                           h->row_amax, h->status);
     if (rc) return rc;
     if (trace) {
