@@ -62,6 +62,8 @@ constexpr uint32_t kSB = kHalfA, kOA = kHalfA + kHalfB, kOB = kOA + kD;  // TMEM
 constexpr int kBarBytes = 256;
 // Per row and 96-key quarter (m, l), double-buffered by tile parity.
 constexpr int kMlBytes = 2 * 4 * kTileQ * 8;
+// K/V double buffer, one Q tile (loaded as soon as the previous tile's S MMAs
+// are done, several microseconds before it is needed), one output tile.
 constexpr int kSmemBytes = 2 * kKVBytes + 2 * kQBytes + kBarBytes + kMlBytes + 1024 /*alignment*/;
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
@@ -138,6 +140,7 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
 template <bool F16, bool ROPE>
 __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     const __grid_constant__ CUtensorMap map_kv, const __grid_constant__ CUtensorMap map_q,
+    const __grid_constant__ CUtensorMap map_out,
     const uint16_t* __restrict__ qkv, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
     uint16_t* __restrict__ out, int pairs, int seq, int heads, float scale_log2, uint32_t* __restrict__ row_amax,
     unsigned* status) {
@@ -145,12 +148,15 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kv_buf = smem;                    // [2][K | V]
-  uint8_t* q_buf = smem + 2 * kKVBytes;      // [2][Q tile]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(q_buf + 2 * kQBytes);
+  uint8_t* q_buf = smem + 2 * kKVBytes;      // Q tile
+  uint8_t* o_buf = q_buf + kQBytes;          // output tile (128 rows x 64 dims, 128-byte swizzle)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(o_buf + kQBytes);
   uint64_t* kv_full = bars + 0;   // [2] loaders staged K/V           (128 arrivals)
   uint64_t* kv_empty = bars + 2;  // [2] MMAs done with K/V            (commit)
-  uint64_t* q_full = bars + 4;    // [2] loaders staged a Q tile       (128 arrivals)
-  uint64_t* q_empty = bars + 6;   // [2] S MMAs done with a Q tile     (commit)
+  uint64_t* q_full = bars + 4;    // loaders staged the Q tile          (tx bytes, or 96 arrivals)
+  uint64_t* q_empty = bars + 5;   // S MMAs done with the Q tile        (commit)
+  uint64_t* out_full = bars + 6;  // output tile written                (512 arrivals)
+  uint64_t* out_free = bars + 7;  // previous tile's store read it      (1 arrival)
   uint64_t* sa_full = bars + 8;   // S_A ready                         (commit)
   uint64_t* sb_full = bars + 9;   // S_B ready                         (commit)
   uint64_t* pa_full = bars + 10;  // P_A written, O read back          (128 arrivals)
@@ -172,10 +178,12 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], kLoadThreads);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&q_full[i], ROPE ? kLoadThreads : 1);
-      mbar_init(&q_empty[i], 1);
       mbar_init(&kv_tma[i], 1);
     }
+    mbar_init(q_full, ROPE ? kLoadThreads : 1);
+    mbar_init(q_empty, 1);
+    mbar_init(out_full, 32 * kSoftWarps);
+    mbar_init(out_free, 1);
     mbar_init(sa_full, 1);
     mbar_init(sb_full, 1);
     mbar_init(pa_full, 256);
@@ -226,14 +234,13 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       mbar_arrive(&kv_full[kb]);
       bool ok = true;
       for (int t = 0; t < tiles; ++t, ++g) {
-        const int qb = g & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&q_empty[qb], ((g >> 1) & 1) ^ 1, abort_flag))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (g & 1) ^ 1, abort_flag))) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          mbar_arrive_expect_tx(&q_full[qb], kQBytes);
-          tma_load_2d(q_buf + qb * kQBytes, &map_q, &q_full[qb], h * kD, b * seq + t * kTileQ);
+          mbar_arrive_expect_tx(q_full, kQBytes);
+          tma_load_2d(q_buf, &map_q, q_full, h * kD, b * seq + t * kTileQ);
         }
       }
       if (!ok) break;
@@ -256,15 +263,14 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       mbar_arrive(&kv_full[kb]);
       bool ok = true;
       for (int t = 0; t < tiles; ++t, ++g) {
-        const int qb = g & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&q_empty[qb], ((g >> 1) & 1) ^ 1, abort_flag))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (g & 1) ^ 1, abort_flag))) {
           ok = false;
           break;
         }
-        stage_rows<F16>(q_buf + qb * kQBytes, base, row_stride, 0, h, heads, rope_cos, rope_sin, t * kTileQ, kTileQ,
-                        seq, tid, kLoadThreads, true);
+        stage_rows<F16>(q_buf, base, row_stride, 0, h, heads, rope_cos, rope_sin, t * kTileQ, kTileQ, seq, tid,
+                        kLoadThreads, true);
         fence_proxy_async_smem();
-        mbar_arrive(&q_full[qb]);
+        mbar_arrive(q_full);
       }
       if (!ok) break;
     }
@@ -286,13 +292,12 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         const uint64_t kdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes));
         const uint64_t vdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes + kKBytes));
         for (int t = 0; t < tiles; ++t, ++g) {
-          const int qb = g & 1;
-          if (!mbar_wait(&q_full[qb], (g >> 1) & 1, abort_flag)) {
+          if (!mbar_wait(q_full, g & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t qdesc = sw128_desc(smem_u32(q_buf + qb * kQBytes));
+          const uint64_t qdesc = sw128_desc(smem_u32(q_buf));
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk)
             mma_issue<kKindBF16>(tmem, qdesc + 2 * kk, kdesc + 2 * kk, id_sa, kk != 0, 0, 0);
@@ -301,7 +306,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           for (int kk = 0; kk < kD / 16; ++kk)
             mma_issue<kKindBF16>(tmem + kSB, qdesc + 2 * kk, kdesc + kHalfOff + 2 * kk, id_sb, kk != 0, 0, 0);
           tc_commit(sb_full);
-          tc_commit(&q_empty[qb]);
+          tc_commit(q_empty);
           // P_A and P_B written (and the previous tile's O read back) by both groups.
           if (!mbar_wait(pa_full, g & 1, abort_flag) || !mbar_wait(pb_full, g & 1, abort_flag)) {
             ok = false;
@@ -352,7 +357,11 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         }
         tc_fence_after();
         float2* mlg = ml + (g & 1) * 4 * kTileQ;
-        float m = __int_as_float(0xff800000);
+        // Row maximum over this warp's keys: 8 independent partial maxima
+        // (short dependency chains), combined at the end.
+        float mp[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mp[j] = __int_as_float(0xff800000);
 #pragma unroll
         for (int ch = 0; ch < kSubKeys / 32; ++ch) {
           uint32_t v[32];
@@ -360,13 +369,14 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           tmem_ld_wait();
           if (valid == kSubKeys || (ch + 1) * 32 <= valid) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) m = fmaxf(m, __uint_as_float(v[i]));
+            for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[i]));
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (ch * 32 + i < valid) m = fmaxf(m, __uint_as_float(v[i]));
+              if (ch * 32 + i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[i]));
           }
         }
+        float m = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         // the half's maximum: this warp's and its partner's (other 96 keys)
         mlg[q_slot * kTileQ + row].x = m;
         mbar_arrive(&mx_full[half]);
@@ -376,7 +386,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         }
         m = fmaxf(m, mlg[(half * 2 + (sub ^ 1)) * kTileQ + row].x);
         const float mc = m * scale_log2;
-        float l = 0.0f;
+        float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // partial sums (short chains)
 #pragma unroll
         for (int ch = 0; ch < kSubKeys / 32; ++ch) {
           uint32_t v[32], pk[16];
@@ -387,7 +397,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
             for (int i = 0; i < 16; ++i) {
               const float p0 = ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc));
               const float p1 = ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc));
-              l += p0 + p1;
+              lp[i & 3] += p0 + p1;
               pk[i] = pack2(p0, p1, F16);
             }
           } else {
@@ -396,13 +406,14 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
               const int k0 = ch * 32 + 2 * i;
               const float p0 = k0 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
               const float p1 = k0 + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
-              l += p0 + p1;
+              lp[i & 3] += p0 + p1;
               pk[i] = pack2(p0, p1, F16);
             }
           }
           // P over S columns this thread has already read (its own 96 keys)
           tmem_st16(lane_base + p_col + ch * 16, pk);
         }
+        const float l = (lp[0] + lp[1]) + (lp[2] + lp[3]);
         mlg[q_slot * kTileQ + row] = make_float2(m, l);
         mbar_arrive(ml_full);
         tmem_st_wait();
@@ -440,20 +451,43 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           w[i] = pack2(x0, x1, F16);
           am = __vmaxu2(am, w[i] & 0x7fff7fffu);
         }
+        // The output tile leaves by one TMA store (rows past `seq` are clipped
+        // by the tensor map): wait until the previous tile's store has read
+        // the staging tile, write this thread's 16 dims (two swizzled 16-byte
+        // chunks of its row), then the storing thread issues the copy.
+        const bool storer = warp == 0 && lane == 0;
+        if (storer) {
+          bulk_wait_read<0>();
+          mbar_arrive(out_free);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(out_free, g & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const int ch0 = dim0 >> 3;
+        *reinterpret_cast<uint4*>(o_buf + sw128(row, ch0)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(o_buf + sw128(row, ch0 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+        fence_proxy_async_smem();
+        mbar_arrive(out_full);
         const int query = t * kTileQ + row;
-        if (query < seq) {
-          uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(b) * seq + query) * c + h * kD + dim0);
-          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-          if (row_amax != nullptr) {
-            const uint32_t m16 = max(am & 0xffffu, am >> 16);
-            atomicMax(row_amax + static_cast<size_t>(b) * seq + query,
-                      F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
+        if (row_amax != nullptr && query < seq) {
+          const uint32_t m16 = max(am & 0xffffu, am >> 16);
+          atomicMax(row_amax + static_cast<size_t>(b) * seq + query,
+                    F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
+        }
+        if (storer) {
+          if (!mbar_wait(out_full, g & 1, abort_flag)) {
+            ok = false;
+          } else {
+            tma_store_3d(&map_out, o_buf, h * kD, t * kTileQ, b);
+            bulk_commit();
           }
         }
+        if (!__all_sync(0xffffffffu, ok)) break;
       }
     }
   }
+  if (threadIdx.x == 0) bulk_wait_all();  // output stores complete before the CTA exits
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -474,9 +508,14 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
     if (e != cudaSuccess) return check_cuda(e, "attention smem attribute");
     configured.fetch_or(bit);
   }
-  CUtensorMap map_kv, map_q;
+  CUtensorMap map_kv, map_q, map_out;
   memset(&map_kv, 0, sizeof(map_kv));
   memset(&map_q, 0, sizeof(map_q));
+  // out [batch, seq, C]: boxes of 64 dims x 128 tokens of one position
+  int rc0 = encode_3d(&map_out, CU_TENSOR_MAP_DATA_TYPE_UINT16, out, static_cast<long>(heads) * kD, seq, batch,
+                      static_cast<long>(heads) * kD * 2, static_cast<long>(seq) * heads * kD * 2, kD, kTileQ, 1,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc0) return rc0;
   if (!ROPE) {
     // [batch * seq rows, 3C columns] 16-bit; boxes of 64 columns (one head) x rows
     const long cols = 3L * heads * kD, rows = static_cast<long>(batch) * seq;
@@ -489,8 +528,8 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
   const float scale_log2 = scale * 1.4426950408889634f;
   const int pairs = batch * heads;
   const int grid = pairs < num_sms(dev) ? pairs : num_sms(dev);
-  kern<<<grid, fa_threads<ROPE>(), kSmemBytes, stream>>>(map_kv, map_q, qkv, cos_t, sin_t, out, pairs, seq, heads,
-                                                        scale_log2, row_amax, status);
+  kern<<<grid, fa_threads<ROPE>(), kSmemBytes, stream>>>(map_kv, map_q, map_out, qkv, cos_t, sin_t, out, pairs, seq,
+                                                        heads, scale_log2, row_amax, status);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 

@@ -711,6 +711,26 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long c
   return KB_OK;
 }
 
+int encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long d0, long d1, long d2, long stride1_bytes,
+              long stride2_bytes, int box0, int box1, int box2, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+    return KB_E_CUDA;
+  }
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride1_bytes), static_cast<cuuint64_t>(stride2_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), static_cast<cuuint32_t>(box2)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (3-D) failed (code " + std::to_string(int(r)) + ")");
+    return KB_E_CUDA;
+  }
+  return KB_OK;
+}
+
 int gemm_pick_bn(int kind, int epi, int n) {
   (void)kind;
   if (epi == kEpiSwiGLU16) return 256;

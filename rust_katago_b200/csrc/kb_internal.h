@@ -99,6 +99,10 @@ int rms_mxfp8_launch(const void* x, int dtype, long ldx, int rows, int width, co
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long cols, long rows,
               long row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swz);
 
+// 3-D tensor map: dims (d0 innermost, d1, d2), byte strides of d1 and d2.
+int encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long d0, long d1, long d2, long stride1_bytes,
+              long stride2_bytes, int box0, int box1, int box2, CUtensorMapSwizzle swz);
+
 // Columns per N tile chosen for a given N (the SwiGLU dual-weight packing
 // depends on it).
 int gemm_pick_bn(int kind, int epi, int n);

@@ -108,6 +108,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
       "r"(smem_u32(src)), "r"(x), "r"(y)
       : "memory");
 }
+// 3-D tiled store shared -> global; parts of the box outside the tensor are clipped.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N committed bulk groups of this thread still read shared memory.
 template <int N>
