@@ -81,6 +81,25 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x for a pair of x <= 0 on the FMA pipe, relieving the special-function
+// unit (which takes the other half of the exponentials): x clamped to -126,
+// n = rint(x) by the 1.5 * 2^23 magic add, f = x - n in [-0.5, 0.5], 2^f by a
+// degree-3 polynomial (least-squares Chebyshev fit of 2^f on [-0.5, 0.5],
+// relative error 1.4e-4: below the 16-bit rounding of P), and 2^n added to
+// the exponent field (the magic sum's low bits are n, shifted by 23).
+__device__ __forceinline__ float2 exp2_poly2(float x0, float x1) {
+  constexpr float kMagic = 12582912.0f;
+  const float2 x = make_float2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const float2 j = add2(x, make_float2(kMagic, kMagic));
+  const float2 n = add2(j, make_float2(-kMagic, -kMagic));
+  const float2 f = fma2(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = fma2(make_float2(0x1.c2ccd4p-5f, 0x1.c2ccd4p-5f), f, make_float2(0x1.f02456p-3f, 0x1.f02456p-3f));
+  p = fma2(p, f, make_float2(0x1.62f21p-1f, 0x1.62f21p-1f));
+  p = fma2(p, f, make_float2(0x1.fff9ap-1f, 0x1.fff9ap-1f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(j.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(j.y) << 23)));
+}
+
 // Rotate one interleaved pair (x, y) by (c, s), rounded to the 16-bit type.
 __device__ __forceinline__ uint32_t rope2(uint32_t w, float c, float s, bool f16) {
   const float x = from16(static_cast<uint16_t>(w & 0xffffu), f16);
@@ -395,8 +414,18 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           if (valid == kSubKeys || (ch + 1) * 32 <= valid) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float p0 = ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc));
-              const float p1 = ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc));
+              // half the exponentials on the special-function unit, half on the FMA pipe
+              const float x0 = __fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc);
+              const float x1 = __fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc);
+              float p0, p1;
+              if (i & 1) {
+                p0 = ex2(x0);
+                p1 = ex2(x1);
+              } else {
+                const float2 e = exp2_poly2(x0, x1);
+                p0 = e.x;
+                p1 = e.y;
+              }
               lp[i & 3] += p0 + p1;
               pk[i] = pack2(p0, p1, F16);
             }
