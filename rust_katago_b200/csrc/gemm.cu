@@ -9,11 +9,12 @@
 //   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, 32 B of K
 //               per instruction) into one of two TMEM accumulators and commits
 //               ring slots / accumulators back through mbarriers;
-//   warps 2-9   epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
-//               output row per thread; two warps per 32-lane quarter, each taking
-//               half of the tile's columns), dequant / bias / activation /
-//               residual / row-amax, then 16-bit results go through a swizzled
-//               2 KiB shared-memory staging tile per warp and a TMA store.
+//   warps 2-17  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
+//               output row per thread; four warps per 32-lane quarter, each taking
+//               a quarter of the tile's columns, 16 columns per step), dequant /
+//               bias / activation / rotary / residual / row-amax, then 16-bit
+//               results go through a swizzled 2 KiB shared-memory staging tile
+//               per warp and a TMA store.
 // The double-buffered accumulator lets the epilogue of tile i overlap the MMAs
 // of tile i+1.  Every wait is bounded (kb_ptx.cuh); a timeout records
 // KB_STATUS_TIMEOUT in the status word and the kernel returns.
@@ -35,18 +36,23 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle row of K per stage
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+// Epilogue warps: 16 (four per TMEM lane quarter) for the arithmetic-heavy
+// 16-bit epilogues of short-K projections (bias + activation, rotary), 8 for
+// the others (residual adds, fp32 / int32 outputs), whose cost is memory.
+template <int EPI>
+constexpr int epi_warps() { return (EPI == 3 /* kEpi16 */ || EPI == 7 /* kEpiRope16 */) ? 16 : 8; }
+template <int EPI>
+constexpr int gemm_threads() { return 64 + 32 * epi_warps<EPI>(); }
 constexpr int kStageTile = 32 * 64;  // one 32x32 16-bit staging tile (2 KiB)
 constexpr int kSmemLimit = 227 * 1024;
 
 // SB = staging tiles per epilogue warp (stores in flight per warp).  Short-K
 // GEMMs are bound by how fast the epilogue can drain results, so they trade
-// one ring stage for four staging tiles per warp; long-K GEMMs keep the deeper
-// ring and two staging tiles.
+// one ring stage for two staging tiles per warp; long-K GEMMs keep the deeper
+// ring and one staging tile.
 constexpr uint32_t pow2_cols(uint32_t c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
 
-template <int KIND, int BN, int SB>
+template <int KIND, int BN, int SB, int EW>
 struct GemmCfg {
   static constexpr int kABytes = kBM * kBKBytes;
   static constexpr int kBBytes = BN * kBKBytes;
@@ -55,7 +61,7 @@ struct GemmCfg {
   // per stage, each copied to 4 TMEM columns by tcgen05.cp.
   static constexpr int kSfBytes = KIND == kGemmMXF8 ? 512 + 512 * (BN / 128) : 0;
   static constexpr int kSfCols = KIND == kGemmMXF8 ? 4 + 4 * (BN / 128) : 0;
-  static constexpr int kStagingBytes = kEpiWarps * SB * kStageTile;
+  static constexpr int kStagingBytes = EW * SB * kStageTile;
   static constexpr int kStages = (kSmemLimit - kStagingBytes - 1024 - 256) / (kStageBytes + kSfBytes);
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kSfRingBytes = kStages * kSfBytes;
@@ -80,6 +86,35 @@ __device__ __forceinline__ float acc_value(uint32_t bits, float sa, float sw) {
   } else {
     return __uint_as_float(bits);
   }
+}
+
+template <int N>
+__device__ __forceinline__ void load_vecn(const float* p, int col0, int n, float (&dst)[N]) {
+  if (p == nullptr) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) dst[i] = 0.0f;
+    return;
+  }
+  if (col0 + N <= n && (reinterpret_cast<uintptr_t>(p + col0) & 15) == 0) {
+    const float4* q = reinterpret_cast<const float4*>(p + col0);
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      const float4 t = __ldg(q + i);
+      dst[4 * i] = t.x;
+      dst[4 * i + 1] = t.y;
+      dst[4 * i + 2] = t.z;
+      dst[4 * i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) dst[i] = col0 + i < n ? __ldg(p + col0 + i) : 0.0f;
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 16) tmem_ld16(taddr, r);
+  else tmem_ld32(taddr, r);
 }
 
 __device__ __forceinline__ void load_vec32(const float* p, int col0, int n, float (&dst)[32]) {
@@ -164,7 +199,7 @@ __device__ __forceinline__ void load16x32(const uint16_t* src, uint32_t (&hw)[16
 // output map the thread's row goes into a 64-byte-swizzled staging tile (16-byte
 // chunk c of row r at c ^ ((r >> 1) & 3): conflict-free, and exactly the layout a
 // SWIZZLE_64B tensor store reads), then lane 0 issues one bulk tensor store.
-// Two staging tiles per warp alternate so a store overlaps the next chunk.
+// With two staging tiles per warp a store overlaps the next chunk.
 struct Out16 {
   const CUtensorMap* map;
   uint8_t* stage;  // this warp's SB staging tiles
@@ -212,11 +247,28 @@ __device__ __forceinline__ float2 acc_pair(const uint32_t (&v)[32], int i, float
   }
 }
 
+// Pair (i, i+1) of an N-column piece of a chunk (same arithmetic as acc_pair).
+template <int KIND, int N>
+__device__ __forceinline__ float2 acc_pairn(const uint32_t (&v)[N], int i, float sa, const float (&sw)[N]) {
+  if constexpr (KIND == kGemmI8) {
+    return make_float2(
+        __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[2 * i])), sa), sw[2 * i]),
+        __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[2 * i + 1])), sa), sw[2 * i + 1]));
+  } else {
+    return make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+  }
+}
+
 template <int KIND, int BN, int EPI, int ACT, int SB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g, const int use_tma_out) {
-  using Cfg = GemmCfg<KIND, BN, SB>;
+  constexpr int kEpiWarps = epi_warps<EPI>();
+  constexpr int kParts = kEpiWarps / 4;  // epilogue warps per TMEM lane quarter
+  // Columns per accumulator read: 16 with 16 epilogue warps (register budget), else 32.
+  constexpr int kSub = kEpiWarps == 16 ? 16 : 32;
+  constexpr int kHalves = 32 / kSub;
+  using Cfg = GemmCfg<KIND, BN, SB, kEpiWarps>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kElemBytes = (KIND == kGemmBF16) ? 2 : 1;
   constexpr int kBKElems = kBKBytes / kElemBytes;
@@ -367,10 +419,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps
-    const int e = warp - 2;          // 0..7
+    // ---------------- epilogue warps: kParts per TMEM lane quarter, each
+    // 1/kParts of the tile's columns, processed 16 columns at a time
+    const int e = warp - 2;          // 0..kEpiWarps-1
     const int quarter = warp & 3;    // TMEM lanes this warp may access: 32*quarter..+31
-    const int half = e >> 2;         // which half of the tile's columns
+    const int part = e >> 2;         // which share of the tile's columns
     Out16 o{use_tma_out ? &tmap_out : nullptr, staging + e * SB * kStageTile, 0};
     const bool f16 = (EPI == kEpiF16) ? true : (g.out_f16 != 0);
     int acc = 0;
@@ -393,26 +446,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == kEpiSwiGLU16) {
         // Tile columns [0, BN/2) are gate channels, [BN/2, BN) the matching up
         // channels (the dual weight is interleaved per tile at load).
-        constexpr int kChunks = BN / 128;
+        constexpr int kChunks = BN / 64 / kParts;
 #pragma unroll 1
         for (int jj = 0; jj < kChunks; ++jj) {
-          const int j = half * kChunks + jj;
-          uint32_t vg[32], vu[32];
-          tmem_ld32(taddr + j * 32, vg);
-          tmem_ld32(taddr + BN / 2 + j * 32, vu);
-          tmem_ld_wait();
+          const int j = part * kChunks + jj;
           const int gcol0 = nb * BN + j * 32;
           const int ocol0 = nb * (BN / 2) + j * 32;
-          if (ocol0 < g.n_out) {
-            float swg[32], swu[32];
-            if constexpr (KIND == kGemmI8) {
-              load_vec32(g.col_scale, gcol0, g.n, swg);
-              load_vec32(g.col_scale, gcol0 + BN / 2, g.n, swu);
-            }
-            const int valid = min(32, g.n_out - ocol0);
-            uint32_t hw[16];
+          if (ocol0 >= g.n_out) continue;  // warp-uniform
+          const int valid = min(32, g.n_out - ocol0);
+          uint32_t hw[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+          for (int hh = 0; hh < kHalves; ++hh) {
+            uint32_t vg[kSub], vu[kSub];
+            tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, vg);
+            tmem_ldn<kSub>(taddr + BN / 2 + j * 32 + hh * kSub, vu);
+            tmem_ld_wait();
+            float swg[kSub], swu[kSub];
+            if constexpr (KIND == kGemmI8) {
+              load_vecn<kSub>(g.col_scale, gcol0 + hh * kSub, g.n, swg);
+              load_vecn<kSub>(g.col_scale, gcol0 + BN / 2 + hh * kSub, g.n, swu);
+            }
+#pragma unroll
+            for (int i = 0; i < kSub / 2; ++i) {
               uint32_t pair = 0;
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
@@ -420,21 +475,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float gv = from16(bits16(acc_value<KIND>(vg[c], sa, KIND == kGemmI8 ? swg[c] : 1.0f), f16), f16);
                 const float uv = from16(bits16(acc_value<KIND>(vu[c], sa, KIND == kGemmI8 ? swu[c] : 1.0f), f16), f16);
                 const uint16_t b = bits16(__fmul_rn(uv, kb_silu(gv)), f16);
-                if (c < valid) amax = max(amax, abs_bits(from16(b, f16)));
+                if (hh * kSub + c < valid) amax = max(amax, abs_bits(from16(b, f16)));
                 pair |= static_cast<uint32_t>(b) << (16 * h);
               }
-              hw[i] = pair;
+              hw[hh * (kSub / 2) + i] = pair;
             }
-            emit16<SB>(o, g, hw, row, row0q, ocol0, lane, row_ok, valid);
           }
+          emit16<SB>(o, g, hw, row, row0q, ocol0, lane, row_ok, valid);
         }
       } else {
-        constexpr int kChunks = BN / 64;
+        constexpr int kChunks = BN / 32 / kParts;
         // Residual epilogue: the 16-bit residual of the next chunk is loaded
         // while the current one is computed (one chunk of prefetch).
         uint32_t res_next[16];
         auto load_res = [&](int jj2) {
-          const int c = nb * BN + (half * kChunks + jj2) * 32;
+          const int c = nb * BN + (part * kChunks + jj2) * 32;
           if (row_ok && c < g.n) {
             const uint16_t* src = static_cast<const uint16_t*>(g.out) + static_cast<size_t>(row) * g.ldo + c;
             load16x32(src, res_next, min(32, g.n - c), (reinterpret_cast<uintptr_t>(src) & 15) == 0);
@@ -443,78 +498,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (EPI == kEpiRes16) load_res(0);
 #pragma unroll 1
         for (int jj = 0; jj < kChunks; ++jj) {
-          const int j = half * kChunks + jj;
-          uint32_t v[32];
-          tmem_ld32(taddr + j * 32, v);
-          tmem_ld_wait();
+          const int j = part * kChunks + jj;
           const int col0 = nb * BN + j * 32;
           if (col0 >= g.n) continue;  // warp-uniform
           const int valid = min(32, g.n - col0);
           if constexpr (EPI == kEpiF16 || EPI == kEpi16 || EPI == kEpiRes16 || EPI == kEpiRope16) {
-            float sw[32];
-            if constexpr (KIND == kGemmI8) load_vec32(g.col_scale, col0, g.n, sw);
             uint32_t hw[16];
             if constexpr (EPI == kEpiRes16) {
 #pragma unroll
               for (int i = 0; i < 16; ++i) hw[i] = res_next[i];
               if (jj + 1 < kChunks) load_res(jj + 1);
             }
-            // Rotary tables of this chunk's 16 pairs (kEpiRope16, Q and K columns).
-            float rc[16], rs[16];
-            bool rope = false;
-            if constexpr (EPI == kEpiRope16) {
-              rope = col0 < g.rope_cols;  // warp-uniform
-              if (rope && row_ok) {
-                const int half_cols = g.rope_cols / 2;
-                const int cc = col0 < half_cols ? col0 : col0 - half_cols;
-                const size_t off = (static_cast<size_t>(token) * g.rope_heads + cc / g.rope_hd) * (g.rope_hd / 2) +
-                                   (cc % g.rope_hd) / 2;
-                const float4* pc = reinterpret_cast<const float4*>(g.rope_cos + off);
-                const float4* ps = reinterpret_cast<const float4*>(g.rope_sin + off);
+            const bool with_bias = EPI != kEpiF16 && g.bias != nullptr;  // warp-uniform
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float4 a = __ldg(pc + i), b2 = __ldg(ps + i);
-                  rc[4 * i] = a.x, rc[4 * i + 1] = a.y, rc[4 * i + 2] = a.z, rc[4 * i + 3] = a.w;
-                  rs[4 * i] = b2.x, rs[4 * i + 1] = b2.y, rs[4 * i + 2] = b2.z, rs[4 * i + 3] = b2.w;
-                }
-              } else {
+            for (int hh = 0; hh < kHalves; ++hh) {
+              const int c0 = col0 + hh * kSub;
+              uint32_t v[kSub];
+              tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, v);
+              tmem_ld_wait();
+              float sw[kSub];
+              if constexpr (KIND == kGemmI8) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
+              // Rotary tables of these kSub / 2 pairs (kEpiRope16, Q and K columns).
+              float rc[kSub / 2], rs[kSub / 2];
+              bool rope = false;
+              if constexpr (EPI == kEpiRope16) {
+                rope = col0 < g.rope_cols;  // warp-uniform
+                if (rope && row_ok) {
+                  const int half_cols = g.rope_cols / 2;
+                  const int cc = c0 < half_cols ? c0 : c0 - half_cols;
+                  const size_t off = (static_cast<size_t>(token) * g.rope_heads + cc / g.rope_hd) * (g.rope_hd / 2) +
+                                     (cc % g.rope_hd) / 2;
+                  const float4* pc = reinterpret_cast<const float4*>(g.rope_cos + off);
+                  const float4* ps = reinterpret_cast<const float4*>(g.rope_sin + off);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) rc[i] = 1.0f, rs[i] = 0.0f;
-              }
-            }
-            // Separate unrolled bodies with and without bias (warp-uniform
-            // choice), so a bias-free projection issues no adds.
-            auto finish = [&](auto with_bias) {
-              constexpr bool kBias = decltype(with_bias)::value;
-              float bias[32];
-              if constexpr (kBias) load_vec32(g.bias, col0, g.n, bias);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                float2 x = acc_pair<KIND>(v, i, sa, sw);
-                if constexpr (kBias) {
-                  x.x = __fadd_rn(x.x, bias[2 * i]);
-                  x.y = __fadd_rn(x.y, bias[2 * i + 1]);
-                }
-                if constexpr (EPI == kEpiRes16) {
-                  const float2 r = unpack16x2(hw[i], f16);
-                  hw[i] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
-                } else if constexpr (EPI == kEpiRope16) {
-                  if (rope) {
-                    // (x, y) -> (x c - y s, x s + y c), each product and sum rounded
-                    const float c = rc[i], sn = rs[i];
-                    x = make_float2(__fsub_rn(__fmul_rn(x.x, c), __fmul_rn(x.y, sn)),
-                                    __fadd_rn(__fmul_rn(x.x, sn), __fmul_rn(x.y, c)));
+                  for (int i = 0; i < kSub / 8; ++i) {
+                    const float4 a = __ldg(pc + i), b2 = __ldg(ps + i);
+                    rc[4 * i] = a.x, rc[4 * i + 1] = a.y, rc[4 * i + 2] = a.z, rc[4 * i + 3] = a.w;
+                    rs[4 * i] = b2.x, rs[4 * i + 1] = b2.y, rs[4 * i + 2] = b2.z, rs[4 * i + 3] = b2.w;
                   }
-                  hw[i] = pack16x2(x, f16);
                 } else {
-                  hw[i] = pack16x2(apply_act2<ACT>(x), f16);
+#pragma unroll
+                  for (int i = 0; i < kSub / 2; ++i) rc[i] = 1.0f, rs[i] = 0.0f;
                 }
               }
-            };
-            if (EPI != kEpiF16 && g.bias != nullptr)
-              finish(std::true_type{});
-            else
-              finish(std::false_type{});
+              // Separate unrolled bodies with and without bias (warp-uniform
+              // choice), so a bias-free projection issues no adds.
+              auto finish = [&](auto bias_tag) {
+                constexpr bool kBias = decltype(bias_tag)::value;
+                float bias[kSub];
+                if constexpr (kBias) load_vecn<kSub>(g.bias, c0, g.n, bias);
+#pragma unroll
+                for (int i = 0; i < kSub / 2; ++i) {
+                  float2 x = acc_pairn<KIND, kSub>(v, i, sa, sw);
+                  if constexpr (kBias) {
+                    x.x = __fadd_rn(x.x, bias[2 * i]);
+                    x.y = __fadd_rn(x.y, bias[2 * i + 1]);
+                  }
+                  uint32_t& out = hw[hh * (kSub / 2) + i];
+                  if constexpr (EPI == kEpiRes16) {
+                    const float2 r = unpack16x2(out, f16);
+                    out = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
+                  } else if constexpr (EPI == kEpiRope16) {
+                    if (rope) {
+                      // (x, y) -> (x c - y s, x s + y c), each product and sum rounded
+                      const float c = rc[i], sn = rs[i];
+                      x = make_float2(__fsub_rn(__fmul_rn(x.x, c), __fmul_rn(x.y, sn)),
+                                      __fadd_rn(__fmul_rn(x.x, sn), __fmul_rn(x.y, c)));
+                    }
+                    out = pack16x2(x, f16);
+                  } else {
+                    out = pack16x2(apply_act2<ACT>(x), f16);
+                  }
+                }
+              };
+              if (with_bias)
+                finish(std::true_type{});
+              else
+                finish(std::false_type{});
+            }
             // |16-bit| maximum of the stored values: the next quantiser's row
             // amax, and the MXFP8 output finite check (Inf/NaN sort highest).
             if (KIND == kGemmMXF8 || (EPI != kEpiRes16 && g.row_amax != nullptr)) {
@@ -534,44 +595,53 @@ __global__ void __launch_bounds__(kThreads, 1)
                 nonfinite |= row_ok && max(amax2 & 0xffffu, amax2 >> 16) >= (f16 ? 0x7c00u : 0x7f80u);
             }
             emit16<SB>(o, g, hw, row, row0q, col0, lane, row_ok, valid);
-          } else if (row_ok) {
-            float sw[32], bias[32];
-            if constexpr (KIND == kGemmI8 && EPI != kEpiI32) load_vec32(g.col_scale, col0, g.n, sw);
-            if constexpr (EPI == kEpiF32) load_vec32(g.bias, col0, g.n, bias);
-            if constexpr (EPI == kEpiI32) {
-              int32_t* dst = static_cast<int32_t*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-              if (valid == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                int4* q = reinterpret_cast<int4*>(dst);
+          } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  q[i] = make_int4(int(v[4 * i]), int(v[4 * i + 1]), int(v[4 * i + 2]), int(v[4 * i + 3]));
-              } else {
+            for (int hh = 0; hh < kHalves; ++hh) {
+              const int c0 = col0 + hh * kSub;
+              const int vh = valid - hh * kSub;  // valid columns of this piece (may be <= 0)
+              uint32_t v[kSub];
+              tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, v);
+              tmem_ld_wait();
+              if (!row_ok || vh <= 0) continue;
+              float sw[kSub], bias[kSub];
+              if constexpr (KIND == kGemmI8 && EPI != kEpiI32) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
+              if constexpr (EPI == kEpiF32) load_vecn<kSub>(g.bias, c0, g.n, bias);
+              if constexpr (EPI == kEpiI32) {
+                int32_t* dst = static_cast<int32_t*>(g.out) + static_cast<size_t>(row) * g.ldo + c0;
+                if (vh >= kSub && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                  int4* q = reinterpret_cast<int4*>(dst);
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (i < valid) dst[i] = static_cast<int32_t>(v[i]);
-              }
-            } else if constexpr (EPI == kEpiResF32) {
-              float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
+                  for (int i = 0; i < kSub / 4; ++i)
+                    q[i] = make_int4(int(v[4 * i]), int(v[4 * i + 1]), int(v[4 * i + 2]), int(v[4 * i + 3]));
+                } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < valid) {
-                  const float x = __fadd_rn(dst[i], acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f));
-                  dst[i] = x;
-                  if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(x);
+                  for (int i = 0; i < kSub; ++i)
+                    if (i < vh) dst[i] = static_cast<int32_t>(v[i]);
                 }
-            } else if constexpr (EPI == kEpiF32) {
-              float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
-              const float* res = g.residual ? static_cast<const float*>(g.residual) +
-                                                  static_cast<size_t>(row) * g.ldr + col0
-                                            : nullptr;
+              } else if constexpr (EPI == kEpiResF32) {
+                float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + c0;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                if (i < valid) {
-                  float x = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
-                  if (g.bias) x = __fadd_rn(x, bias[i]);
-                  if (res) x = __fadd_rn(res[i], x);
-                  dst[i] = x;
-                  if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(x);
+                for (int i = 0; i < kSub; ++i)
+                  if (i < vh) {
+                    const float x = __fadd_rn(dst[i], acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f));
+                    dst[i] = x;
+                    if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(x);
+                  }
+              } else if constexpr (EPI == kEpiF32) {
+                float* dst = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo + c0;
+                const float* res = g.residual ? static_cast<const float*>(g.residual) +
+                                                    static_cast<size_t>(row) * g.ldr + c0
+                                              : nullptr;
+#pragma unroll
+                for (int i = 0; i < kSub; ++i) {
+                  if (i < vh) {
+                    float x = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
+                    if (g.bias) x = __fadd_rn(x, bias[i]);
+                    if (res) x = __fadd_rn(res[i], x);
+                    dst[i] = x;
+                    if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(x);
+                  }
                 }
               }
             }
@@ -634,10 +704,14 @@ bool epi_16bit(int epi) {
   return epi == kEpiF16 || epi == kEpi16 || epi == kEpiRes16 || epi == kEpiSwiGLU16 || epi == kEpiRope16;
 }
 
-template <int KIND, int BN, int EPI, int ACT, int SB>
+// DEEP: short K, where draining the epilogue bounds the tile time: more
+// staging tiles per warp (4 with 8 epilogue warps, 2 with 16), fewer otherwise.
+template <int KIND, int BN, int EPI, int ACT, int DEEP>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int use_tma_out,
                const GemmArgs& g, cudaStream_t stream) {
-  using Cfg = GemmCfg<KIND, BN, SB>;
+  constexpr int EW = epi_warps<EPI>();
+  constexpr int SB = DEEP ? (EW == 16 ? 2 : 4) : (EW == 16 ? 1 : 2);
+  using Cfg = GemmCfg<KIND, BN, SB, EW>;
   auto kern = gemm_kernel<KIND, BN, EPI, ACT, SB>;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -651,29 +725,29 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   }
   const int tiles = ((g.m + kBM - 1) / kBM) * ((g.n + BN - 1) / BN);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, g, use_tma_out);
+  kern<<<grid, gemm_threads<EPI>(), Cfg::kSmemBytes, stream>>>(ma, mb, mo, g, use_tma_out);
   return check_cuda(cudaGetLastError(), "gemm launch");
 }
 
-template <int KIND, int BN, int SB>
+template <int KIND, int BN, int DEEP>
 int dispatch_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int tma_out,
                  const GemmArgs& g, cudaStream_t s) {
   switch (epi) {
     case kEpiI32:
-      if constexpr (KIND != kGemmMXF8) return launch_one<KIND, BN, kEpiI32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+      if constexpr (KIND != kGemmMXF8) return launch_one<KIND, BN, kEpiI32, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
       break;
-    case kEpiF16: return launch_one<KIND, BN, kEpiF16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
-    case kEpiResF32: return launch_one<KIND, BN, kEpiResF32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiF16: return launch_one<KIND, BN, kEpiF16, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
+    case kEpiResF32: return launch_one<KIND, BN, kEpiResF32, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
     case kEpi16:
-      if (g.act == kActGelu) return launch_one<KIND, BN, kEpi16, kActGelu, SB>(ma, mb, mo, tma_out, g, s);
-      if (g.act == kActSilu) return launch_one<KIND, BN, kEpi16, kActSilu, SB>(ma, mb, mo, tma_out, g, s);
-      return launch_one<KIND, BN, kEpi16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
-    case kEpiRes16: return launch_one<KIND, BN, kEpiRes16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
-    case kEpiRope16: return launch_one<KIND, BN, kEpiRope16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+      if (g.act == kActGelu) return launch_one<KIND, BN, kEpi16, kActGelu, DEEP>(ma, mb, mo, tma_out, g, s);
+      if (g.act == kActSilu) return launch_one<KIND, BN, kEpi16, kActSilu, DEEP>(ma, mb, mo, tma_out, g, s);
+      return launch_one<KIND, BN, kEpi16, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
+    case kEpiRes16: return launch_one<KIND, BN, kEpiRes16, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
+    case kEpiRope16: return launch_one<KIND, BN, kEpiRope16, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
     case kEpiSwiGLU16:
-      if constexpr (KIND != kGemmMXF8) return launch_one<KIND, BN, kEpiSwiGLU16, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+      if constexpr (KIND != kGemmMXF8) return launch_one<KIND, BN, kEpiSwiGLU16, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
       break;
-    case kEpiF32: return launch_one<KIND, BN, kEpiF32, kActNone, SB>(ma, mb, mo, tma_out, g, s);
+    case kEpiF32: return launch_one<KIND, BN, kEpiF32, kActNone, DEEP>(ma, mb, mo, tma_out, g, s);
   }
   set_error("unknown GEMM epilogue");
   return KB_E_INVALID;
@@ -684,8 +758,8 @@ int dispatch_sb(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUt
                 const GemmArgs& g, cudaStream_t s) {
   // Deep staging when the epilogue, not the K loop, bounds the tile time.
   const int k_bytes = g.k * (KIND == kGemmBF16 ? 2 : 1);
-  if (tma_out && k_bytes <= 1024) return dispatch_epi<KIND, BN, 4>(epi, ma, mb, mo, tma_out, g, s);
-  return dispatch_epi<KIND, BN, 2>(epi, ma, mb, mo, tma_out, g, s);
+  if (tma_out && k_bytes <= 1024) return dispatch_epi<KIND, BN, 1>(epi, ma, mb, mo, tma_out, g, s);
+  return dispatch_epi<KIND, BN, 0>(epi, ma, mb, mo, tma_out, g, s);
 }
 
 }  // namespace
