@@ -168,23 +168,24 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kv_buf = smem;                    // [2][K | V]
   uint8_t* q_buf = smem + 2 * kKVBytes;      // Q tile
-  uint8_t* o_buf = q_buf + kQBytes;          // output tile (128 rows x 64 dims, 128-byte swizzle)
+  uint8_t* o_buf = q_buf + kQBytes;          // output pieces: 1 KB per softmax warp (32 rows x 16 dims)
   uint64_t* bars = reinterpret_cast<uint64_t*>(o_buf + kQBytes);
   uint64_t* kv_full = bars + 0;   // [2] loaders staged K/V           (128 arrivals)
   uint64_t* kv_empty = bars + 2;  // [2] MMAs done with K/V            (commit)
   uint64_t* q_full = bars + 4;    // loaders staged the Q tile          (tx bytes, or 96 arrivals)
   uint64_t* q_empty = bars + 5;   // S MMAs done with the Q tile        (commit)
-  uint64_t* out_full = bars + 6;  // output tile written                (512 arrivals)
-  uint64_t* out_free = bars + 7;  // previous tile's store read it      (1 arrival)
+  // bars + 6, + 7: unused
   uint64_t* sa_full = bars + 8;   // S_A ready                         (commit)
   uint64_t* sb_full = bars + 9;   // S_B ready                         (commit)
   uint64_t* pa_full = bars + 10;  // P_A written, O read back          (128 arrivals)
   uint64_t* pb_full = bars + 11;  // P_B written, O read back          (128 arrivals)
   uint64_t* o_full = bars + 12;   // O_A and O_B ready                 (commit)
-  uint64_t* ml_full = bars + 13;  // all quarters' (m, l) of a tile    (512 arrivals)
-  uint64_t* mx_full = bars + 14;  // [2] both quarter maxima of a half (256 arrivals)
-  uint64_t* kv_tma = bars + 16;   // [2] K/V TMA copies landed         (tx bytes)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* kv_tma = bars + 13;   // [2] K/V TMA copies landed         (tx bytes)
+  // Per TMEM lane quarter (the rows a warp owns), so warps only wait for the
+  // other warps holding the same query rows:
+  uint64_t* ml_full = bars + 16;  // [4] (m, l) of the 4 key quarters   (128 arrivals)
+  uint64_t* mx_full = bars + 20;  // [2][4] maxima of a half's 2 warps  (64 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float2* ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][4][128]
 
@@ -201,16 +202,14 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     }
     mbar_init(q_full, ROPE ? kLoadThreads : 1);
     mbar_init(q_empty, 1);
-    mbar_init(out_full, 32 * kSoftWarps);
-    mbar_init(out_free, 1);
+
     mbar_init(sa_full, 1);
     mbar_init(sb_full, 1);
     mbar_init(pa_full, 256);
     mbar_init(pb_full, 256);
     mbar_init(o_full, 1);
-    mbar_init(ml_full, 512);
-    mbar_init(&mx_full[0], 256);
-    mbar_init(&mx_full[1], 256);
+    for (int i = 0; i < 4; ++i) mbar_init(&ml_full[i], 128);
+    for (int i = 0; i < 8; ++i) mbar_init(&mx_full[i], 64);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -398,8 +397,8 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         float m = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         // the half's maximum: this warp's and its partner's (other 96 keys)
         mlg[q_slot * kTileQ + row].x = m;
-        mbar_arrive(&mx_full[half]);
-        if (!__all_sync(0xffffffffu, mbar_wait(&mx_full[half], g & 1, abort_flag))) {
+        mbar_arrive(&mx_full[half * 4 + quarter]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&mx_full[half * 4 + quarter], g & 1, abort_flag))) {
           ok = false;
           break;
         }
@@ -444,7 +443,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         }
         const float l = (lp[0] + lp[1]) + (lp[2] + lp[3]);
         mlg[q_slot * kTileQ + row] = make_float2(m, l);
-        mbar_arrive(ml_full);
+        mbar_arrive(&ml_full[quarter]);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(p_bar);
@@ -454,7 +453,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         }
         tc_fence_after();
         // every quarter's (m, l) of this tile is in shared memory
-        if (!__all_sync(0xffffffffu, mbar_wait(ml_full, g & 1, abort_flag))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&ml_full[quarter], g & 1, abort_flag))) {
           ok = false;
           break;
         }
@@ -480,43 +479,33 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           w[i] = pack2(x0, x1, F16);
           am = __vmaxu2(am, w[i] & 0x7fff7fffu);
         }
-        // The output tile leaves by one TMA store (rows past `seq` are clipped
-        // by the tensor map): wait until the previous tile's store has read
-        // the staging tile, write this thread's 16 dims (two swizzled 16-byte
-        // chunks of its row), then the storing thread issues the copy.
-        const bool storer = warp == 0 && lane == 0;
-        if (storer) {
-          bulk_wait_read<0>();
-          mbar_arrive(out_free);
-        }
-        if (!__all_sync(0xffffffffu, mbar_wait(out_free, g & 1, abort_flag))) {
-          ok = false;
-          break;
-        }
-        const int ch0 = dim0 >> 3;
-        *reinterpret_cast<uint4*>(o_buf + sw128(row, ch0)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(o_buf + sw128(row, ch0 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+        // Each warp's 32 rows x 16 dims leave by one TMA store of its own 1 KB
+        // piece (rows past `seq` are clipped by the tensor map): wait until the
+        // warp's previous store has read the piece, write it, store it.
+        uint8_t* piece = o_buf + warp * 1024;
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        *reinterpret_cast<uint4*>(piece + lane * 32 + (((0 ^ (lane >> 2)) & 1) << 4)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(piece + lane * 32 + (((1 ^ (lane >> 2)) & 1) << 4)) =
+            make_uint4(w[4], w[5], w[6], w[7]);
         fence_proxy_async_smem();
-        mbar_arrive(out_full);
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&map_out, piece, h * kD + dim0, t * kTileQ + quarter * 32, b);
+          bulk_commit();
+        }
         const int query = t * kTileQ + row;
         if (row_amax != nullptr && query < seq) {
           const uint32_t m16 = max(am & 0xffffu, am >> 16);
           atomicMax(row_amax + static_cast<size_t>(b) * seq + query,
                     F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
         }
-        if (storer) {
-          if (!mbar_wait(out_full, g & 1, abort_flag)) {
-            ok = false;
-          } else {
-            tma_store_3d(&map_out, o_buf, h * kD, t * kTileQ, b);
-            bulk_commit();
-          }
-        }
         if (!__all_sync(0xffffffffu, ok)) break;
       }
     }
   }
-  if (threadIdx.x == 0) bulk_wait_all();  // output stores complete before the CTA exits
+  if (lane == 0 && warp < kSoftWarps) bulk_wait_all();  // output stores complete before the CTA exits
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -540,10 +529,10 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
   CUtensorMap map_kv, map_q, map_out;
   memset(&map_kv, 0, sizeof(map_kv));
   memset(&map_q, 0, sizeof(map_q));
-  // out [batch, seq, C]: boxes of 64 dims x 128 tokens of one position
+  // out [batch, seq, C]: boxes of 16 dims x 32 tokens of one position, 32-byte swizzle
   int rc0 = encode_3d(&map_out, CU_TENSOR_MAP_DATA_TYPE_UINT16, out, static_cast<long>(heads) * kD, seq, batch,
-                      static_cast<long>(heads) * kD * 2, static_cast<long>(seq) * heads * kD * 2, kD, kTileQ, 1,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
+                      static_cast<long>(heads) * kD * 2, static_cast<long>(seq) * heads * kD * 2, 16, 32, 1,
+                      CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc0) return rc0;
   if (!ROPE) {
     // [batch * seq rows, 3C columns] 16-bit; boxes of 64 columns (one head) x rows
