@@ -8,8 +8,8 @@ one whole forward) twice, so `ncu -s 1 -c 1` captures a warm launch:
   trunk   two forwards without a graph (104 kernels each)
   up      INT8 GEMM 92416x3072x768 + bias + GELU (the FFN up projection)
   down    INT8 GEMM 92416x768x3072 + bias + bf16 residual
-  qkv     INT8 GEMM 92416x2304x768
-  attn    RoPE attention, 256 positions x 12 heads x 64
+  attn    attention, 256 positions x 12 heads x 64 (Q and K already rotated, the trunk's path)
+  qkv     INT8 GEMM 92416x2304x768 with the rotary epilogue (the trunk's QKV projection)
   quant   streaming quantiser of the 92416x3072 bf16 FFN hidden
   rms     fused RMSNorm -> bf16 -> INT8 quantiser, 92416x768
   mxup    MXFP8 block-scaled GEMM 92416x3072x768 -> bf16 (the up projection)
@@ -43,6 +43,7 @@ def main(argv):
         n, k, epi, act = {"up": (3072, 768, _capi.EPI_16, _capi.ACT_GELU),
                           "down": (768, 3072, _capi.EPI_RES16, 0),
                           "qkv": (2304, 768, _capi.EPI_16, 0)}[case]
+        # (the qkv case times the plain 16-bit epilogue; the trunk adds the rotary tables)
         a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda")
         w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda")
         sa = torch.rand(m, device="cuda") * 0.01
@@ -58,7 +59,7 @@ def main(argv):
         sn = torch.zeros_like(cs)
         out = torch.empty(m, heads * d, dtype=torch.bfloat16, device="cuda")
         for _ in range(2):
-            _capi.call("kb_attention", qkv.data_ptr(), cs.data_ptr(), sn.data_ptr(), out.data_ptr(), batch, heads,
+            _capi.call("kb_attention", qkv.data_ptr(), 0, 0, out.data_ptr(), batch, heads,
                        d, 0.125, _capi.DT_BF16, int(torch.cuda.current_stream().cuda_stream))
     elif case == "quant":
         x = torch.randn(m, 3072, device="cuda").to(torch.bfloat16).view(torch.int16)
