@@ -551,60 +551,76 @@ int launch_quant(const void* x, long ldx, const float* gamma, float eps, int row
 
 // Streaming quantiser for rows whose absolute maximum was already produced by
 // the kernel that wrote them (the GEMM / attention epilogue's row_amax): no row
-// reduction.  A thread owns four 8-column groups, strided by the block size so
-// each of its four 16-byte loads is coalesced across the warp and all four are
-// in flight together; results leave as 8-byte stores.  Same scale and
-// rounding as quantize_row16 (bit-identical results).
-constexpr int kStreamGroups = 4;
+// reduction.  Same scale and rounding as quantize_row16 (bit-identical results).
 
-template <bool F16>
+// One warp per row, persistent over rows: lane l loads the groups l, l+32, ...
+// of the row (all G 16-byte loads issued before any is used, so a warp keeps
+// G x 512 bytes in flight), the scale and its reciprocal are computed once per
+// row, and 8-byte stores leave the int8 groups.
+template <bool F16, int G>
 __global__ void __launch_bounds__(256) quantize_rows_amax_kernel(
     const uint16_t* __restrict__ x, long ldx, const uint32_t* __restrict__ row_amax, int rows, int width,
-    int kp, FastDiv groups_div, int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status,
-    unsigned layer) {
+    int kp, int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int out_groups = kp / 8;
-  // total < 2^31 is checked by the launcher: 32-bit indices, no division instruction.
-  const int total = rows * out_groups;
-  const int step = gridDim.x * blockDim.x * kStreamGroups;
-  for (int base = blockIdx.x * blockDim.x * kStreamGroups + threadIdx.x; base < total; base += step) {
-    uint32_t w[kStreamGroups][4];
-    int row[kStreamGroups], c0[kStreamGroups];
+  const int step = gridDim.x * 8;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += step) {  // warp-uniform
+    const uint16_t* src = x + static_cast<size_t>(row) * ldx;
+    uint32_t w[G][4];
 #pragma unroll
-    for (int j = 0; j < kStreamGroups; ++j) {
-      const int idx = base + j * blockDim.x;
+    for (int j = 0; j < G; ++j) {
+      const int c0 = 8 * (lane + 32 * j);
       w[j][0] = w[j][1] = w[j][2] = w[j][3] = 0;
-      row[j] = -1;
-      if (idx < total) {
-        row[j] = static_cast<int>(groups_div.div(static_cast<uint32_t>(idx)));
-        c0[j] = 8 * (idx - row[j] * out_groups);
-        const uint16_t* src = x + static_cast<size_t>(row[j]) * ldx + c0[j];
-        if (c0[j] + 8 <= width) {
-          const uint4 a = __ldg(reinterpret_cast<const uint4*>(src));
-          w[j][0] = a.x; w[j][1] = a.y; w[j][2] = a.z; w[j][3] = a.w;
-        } else {
+      if (c0 + 8 <= width) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(src + c0));
+        w[j][0] = a.x; w[j][1] = a.y; w[j][2] = a.z; w[j][3] = a.w;
+      } else if (c0 < width) {
 #pragma unroll
-          for (int t = 0; t < 8; ++t)
-            if (c0[j] + t < width) w[j][t / 2] |= static_cast<uint32_t>(src[t]) << (16 * (t & 1));
-        }
+        for (int t = 0; t < 8; ++t)
+          if (c0 + t < width) w[j][t / 2] |= static_cast<uint32_t>(src[c0 + t]) << (16 * (t & 1));
       }
     }
+    const uint32_t amax = __ldg(row_amax + row);
+    const float scale = int8_scale_from_amax(amax);
+    const bool bad = amax >= 0x7f800000u;
+    if (lane == 0) {
+      scales[row] = scale;
+      if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+    }
+    int8_t* dst = q + static_cast<size_t>(row) * kp;
+    if (!bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u) {
+      const float r = __frcp_rn(scale);
 #pragma unroll
-    for (int j = 0; j < kStreamGroups; ++j) {
-      if (row[j] < 0) continue;
-      const uint32_t amax = __ldg(row_amax + row[j]);
-      const float scale = int8_scale_from_amax(amax);
-      const bool bad = amax >= 0x7f800000u;
-      if (c0[j] == 0) {
-        scales[row[j]] = scale;
-        if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+      for (int j = 0; j < G; ++j) {
+        const int g = lane + 32 * j;
+        if (g < out_groups) *reinterpret_cast<uint2*>(dst + 8 * g) = quant_group_fast<F16>(w[j], scale, r);
       }
-      int8_t* dst = q + static_cast<size_t>(row[j]) * kp + c0[j];
-      if (!bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u)
-        *reinterpret_cast<uint2*>(dst) = quant_group_fast<F16>(w[j], scale, __frcp_rn(scale));
-      else
-        quantize_group_slow(make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]), F16, scale, bad, dst);
+    } else {
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const int g = lane + 32 * j;
+        if (g < out_groups)
+          quantize_group_slow(make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]), F16, scale, bad, dst + 8 * g);
+      }
     }
   }
+}
+
+template <bool F16, int G>
+int launch_amax(const void* x, long ldx, const uint32_t* row_amax, int rows, int width, int kp, int8_t* q,
+                float* scales, unsigned* status, unsigned layer, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quantize_rows_amax_kernel<F16, G>, 256, 0) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int want = (rows + 7) / 8;
+  const int cap = per_sm * num_sms(dev);
+  quantize_rows_amax_kernel<F16, G><<<want < cap ? want : cap, 256, 0, stream>>>(
+      static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, q, scales, status, layer);
+  return check_cuda(cudaGetLastError(), "amax quantiser launch");
 }
 
 }  // namespace
@@ -657,24 +673,20 @@ int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t
     set_error("amax quantiser: need 16-bit rows with 16-byte aligned starts, kp % 16 == 0, and row_amax");
     return KB_E_INVALID;
   }
-  const long total = static_cast<long>(rows) * (kp / 8);
-  if (total + 256L * kStreamGroups * 8 * 1024 > 0x7fffffffL) {
-    set_error("amax quantiser: rows * kp / 8 must stay below 2^31");
+  if (kp > 4096) {
+    set_error("amax quantiser: padded width above 4096 is not supported");
     return KB_E_INVALID;
   }
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const long max_blocks = static_cast<long>(num_sms(dev)) * 8;
-  const long need = (total + 256 * kStreamGroups - 1) / (256 * kStreamGroups);
-  const long blocks = need < max_blocks ? need : max_blocks;
-  const FastDiv gdiv(static_cast<uint32_t>(kp / 8));
-  if (dtype == kInF16)
-    quantize_rows_amax_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, gdiv, q, scales, status, layer);
-  else
-    quantize_rows_amax_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const uint16_t*>(x), ldx, row_amax, rows, width, kp, gdiv, q, scales, status, layer);
-  return check_cuda(cudaGetLastError(), "amax quantiser launch");
+  const int need = (kp / 8 + 31) / 32;  // 16-byte groups per lane
+  const bool f16 = dtype == kInF16;
+#define KB_AQ(GG)                                                                                          \
+  if (need <= GG)                                                                                          \
+    return f16 ? launch_amax<true, GG>(x, ldx, row_amax, rows, width, kp, q, scales, status, layer, stream) \
+               : launch_amax<false, GG>(x, ldx, row_amax, rows, width, kp, q, scales, status, layer, stream);
+  KB_AQ(1) KB_AQ(2) KB_AQ(3) KB_AQ(4) KB_AQ(6) KB_AQ(8) KB_AQ(12) KB_AQ(16)
+#undef KB_AQ
+  set_error("amax quantiser: unsupported width");
+  return KB_E_INVALID;
 }
 
 // dtype: 0 = f32, 1 = f16, 2 = bf16.  rms: apply RMSNorm with gamma/eps and a
