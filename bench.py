@@ -248,6 +248,8 @@ class TrunkWorkload:
         if not build_device:
             return
         self.spatial, self.glob = self.spatial[:batch], self.glob[:batch]
+        # one random board symmetry per row, as MCTS submits them (applied on the device)
+        self.symmetry = np.random.default_rng(seed + 3 + rank).integers(0, 8, batch).astype(np.int32)
         self.model = backend.CudaBackend.load_model(self.topo, self.blob, torch.cuda.current_device())
         self.handle = backend.CudaBackend.create_compute_handle(self.model, batch)
         self.d_spatial = torch.from_numpy(self.spatial).cuda()
@@ -265,12 +267,13 @@ class TrunkWorkload:
         self.handle.forward_device(self.batch, self.d_spatial, self.d_global, self.d_out, use_graph=True)
 
     def e2e_step(self):
-        self.handle.get_output(self.spatial, self.glob)
+        self.handle.get_output(self.spatial, self.glob, self.symmetry)
 
     def e2e_bytes(self):
         from rust_katago_b200 import backend
 
-        return self.spatial.nbytes + self.glob.nbytes, self.batch * backend.OUT_PER_POS * 4
+        return (self.spatial.nbytes + self.glob.nbytes + self.symmetry.nbytes,
+                self.batch * backend.OUT_PER_POS * 4 + 8)
 
     def gemms(self):
         """The trunk's INT8 GEMM shapes: (label, m, n, k, epilogue, act, launches per forward)."""
@@ -506,7 +509,8 @@ def main():
                        "parallelism": f"batch-sharded x{world}, weights replicated, no collective",
                        "l2": "256 MiB flush between timed steps (working set also exceeds L2)"},
             "e2e": {"value": e2e_value, "unit": "positions/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "how": "public API (kb_submit/kb_finish: pinned staging, H2D, graph, D2H, status check), "
+                    "how": "public API (kb_submit with a random board symmetry per row, applied on the device / kb_finish: "
+                           "pinned staging, H2D, graph, D2H, status check), "
                            "host clock around the steps, max over ranks"},
             "gpu_launches": wl.launches_per_step * args.steps,
             "roofline": roofline,

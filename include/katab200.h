@@ -359,10 +359,16 @@ KB_API int kb_warmup(kb_handle* handle, const int* batches, int count);
 
 /* Asynchronous evaluation of n positions from host memory: spatial fp32
  * [n, 22, 19, 19] (NCHW, or [n, 19, 19, 22] if the handle is NHWC), global
- * fp32 [n, 19].  Returns a token.  Replaces: Backend::submit_output
- * (cuda.rs:2196-2480). */
+ * fp32 [n, 19], symmetry int [n] in 0..7 (bit 2 transpose, bit 1 flip x,
+ * bit 0 flip y; NULL = identity for every row).  Each row's symmetry is applied
+ * on the device as the stem gathers its input, with the result of
+ * copy_inputs_with_symmetry (crates/kata_game/src/symmetry.rs:108-224), which
+ * the reference runs on the host at cuda.rs:2234-2245; outputs stay in the
+ * network's frame, as the reference's raw heads do (decode_raw_outputs,
+ * output_postprocess.rs:29-112, reverses them).  Returns a token.
+ * Replaces: Backend::submit_output (cuda.rs:2196-2480). */
 KB_API int kb_submit(kb_handle* handle, int n, const float* spatial, const float* global,
-                     uint64_t* token);
+                     const int* symmetry, uint64_t* token);
 
 /* 1 if the token's outputs are ready, 0 if not, negative KB_E_* on error.
  * Replaces: Backend::query_output_done. */

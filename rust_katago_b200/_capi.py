@@ -60,7 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_handle_destroy": (None, [P]),
     "kb_handle_stream": (I, [P, ctypes.POINTER(ctypes.c_size_t)]),
     "kb_warmup": (I, [P, ctypes.POINTER(ctypes.c_int), I]),
-    "kb_submit": (I, [P, I, P, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "kb_submit": (I, [P, I, P, P, P, ctypes.POINTER(ctypes.c_uint64)]),
     "kb_query": (I, [P, ctypes.c_uint64]),
     "kb_finish": (I, [P, ctypes.c_uint64, P, P, P, P, P, ctypes.POINTER(ctypes.c_uint32)]),
     "kb_forward_device": (I, [P, I, P, P, P, I]),

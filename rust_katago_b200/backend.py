@@ -107,12 +107,23 @@ class ComputeHandle:
         arr = (ctypes.c_int * len(batches))(*batches)
         call("kb_warmup", self._h, arr, len(batches))
 
-    def submit_output(self, spatial: np.ndarray, glob: np.ndarray) -> int:
+    def submit_output(self, spatial: np.ndarray, glob: np.ndarray, symmetry=None) -> int:
+        """Enqueue n positions; `symmetry` ([n] ints in 0..7, or None for the
+        identity) is each row's board symmetry, applied on the device as the
+        input is gathered (the reference applies copy_inputs_with_symmetry on
+        the host, cuda.rs:2234-2245).  Outputs come back in the network's frame,
+        as the reference's raw heads do; decode_raw_outputs reverses them."""
         spatial = np.ascontiguousarray(spatial, dtype=np.float32)
         glob = np.ascontiguousarray(glob, dtype=np.float32)
         n = spatial.shape[0]
+        sym_ptr = None
+        if symmetry is not None:
+            symmetry = np.ascontiguousarray(symmetry, dtype=np.int32)
+            if symmetry.shape != (n,):
+                raise ValueError("symmetry must hold one entry per position")
+            sym_ptr = symmetry.ctypes.data
         tok = ctypes.c_uint64()
-        call("kb_submit", self._h, n, spatial.ctypes.data, glob.ctypes.data, ctypes.byref(tok))
+        call("kb_submit", self._h, n, spatial.ctypes.data, glob.ctypes.data, sym_ptr, ctypes.byref(tok))
         self._pending = getattr(self, "_pending", {})
         self._pending[tok.value] = n
         return tok.value
@@ -132,8 +143,8 @@ class ComputeHandle:
              out.moremisc.ctypes.data, out.ownership.ctypes.data, status)
         return out
 
-    def get_output(self, spatial: np.ndarray, glob: np.ndarray) -> NNOutputs:
-        return self.finish_output(self.submit_output(spatial, glob))
+    def get_output(self, spatial: np.ndarray, glob: np.ndarray, symmetry=None) -> NNOutputs:
+        return self.finish_output(self.submit_output(spatial, glob, symmetry))
 
     def forward_device(self, n: int, d_spatial, d_global, d_out, use_graph: bool = True):
         call("kb_forward_device", self._h, n, int(d_spatial.data_ptr()), int(d_global.data_ptr()),

@@ -35,8 +35,8 @@ namespace kb {
 int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
                      int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
                      uint32_t* row_amax = nullptr, unsigned* status = nullptr);
-int stem_gather_launch(const float* spatial, const float* global, uint16_t* a, int batch, int nhwc,
-                       cudaStream_t s);
+int stem_gather_launch(const float* spatial, const float* global, const int* sym, uint16_t* a, int batch,
+                       int nhwc, cudaStream_t s);
 int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, uint16_t* g, long rows, int c,
                      cudaStream_t s);
 int heads_launch(const float* hp, const float* const* wts, float* policy, float* value, float* misc,
@@ -148,7 +148,7 @@ namespace {
 
 struct Slot {
   float* h_spatial = nullptr;  // pinned
-  float* h_global = nullptr;
+  float* h_global = nullptr;  // [n, 19] global features, then n int32 symmetries
   float* h_out = nullptr;      // pinned [policy | value | misc | moremisc | ownership]
   float* d_spatial = nullptr;
   float* d_global = nullptr;
@@ -185,8 +185,8 @@ struct kb_handle {
   unsigned* status = nullptr;   // [2]
   Slot slots[2];
   uint64_t next_token = 1;
-  // Graphs bake in buffer addresses: one per (batch size, input and output buffers).
-  using GraphKey = std::tuple<int, const void*, const void*, const void*>;
+  // Graphs bake in buffer addresses: one per (batch size, input, symmetry and output buffers).
+  using GraphKey = std::tuple<int, const void*, const void*, const void*, const void*>;
   std::map<GraphKey, cudaGraphExec_t> graphs;
   std::map<GraphKey, int> warmed;
   std::mutex mu;
@@ -295,7 +295,7 @@ int mxfp8_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale
 // One forward pass of n positions on device buffers, enqueued on `s`.  When
 // `trace` is non-null it receives bf16 [(num_blocks + 2), n*361, C]: the stem
 // output, each block's attention output, and the final residual stream.
-int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, float* d_out,
+int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, const int* d_sym, float* d_out,
             uint16_t* trace = nullptr) {
   kb_model* m = h->model;
   const kb_model_desc& d = m->desc;
@@ -304,7 +304,7 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
   int rc = check_cuda(cudaMemsetAsync(h->status, 0, sizeof(unsigned), s), "status reset");
   if (!rc) rc = check_cuda(cudaMemsetAsync(h->status + 1, 0xff, sizeof(unsigned), s), "status reset");
   if (rc) return rc;
-  rc = stem_gather_launch(d_spatial, d_global, h->stem_a, n, h->nhwc, s);
+  rc = stem_gather_launch(d_spatial, d_global, d_sym, h->stem_a, n, h->nhwc, s);
   if (rc) return rc;
   {
     GemmArgs g;
@@ -445,19 +445,20 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
 // Forward through a CUDA graph per batch size: the first call for a size runs
 // directly (so lazy module loading and function attributes happen outside
 // capture), the second captures and instantiates, later calls replay.
-int run_forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, float* d_out, bool use_graph) {
-  if (!use_graph) return forward(h, n, d_spatial, d_global, d_out);
-  const kb_handle::GraphKey key{n, d_spatial, d_global, d_out};
+int run_forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, const int* d_sym, float* d_out,
+                bool use_graph) {
+  if (!use_graph) return forward(h, n, d_spatial, d_global, d_sym, d_out);
+  const kb_handle::GraphKey key{n, d_spatial, d_global, d_sym, d_out};
   auto it = h->graphs.find(key);
   if (it != h->graphs.end()) return check_cuda(cudaGraphLaunch(it->second, h->stream), "graph launch");
   if (!h->warmed[key]) {
     h->warmed[key] = 1;
-    return forward(h, n, d_spatial, d_global, d_out);
+    return forward(h, n, d_spatial, d_global, d_sym, d_out);
   }
   cudaGraph_t graph = nullptr;
   int rc = check_cuda(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
   if (rc) return rc;
-  const int frc = forward(h, n, d_spatial, d_global, d_out);
+  const int frc = forward(h, n, d_spatial, d_global, d_sym, d_out);
   rc = check_cuda(cudaStreamEndCapture(h->stream, &graph), "end capture");
   if (frc) {
     if (graph) cudaGraphDestroy(graph);
@@ -703,7 +704,7 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
   if (!rc) rc = dev_alloc(&h->hp, M * kHeadN, "workspace");
   if (!rc) rc = dev_alloc(&h->status, 2, "status word");
   for (auto& sl : h->slots) {
-    const size_t ns = static_cast<size_t>(max_batch) * kInC * kSeq, ng = static_cast<size_t>(max_batch) * kInG,
+    const size_t ns = static_cast<size_t>(max_batch) * kInC * kSeq, ng = static_cast<size_t>(max_batch) * (kInG + 1),
                  no = static_cast<size_t>(max_batch) * kOutPerPos;
     if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_spatial, ns * sizeof(float)), "pinned input");
     if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_global, ng * sizeof(float)), "pinned input");
@@ -747,7 +748,7 @@ int kb_forward_device(kb_handle* h, int n, const float* d_spatial, const float* 
   std::lock_guard<std::mutex> lock(h->mu);
   int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
   if (rc) return rc;
-  return run_forward(h, n, d_spatial, d_global, d_out, use_graph != 0);
+  return run_forward(h, n, d_spatial, d_global, nullptr, d_out, use_graph != 0);
 }
 
 int kb_forward_trace(kb_handle* h, int n, const float* d_spatial, const float* d_global, float* d_out,
@@ -759,7 +760,7 @@ int kb_forward_trace(kb_handle* h, int n, const float* d_spatial, const float* d
   std::lock_guard<std::mutex> lock(h->mu);
   int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
   if (rc) return rc;
-  return forward(h, n, d_spatial, d_global, d_out, d_trace);
+  return forward(h, n, d_spatial, d_global, nullptr, d_out, d_trace);
 }
 
 int kb_read_status(kb_handle* h, uint32_t status[2]) {
@@ -773,11 +774,18 @@ int kb_read_status(kb_handle* h, uint32_t status[2]) {
   return rc;
 }
 
-int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, uint64_t* token) {
+int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, const int* symmetry,
+              uint64_t* token) {
   if (!h || !spatial || !global || !token || n <= 0 || n > h->max_batch) {
     set_error("kb_submit: need 1 <= n <= max_batch, host inputs and a token");
     return KB_E_INVALID;
   }
+  if (symmetry)
+    for (int i = 0; i < n; ++i)
+      if (symmetry[i] < 0 || symmetry[i] > 7) {
+        set_error("kb_submit: symmetry must be in 0..7");
+        return KB_E_INVALID;
+      }
   std::lock_guard<std::mutex> lock(h->mu);
   int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
   if (rc) return rc;
@@ -794,10 +802,19 @@ int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, ui
   const size_t ns = static_cast<size_t>(n) * kInC * kSeq, ng = static_cast<size_t>(n) * kInG;
   memcpy(sl->h_spatial, spatial, ns * sizeof(float));
   memcpy(sl->h_global, global, ng * sizeof(float));
+  // The symmetries ride behind the global features: one copy carries both.
+  int* h_sym = reinterpret_cast<int*>(sl->h_global + ng);
+  if (symmetry)
+    memcpy(h_sym, symmetry, static_cast<size_t>(n) * sizeof(int));
+  else
+    memset(h_sym, 0, static_cast<size_t>(n) * sizeof(int));
+  const int* d_sym = reinterpret_cast<const int*>(sl->d_global + ng);
   cudaStream_t s = h->stream;
   rc = check_cuda(cudaMemcpyAsync(sl->d_spatial, sl->h_spatial, ns * sizeof(float), cudaMemcpyHostToDevice, s), "H2D");
-  if (!rc) rc = check_cuda(cudaMemcpyAsync(sl->d_global, sl->h_global, ng * sizeof(float), cudaMemcpyHostToDevice, s), "H2D");
-  if (!rc) rc = run_forward(h, n, sl->d_spatial, sl->d_global, sl->d_out, true);
+  if (!rc)
+    rc = check_cuda(cudaMemcpyAsync(sl->d_global, sl->h_global, (ng + n) * sizeof(float), cudaMemcpyHostToDevice, s),
+                    "H2D");
+  if (!rc) rc = run_forward(h, n, sl->d_spatial, sl->d_global, d_sym, sl->d_out, true);
   if (!rc)
     rc = check_cuda(cudaMemcpyAsync(sl->h_out, sl->d_out, static_cast<size_t>(n) * kOutPerPos * sizeof(float),
                                     cudaMemcpyDeviceToHost, s), "D2H");
@@ -886,8 +903,9 @@ int kb_warmup(kb_handle* h, const int* batches, int count) {
     // each pipeline slot one direct run and one captured run.
     for (auto& sl : h->slots) {
       if (!rc) rc = check_cuda(cudaMemsetAsync(sl.d_spatial, 0, static_cast<size_t>(n) * kInC * kSeq * sizeof(float), h->stream), "memset");
-      if (!rc) rc = check_cuda(cudaMemsetAsync(sl.d_global, 0, static_cast<size_t>(n) * kInG * sizeof(float), h->stream), "memset");
-      for (int k = 0; k < 2 && !rc; ++k) rc = run_forward(h, n, sl.d_spatial, sl.d_global, sl.d_out, true);
+      if (!rc) rc = check_cuda(cudaMemsetAsync(sl.d_global, 0, static_cast<size_t>(n) * (kInG + 1) * sizeof(float), h->stream), "memset");
+      const int* d_sym = reinterpret_cast<const int*>(sl.d_global + static_cast<size_t>(n) * kInG);
+      for (int k = 0; k < 2 && !rc; ++k) rc = run_forward(h, n, sl.d_spatial, sl.d_global, d_sym, sl.d_out, true);
     }
   }
   if (!rc) rc = check_cuda(cudaStreamSynchronize(h->stream), "warmup sync");

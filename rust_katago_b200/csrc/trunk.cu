@@ -27,10 +27,29 @@ constexpr int kInC = 22;
 constexpr int kInG = 19;
 constexpr int kStemK = 224;  // 22*9 + 19 = 217, padded to a multiple of 8 (16 bytes of bf16)
 
+// Board symmetry of one position (0..7: bit 2 transpose, bit 1 flip x, bit 0
+// flip y).  The network sees copy_inputs_with_symmetry(input, sym)
+// (crates/kata_game/src/symmetry.rs:108-224, reverse = false on a square
+// board): the input at (row h, col w) lands at network (r, c) with
+// r = flip_y' ? 18 - w : w, c = flip_x' ? 18 - h : h under transpose (flips
+// swapped), else r = flip_y ? 18 - h : h, c = flip_x ? 18 - w : w.  The gather
+// needs the inverse: the input cell that network cell (r, c) reads.
+__device__ __forceinline__ int sym_source(int sym, int r, int c) {
+  int a = r, b = c;
+  if (sym & 4) {
+    a = c;
+    b = r;
+  }
+  if (sym & 1) a = kSide - 1 - a;
+  if (sym & 2) b = kSide - 1 - b;
+  return a * kSide + b;
+}
+
 // A[(b*361 + t), k] for the stem GEMM.  spatial: [B, 22, 19, 19] (NCHW) or
-// [B, 19, 19, 22] (NHWC), global: [B, 19], both fp32.
+// [B, 19, 19, 22] (NHWC), global: [B, 19], both fp32; sym: [B] board
+// symmetries (NULL = identity), applied as the input is gathered.
 __global__ void stem_gather_kernel(const float* __restrict__ spatial, const float* __restrict__ global,
-                                   uint16_t* __restrict__ a, int batch, int nhwc) {
+                                   const int* __restrict__ sym, uint16_t* __restrict__ a, int batch, int nhwc) {
   const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long total = static_cast<long>(batch) * kSeq * (kStemK / 2);
   if (idx >= total) return;
@@ -39,6 +58,7 @@ __global__ void stem_gather_kernel(const float* __restrict__ spatial, const floa
   const int b = static_cast<int>(row / kSeq);
   const int t = static_cast<int>(row % kSeq);
   const int y = t / kSide, x = t % kSide;
+  const int sm = sym ? (__ldg(sym + b) & 7) : 0;
   float v[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -48,8 +68,9 @@ __global__ void stem_gather_kernel(const float* __restrict__ spatial, const floa
       const int ic = k / 9, ky = (k % 9) / 3, kx = k % 3;
       const int sy = y + ky - 1, sx = x + kx - 1;
       if (sy >= 0 && sy < kSide && sx >= 0 && sx < kSide) {
-        const long off = nhwc ? ((static_cast<long>(b) * kSeq + sy * kSide + sx) * kInC + ic)
-                              : ((static_cast<long>(b) * kInC + ic) * kSeq + sy * kSide + sx);
+        const int cell = sym_source(sm, sy, sx);
+        const long off = nhwc ? ((static_cast<long>(b) * kSeq + cell) * kInC + ic)
+                              : ((static_cast<long>(b) * kInC + ic) * kSeq + cell);
         val = __ldg(spatial + off);
       }
     } else if (k < kInC * 9 + kInG) {
@@ -197,10 +218,11 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
 
 }  // namespace
 
-int stem_gather_launch(const float* spatial, const float* global, uint16_t* a, int batch, int nhwc,
-                       cudaStream_t s) {
+int stem_gather_launch(const float* spatial, const float* global, const int* sym, uint16_t* a, int batch,
+                       int nhwc, cudaStream_t s) {
   const long total = static_cast<long>(batch) * kSeq * (kStemK / 2);
-  stem_gather_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(spatial, global, a, batch, nhwc);
+  stem_gather_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(spatial, global, sym, a, batch,
+                                                                                 nhwc);
   return check_cuda(cudaGetLastError(), "stem gather launch");
 }
 

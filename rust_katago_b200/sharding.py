@@ -76,8 +76,9 @@ class ShardedEvaluator:
         self.models = [CudaBackend.load_model(topology, blob, d) for d in self.devices]
         self.handles = [CudaBackend.create_compute_handle(m, max_batch_per_device) for m in self.models]
 
-    def get_output(self, spatial: np.ndarray, glob: np.ndarray):
+    def get_output(self, spatial: np.ndarray, glob: np.ndarray, symmetry=None):
         shards = split_batch(spatial, glob, len(self.devices))
+        syms = [None if symmetry is None else np.asarray(symmetry, np.int32)[lo:hi] for lo, hi, _, _ in shards]
         if max(hi - lo for lo, hi, _, _ in shards) > self.max_batch:
             raise ValueError("batch exceeds devices x max_batch_per_device")
         results: list = [None] * len(shards)
@@ -86,7 +87,7 @@ class ShardedEvaluator:
         def work(i, sp, gl):
             try:
                 if sp.shape[0] > 0:
-                    results[i] = self.handles[i].get_output(sp, gl)
+                    results[i] = self.handles[i].get_output(sp, gl, syms[i])
             except Exception as e:  # re-raised on the calling thread
                 errors.append(e)
 
