@@ -11,22 +11,25 @@
 // Persistent: one CTA per SM walks (position, head) pairs.  All 361 keys fit
 // on chip, so nothing streams inside a pair:
 //   shared memory  K and V of two pairs (double buffer, 368 keys x 128 B each,
-//                  keys padded to a multiple of 16) and two 128-query Q tiles,
-//                  all in the UMMA 128-byte-swizzled layout, written by four
-//                  loader warps with RoPE applied on the way in;
+//                  keys padded to a multiple of 16) and one 128-query Q tile,
+//                  all in the UMMA 128-byte-swizzled layout, loaded by TMA
+//                  (or by three staging warps that rotate on the way in);
 //   TMEM (512 col) S_A = Q K[0:192]^T (192 columns), S_B = Q K[192:368]^T (176),
-//                  O_A = P_A V[0:192] and O_B = P_B V[192:368] (64 each).
-// Per 128-query tile the two key halves are independent: softmax warps 0-7
-// take half A and warps 8-15 half B, four warps per TMEM lane quarter, each
-// thread one query row and 96 keys; the two warps of a half exchange their
-// partial maxima through shared memory, then write P = exp2((S - m) c) as
-// packed 16-bit values over the first 48 of their own 96 S columns (the A
-// operand of the P.V MMA, read from TMEM).  The epilogue combines the halves:
-// O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) / (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)),
-// each warp writing 16 of the 64 dims, plus the row |max| for the next
-// quantiser.  Warp 16 issues the MMAs; the S MMAs of the next tile overlap
-// this tile's epilogue, and warps 17-19 stage the next pair while this one
-// computes.  Every wait is bounded.
+//                  O_A = P_A V[0:192] and O_B = P_B V[192:368] (64 each), and
+//                  the 16 row sums of two tiles (16).
+// The two key halves keep their own maxima (no rescaling: the epilogue
+// combines them), so they form a two-stage pipeline.  All 16 softmax warps
+// (four per TMEM lane quarter, one query row per thread, 48 keys of each half
+// per warp) take half A of a tile, then half B; meanwhile warp 16 runs the
+// tensor cores on the other half: PV_A of this tile and S_A of the next while
+// the softmax works on half B, PV_B and S_B of the next while it works on the
+// next half A.  Within a half the four warps of a lane quarter exchange their
+// slice maxima through shared memory, then write P = exp2((S - m) c) as packed
+// 16-bit pairs over their own, already read S columns (the A operand of the
+// P.V MMA, read from TMEM).  Between the halves the softmax warps finish the
+// previous tile: O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) /
+// (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), each warp writing 16 of the 64 dims
+// by TMA, plus the row |max| for the next quantiser.  Every wait is bounded.
 #include <stdint.h>
 #include <string.h>
 
@@ -49,19 +52,23 @@ constexpr int kKVBytes = 2 * kKBytes;     // K then V of one pair
 constexpr int kQBytes = kTileQ * kRowBytes;
 constexpr int kSoftWarps = 16;
 constexpr int kMmaWarp = kSoftWarps;
-// Loader warps: one issuing TMA copies (Q and K arrive rotated), or three
-// staging and rotating with the CTA's threads (the table-driven RoPE path).
+// Loader warps: two issuing TMA copies (K/V and Q; Q and K arrive rotated),
+// or three staging and rotating with the CTA's threads (the table-driven RoPE
+// path).
 template <bool ROPE>
-constexpr int load_warps() { return ROPE ? 3 : 1; }
+constexpr int load_warps() { return ROPE ? 3 : 2; }
 template <bool ROPE>
-constexpr int fa_threads() { return 32 * (kSoftWarps + 1 + load_warps<ROPE>()); }  // 640 / 576
+constexpr int fa_threads() { return 32 * (kSoftWarps + 1 + load_warps<ROPE>()); }  // 640 / 608
 constexpr int kKvBox = 184;               // rows per K/V TMA box (2 boxes = 368 rows)
-constexpr int kSubKeys = 96;              // keys per softmax warp (4 warps per TMEM lane quarter)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSB = kHalfA, kOA = kHalfA + kHalfB, kOB = kOA + kD;  // TMEM columns
+// Row sums l of the 8 key slices of a tile (4 per half), double-buffered by
+// tile parity, in the 16 TMEM columns left over: 496..511.
+constexpr uint32_t kLCol = kOB + kD;
 constexpr int kBarBytes = 256;
-// Per row and 96-key quarter (m, l), double-buffered by tile parity.
-constexpr int kMlBytes = 2 * 4 * kTileQ * 8;
+// Slice maxima exchanged between the 4 warps of a TMEM lane quarter:
+// [tile parity][half][slice][row] floats.
+constexpr int kMlBytes = 2 * 2 * 4 * kTileQ * 4;
 // K/V double buffer, one Q tile (loaded as soon as the previous tile's S MMAs
 // are done, several microseconds before it is needed), one output tile.
 constexpr int kSmemBytes = 2 * kKVBytes + 2 * kQBytes + kBarBytes + kMlBytes + 1024 /*alignment*/;
@@ -156,6 +163,84 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
   }
 }
 
+// Softmax of one key slice for this thread's query row: NK keys (48, or 32
+// for the last slice of half B) at S columns [col, col + NK), `valid` of them
+// below seq.  The slice maxima of the half's four warps are exchanged through
+// shared memory (mx: [slice][row] of this parity and half, barrier `mx_bar`
+// with 128 arrivals), then P = 2^((S - m) c) is written as packed 16-bit
+// pairs over columns [col, col + NK/2) (keys 2j, 2j+1 at column col + j:
+// columns this thread has already read), and the slice's row sum l to TMEM
+// column `lcol`.  Returns false if a wait gave up.
+template <int NK, bool F16>
+__device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, int valid, float scale_log2, float* mx,
+                                              int sub, int row, uint64_t* mx_bar, uint32_t parity,
+                                              volatile int* abort_flag, uint32_t lcol, float& m_out) {
+  uint32_t v[NK];
+  {
+    uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(v);
+    tmem_ld32(lane_base + col, v0);
+    if constexpr (NK == 48) {
+      uint32_t (&v1)[16] = *reinterpret_cast<uint32_t(*)[16]>(v + 32);
+      tmem_ld16(lane_base + col + 32, v1);
+    }
+    tmem_ld_wait();
+  }
+  // Row maximum over the slice: 8 independent partial maxima (short chains).
+  float mp[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mp[j] = __int_as_float(0xff800000);
+  if (valid >= NK) {
+#pragma unroll
+    for (int i = 0; i < NK; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[i]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < NK; ++i)
+      if (i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[i]));
+  }
+  float m = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+  mx[sub * kTileQ + row] = m;
+  mbar_arrive(mx_bar);
+  if (!__all_sync(0xffffffffu, mbar_wait(mx_bar, parity, abort_flag))) return false;
+  m = fmaxf(fmaxf(mx[row], mx[kTileQ + row]), fmaxf(mx[2 * kTileQ + row], mx[3 * kTileQ + row]));
+  m_out = m;
+  const float mc = m * scale_log2;
+  float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // partial sums (short chains)
+  uint32_t pk[NK / 2];
+  if (valid >= NK) {
+#pragma unroll
+    for (int i = 0; i < NK / 2; ++i) {
+      // half the exponentials on the special-function unit, half on the FMA pipe
+      const float x0 = __fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc);
+      const float x1 = __fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc);
+      float p0, p1;
+      if (i & 1) {
+        p0 = ex2(x0);
+        p1 = ex2(x1);
+      } else {
+        const float2 e = exp2_poly2(x0, x1);
+        p0 = e.x;
+        p1 = e.y;
+      }
+      lp[i & 3] += p0 + p1;
+      pk[i] = pack2(p0, p1, F16);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NK / 2; ++i) {
+      const float p0 = 2 * i < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
+      const float p1 = 2 * i + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
+      lp[i & 3] += p0 + p1;
+      pk[i] = pack2(p0, p1, F16);
+    }
+  }
+  tmem_st16(lane_base + col, *reinterpret_cast<const uint32_t(*)[16]>(pk));
+  if constexpr (NK == 48) tmem_st8(lane_base + col + 16, *reinterpret_cast<const uint32_t(*)[8]>(pk + 16));
+  tmem_st1(lane_base + lcol, __float_as_uint((lp[0] + lp[1]) + (lp[2] + lp[3])));
+  tmem_st_wait();
+  tc_fence_before();
+  return true;
+}
+
 template <bool F16, bool ROPE>
 __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     const __grid_constant__ CUtensorMap map_kv, const __grid_constant__ CUtensorMap map_q,
@@ -174,20 +259,19 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   uint64_t* kv_empty = bars + 2;  // [2] MMAs done with K/V            (commit)
   uint64_t* q_full = bars + 4;    // loaders staged the Q tile          (tx bytes, or 96 arrivals)
   uint64_t* q_empty = bars + 5;   // S MMAs done with the Q tile        (commit)
-  // bars + 6, + 7: unused
+  uint64_t* pva_done = bars + 6;  // PV_A done: P_A consumed           (commit)
+  uint64_t* o_free = bars + 7;    // O of the previous tile read back  (512 arrivals)
   uint64_t* sa_full = bars + 8;   // S_A ready                         (commit)
   uint64_t* sb_full = bars + 9;   // S_B ready                         (commit)
-  uint64_t* pa_full = bars + 10;  // P_A written, O read back          (128 arrivals)
-  uint64_t* pb_full = bars + 11;  // P_B written, O read back          (128 arrivals)
+  uint64_t* pa_full = bars + 10;  // P_A and its row sums written      (512 arrivals)
+  uint64_t* pb_full = bars + 11;  // P_B and its row sums written      (512 arrivals)
   uint64_t* o_full = bars + 12;   // O_A and O_B ready                 (commit)
   uint64_t* kv_tma = bars + 13;   // [2] K/V TMA copies landed         (tx bytes)
-  // Per TMEM lane quarter (the rows a warp owns), so warps only wait for the
-  // other warps holding the same query rows:
-  uint64_t* ml_full = bars + 16;  // [4] (m, l) of the 4 key quarters   (128 arrivals)
-  uint64_t* mx_full = bars + 20;  // [2][4] maxima of a half's 2 warps  (64 arrivals)
+  // [half][quarter]: slice maxima of the 4 warps holding the same query rows
+  uint64_t* mx_full = bars + 16;  // (128 arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float2* ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][4][128]
+  float* mx_ex = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][2][4][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = heads * kD;
@@ -196,20 +280,21 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], kLoadThreads);
+      mbar_init(&kv_full[i], ROPE ? kLoadThreads : 32);  // the K/V loader warp (or every staging thread)
       mbar_init(&kv_empty[i], 1);
       mbar_init(&kv_tma[i], 1);
     }
     mbar_init(q_full, ROPE ? kLoadThreads : 1);
     mbar_init(q_empty, 1);
 
+    mbar_init(pva_done, 1);
+    mbar_init(o_free, 32 * kSoftWarps);
     mbar_init(sa_full, 1);
     mbar_init(sb_full, 1);
-    mbar_init(pa_full, 256);
-    mbar_init(pb_full, 256);
+    mbar_init(pa_full, 32 * kSoftWarps);
+    mbar_init(pb_full, 32 * kSoftWarps);
     mbar_init(o_full, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&ml_full[i], 128);
-    for (int i = 0; i < 8; ++i) mbar_init(&mx_full[i], 64);
+    for (int i = 0; i < 8; ++i) mbar_init(&mx_full[i], 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -223,45 +308,52 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   const uint32_t tmem = *tmem_slot;
 
   if (warp > kMmaWarp && !ROPE) {
-    // ------------------------------------------------------------ TMA loader
-    // Q and K arrive rotated: K and V of a pair are two 184-row boxes each and
-    // a Q tile one 128-row box, landing in the UMMA 128-byte-swizzled layout.
-    if (lane == 0) {
-      tma_prefetch_desc(&map_kv);
-      tma_prefetch_desc(&map_q);
-    }
+    // ------------------------------------------------------------ TMA loaders
+    // Q and K arrive rotated.  Warp kMmaWarp + 1 loads K and V of each pair
+    // (two 184-row boxes each) into the free half of the double buffer as soon
+    // as it is released; warp kMmaWarp + 2 loads the 128-row Q tiles, each as
+    // soon as the S MMAs of the previous tile have read the Q buffer.  Both
+    // land in the UMMA 128-byte-swizzled layout.
+    const bool kv_loader = warp == kMmaWarp + 1;
+    if (lane == 0) tma_prefetch_desc(kv_loader ? &map_kv : &map_q);
     int g = 0;  // global Q tile counter
     for (int it = 0, p = blockIdx.x; p < pairs; ++it, p += gridDim.x) {
       const int kb = it & 1;
       const int b = p / heads, h = p % heads;
-      if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
-      uint8_t* ks = kv_buf + kb * kKVBytes;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&kv_tma[kb], 2 * kKBytes);
-        tma_load_2d(ks, &map_kv, &kv_tma[kb], c + h * kD, b * seq);
-        tma_load_2d(ks + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], c + h * kD, b * seq + kKvBox);
-        tma_load_2d(ks + kKBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD, b * seq);
-        tma_load_2d(ks + kKBytes + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD, b * seq + kKvBox);
-      }
-      // V rows [seq, 368) hold the next position's values (or TMA zeros):
-      // clear them, their P is zero but 0 * Inf would not be.
-      if (!__all_sync(0xffffffffu, mbar_wait(&kv_tma[kb], (it >> 1) & 1, abort_flag))) break;
-      for (int i = lane; i < (kKeysPad - seq) * 8; i += 32)
-        *reinterpret_cast<uint4*>(ks + kKBytes + sw128(seq + (i >> 3), i & 7)) = make_uint4(0, 0, 0, 0);
-      fence_proxy_async_smem();
-      mbar_arrive(&kv_full[kb]);
-      bool ok = true;
-      for (int t = 0; t < tiles; ++t, ++g) {
-        if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (g & 1) ^ 1, abort_flag))) {
-          ok = false;
-          break;
-        }
+      if (kv_loader) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
+        uint8_t* ks = kv_buf + kb * kKVBytes;
         if (lane == 0) {
-          mbar_arrive_expect_tx(q_full, kQBytes);
-          tma_load_2d(q_buf, &map_q, q_full, h * kD, b * seq + t * kTileQ);
+          mbar_arrive_expect_tx(&kv_tma[kb], 2 * kKBytes);
+          tma_load_2d(ks, &map_kv, &kv_tma[kb], c + h * kD, b * seq);
+          tma_load_2d(ks + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], c + h * kD, b * seq + kKvBox);
+          tma_load_2d(ks + kKBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD, b * seq);
+          tma_load_2d(ks + kKBytes + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD,
+                      b * seq + kKvBox);
+          // the pair's Q tiles into L2, so each later Q load is an L2 hit
+          for (int t = 0; t < tiles; ++t) tma_prefetch_2d(&map_q, h * kD, b * seq + t * kTileQ);
         }
+        // V rows [seq, 368) hold the next position's values (or TMA zeros):
+        // clear them, their P is zero but 0 * Inf would not be.
+        if (!__all_sync(0xffffffffu, mbar_wait(&kv_tma[kb], (it >> 1) & 1, abort_flag))) break;
+        for (int i = lane; i < (kKeysPad - seq) * 8; i += 32)
+          *reinterpret_cast<uint4*>(ks + kKBytes + sw128(seq + (i >> 3), i & 7)) = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
+        mbar_arrive(&kv_full[kb]);
+      } else {
+        bool ok = true;
+        for (int t = 0; t < tiles; ++t, ++g) {
+          if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (g & 1) ^ 1, abort_flag))) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, kQBytes);
+            tma_load_2d(q_buf, &map_q, q_full, h * kD, b * seq + t * kTileQ);
+          }
+        }
+        if (!ok) break;
       }
-      if (!ok) break;
     }
   } else if (warp > kMmaWarp) {
     // ------------------------------------------------------------ staging loaders (RoPE here)
@@ -294,6 +386,11 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // Per tile g: S_A(g), S_B(g), then PV_A(g) once P_A(g) is written and the
+    // previous tile's O has been read, then PV_B(g).  The next tile's S_A is
+    // issued as soon as PV_A(g) has consumed P_A(g) (it overwrites those
+    // columns), and its S_B once PV_B(g) has consumed P_B(g); so the softmax
+    // of one half always overlaps the tensor-core work of the other.
     if (lane == 0) {
       constexpr uint32_t kFmt = F16 ? 0u : 1u;
       const uint32_t id_common = (1u << 4) | (kFmt << 7) | (kFmt << 10) | (static_cast<uint32_t>(128 >> 4) << 24);
@@ -302,208 +399,171 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       const uint32_t id_pv = id_common | (1u << 16) /* B MN-major */ | (static_cast<uint32_t>(kD >> 3) << 17);
       constexpr uint64_t kHalfOff = (kHalfA * kRowBytes) >> 4;  // 192 rows, descriptor units
       constexpr uint64_t kStep16 = (16 * kRowBytes) >> 4;       // 16 keys of V along K
-      int g = 0;
-      bool ok = true;
-      for (int it = 0, p = blockIdx.x; p < pairs && ok; ++it, p += gridDim.x) {
-        const int kb = it & 1;
-        if (!mbar_wait(&kv_full[kb], (it >> 1) & 1, abort_flag)) break;
+      const int my_pairs = blockIdx.x < pairs ? (pairs - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+      const int n = my_pairs * tiles;
+      auto issue_sa = [&](int g) -> bool {
+        const int it = g / tiles, t = g % tiles, kb = it & 1;
+        if (t == 0 && !mbar_wait(&kv_full[kb], (it >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(q_full, g & 1, abort_flag)) return false;
+        tc_fence_after();
         const uint64_t kdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes));
+        const uint64_t qdesc = sw128_desc(smem_u32(q_buf));
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_issue<kKindBF16>(tmem, qdesc + 2 * kk, kdesc + 2 * kk, id_sa, kk != 0, 0, 0);
+        tc_commit(sa_full);
+        return true;
+      };
+      auto issue_sb = [&](int g) {
+        const int kb = (g / tiles) & 1;
+        const uint64_t kdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes));
+        const uint64_t qdesc = sw128_desc(smem_u32(q_buf));
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_issue<kKindBF16>(tmem + kSB, qdesc + 2 * kk, kdesc + kHalfOff + 2 * kk, id_sb, kk != 0, 0, 0);
+        tc_commit(sb_full);
+        tc_commit(q_empty);
+      };
+      bool ok = n == 0 || issue_sa(0);
+      if (ok && n > 0) issue_sb(0);
+      for (int g = 0; g < n && ok; ++g) {
+        const int kb = (g / tiles) & 1;
         const uint64_t vdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes + kKBytes));
-        for (int t = 0; t < tiles; ++t, ++g) {
-          if (!mbar_wait(q_full, g & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t qdesc = sw128_desc(smem_u32(q_buf));
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)
-            mma_issue<kKindBF16>(tmem, qdesc + 2 * kk, kdesc + 2 * kk, id_sa, kk != 0, 0, 0);
-          tc_commit(sa_full);
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)
-            mma_issue<kKindBF16>(tmem + kSB, qdesc + 2 * kk, kdesc + kHalfOff + 2 * kk, id_sb, kk != 0, 0, 0);
-          tc_commit(sb_full);
-          tc_commit(q_empty);
-          // P_A and P_B written (and the previous tile's O read back) by both groups.
-          if (!mbar_wait(pa_full, g & 1, abort_flag) || !mbar_wait(pb_full, g & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // P of keys 16i..16i+15 of a half: column 8i of the half, plus 48 for
-          // the second 96 keys (written over that softmax warp's own S columns).
-          for (int i = 0; i < kHalfA / 16; ++i)
-            mma_f16_ts(tmem + kOA, tmem + 8 * i + (i >= 6 ? 48 : 0), vdesc + kStep16 * i, id_pv, i != 0);
-          for (int i = 0; i < kHalfB / 16; ++i)
-            mma_f16_ts(tmem + kOB, tmem + kSB + 8 * i + (i >= 6 ? 48 : 0), vdesc + kHalfOff + kStep16 * i, id_pv,
-                       i != 0);
-          tc_commit(o_full);
-          if (t + 1 == tiles) tc_commit(&kv_empty[kb]);
-          // P consumed before the next tile's S MMAs overwrite it.
-          if (!mbar_wait(o_full, g & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
+        if (!mbar_wait(pa_full, g & 1, abort_flag) || (g > 0 && !mbar_wait(o_free, (g - 1) & 1, abort_flag))) break;
+        tc_fence_after();
+        // P of keys 16i..16i+15 of a half: softmax warp i/3 holds 48 keys at
+        // its own S columns 48(i/3).., two keys per column.
+        for (int i = 0; i < kHalfA / 16; ++i)
+          mma_f16_ts(tmem + kOA, tmem + 48 * (i / 3) + 8 * (i % 3), vdesc + kStep16 * i, id_pv, i != 0);
+        tc_commit(pva_done);
+        if (g + 1 < n && (!mbar_wait(pva_done, g & 1, abort_flag) || !issue_sa(g + 1))) break;
+        if (!mbar_wait(pb_full, g & 1, abort_flag)) break;
+        tc_fence_after();
+        for (int i = 0; i < kHalfB / 16; ++i)
+          mma_f16_ts(tmem + kOB, tmem + kSB + 48 * (i / 3) + 8 * (i % 3), vdesc + kHalfOff + kStep16 * i, id_pv,
+                     i != 0);
+        tc_commit(o_full);
+        if (g % tiles == tiles - 1) tc_commit(&kv_empty[kb]);
+        if (g + 1 < n) {
+          if (!mbar_wait(o_full, g & 1, abort_flag)) break;
+          issue_sb(g + 1);
         }
       }
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int half = warp >> 3;               // 0: keys [0, 192), 1: keys [192, 368)
-    const int sub = (warp >> 2) & 1;          // which 96 keys of the half
-    const int quarter = warp & 3;             // TMEM lanes 32*quarter..
+    // Warp (sub, quarter): TMEM lanes 32*quarter.. (one query row per thread),
+    // keys 48*sub.. of half A and 192 + 48*sub.. of half B (32 keys for sub 3).
+    const int sub = warp >> 2;
+    const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t s_col = (half ? kSB : 0u) + sub * kSubKeys;          // first S column of this warp
-    // P (2 keys per column) goes over this warp's own, already read S columns:
-    // keys 96s..96s+95 of a half at columns 96s..96s+47 of that half.
-    const uint32_t p_col = s_col;
-    // keys of this warp below seq (only half B's second quarter is partial)
-    const int valid = min(kSubKeys, seq - (half * kHalfA + sub * kSubKeys));
-    uint64_t* s_bar = half ? sb_full : sa_full;
-    uint64_t* p_bar = half ? pb_full : pa_full;
-    const int q_slot = half * 2 + sub;        // (m, l) slot of this warp
+    const uint32_t col_a = 48 * sub, col_b = kSB + 48 * sub;
+    const int valid_a = min(48, seq - 48 * sub);
+    const int valid_b = min(sub == 3 ? 32 : 48, seq - kHalfA - 48 * sub);
+    // previous tile, whose epilogue runs between this tile's two halves
+    int pb = 0, ph = 0, pt = 0, pg = -1;
+    float pma = 0.0f, pmb = 0.0f;
+    // The epilogue of tile pg: O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) /
+    // (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), 16 of the 64 dims per warp.
+    auto epilogue = [&]() -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(o_full, pg & 1, abort_flag))) return false;
+      tc_fence_after();
+      uint32_t lv[8], oa[16], ob[16], w[8];
+      const int dim0 = sub * 16;
+      tmem_ld8(lane_base + kLCol + (pg & 1) * 8, lv);
+      tmem_ld16(lane_base + kOA + dim0, oa);
+      tmem_ld16(lane_base + kOB + dim0, ob);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(o_free);
+      const float la = (__uint_as_float(lv[0]) + __uint_as_float(lv[1])) +
+                       (__uint_as_float(lv[2]) + __uint_as_float(lv[3]));
+      const float lb = (__uint_as_float(lv[4]) + __uint_as_float(lv[5])) +
+                       (__uint_as_float(lv[6]) + __uint_as_float(lv[7]));
+      const float mx = fmaxf(pma, pmb);
+      const float fa = pma == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(pma, mx), scale_log2));
+      const float fb = pmb == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(pmb, mx), scale_log2));
+      const float inv = 1.0f / (la * fa + lb * fb);
+      const float wa = fa * inv, wb = fb * inv;
+      uint32_t am = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x0 = __uint_as_float(oa[2 * i]) * wa + __uint_as_float(ob[2 * i]) * wb;
+        const float x1 = __uint_as_float(oa[2 * i + 1]) * wa + __uint_as_float(ob[2 * i + 1]) * wb;
+        w[i] = pack2(x0, x1, F16);
+        am = __vmaxu2(am, w[i] & 0x7fff7fffu);
+      }
+      // Each warp's 32 rows x 16 dims leave by one TMA store of its own 1 KB
+      // piece (rows past `seq` are clipped by the tensor map): wait until the
+      // warp's previous store has read the piece, write it, store it.
+      uint8_t* piece = o_buf + warp * 1024;
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+      *reinterpret_cast<uint4*>(piece + lane * 32 + (((0 ^ (lane >> 2)) & 1) << 4)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(piece + lane * 32 + (((1 ^ (lane >> 2)) & 1) << 4)) =
+          make_uint4(w[4], w[5], w[6], w[7]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&map_out, piece, ph * kD + dim0, pt * kTileQ + quarter * 32, pb);
+        bulk_commit();
+      }
+      const int query = pt * kTileQ + row;
+      if (row_amax != nullptr && query < seq) {
+        const uint32_t m16 = max(am & 0xffffu, am >> 16);
+        atomicMax(row_amax + static_cast<size_t>(pb) * seq + query,
+                  F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
+      }
+      return true;
+    };
     int g = 0;
     bool ok = true;
     for (int p = blockIdx.x; p < pairs && ok; p += gridDim.x) {
       const int b = p / heads, h = p % heads;
       for (int t = 0; t < tiles; ++t, ++g) {
-        if (!__all_sync(0xffffffffu, mbar_wait(s_bar, g & 1, abort_flag))) {
+        float* mxg = mx_ex + (g & 1) * (2 * 4 * kTileQ);
+        const uint32_t lcol = kLCol + (g & 1) * 8;
+        // half A
+        if (!__all_sync(0xffffffffu, mbar_wait(sa_full, g & 1, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        float2* mlg = ml + (g & 1) * 4 * kTileQ;
-        // Row maximum over this warp's keys: 8 independent partial maxima
-        // (short dependency chains), combined at the end.
-        float mp[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mp[j] = __int_as_float(0xff800000);
-#pragma unroll
-        for (int ch = 0; ch < kSubKeys / 32; ++ch) {
-          uint32_t v[32];
-          tmem_ld32(lane_base + s_col + ch * 32, v);
-          tmem_ld_wait();
-          if (valid == kSubKeys || (ch + 1) * 32 <= valid) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[i]));
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (ch * 32 + i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[i]));
-          }
-        }
-        float m = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-        // the half's maximum: this warp's and its partner's (other 96 keys)
-        mlg[q_slot * kTileQ + row].x = m;
-        mbar_arrive(&mx_full[half * 4 + quarter]);
-        if (!__all_sync(0xffffffffu, mbar_wait(&mx_full[half * 4 + quarter], g & 1, abort_flag))) {
+        float ma;
+        if (!softmax_slice<48, F16>(lane_base, col_a, valid_a, scale_log2, mxg, sub, row, &mx_full[quarter],
+                                    g & 1, abort_flag, lcol + sub, ma)) {
           ok = false;
           break;
         }
-        m = fmaxf(m, mlg[(half * 2 + (sub ^ 1)) * kTileQ + row].x);
-        const float mc = m * scale_log2;
-        float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // partial sums (short chains)
-#pragma unroll
-        for (int ch = 0; ch < kSubKeys / 32; ++ch) {
-          uint32_t v[32], pk[16];
-          tmem_ld32(lane_base + s_col + ch * 32, v);
-          tmem_ld_wait();
-          if (valid == kSubKeys || (ch + 1) * 32 <= valid) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              // half the exponentials on the special-function unit, half on the FMA pipe
-              const float x0 = __fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc);
-              const float x1 = __fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc);
-              float p0, p1;
-              if (i & 1) {
-                p0 = ex2(x0);
-                p1 = ex2(x1);
-              } else {
-                const float2 e = exp2_poly2(x0, x1);
-                p0 = e.x;
-                p1 = e.y;
-              }
-              lp[i & 3] += p0 + p1;
-              pk[i] = pack2(p0, p1, F16);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int k0 = ch * 32 + 2 * i;
-              const float p0 = k0 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
-              const float p1 = k0 + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
-              lp[i & 3] += p0 + p1;
-              pk[i] = pack2(p0, p1, F16);
-            }
-          }
-          // P over S columns this thread has already read (its own 96 keys)
-          tmem_st16(lane_base + p_col + ch * 16, pk);
+        mbar_arrive(pa_full);
+        if (pg >= 0 && !epilogue()) {
+          ok = false;
+          break;
         }
-        const float l = (lp[0] + lp[1]) + (lp[2] + lp[3]);
-        mlg[q_slot * kTileQ + row] = make_float2(m, l);
-        mbar_arrive(&ml_full[quarter]);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(p_bar);
-        if (!__all_sync(0xffffffffu, mbar_wait(o_full, g & 1, abort_flag))) {
+        // half B
+        if (!__all_sync(0xffffffffu, mbar_wait(sb_full, g & 1, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // every quarter's (m, l) of this tile is in shared memory
-        if (!__all_sync(0xffffffffu, mbar_wait(&ml_full[quarter], g & 1, abort_flag))) {
+        float mb;
+        const bool done = sub == 3 ? softmax_slice<32, F16>(lane_base, col_b, valid_b, scale_log2, mxg + 4 * kTileQ,
+                                                            sub, row, &mx_full[4 + quarter], g & 1, abort_flag,
+                                                            lcol + 4 + sub, mb)
+                                   : softmax_slice<48, F16>(lane_base, col_b, valid_b, scale_log2, mxg + 4 * kTileQ,
+                                                            sub, row, &mx_full[4 + quarter], g & 1, abort_flag,
+                                                            lcol + 4 + sub, mb);
+        if (!done) {
           ok = false;
           break;
         }
-        const float2 a0 = mlg[0 * kTileQ + row], a1 = mlg[1 * kTileQ + row];
-        const float2 b0 = mlg[2 * kTileQ + row], b1 = mlg[3 * kTileQ + row];
-        const float ma = a0.x, mb = b0.x;  // both quarters of a half share its maximum
-        const float mx = fmaxf(ma, mb);
-        const float fa = ma == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(ma, mx), scale_log2));
-        const float fb = mb == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(mb, mx), scale_log2));
-        const float inv = 1.0f / ((a0.y + a1.y) * fa + (b0.y + b1.y) * fb);
-        const float wa = fa * inv, wb = fb * inv;
-        const int dim0 = (warp >> 2) * 16;    // this warp's 16 output dims
-        uint32_t oa[16], ob[16], w[8];
-        tmem_ld16(lane_base + kOA + dim0, oa);
-        tmem_ld16(lane_base + kOB + dim0, ob);
-        tmem_ld_wait();
-        tc_fence_before();
-        uint32_t am = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float x0 = __uint_as_float(oa[2 * i]) * wa + __uint_as_float(ob[2 * i]) * wb;
-          const float x1 = __uint_as_float(oa[2 * i + 1]) * wa + __uint_as_float(ob[2 * i + 1]) * wb;
-          w[i] = pack2(x0, x1, F16);
-          am = __vmaxu2(am, w[i] & 0x7fff7fffu);
-        }
-        // Each warp's 32 rows x 16 dims leave by one TMA store of its own 1 KB
-        // piece (rows past `seq` are clipped by the tensor map): wait until the
-        // warp's previous store has read the piece, write it, store it.
-        uint8_t* piece = o_buf + warp * 1024;
-        if (lane == 0) bulk_wait_read<0>();
-        __syncwarp();
-        *reinterpret_cast<uint4*>(piece + lane * 32 + (((0 ^ (lane >> 2)) & 1) << 4)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(piece + lane * 32 + (((1 ^ (lane >> 2)) & 1) << 4)) =
-            make_uint4(w[4], w[5], w[6], w[7]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&map_out, piece, h * kD + dim0, t * kTileQ + quarter * 32, b);
-          bulk_commit();
-        }
-        const int query = t * kTileQ + row;
-        if (row_amax != nullptr && query < seq) {
-          const uint32_t m16 = max(am & 0xffffu, am >> 16);
-          atomicMax(row_amax + static_cast<size_t>(b) * seq + query,
-                    F16 ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16));
-        }
-        if (!__all_sync(0xffffffffu, ok)) break;
+        mbar_arrive(pb_full);
+        pb = b, ph = h, pt = t, pg = g, pma = ma, pmb = mb;
       }
     }
+    if (ok && pg >= 0) epilogue();
   }
   if (lane == 0 && warp < kSoftWarps) bulk_wait_all();  // output stores complete before the CTA exits
   tc_fence_before();

@@ -633,14 +633,38 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
                 const float* res = g.residual ? static_cast<const float*>(g.residual) +
                                                     static_cast<size_t>(row) * g.ldr + c0
                                               : nullptr;
+                float x[kSub];
 #pragma unroll
                 for (int i = 0; i < kSub; ++i) {
-                  if (i < vh) {
-                    float x = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
-                    if (g.bias) x = __fadd_rn(x, bias[i]);
-                    if (res) x = __fadd_rn(res[i], x);
-                    dst[i] = x;
-                    if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(x);
+                  x[i] = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
+                  if (g.bias) x[i] = __fadd_rn(x[i], bias[i]);
+                }
+                // A full, 16-byte-aligned piece leaves by 16-byte stores (the row's
+                // kSub * 4 bytes are contiguous); edges element by element.
+                const bool vec = vh >= kSub && ((reinterpret_cast<uintptr_t>(dst) |
+                                                 reinterpret_cast<uintptr_t>(res)) & 15) == 0;
+                if (vec) {
+#pragma unroll
+                  for (int i = 0; i < kSub / 4; ++i) {
+                    float4 y = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+                    if (res) {
+                      const float4 r = *reinterpret_cast<const float4*>(res + 4 * i);
+                      y = make_float4(__fadd_rn(r.x, y.x), __fadd_rn(r.y, y.y), __fadd_rn(r.z, y.z),
+                                      __fadd_rn(r.w, y.w));
+                    }
+                    *reinterpret_cast<float4*>(dst + 4 * i) = y;
+                    if constexpr (KIND == kGemmMXF8)
+                      nonfinite |= !isfinite(y.x) || !isfinite(y.y) || !isfinite(y.z) || !isfinite(y.w);
+                  }
+                } else {
+#pragma unroll
+                  for (int i = 0; i < kSub; ++i) {
+                    if (i < vh) {
+                      float y = x[i];
+                      if (res) y = __fadd_rn(res[i], y);
+                      dst[i] = y;
+                      if constexpr (KIND == kGemmMXF8) nonfinite |= !isfinite(y);
+                    }
                   }
                 }
               }

@@ -382,8 +382,10 @@ __global__ void __launch_bounds__(256) rms_mxfp8_kernel(
 // normalises and quantises the current one (the single-row form is bound by
 // the load latency of its one row).  MX = false: INT8 per-token output
 // (q int8 [rows, kp] + fp32 scales); MX = true: MXFP8 (q E4M3 + packed scales).
+// Up to 4 groups per lane (rows of <= 1024) the registers are capped so that
+// three CTAs (24 warps) share an SM: more rows in flight per SM.
 template <bool F16IN, bool MX, int G>
-__global__ void __launch_bounds__(256) rms_rows16_kernel(
+__global__ void __launch_bounds__(256, G <= 4 ? 3 : 1) rms_rows16_kernel(
     const uint16_t* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows, int width,
     int kp, int blocks4, int bound_f16, void* __restrict__ q, void* __restrict__ scales, unsigned* status,
     unsigned layer) {

@@ -82,14 +82,32 @@ __global__ void stem_gather_kernel(const float* __restrict__ spatial, const floa
   reinterpret_cast<uint32_t*>(a)[idx] = *reinterpret_cast<const uint32_t*>(&p);
 }
 
-// g = bf16(silu(x * gamma + beta)) over [rows, c] bf16.
+// g = bf16(silu(x * gamma + beta)) over [rows, c] bf16, c a multiple of 8:
+// each thread converts 8 consecutive values (one 16-byte load and store).
 __global__ void trunk_tip_kernel(const uint16_t* __restrict__ x, const float* __restrict__ gamma,
-                                 const float* __restrict__ beta, uint16_t* __restrict__ g, long total, int c) {
-  const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= total) return;
-  const int col = static_cast<int>(i % c);
-  const float v = __fadd_rn(__fmul_rn(from_bf16(x[i]), __ldg(gamma + col)), __ldg(beta + col));
-  g[i] = bits_bf16(kb_silu(v));
+                                 const float* __restrict__ beta, uint16_t* __restrict__ g, long total8, int c8) {
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total8;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int col = static_cast<int>(i % c8) * 8;
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x) + i);
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + col));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + col) + 1);
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta + col));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta + col) + 1);
+    const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float bt[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = from_bf16(static_cast<uint16_t>(w[j] & 0xffffu));
+      const float hi = from_bf16(static_cast<uint16_t>(w[j] >> 16));
+      const float v0 = __fadd_rn(__fmul_rn(lo, gm[2 * j]), bt[2 * j]);
+      const float v1 = __fadd_rn(__fmul_rn(hi, gm[2 * j + 1]), bt[2 * j + 1]);
+      o[j] = static_cast<uint32_t>(bits_bf16(kb_silu(v0))) | (static_cast<uint32_t>(bits_bf16(kb_silu(v1))) << 16);
+    }
+    reinterpret_cast<uint4*>(g)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 struct HeadWeights {
@@ -111,13 +129,35 @@ struct HeadWeights {
 };
 
 constexpr int kHeadThreads = 384;
+constexpr int kHeadWarps = kHeadThreads / 32;
 
-// One CTA per position.  hp: [B*361, 384] fp32 = [p1 | g1 + bias | v1 + bias].
+// SiLU for the fp32 heads (compared with a tolerance, not bit for bit):
+// x / (1 + e^-x) with the fast exponential and division.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// Warp-cooperative dot product of a weight row (k floats, global) with a
+// vector in shared memory; every lane returns the sum (fixed reduction order).
+__device__ __forceinline__ float warp_dot(const float* __restrict__ wrow, const float* vec, int k, int lane) {
+  float a = 0.0f;
+  for (int i = lane; i < k; i += 32) a = __fmaf_rn(__ldg(wrow + i), vec[i], a);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  return a;
+}
+
+// One CTA (12 warps) per position.  hp: [B*361, 384] fp32 = [p1 | g1 + bias | v1 + bias].
+// Pass 1: warp w pools tokens w, w+12, ...; lane l owns float4 columns l,
+// l+32 and l+64 (< 72) of the 288 [g1 | v1] columns, so every row is read
+// coalesced; per-warp partial sums / maxima are combined in a fixed order.
+// Then the small matrix-vector products, one warp per output, and pass 2:
+// per token, lanes split the 96 p1 and 192 v1 channels and the 7 outputs
+// (6 policy moves, ownership) are warp reductions.
 __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __restrict__ hp, HeadWeights w,
                                                             float* __restrict__ policy, float* __restrict__ value,
                                                             float* __restrict__ misc, float* __restrict__ moremisc,
                                                             float* __restrict__ ownership, unsigned* status) {
-  bool bad = false;
+  __shared__ float part_sum[kHeadWarps][288];
+  __shared__ float part_max[kHeadWarps][96];
   __shared__ float pooled_p[288];
   __shared__ float pooled_v[576];
   __shared__ float gproj[96];
@@ -125,95 +165,173 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
   __shared__ float vhid[192];
   __shared__ float conv2p[6 * 96];
   __shared__ float ownw[192];
+  __shared__ int bad_any;
   const int b = blockIdx.x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float* rows = hp + static_cast<size_t>(b) * kSeq * 384;
-  // Pooling: thread c < 96 handles g1 channel c (SiLU then mean, max);
-  // threads 96..287 handle v1 channels (SiLU then mean).
-  if (tid < 96) {
-    float sum = 0.0f, mx = __int_as_float(0xff800000);
-    for (int t = 0; t < kSeq; ++t) {
-      const float a = kb_silu(rows[t * 384 + 96 + tid]);
-      sum += a;
-      mx = fmaxf(mx, a);
-    }
-    const float mean = sum / static_cast<float>(kSeq);
-    pooled_p[tid] = mean;
-    pooled_p[96 + tid] = mean * 0.5f;
-    pooled_p[192 + tid] = mx;
-  } else if (tid < 288) {
-    const int ch = tid - 96;
-    float sum = 0.0f;
-    for (int t = 0; t < kSeq; ++t) sum += kb_silu(rows[t * 384 + 192 + ch]);
-    const float mean = sum / static_cast<float>(kSeq);
-    pooled_v[ch] = mean;
-    pooled_v[192 + ch] = mean * 0.5f;
-    pooled_v[384 + ch] = mean * 0.15f;
-  }
+  if (tid == 0) bad_any = 0;
   for (int i = tid; i < 6 * 96; i += kHeadThreads) conv2p[i] = w.conv2p_w[i];
   for (int i = tid; i < 192; i += kHeadThreads) ownw[i] = w.own_w[i];
-  __syncthreads();
-  // Small matrix-vector products.
-  if (tid < 96) {
-    float a = 0.0f, p = 0.0f;
-    for (int k = 0; k < 288; ++k) {
-      a += pooled_p[k] * w.g_matmul[tid * 288 + k];
-      p += pooled_p[k] * w.pass1_w[tid * 288 + k];
+  {
+    // ---- pass 1: SiLU then mean (g1 and v1) and max (g1)
+    const int nq = lane < 8 ? 3 : 2;  // float4 columns of this lane
+    float sum[12], mx[4];
+#pragma unroll
+    for (int i = 0; i < 12; ++i) sum[i] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mx[i] = __int_as_float(0xff800000);
+    for (int t = warp; t < kSeq; t += kHeadWarps) {
+      const float4* r4 = reinterpret_cast<const float4*>(rows + static_cast<size_t>(t) * 384 + 96);
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        if (q < nq) {
+          const float4 v = __ldg(r4 + lane + 32 * q);
+          const float a[4] = {silu_fast(v.x), silu_fast(v.y), silu_fast(v.z), silu_fast(v.w)};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            sum[4 * q + e] += a[e];
+            if (q == 0) mx[e] = fmaxf(mx[e], a[e]);
+          }
+        }
+      }
     }
-    gproj[tid] = a + w.bias2[tid];
-    pass1[tid] = kb_silu(p + w.pass1_b[tid]);
-  } else if (tid < 288) {
-    const int ch = tid - 96;
-    float a = 0.0f;
-    for (int k = 0; k < 576; ++k) a += pooled_v[k] * w.v2_w[ch * 576 + k];
-    vhid[ch] = kb_silu(a + w.v2_b[ch]);
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+      if (q < nq)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) part_sum[warp][4 * (lane + 32 * q) + e] = sum[4 * q + e];
+    if (lane < 24)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) part_max[warp][4 * lane + e] = mx[e];
+  }
+  __syncthreads();
+  if (tid < 288) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kHeadWarps; ++i) s += part_sum[i][tid];
+    const float mean = s * (1.0f / static_cast<float>(kSeq));
+    if (tid < 96) {
+      float m = part_max[0][tid];
+#pragma unroll
+      for (int i = 1; i < kHeadWarps; ++i) m = fmaxf(m, part_max[i][tid]);
+      pooled_p[tid] = mean;
+      pooled_p[96 + tid] = mean * 0.5f;
+      pooled_p[192 + tid] = m;
+    } else {
+      const int ch = tid - 96;
+      pooled_v[ch] = mean;
+      pooled_v[192 + ch] = mean * 0.5f;
+      pooled_v[384 + ch] = mean * 0.15f;
+    }
+  }
+  __syncthreads();
+  // ---- small matrix-vector products: outputs 0..95 gproj, 96..191 pass1, 192..383 v2
+  for (int o = warp; o < 384; o += kHeadWarps) {
+    if (o < 96) {
+      const float a = warp_dot(w.g_matmul + o * 288, pooled_p, 288, lane);
+      if (lane == 0) gproj[o] = a + w.bias2[o];
+    } else if (o < 192) {
+      const float a = warp_dot(w.pass1_w + (o - 96) * 288, pooled_p, 288, lane);
+      if (lane == 0) pass1[o - 96] = silu_fast(a + w.pass1_b[o - 96]);
+    } else {
+      const float a = warp_dot(w.v2_w + (o - 192) * 576, pooled_v, 576, lane);
+      if (lane == 0) vhid[o - 192] = silu_fast(a + w.v2_b[o - 192]);
+    }
   }
   __syncthreads();
   float* pol = policy + static_cast<size_t>(b) * 6 * 362;
-  if (tid < 6) {
-    float a = 0.0f;
-    for (int k = 0; k < 96; ++k) a += pass1[k] * w.pass2_w[tid * 96 + k];
-    pol[tid * 362 + 361] = a;
-    bad |= !isfinite(a);
-  } else if (tid >= 32 && tid < 32 + 21) {
-    const int o = tid - 32;
-    const float* wr;
-    float bias;
-    float* dst;
-    if (o < 3) {
-      wr = w.value_w + o * 192, bias = w.value_b[o], dst = value + b * 3 + o;
-    } else if (o < 13) {
-      wr = w.misc_w + (o - 3) * 192, bias = w.misc_b[o - 3], dst = misc + b * 10 + (o - 3);
+  bool bad = false;
+  // ---- pass logits (6) and value / misc / moremisc (21), one warp per output
+  for (int o = warp; o < 27; o += kHeadWarps) {
+    if (o < 6) {
+      const float a = warp_dot(w.pass2_w + o * 96, pass1, 96, lane);
+      if (lane == 0) {
+        pol[o * 362 + 361] = a;
+        bad |= !isfinite(a);
+      }
     } else {
-      wr = w.moremisc_w + (o - 13) * 192, bias = w.moremisc_b[o - 13], dst = moremisc + b * 8 + (o - 13);
+      const int v = o - 6;
+      const float* wr;
+      float bias;
+      float* dst;
+      if (v < 3) {
+        wr = w.value_w + v * 192, bias = w.value_b[v], dst = value + b * 3 + v;
+      } else if (v < 13) {
+        wr = w.misc_w + (v - 3) * 192, bias = w.misc_b[v - 3], dst = misc + b * 10 + (v - 3);
+      } else {
+        wr = w.moremisc_w + (v - 13) * 192, bias = w.moremisc_b[v - 13], dst = moremisc + b * 8 + (v - 13);
+      }
+      const float a = warp_dot(wr, vhid, 192, lane) + bias;
+      if (lane == 0) {
+        *dst = a;
+        bad |= !isfinite(a);
+      }
     }
-    float a = 0.0f;
-    for (int k = 0; k < 192; ++k) a += vhid[k] * wr[k];
-    *dst = a + bias;
-    bad |= !isfinite(a + bias);
   }
-  // Per-token policy moves and ownership.
-  for (int t = tid; t < kSeq; t += kHeadThreads) {
-    const float* r = rows + t * 384;
-    float mv[6] = {0, 0, 0, 0, 0, 0};
-    for (int ch = 0; ch < 96; ++ch) {
-      const float pa = kb_silu(r[ch] + gproj[ch]);
+  // ---- pass 2: per token, policy moves (6) and ownership
+  {
+    float gp[4], cw[6][4], ow[8];
+    if (lane < 24)
 #pragma unroll
-      for (int o = 0; o < 6; ++o) mv[o] += pa * conv2p[o * 96 + ch];
-    }
+      for (int e = 0; e < 4; ++e) {
+        gp[e] = gproj[4 * lane + e];
 #pragma unroll
-    for (int o = 0; o < 6; ++o) {
-      pol[o * 362 + t] = mv[o];
-      bad |= !isfinite(mv[o]);
+        for (int o = 0; o < 6; ++o) cw[o][e] = conv2p[o * 96 + 4 * lane + e];
+      }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      ow[e] = ownw[4 * lane + e];
+      ow[4 + e] = lane < 16 ? ownw[128 + 4 * lane + e] : 0.0f;
     }
-    float own = 0.0f;
-    for (int ch = 0; ch < 192; ++ch) own += kb_silu(r[192 + ch]) * ownw[ch];
-    ownership[static_cast<size_t>(b) * kSeq + t] = own;
-    bad |= !isfinite(own);
+    for (int t = warp; t < kSeq; t += kHeadWarps) {
+      const float* r = rows + static_cast<size_t>(t) * 384;
+      float acc[7] = {0, 0, 0, 0, 0, 0, 0};
+      if (lane < 24) {
+        const float4 p = __ldg(reinterpret_cast<const float4*>(r) + lane);
+        const float pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pa = silu_fast(pv[e] + gp[e]);
+#pragma unroll
+          for (int o = 0; o < 6; ++o) acc[o] = __fmaf_rn(pa, cw[o][e], acc[o]);
+        }
+      }
+      {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(r + 192) + lane);
+        acc[6] = __fmaf_rn(silu_fast(v.x), ow[0], acc[6]);
+        acc[6] = __fmaf_rn(silu_fast(v.y), ow[1], acc[6]);
+        acc[6] = __fmaf_rn(silu_fast(v.z), ow[2], acc[6]);
+        acc[6] = __fmaf_rn(silu_fast(v.w), ow[3], acc[6]);
+        if (lane < 16) {
+          const float4 u = __ldg(reinterpret_cast<const float4*>(r + 320) + lane);
+          acc[6] = __fmaf_rn(silu_fast(u.x), ow[4], acc[6]);
+          acc[6] = __fmaf_rn(silu_fast(u.y), ow[5], acc[6]);
+          acc[6] = __fmaf_rn(silu_fast(u.z), ow[6], acc[6]);
+          acc[6] = __fmaf_rn(silu_fast(u.w), ow[7], acc[6]);
+        }
+      }
+#pragma unroll
+      for (int o = 0; o < 7; ++o)
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], sh);
+      if (lane < 6) {
+        float a = acc[0];
+#pragma unroll
+        for (int o = 1; o < 6; ++o)
+          if (lane == o) a = acc[o];
+        pol[lane * 362 + t] = a;
+        bad |= !isfinite(a);
+      } else if (lane == 6) {
+        ownership[static_cast<size_t>(b) * kSeq + t] = acc[6];
+        bad |= !isfinite(acc[6]);
+      }
+    }
   }
   // Sticky status: a non-finite value reached an output (reference
   // mxfp8_check_final_outputs_kernel, cuda-kernels/mxfp8.cu:162-177).
-  if (bad) record_status(status, KB_STATUS_OUTPUT_NONFINITE, 0xfffffffeu);
+  if (bad) atomicOr(&bad_any, 1);
+  __syncthreads();
+  if (tid == 0 && bad_any) record_status(status, KB_STATUS_OUTPUT_NONFINITE, 0xfffffffeu);
 }
 
 }  // namespace
@@ -228,8 +346,16 @@ int stem_gather_launch(const float* spatial, const float* global, const int* sym
 
 int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, uint16_t* g, long rows, int c,
                      cudaStream_t s) {
-  const long total = rows * c;
-  trunk_tip_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(x, gamma, beta, g, total, c);
+  if (c % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(g) & 15) ||
+      (reinterpret_cast<uintptr_t>(gamma) & 15) || (reinterpret_cast<uintptr_t>(beta) & 15)) {
+    set_error("trunk tip: channels must be a multiple of 8 and buffers 16-byte aligned");
+    return KB_E_INVALID;
+  }
+  const long total8 = rows * c / 8;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long want = (total8 + 255) / 256, cap = 8L * num_sms(dev);
+  trunk_tip_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(x, gamma, beta, g, total8, c / 8);
   return check_cuda(cudaGetLastError(), "trunk tip launch");
 }
 

@@ -47,6 +47,27 @@ def test_attention_matches_oracle(cuda, oracle, heads, hd, batch):
     assert np.abs(got - ref).max() < 3e-2 * np.abs(ref).max()
 
 
+@pytest.mark.parametrize("batch,scale", [(1, 1.5), (5, 1.5), (3, 6.0)])
+def test_attention_prerotated_matches_oracle(cuda, oracle, batch, scale):
+    """The trunk's path: NULL rope tables (Q and K already rotated by the QKV
+    projection), head_dim 64, 12 heads; several positions per CTA and large
+    logits (scale 6: sharply peaked softmax, so the half maxima differ)."""
+    torch = cuda
+    rng = np.random.default_rng(batch * 7 + int(scale))
+    heads, hd = 12, 64
+    c = heads * hd
+    qkv = oracle.bf16_encode((rng.standard_normal((batch * 361, 3 * c)) * scale).astype(np.float32))
+    out = torch.zeros((batch * 361, c), dtype=torch.int16, device="cuda")
+    dq = torch.from_numpy(np.ascontiguousarray(qkv.view(np.int16))).cuda()
+    _capi.call("kb_attention", dq.data_ptr(), None, None, out.data_ptr(), batch, heads, hd,
+               1.0 / math.sqrt(hd), _capi.DT_BF16, int(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    got = oracle.decode16(out.cpu().numpy().view(np.uint16), False)
+    ref = otrunk.attention(oracle.decode16(qkv, False), None, None, batch, heads, hd, rotate=False)
+    assert rel_l2(got, ref) < 5e-3
+    assert np.abs(got - ref).max() < 3e-2 * np.abs(ref).max()
+
+
 def run_trunk(topo, blob, spatial, glob, max_batch=None):
     model = backend.CudaBackend.load_model(topo, blob)
     h = backend.CudaBackend.create_compute_handle(model, max_batch or spatial.shape[0])
@@ -185,3 +206,31 @@ def test_full_batch_256_properties(cuda):
         one = h1.get_output(spatial[i:i + 1], glob[i:i + 1])
         assert np.array_equal(one.policy[0], full.policy[i])
         assert np.array_equal(one.value[0], full.value[i])
+
+
+@pytest.mark.parametrize("nhwc", [False, True], ids=["nchw", "nhwc"])
+def test_submit_symmetry_matches_host_copy(cuda, nhwc):
+    """kb_submit with per-row symmetries gives, bit for bit, what the reference's
+    host-side copy_inputs_with_symmetry (cuda.rs:2234-2245, restated in
+    oracle/symmetry.py) followed by an identity submit gives, in either input
+    layout."""
+    from oracle import symmetry as osym
+
+    topo = SMALL
+    blob = synthetic.make_blob(topo, 5)
+    spatial, glob = synthetic.make_positions(8, 31)
+    if nhwc:
+        spatial = np.ascontiguousarray(spatial.transpose(0, 2, 3, 1))
+    sym = np.arange(8, dtype=np.int32)
+    model = backend.CudaBackend.load_model(topo, blob)
+    h = backend.CudaBackend.create_compute_handle(model, 8, inputs_nhwc=nhwc)
+    got = h.get_output(spatial, glob, sym)
+    host = h.get_output(osym.apply_to_positions(spatial, sym, nhwc), glob)
+    for f in ("policy", "value", "misc", "moremisc", "ownership"):
+        assert np.array_equal(getattr(got, f), getattr(host, f)), f
+    ident = h.get_output(spatial, glob, np.zeros(8, np.int32))
+    plain = h.get_output(spatial, glob)
+    assert np.array_equal(ident.policy, plain.policy)
+    with pytest.raises(_capi.KbError, match="0..7"):
+        h.get_output(spatial, glob, np.full(8, 8, np.int32))
+
