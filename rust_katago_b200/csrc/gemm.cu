@@ -429,16 +429,17 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     int acc = 0;
     uint32_t aph = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag))) break;
-      tc_fence_after();
       const int mb = tile / tiles_n, nb = tile % tiles_n;
       const int row0q = mb * kBM + quarter * 32;
       const int row = row0q + lane;
       const bool row_ok = row < g.m;
       int token = 0;
       if constexpr (EPI == kEpiRope16) token = row_ok ? row % g.rope_seq : 0;
+      // the row scale is loaded while the accumulator is still being computed
       float sa = 1.0f;
       if constexpr (KIND == kGemmI8 && EPI != kEpiI32) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag))) break;
+      tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
       uint32_t amax = 0;
@@ -513,11 +514,14 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
 #pragma unroll
             for (int hh = 0; hh < kHalves; ++hh) {
               const int c0 = col0 + hh * kSub;
+              // The accumulator read and this piece's column scales, bias and
+              // rotary tables are all in flight before the wait.
               uint32_t v[kSub];
               tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, v);
-              tmem_ld_wait();
               float sw[kSub];
               if constexpr (KIND == kGemmI8) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
+              float bias[kSub];
+              if (with_bias) load_vecn<kSub>(g.bias, c0, g.n, bias);
               // Rotary tables of these kSub / 2 pairs (kEpiRope16, Q and K columns).
               float rc[kSub / 2], rs[kSub / 2];
               bool rope = false;
@@ -541,12 +545,11 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
                   for (int i = 0; i < kSub / 2; ++i) rc[i] = 1.0f, rs[i] = 0.0f;
                 }
               }
+              tmem_ld_wait();
               // Separate unrolled bodies with and without bias (warp-uniform
               // choice), so a bias-free projection issues no adds.
               auto finish = [&](auto bias_tag) {
                 constexpr bool kBias = decltype(bias_tag)::value;
-                float bias[kSub];
-                if constexpr (kBias) load_vecn<kSub>(g.bias, c0, g.n, bias);
 #pragma unroll
                 for (int i = 0; i < kSub / 2; ++i) {
                   float2 x = acc_pairn<KIND, kSub>(v, i, sa, sw);
