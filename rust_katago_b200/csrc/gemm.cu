@@ -62,12 +62,12 @@ struct GemmCfg {
   static constexpr int kSfBytes = KIND == kGemmMXF8 ? 512 + 512 * (BN / 128) : 0;
   static constexpr int kSfCols = KIND == kGemmMXF8 ? 4 + 4 * (BN / 128) : 0;
   static constexpr int kStagingBytes = EW * SB * kStageTile;
-  static constexpr int kStages = (kSmemLimit - kStagingBytes - 1024 - 256) / (kStageBytes + kSfBytes);
+  static constexpr int kStages = (kSmemLimit - kStagingBytes - 1024 - 512) / (kStageBytes + kSfBytes);
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kSfRingBytes = kStages * kSfBytes;
   static constexpr uint32_t kTmemCols = pow2_cols(2 * BN + kStages * kSfCols);
   static constexpr int kSmemBytes =
-      kRingBytes + kStagingBytes + kSfRingBytes + 1024 /*align*/ + 256 /*barriers*/;
+      kRingBytes + kStagingBytes + kSfRingBytes + 1024 /*align*/ + 512 /*barriers*/;
   static_assert(kStages >= 3, "ring too shallow");
   static_assert(2 * BN + kStages * kSfCols <= 512, "TMEM columns exceeded");
 };
@@ -285,6 +285,8 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* res_bar = tempty + 3;  // [epilogue warp][SB]: residual tiles landed (Res16 through TMA)
+  static_assert((2 * kStages + 5 + kEpiWarps * SB) * 8 <= 512, "barrier area exceeded");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -302,6 +304,8 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], kEpiWarps);
     }
+    if constexpr (EPI == kEpiRes16)
+      for (int i = 0; i < kEpiWarps * SB; ++i) mbar_init(&res_bar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -428,6 +432,130 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     const bool f16 = (EPI == kEpiF16) ? true : (g.out_f16 != 0);
     int acc = 0;
     uint32_t aph = 0;
+    bool handled = false;
+    if constexpr (EPI == kEpiRes16) {
+      if (use_tma_out) {
+        handled = true;
+        // ---- residual through shared memory.  Each warp walks a stream of
+        // 32x32 chunks (its columns of each tile, tile after tile); the 16-bit
+        // residual of a chunk is TMA-loaded into a staging tile kLook chunks
+        // ahead (the stream runs across tiles, so the next tile's first
+        // residuals are in flight while this one finishes), the dequantised
+        // accumulator is added in place and the tile is TMA-stored back with
+        // the same tensor map (64-byte swizzle, out-of-range rows and columns
+        // read as zero and are clipped on the store).
+        constexpr int kLook = SB >= 4 ? 2 : 1;
+        static_assert(SB - kLook - 1 >= 0, "residual staging needs SB > kLook");
+        constexpr int kChunksR = BN / 32 / kParts;
+        uint8_t* stage = staging + e * SB * kStageTile;
+        uint64_t* rbar = res_bar + e * SB;
+        auto chunk_col = [&](int t, int jj) { return (t % tiles_n) * BN + (part * kChunksR + jj) * 32; };
+        int ld_tile = blockIdx.x, ld_jj = 0, ld_n = 0;  // next chunk to load; loads issued
+        auto issue_load = [&]() {  // lane 0
+          while (ld_tile < num_tiles && chunk_col(ld_tile, ld_jj) >= g.n)
+            if (++ld_jj == kChunksR) ld_jj = 0, ld_tile += gridDim.x;
+          if (ld_tile >= num_tiles) return;
+          const int b = ld_n % SB;
+          mbar_arrive_expect_tx(&rbar[b], kStageTile);
+          tma_load_2d(stage + b * kStageTile, &tmap_out, &rbar[b], chunk_col(ld_tile, ld_jj),
+                      (ld_tile / tiles_n) * kBM + quarter * 32);
+          ++ld_n;
+          if (++ld_jj == kChunksR) ld_jj = 0, ld_tile += gridDim.x;
+        };
+        if (lane == 0)
+          for (int i = 0; i < kLook; ++i) issue_load();
+        int sq = 0;  // chunks processed
+        bool ok = true;
+        const bool with_bias = g.bias != nullptr;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+          const int mb = tile / tiles_n;
+          const int row0q = mb * kBM + quarter * 32;
+          const int row = row0q + lane;
+          const bool row_ok = row < g.m;
+          float sa = 1.0f;
+          if constexpr (KIND == kGemmI8) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
+          if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                 static_cast<uint32_t>(acc * BN);
+          bool nonfinite = false;
+#pragma unroll 1
+          for (int jj = 0; jj < kChunksR; ++jj) {
+            const int j = part * kChunksR + jj;
+            const int col0 = chunk_col(tile, jj);
+            if (col0 >= g.n) continue;  // warp-uniform
+            // the load kLook chunks ahead reuses the staging tile of chunk
+            // sq + kLook - SB, whose store must have read it
+            if (lane == 0) {
+              bulk_wait_read<SB - kLook - 1>();
+              issue_load();
+            }
+            uint8_t* buf = stage + (sq % SB) * kStageTile;
+            uint32_t v[32];
+            tmem_ldn<32>(taddr + j * 32, v);
+            float sw[32], bias[32];
+            if constexpr (KIND == kGemmI8) load_vecn<32>(g.col_scale, col0, g.n, sw);
+            if (with_bias) load_vecn<32>(g.bias, col0, g.n, bias);
+            tmem_ld_wait();
+            if (!__all_sync(0xffffffffu, mbar_wait(&rbar[sq % SB], (sq / SB) & 1, abort_flag))) {
+              ok = false;
+              break;
+            }
+            const int swz = (lane >> 1) & 3;
+            uint32_t amax2 = 0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint4* cell = reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ swz) << 4));
+              const uint4 r4 = *cell;
+              const uint32_t rw[4] = {r4.x, r4.y, r4.z, r4.w};
+              uint32_t ow[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int i = 4 * c + q;
+                float2 x = acc_pairn<KIND, 32>(v, i, sa, sw);
+                if (with_bias) {
+                  x.x = __fadd_rn(x.x, bias[2 * i]);
+                  x.y = __fadd_rn(x.y, bias[2 * i + 1]);
+                }
+                const float2 r = unpack16x2(rw[q], f16);
+                ow[q] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
+                if constexpr (KIND == kGemmMXF8) amax2 = __vmaxu2(amax2, ow[q] & 0x7fff7fffu);
+              }
+              *cell = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            }
+            if constexpr (KIND == kGemmMXF8)
+              nonfinite |= row_ok && max(amax2 & 0xffffu, amax2 >> 16) >= (f16 ? 0x7c00u : 0x7f80u);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmap_out, buf, col0, row0q);
+              bulk_commit();
+            }
+            ++sq;
+          }
+          if (!ok) break;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+          if constexpr (KIND == kGemmMXF8) {
+            if (__any_sync(0xffffffffu, nonfinite) && lane == 0)
+              record_status(g.status, KB_STATUS_OUTPUT_NONFINITE, g.layer);
+          }
+          acc ^= 1;
+          if (acc == 0) aph ^= 1;
+        }
+        if (lane == 0) {
+          // residual loads still in flight (an aborted walk) land before exit
+          int local_abort = 0;
+          for (int i = sq; i < ld_n; ++i) mbar_wait(&rbar[i % SB], (i / SB) & 1, &local_abort);
+          bulk_wait_all();
+        }
+      }
+    }
+    if (!handled) {
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int mb = tile / tiles_n, nb = tile % tiles_n;
       const int row0q = mb * kBM + quarter * 32;
@@ -689,6 +817,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
       if (acc == 0) aph ^= 1;
     }
     if (lane == 0 && use_tma_out) bulk_wait_all();
+    }
   }
 
   tc_fence_before();
