@@ -102,7 +102,10 @@ KB_API int kb_int8_gemm_i32(const int8_t* a, const int8_t* w, int32_t* dots, int
                      uintptr_t stream);
 
 /* tcgen05 INT8 GEMM with a fused epilogue (KB_EPI_*).  out has row stride ldo
- * elements; for KB_EPI_RES_* it is read and written in place.  out_dtype selects
+ * elements; for KB_EPI_RES_* it is read and written in place.  The dequantised
+ * value is (f32(dot) * sa) * sw with two rounded multiplies (the reference's
+ * order); with a bias (nullable, [n]) it is fma(f32(dot) * sa, sw, bias), the
+ * bias added by the same fused multiply-add.  out_dtype selects
  * fp16/bf16 for the 16-bit epilogues.  row_amax (nullable, [m] uint32) receives
  * an atomic max of |output| bits for a following per-token quantiser.
  * n_out: logical output width for KB_EPI_SWIGLU16 (hidden), ignored otherwise.

@@ -73,6 +73,7 @@ def lib() -> ctypes.CDLL:
             "or_int8_rms_quantize": (None, [P, I, I, I, P, F, I, I, P, P, P]),
             "or_igemm": (None, [P, P, I, I, I, P, I]),
             "or_dequant": (None, [P, P, P, I, I, P]),
+            "or_dequant_bias": (None, [P, P, P, P, I, I, P]),
             "or_w8a8_project_half": (None, [P, I, I, P, P, I, I, P]),
             "or_max_threads": (I, []),
         }
@@ -176,6 +177,17 @@ def igemm(a: np.ndarray, w: np.ndarray, threads: int = 0) -> np.ndarray:
     return out
 
 
+def dequant_bias(dots: np.ndarray, sa: np.ndarray, sw: np.ndarray, bias: np.ndarray) -> np.ndarray:
+    """fma(f32(dot) * sa, sw, bias): the dequant plus bias of the BASELINE
+    topology's projections, the bias added by one fused multiply-add."""
+    dots = np.ascontiguousarray(dots, dtype=np.int32)
+    m, n = dots.shape
+    out = np.zeros((m, n), np.float32)
+    lib().or_dequant_bias(_p(dots), _p(np.ascontiguousarray(sa, np.float32)), _p(np.ascontiguousarray(sw, np.float32)),
+                          _p(np.ascontiguousarray(bias, np.float32)), m, n, _p(out))
+    return out
+
+
 def dequant(dots: np.ndarray, sa: np.ndarray, sw: np.ndarray) -> np.ndarray:
     """(f32(dot) * sa) * sw with two rounded multiplies (int8_ops.cu:182)."""
     dots = np.ascontiguousarray(dots, dtype=np.int32)
@@ -235,13 +247,11 @@ def gelu_ffn_bf16(residual_bf16: np.ndarray, gamma, eps, up_w, up_b, down_w, dow
     uq, us = quantize_weights(up_w)
     dq, ds = quantize_weights(down_w)
     q, sa, normed = rms_quantize(x, gamma, eps, False, kp=uq.shape[1])
-    v = dequant(igemm(q, uq, threads), sa, us)
-    if up_b is not None:
-        v = (v + up_b[None, :].astype(np.float32)).astype(np.float32)
+    dots = igemm(q, uq, threads)
+    v = dequant(dots, sa, us) if up_b is None else dequant_bias(dots, sa, us, up_b)
     hidden = round16(act(v, 1), False)
     q2, s2 = quantize_rows(hidden, kp=dq.shape[1])
-    d = dequant(igemm(q2, dq, threads), s2, ds)
-    if down_b is not None:
-        d = (d + down_b[None, :].astype(np.float32)).astype(np.float32)
+    dots2 = igemm(q2, dq, threads)
+    d = dequant(dots2, s2, ds) if down_b is None else dequant_bias(dots2, s2, ds, down_b)
     out = bf16_encode((x + d).astype(np.float32))
     return out, {"q": q, "sa": sa, "hidden": hidden, "q2": q2, "s2": s2}

@@ -275,6 +275,18 @@ void or_dequant(const int32_t* dots, const float* sa, const float* sw, int m, in
     for (int j = 0; j < n; ++j) out[(size_t)i * n + j] = ((float)dots[(size_t)i * n + j] * sa[i]) * sw[j];
 }
 
+/* value = fma(f32(dot) * sa[row], sw[col], bias[col]): the dequant with the
+ * bias of the BASELINE topology's projections added by one fused multiply-add
+ * (the product f32(dot)*sa is rounded, then t*sw + bias is rounded once),
+ * the arithmetic of the GPU epilogue when a bias is given.  C99 fmaf is
+ * correctly rounded. */
+void or_dequant_bias(const int32_t* dots, const float* sa, const float* sw, const float* bias, int m, int n,
+                     float* out) {
+  for (int i = 0; i < m; ++i)
+    for (int j = 0; j < n; ++j)
+      out[(size_t)i * n + j] = fmaf((float)dots[(size_t)i * n + j] * sa[i], sw[j], bias[j]);
+}
+
 /* The reference's complete CPU W8A8 projection (tests/int8_kernels.rs:273-301):
  * quantise fp16 rows, integer dot, dequant, round to fp16.  Used as the timed
  * CPU baseline.  x16: [m, k] fp16 bits; wq: [n, kp]; out16: [m, n]. */

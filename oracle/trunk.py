@@ -23,7 +23,7 @@ import math
 
 import numpy as np
 
-from . import bf16_encode, decode16, dequant, igemm, quantize_rows, quantize_weights, rms_quantize, round16
+from . import bf16_encode, decode16, dequant, dequant_bias, igemm, quantize_rows, quantize_weights, rms_quantize, round16
 
 SEQ, SIDE = 361, 19
 EPS = 1e-6
@@ -200,10 +200,10 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
         q2, s2 = quantize_rows(att, kp=ow.shape[1])
         x = bf((x + dequant(igemm(q2, ow), s2, os_)).astype(np.float32))
         q3, s3, _ = rms_quantize(x, w[f"{i}.rms2"], EPS, False, kp=uw.shape[1])
-        v = (dequant(igemm(q3, uw), s3, us) + w[f"{i}.up_b"][None, :]).astype(np.float32)
+        v = dequant_bias(igemm(q3, uw), s3, us, w[f"{i}.up_b"])
         hidden = bf(act(v, 1))
         q4, s4 = quantize_rows(hidden, kp=dw.shape[1])
-        d = (dequant(igemm(q4, dw), s4, ds) + w[f"{i}.down_b"][None, :]).astype(np.float32)
+        d = dequant_bias(igemm(q4, dw), s4, ds, w[f"{i}.down_b"])
         x = bf((x + d).astype(np.float32))
     # trunk tip: silu(x*gamma + beta) (debug_exec_units.rs:272-282)
     g = bf(act(((x * w["tip_g"][None, :]).astype(np.float32) + w["tip_b"][None, :]).astype(np.float32), 2))

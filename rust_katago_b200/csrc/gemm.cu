@@ -154,6 +154,19 @@ __device__ __forceinline__ float2 unpack16x2(uint32_t w, bool f16) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
+// Running max(|acc|, |v|) per 16-bit lane of a packed pair: the magnitude is
+// exact, NaN propagates as the canonical NaN, the sign bit is an xor (callers
+// mask it).
+template <bool F16>
+__device__ __forceinline__ uint32_t hmax_abs2(uint32_t acc, uint32_t v) {
+  uint32_t r;
+  if constexpr (F16)
+    asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(v));
+  else
+    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(v));
+  return r;
+}
+
 // 32-bit float bits of the larger |half| held in a packed pair of |16-bit| values.
 __device__ __forceinline__ uint32_t amax16_to_f32bits(uint32_t m2, bool f16) {
   const uint32_t m = max(m2 & 0xffffu, m2 >> 16);
@@ -248,6 +261,9 @@ __device__ __forceinline__ float2 acc_pair(const uint32_t (&v)[32], int i, float
 }
 
 // Pair (i, i+1) of an N-column piece of a chunk (same arithmetic as acc_pair).
+// Scalar rounded multiplies: a packed multiply followed by an add (a bias, the
+// residual) may be fused by the assembler, which changes the rounding of a few
+// outputs (measured).
 template <int KIND, int N>
 __device__ __forceinline__ float2 acc_pairn(const uint32_t (&v)[N], int i, float sa, const float (&sw)[N]) {
   if constexpr (KIND == kGemmI8) {
@@ -256,6 +272,24 @@ __device__ __forceinline__ float2 acc_pairn(const uint32_t (&v)[N], int i, float
         __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[2 * i + 1])), sa), sw[2 * i + 1]));
   } else {
     return make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+  }
+}
+
+// Pair (i, i+1) plus the bias.  INT8: fma(f32(dot)*sa, sw, bias): the first
+// product rounded, then one fused multiply-add (packed; a multiply feeding an
+// explicit FMA leaves nothing for the assembler to contract).  Other kinds:
+// acc + bias.
+template <int KIND, int N>
+__device__ __forceinline__ float2 acc_bias_pairn(const uint32_t (&v)[N], int i, float sa, const float (&sw)[N],
+                                                 const float (&bias)[N]) {
+  if constexpr (KIND == kGemmI8) {
+    const float2 d = make_float2(static_cast<float>(static_cast<int>(v[2 * i])),
+                                 static_cast<float>(static_cast<int>(v[2 * i + 1])));
+    return fma2(mul2(d, make_float2(sa, sa)), make_float2(sw[2 * i], sw[2 * i + 1]),
+                make_float2(bias[2 * i], bias[2 * i + 1]));
+  } else {
+    return make_float2(__fadd_rn(__uint_as_float(v[2 * i]), bias[2 * i]),
+                       __fadd_rn(__uint_as_float(v[2 * i + 1]), bias[2 * i + 1]));
   }
 }
 
@@ -515,11 +549,8 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 const int i = 4 * c + q;
-                float2 x = acc_pairn<KIND, 32>(v, i, sa, sw);
-                if (with_bias) {
-                  x.x = __fadd_rn(x.x, bias[2 * i]);
-                  x.y = __fadd_rn(x.y, bias[2 * i + 1]);
-                }
+                const float2 x =
+                    with_bias ? acc_bias_pairn<KIND, 32>(v, i, sa, sw, bias) : acc_pairn<KIND, 32>(v, i, sa, sw);
                 const float2 r = unpack16x2(rw[q], f16);
                 ow[q] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
                 if constexpr (KIND == kGemmMXF8) amax2 = __vmaxu2(amax2, ow[q] & 0x7fff7fffu);
@@ -680,11 +711,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
                 constexpr bool kBias = decltype(bias_tag)::value;
 #pragma unroll
                 for (int i = 0; i < kSub / 2; ++i) {
-                  float2 x = acc_pairn<KIND, kSub>(v, i, sa, sw);
-                  if constexpr (kBias) {
-                    x.x = __fadd_rn(x.x, bias[2 * i]);
-                    x.y = __fadd_rn(x.y, bias[2 * i + 1]);
-                  }
+                  float2 x = kBias ? acc_bias_pairn<KIND, kSub>(v, i, sa, sw, bias) : acc_pairn<KIND, kSub>(v, i, sa, sw);
                   uint32_t& out = hw[hh * (kSub / 2) + i];
                   if constexpr (EPI == kEpiRes16) {
                     const float2 r = unpack16x2(out, f16);
@@ -712,8 +739,16 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
             if (KIND == kGemmMXF8 || (EPI != kEpiRes16 && g.row_amax != nullptr)) {
               uint32_t amax2 = 0;
               if (valid == 32) {
+                // max(|a|, |b|) per 16-bit lane in one instruction (NaN wins;
+                // the sign bits are masked off below)
+                if (f16) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) amax2 = __vmaxu2(amax2, hw[i] & 0x7fff7fffu);
+                  for (int i = 0; i < 16; ++i) amax2 = hmax_abs2<true>(amax2, hw[i]);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) amax2 = hmax_abs2<false>(amax2, hw[i]);
+                }
+                amax2 &= 0x7fff7fffu;
               } else {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
@@ -767,8 +802,12 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
                 float x[kSub];
 #pragma unroll
                 for (int i = 0; i < kSub; ++i) {
-                  x[i] = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
-                  if (g.bias) x[i] = __fadd_rn(x[i], bias[i]);
+                  if (g.bias && KIND == kGemmI8)
+                    x[i] = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[i])), sa), sw[i], bias[i]);
+                  else if (g.bias)
+                    x[i] = __fadd_rn(acc_value<KIND>(v[i], sa, 1.0f), bias[i]);
+                  else
+                    x[i] = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
                 }
                 // A full, 16-byte-aligned piece leaves by 16-byte stores (the row's
                 // kSub * 4 bytes are contiguous); edges element by element.
