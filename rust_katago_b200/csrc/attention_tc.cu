@@ -107,6 +107,13 @@ __device__ __forceinline__ float2 exp2_poly2(float x0, float x1) {
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(j.y) << 23)));
 }
 
+// Three-input maximum (fmaxf semantics: NaN operands are ignored).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Rotate one interleaved pair (x, y) by (c, s), rounded to the 16-bit type.
 __device__ __forceinline__ uint32_t rope2(uint32_t w, float c, float s, bool f16) {
   const float x = from16(static_cast<uint16_t>(w & 0xffffu), f16);
@@ -191,7 +198,8 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
   for (int j = 0; j < 8; ++j) mp[j] = __int_as_float(0xff800000);
   if (valid >= NK) {
 #pragma unroll
-    for (int i = 0; i < NK; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[i]));
+    for (int i = 0; i < NK / 2; ++i)
+      mp[i & 7] = max3(mp[i & 7], __uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
   } else {
 #pragma unroll
     for (int i = 0; i < NK; ++i)
@@ -210,19 +218,15 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
 #pragma unroll
     for (int i = 0; i < NK / 2; ++i) {
       // half the exponentials on the special-function unit, half on the FMA pipe
-      const float x0 = __fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc);
-      const float x1 = __fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc);
-      float p0, p1;
-      if (i & 1) {
-        p0 = ex2(x0);
-        p1 = ex2(x1);
-      } else {
-        const float2 e = exp2_poly2(x0, x1);
-        p0 = e.x;
-        p1 = e.y;
-      }
-      lp[i & 3] += p0 + p1;
-      pk[i] = pack2(p0, p1, F16);
+      const float2 x = fma2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                            make_float2(scale_log2, scale_log2), make_float2(-mc, -mc));
+      float2 p;
+      if (i & 1)
+        p = make_float2(ex2(x.x), ex2(x.y));
+      else
+        p = exp2_poly2(x.x, x.y);
+      lp[i & 3] += p.x + p.y;
+      pk[i] = pack2(p.x, p.y, F16);
     }
   } else {
 #pragma unroll
