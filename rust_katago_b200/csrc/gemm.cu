@@ -594,6 +594,31 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
       const bool row_ok = row < g.m;
       int token = 0;
       if constexpr (EPI == kEpiRope16) token = row_ok ? row % g.rope_seq : 0;
+      // Rotary tables (kEpiRope16) of the next kSub-column piece: each piece
+      // issues the loads of the one after it, so the tables' L2 latency
+      // overlaps a piece of work; the first piece's are loaded while the
+      // accumulator is still being computed.  [token][head][pair] layout: the
+      // pairs of Q or K column cc (even) start at token * rope_cols / 4 + cc / 2.
+      float rcn[kSub / 2], rsn[kSub / 2];
+      auto fetch_rope = [&](int c0n) {
+        if (row_ok && c0n < g.rope_cols) {
+          const int half_cols = g.rope_cols / 2;
+          const int cc = c0n < half_cols ? c0n : c0n - half_cols;
+          const size_t off = static_cast<size_t>(token) * (g.rope_cols / 4) + cc / 2;
+          const float4* pc = reinterpret_cast<const float4*>(g.rope_cos + off);
+          const float4* ps = reinterpret_cast<const float4*>(g.rope_sin + off);
+#pragma unroll
+          for (int i = 0; i < kSub / 8; ++i) {
+            const float4 a = __ldg(pc + i), b2 = __ldg(ps + i);
+            rcn[4 * i] = a.x, rcn[4 * i + 1] = a.y, rcn[4 * i + 2] = a.z, rcn[4 * i + 3] = a.w;
+            rsn[4 * i] = b2.x, rsn[4 * i + 1] = b2.y, rsn[4 * i + 2] = b2.z, rsn[4 * i + 3] = b2.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < kSub / 2; ++i) rcn[i] = 1.0f, rsn[i] = 0.0f;
+        }
+      };
+      if constexpr (EPI == kEpiRope16) fetch_rope(nb * BN + part * (BN / 32 / kParts) * 32);
       // the row scale is loaded while the accumulator is still being computed
       float sa = 1.0f;
       if constexpr (KIND == kGemmI8 && EPI != kEpiI32) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
@@ -669,7 +694,8 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
               for (int i = 0; i < 16; ++i) hw[i] = res_next[i];
               if (jj + 1 < kChunks) load_res(jj + 1);
             }
-            const bool with_bias = EPI != kEpiF16 && g.bias != nullptr;  // warp-uniform
+            // (the rotary epilogue takes no bias: its registers hold the tables)
+            const bool with_bias = EPI != kEpiF16 && EPI != kEpiRope16 && g.bias != nullptr;  // warp-uniform
 #pragma unroll
             for (int hh = 0; hh < kHalves; ++hh) {
               const int c0 = col0 + hh * kSub;
@@ -686,23 +712,10 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
               bool rope = false;
               if constexpr (EPI == kEpiRope16) {
                 rope = col0 < g.rope_cols;  // warp-uniform
-                if (rope && row_ok) {
-                  const int half_cols = g.rope_cols / 2;
-                  const int cc = c0 < half_cols ? c0 : c0 - half_cols;
-                  const size_t off = (static_cast<size_t>(token) * g.rope_heads + cc / g.rope_hd) * (g.rope_hd / 2) +
-                                     (cc % g.rope_hd) / 2;
-                  const float4* pc = reinterpret_cast<const float4*>(g.rope_cos + off);
-                  const float4* ps = reinterpret_cast<const float4*>(g.rope_sin + off);
 #pragma unroll
-                  for (int i = 0; i < kSub / 8; ++i) {
-                    const float4 a = __ldg(pc + i), b2 = __ldg(ps + i);
-                    rc[4 * i] = a.x, rc[4 * i + 1] = a.y, rc[4 * i + 2] = a.z, rc[4 * i + 3] = a.w;
-                    rs[4 * i] = b2.x, rs[4 * i + 1] = b2.y, rs[4 * i + 2] = b2.z, rs[4 * i + 3] = b2.w;
-                  }
-                } else {
-#pragma unroll
-                  for (int i = 0; i < kSub / 2; ++i) rc[i] = 1.0f, rs[i] = 0.0f;
-                }
+                for (int i = 0; i < kSub / 2; ++i) rc[i] = rcn[i], rs[i] = rsn[i];
+                // the next piece: kSub columns on, or this warp's next chunk
+                fetch_rope(hh + 1 < kHalves ? c0 + kSub : (jj + 1 < kChunks ? col0 + 32 : 1 << 30));
               }
               tmem_ld_wait();
               // Separate unrolled bodies with and without bias (warp-uniform
@@ -729,7 +742,9 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
                   }
                 }
               };
-              if (with_bias)
+              if constexpr (EPI == kEpiRope16)
+                finish(std::false_type{});
+              else if (with_bias)
                 finish(std::true_type{});
               else
                 finish(std::false_type{});
@@ -1046,6 +1061,10 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
        (g.rope_hd != 32 && g.rope_hd != 64) || g.rope_cols != 2 * g.rope_heads * g.rope_hd || g.rope_cols > g.n ||
        (reinterpret_cast<uintptr_t>(g.rope_cos) & 15) || (reinterpret_cast<uintptr_t>(g.rope_sin) & 15))) {
     set_error("rotary epilogue: needs 16-byte aligned tables, head_dim 32 or 64, rope_cols = 2 * heads * head_dim <= N");
+    return KB_E_INVALID;
+  }
+  if (epi == kEpiRope16 && g.bias != nullptr) {
+    set_error("rotary epilogue: the QKV projection takes no bias");
     return KB_E_INVALID;
   }
   if (g.act < kActNone || g.act > kActSilu) {
