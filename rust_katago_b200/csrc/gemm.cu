@@ -111,6 +111,20 @@ __device__ __forceinline__ void load_vecn(const float* p, int col0, int n, float
   }
 }
 
+// N floats from a 16-byte aligned address, no checks (GemmArgs::cols_vec).
+template <int N>
+__device__ __forceinline__ void load_vec_aligned(const float* p, float (&dst)[N]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < N / 4; ++i) {
+    const float4 t = __ldg(q + i);
+    dst[4 * i] = t.x;
+    dst[4 * i + 1] = t.y;
+    dst[4 * i + 2] = t.z;
+    dst[4 * i + 3] = t.w;
+  }
+}
+
 template <int N>
 __device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
   if constexpr (N == 16) tmem_ld16(taddr, r);
@@ -531,8 +545,13 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
             uint32_t v[32];
             tmem_ldn<32>(taddr + j * 32, v);
             float sw[32], bias[32];
-            if constexpr (KIND == kGemmI8) load_vecn<32>(g.col_scale, col0, g.n, sw);
-            if (with_bias) load_vecn<32>(g.bias, col0, g.n, bias);
+            if (g.cols_vec) {  // warp-uniform
+              if constexpr (KIND == kGemmI8) load_vec_aligned<32>(g.col_scale + col0, sw);
+              if (with_bias) load_vec_aligned<32>(g.bias + col0, bias);
+            } else {
+              if constexpr (KIND == kGemmI8) load_vecn<32>(g.col_scale, col0, g.n, sw);
+              if (with_bias) load_vecn<32>(g.bias, col0, g.n, bias);
+            }
             tmem_ld_wait();
             if (!__all_sync(0xffffffffu, mbar_wait(&rbar[sq % SB], (sq / SB) & 1, abort_flag))) {
               ok = false;
@@ -704,9 +723,14 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
               uint32_t v[kSub];
               tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, v);
               float sw[kSub];
-              if constexpr (KIND == kGemmI8) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
               float bias[kSub];
-              if (with_bias) load_vecn<kSub>(g.bias, c0, g.n, bias);
+              if (g.cols_vec) {  // warp-uniform
+                if constexpr (KIND == kGemmI8) load_vec_aligned<kSub>(g.col_scale + c0, sw);
+                if (with_bias) load_vec_aligned<kSub>(g.bias + c0, bias);
+              } else {
+                if constexpr (KIND == kGemmI8) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
+                if (with_bias) load_vecn<kSub>(g.bias, c0, g.n, bias);
+              }
               // Rotary tables of these kSub / 2 pairs (kEpiRope16, Q and K columns).
               float rc[kSub / 2], rs[kSub / 2];
               bool rope = false;
@@ -1096,15 +1120,18 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     if (rc) return rc;
     tma_out = 1;
   }
+  GemmArgs ga = g;
+  ga.cols_vec = g.n % 32 == 0 && (reinterpret_cast<uintptr_t>(g.col_scale) & 15) == 0 &&
+                (reinterpret_cast<uintptr_t>(g.bias) & 15) == 0;
   if (kind == kGemmI8) {
-    return bn == 256 ? dispatch_sb<kGemmI8, 256>(epi, ma, mb, mo, tma_out, g, stream)
-                     : dispatch_sb<kGemmI8, 128>(epi, ma, mb, mo, tma_out, g, stream);
+    return bn == 256 ? dispatch_sb<kGemmI8, 256>(epi, ma, mb, mo, tma_out, ga, stream)
+                     : dispatch_sb<kGemmI8, 128>(epi, ma, mb, mo, tma_out, ga, stream);
   }
   if (kind == kGemmBF16) {
-    return bn == 256 ? dispatch_sb<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, g, stream)
-                     : dispatch_sb<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, g, stream);
+    return bn == 256 ? dispatch_sb<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, ga, stream)
+                     : dispatch_sb<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, ga, stream);
   }
-  if (kind == kGemmMXF8) return dispatch_sb<kGemmMXF8, 128>(epi, ma, mb, mo, tma_out, g, stream);
+  if (kind == kGemmMXF8) return dispatch_sb<kGemmMXF8, 128>(epi, ma, mb, mo, tma_out, ga, stream);
   set_error("GEMM kind not supported");
   return KB_E_UNSUPPORTED;
 }

@@ -61,6 +61,9 @@ struct GemmArgs {
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
   int rope_cols = 0, rope_heads = 0, rope_seq = 0, rope_hd = 0;
+  // Set by gemm_launch: n % 32 == 0 and col_scale / bias 16-byte aligned, so
+  // the epilogue reads their pieces with unchecked 16-byte loads.
+  int cols_vec = 0;
 };
 
 enum GemmKind : int { kGemmI8 = 0, kGemmBF16 = 1, kGemmMXF8 = 2 };
