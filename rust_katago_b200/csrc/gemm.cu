@@ -125,6 +125,15 @@ __device__ __forceinline__ void load_vec_aligned(const float* p, float (&dst)[N]
   }
 }
 
+// Eight floats from a 32-byte aligned global address in one 256-bit load
+// (read-only path): one L1 wavefront per 32-byte sector instead of one per
+// 16 bytes when the lanes of a warp read different rows.
+__device__ __forceinline__ void ldg256(const float* p, float* r) {
+  asm volatile("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]), "=f"(r[7])
+               : "l"(p));
+}
+
 template <int N>
 __device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
   if constexpr (N == 16) tmem_ld16(taddr, r);
@@ -613,31 +622,6 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
       const bool row_ok = row < g.m;
       int token = 0;
       if constexpr (EPI == kEpiRope16) token = row_ok ? row % g.rope_seq : 0;
-      // Rotary tables (kEpiRope16) of the next kSub-column piece: each piece
-      // issues the loads of the one after it, so the tables' L2 latency
-      // overlaps a piece of work; the first piece's are loaded while the
-      // accumulator is still being computed.  [token][head][pair] layout: the
-      // pairs of Q or K column cc (even) start at token * rope_cols / 4 + cc / 2.
-      float rcn[kSub / 2], rsn[kSub / 2];
-      auto fetch_rope = [&](int c0n) {
-        if (row_ok && c0n < g.rope_cols) {
-          const int half_cols = g.rope_cols / 2;
-          const int cc = c0n < half_cols ? c0n : c0n - half_cols;
-          const size_t off = static_cast<size_t>(token) * (g.rope_cols / 4) + cc / 2;
-          const float4* pc = reinterpret_cast<const float4*>(g.rope_cos + off);
-          const float4* ps = reinterpret_cast<const float4*>(g.rope_sin + off);
-#pragma unroll
-          for (int i = 0; i < kSub / 8; ++i) {
-            const float4 a = __ldg(pc + i), b2 = __ldg(ps + i);
-            rcn[4 * i] = a.x, rcn[4 * i + 1] = a.y, rcn[4 * i + 2] = a.z, rcn[4 * i + 3] = a.w;
-            rsn[4 * i] = b2.x, rsn[4 * i + 1] = b2.y, rsn[4 * i + 2] = b2.z, rsn[4 * i + 3] = b2.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < kSub / 2; ++i) rcn[i] = 1.0f, rsn[i] = 0.0f;
-        }
-      };
-      if constexpr (EPI == kEpiRope16) fetch_rope(nb * BN + part * (BN / 32 / kParts) * 32);
       // the row scale is loaded while the accumulator is still being computed
       float sa = 1.0f;
       if constexpr (KIND == kGemmI8 && EPI != kEpiI32) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
@@ -736,10 +720,22 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
               bool rope = false;
               if constexpr (EPI == kEpiRope16) {
                 rope = col0 < g.rope_cols;  // warp-uniform
+                if (rope && row_ok) {
+                  // [token][head][pair]: the pairs of Q or K column cc (even)
+                  // start at token * rope_cols / 4 + cc / 2
+                  const int half_cols = g.rope_cols / 2;
+                  const int cc = c0 < half_cols ? c0 : c0 - half_cols;
+                  // (32-byte aligned: token * rope_cols / 4 and cc / 2 are multiples of 8)
+                  const size_t off = static_cast<size_t>(token) * (g.rope_cols / 4) + cc / 2;
 #pragma unroll
-                for (int i = 0; i < kSub / 2; ++i) rc[i] = rcn[i], rs[i] = rsn[i];
-                // the next piece: kSub columns on, or this warp's next chunk
-                fetch_rope(hh + 1 < kHalves ? c0 + kSub : (jj + 1 < kChunks ? col0 + 32 : 1 << 30));
+                  for (int i = 0; i < kSub / 16; ++i) {
+                    ldg256(g.rope_cos + off + 8 * i, rc + 8 * i);
+                    ldg256(g.rope_sin + off + 8 * i, rs + 8 * i);
+                  }
+                } else {
+#pragma unroll
+                  for (int i = 0; i < kSub / 2; ++i) rc[i] = 1.0f, rs[i] = 0.0f;
+                }
               }
               tmem_ld_wait();
               // Separate unrolled bodies with and without bias (warp-uniform
@@ -1083,8 +1079,8 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
   if (epi == kEpiRope16 &&
       (g.rope_cos == nullptr || g.rope_sin == nullptr || g.rope_seq <= 0 || g.rope_heads <= 0 ||
        (g.rope_hd != 32 && g.rope_hd != 64) || g.rope_cols != 2 * g.rope_heads * g.rope_hd || g.rope_cols > g.n ||
-       (reinterpret_cast<uintptr_t>(g.rope_cos) & 15) || (reinterpret_cast<uintptr_t>(g.rope_sin) & 15))) {
-    set_error("rotary epilogue: needs 16-byte aligned tables, head_dim 32 or 64, rope_cols = 2 * heads * head_dim <= N");
+       (reinterpret_cast<uintptr_t>(g.rope_cos) & 31) || (reinterpret_cast<uintptr_t>(g.rope_sin) & 31))) {
+    set_error("rotary epilogue: needs 32-byte aligned tables, head_dim 32 or 64, rope_cols = 2 * heads * head_dim <= N");
     return KB_E_INVALID;
   }
   if (epi == kEpiRope16 && g.bias != nullptr) {
