@@ -111,20 +111,6 @@ __device__ __forceinline__ void load_vecn(const float* p, int col0, int n, float
   }
 }
 
-// N floats from a 16-byte aligned address, no checks (GemmArgs::cols_vec).
-template <int N>
-__device__ __forceinline__ void load_vec_aligned(const float* p, float (&dst)[N]) {
-  const float4* q = reinterpret_cast<const float4*>(p);
-#pragma unroll
-  for (int i = 0; i < N / 4; ++i) {
-    const float4 t = __ldg(q + i);
-    dst[4 * i] = t.x;
-    dst[4 * i + 1] = t.y;
-    dst[4 * i + 2] = t.z;
-    dst[4 * i + 3] = t.w;
-  }
-}
-
 // Eight floats from a 32-byte aligned global address in one 256-bit load
 // (read-only path): one L1 wavefront per 32-byte sector instead of one per
 // 16 bytes when the lanes of a warp read different rows.
@@ -133,6 +119,15 @@ __device__ __forceinline__ void ldg256(const float* p, float* r) {
                : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]), "=f"(r[7])
                : "l"(p));
 }
+
+// N floats (N a multiple of 8) from a 32-byte aligned address, no checks
+// (GemmArgs::cols_vec), in 256-bit loads.
+template <int N>
+__device__ __forceinline__ void load_vec_aligned(const float* p, float (&dst)[N]) {
+#pragma unroll
+  for (int i = 0; i < N / 8; ++i) ldg256(p + 8 * i, dst + 8 * i);
+}
+
 
 template <int N>
 __device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
@@ -1117,8 +1112,8 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     tma_out = 1;
   }
   GemmArgs ga = g;
-  ga.cols_vec = g.n % 32 == 0 && (reinterpret_cast<uintptr_t>(g.col_scale) & 15) == 0 &&
-                (reinterpret_cast<uintptr_t>(g.bias) & 15) == 0;
+  ga.cols_vec = g.n % 32 == 0 && (reinterpret_cast<uintptr_t>(g.col_scale) & 31) == 0 &&
+                (reinterpret_cast<uintptr_t>(g.bias) & 31) == 0;
   if (kind == kGemmI8) {
     return bn == 256 ? dispatch_sb<kGemmI8, 256>(epi, ma, mb, mo, tma_out, ga, stream)
                      : dispatch_sb<kGemmI8, 128>(epi, ma, mb, mo, tma_out, ga, stream);

@@ -61,8 +61,8 @@ struct GemmArgs {
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
   int rope_cols = 0, rope_heads = 0, rope_seq = 0, rope_hd = 0;
-  // Set by gemm_launch: n % 32 == 0 and col_scale / bias 16-byte aligned, so
-  // the epilogue reads their pieces with unchecked 16-byte loads.
+  // Set by gemm_launch: n % 32 == 0 and col_scale / bias 32-byte aligned, so
+  // the epilogue reads their pieces with unchecked 32-byte loads.
   int cols_vec = 0;
 };
 
