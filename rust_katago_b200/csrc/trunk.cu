@@ -48,39 +48,55 @@ __device__ __forceinline__ int sym_source(int sym, int r, int c) {
 // A[(b*361 + t), k] for the stem GEMM.  spatial: [B, 22, 19, 19] (NCHW) or
 // [B, 19, 19, 22] (NHWC), global: [B, 19], both fp32; sym: [B] board
 // symmetries (NULL = identity), applied as the input is gathered.
+// One thread per (token, group of 8 columns): the 8 values leave as one
+// 16-byte store; the tap index (ic, ky, kx) advances incrementally.
+constexpr int kStemGroups = kStemK / 8;  // 28
 __global__ void stem_gather_kernel(const float* __restrict__ spatial, const float* __restrict__ global,
                                    const int* __restrict__ sym, uint16_t* __restrict__ a, int batch, int nhwc) {
-  const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long total = static_cast<long>(batch) * kSeq * (kStemK / 2);
-  if (idx >= total) return;
-  const int kpair = static_cast<int>(idx % (kStemK / 2));
-  const long row = idx / (kStemK / 2);
-  const int b = static_cast<int>(row / kSeq);
-  const int t = static_cast<int>(row % kSeq);
-  const int y = t / kSide, x = t % kSide;
-  const int sm = sym ? (__ldg(sym + b) & 7) : 0;
-  float v[2];
+  const long total = static_cast<long>(batch) * kSeq * kStemGroups;
+  for (long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int grp = static_cast<int>(idx % kStemGroups);
+    const long row = idx / kStemGroups;
+    const int b = static_cast<int>(row / kSeq);
+    const int t = static_cast<int>(row - static_cast<long>(b) * kSeq);
+    const int y = t / kSide, x = t - (t / kSide) * kSide;
+    const int sm = sym ? (__ldg(sym + b) & 7) : 0;
+    int k = grp * 8;
+    int ic = k / 9, r9 = k - 9 * ic;
+    float v[8];
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int k = 2 * kpair + h;
-    float val = 0.0f;
-    if (k < kInC * 9) {
-      const int ic = k / 9, ky = (k % 9) / 3, kx = k % 3;
-      const int sy = y + ky - 1, sx = x + kx - 1;
-      if (sy >= 0 && sy < kSide && sx >= 0 && sx < kSide) {
-        const int cell = sym_source(sm, sy, sx);
-        const long off = nhwc ? ((static_cast<long>(b) * kSeq + cell) * kInC + ic)
-                              : ((static_cast<long>(b) * kInC + ic) * kSeq + cell);
-        val = __ldg(spatial + off);
+    for (int e = 0; e < 8; ++e, ++k) {
+      float val = 0.0f;
+      if (k < kInC * 9) {
+        const int ky = r9 / 3, kx = r9 - 3 * (r9 / 3);
+        const int sy = y + ky - 1, sx = x + kx - 1;
+        if (sy >= 0 && sy < kSide && sx >= 0 && sx < kSide) {
+          const int cell = sym_source(sm, sy, sx);
+          const long off = nhwc ? ((static_cast<long>(b) * kSeq + cell) * kInC + ic)
+                                : ((static_cast<long>(b) * kInC + ic) * kSeq + cell);
+          val = __ldg(spatial + off);
+        }
+      } else if (k < kInC * 9 + kInG) {
+        val = __ldg(global + static_cast<long>(b) * kInG + (k - kInC * 9));
       }
-    } else if (k < kInC * 9 + kInG) {
-      val = __ldg(global + static_cast<long>(b) * kInG + (k - kInC * 9));
+      v[e] = val;
+      if (++r9 == 9) r9 = 0, ++ic;
     }
-    v[h] = val;
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+      w[q] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    reinterpret_cast<uint4*>(a)[idx] = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  const __nv_bfloat162 p = __floats2bfloat162_rn(v[0], v[1]);
-  reinterpret_cast<uint32_t*>(a)[idx] = *reinterpret_cast<const uint32_t*>(&p);
 }
+
+// SiLU for the trunk tip and the fp32 heads (their outputs are compared with
+// a tolerance, not bit for bit): x / (1 + e^-x) with the fast exponential and
+// division.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // g = bf16(silu(x * gamma + beta)) over [rows, c] bf16, c a multiple of 8:
 // each thread converts 8 consecutive values (one 16-byte load and store).
@@ -104,7 +120,7 @@ __global__ void trunk_tip_kernel(const uint16_t* __restrict__ x, const float* __
       const float hi = from_bf16(static_cast<uint16_t>(w[j] >> 16));
       const float v0 = __fadd_rn(__fmul_rn(lo, gm[2 * j]), bt[2 * j]);
       const float v1 = __fadd_rn(__fmul_rn(hi, gm[2 * j + 1]), bt[2 * j + 1]);
-      o[j] = static_cast<uint32_t>(bits_bf16(kb_silu(v0))) | (static_cast<uint32_t>(bits_bf16(kb_silu(v1))) << 16);
+      o[j] = static_cast<uint32_t>(bits_bf16(silu_fast(v0))) | (static_cast<uint32_t>(bits_bf16(silu_fast(v1))) << 16);
     }
     reinterpret_cast<uint4*>(g)[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -131,9 +147,6 @@ struct HeadWeights {
 constexpr int kHeadThreads = 384;
 constexpr int kHeadWarps = kHeadThreads / 32;
 
-// SiLU for the fp32 heads (compared with a tolerance, not bit for bit):
-// x / (1 + e^-x) with the fast exponential and division.
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // Warp-cooperative dot product of a weight row (k floats, global) with a
 // vector in shared memory; every lane returns the sum (fixed reduction order).
@@ -338,9 +351,16 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
 
 int stem_gather_launch(const float* spatial, const float* global, const int* sym, uint16_t* a, int batch,
                        int nhwc, cudaStream_t s) {
-  const long total = static_cast<long>(batch) * kSeq * (kStemK / 2);
-  stem_gather_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(spatial, global, sym, a, batch,
-                                                                                 nhwc);
+  if (reinterpret_cast<uintptr_t>(a) & 15) {
+    set_error("stem gather: the operand must be 16-byte aligned");
+    return KB_E_INVALID;
+  }
+  const long total = static_cast<long>(batch) * kSeq * kStemGroups;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long want = (total + 255) / 256, cap = 16L * num_sms(dev);
+  stem_gather_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(spatial, global, sym, a, batch,
+                                                                                     nhwc);
   return check_cuda(cudaGetLastError(), "stem gather launch");
 }
 
