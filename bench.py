@@ -132,6 +132,8 @@ class FfnWorkload:
     stream.  Weights N(0, 0.02) int8 per channel, residual N(0, 1)."""
 
     name = "config2: one b11c768 FFN block (RMSNorm, W8A8 768->3072 GELU, W8A8 3072->768 + residual)"
+    e2e_how = ("public API (Int8Workspace.ffn_gelu_rms on the residual copied in from pinned host memory and "
+               "copied back each step)")
 
     def __init__(self, batch: int, torch, seed: int = 1234, build_device: bool = True):
         self.torch = torch
@@ -227,6 +229,9 @@ class TrunkWorkload:
     N(0,1)); one CUDA graph per forward."""
 
     name = "config3: full b11c768 W8A8 trunk forward (11 blocks, 12x64 attention, FFN 768->3072->768, heads)"
+    e2e_how = ("public API (kb_submit_rows with a random board symmetry per row, applied on the device, and the "
+               "outputs decoded on the device as the reference's finish_output decodes them / kb_finish_rows: "
+               "pinned staging, H2D, graph, decode, D2H of the decoded rows, status check)")
     dtype = "int8"
     kernel = "gemm_kernel<i8,256>"
     precision = "int8"
@@ -250,6 +255,8 @@ class TrunkWorkload:
         self.spatial, self.glob = self.spatial[:batch], self.glob[:batch]
         # one random board symmetry per row, as MCTS submits them (applied on the device)
         self.symmetry = np.random.default_rng(seed + 3 + rank).integers(0, 8, batch).astype(np.int32)
+        # decoded on the device as the reference's finish_output decodes on the host
+        self.rows = backend.row_params(batch, symmetry=self.symmetry)
         self.model = backend.CudaBackend.load_model(self.topo, self.blob, torch.cuda.current_device())
         self.handle = backend.CudaBackend.create_compute_handle(self.model, batch)
         self.d_spatial = torch.from_numpy(self.spatial).cuda()
@@ -267,13 +274,13 @@ class TrunkWorkload:
         self.handle.forward_device(self.batch, self.d_spatial, self.d_global, self.d_out, use_graph=True)
 
     def e2e_step(self):
-        self.handle.get_output(self.spatial, self.glob, self.symmetry)
+        self.handle.finish_rows(self.handle.submit_rows(self.spatial, self.glob, self.rows))
 
     def e2e_bytes(self):
         from rust_katago_b200 import backend
 
-        return (self.spatial.nbytes + self.glob.nbytes + self.symmetry.nbytes,
-                self.batch * backend.OUT_PER_POS * 4 + 8)
+        return (self.spatial.nbytes + self.glob.nbytes + self.symmetry.nbytes + self.rows.nbytes,
+                self.batch * backend.DEC_PER_POS * 4 + 8)
 
     def gemms(self):
         """The trunk's INT8 GEMM shapes: (label, m, n, k, epilogue, act, launches per forward)."""
@@ -509,9 +516,7 @@ def main():
                        "parallelism": f"batch-sharded x{world}, weights replicated, no collective",
                        "l2": "256 MiB flush between timed steps (working set also exceeds L2)"},
             "e2e": {"value": e2e_value, "unit": "positions/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "how": "public API (kb_submit with a random board symmetry per row, applied on the device / kb_finish: "
-                           "pinned staging, H2D, graph, D2H, status check), "
-                           "host clock around the steps, max over ranks"},
+                    "how": wl.e2e_how + ", host clock around the steps, max over ranks"},
             "gpu_launches": wl.launches_per_step * args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu,

@@ -403,6 +403,66 @@ KB_API int kb_forward_trace(kb_handle* handle, int n, const float* d_spatial, co
  * Replaces: mxfp8.rs validate_completed_status (:1181). */
 KB_API int kb_read_status(kb_handle* handle, uint32_t status[2]);
 
+/* ---- Output decoding on the device -------------------------------------- */
+
+/* One row's decoding parameters: the NNResultBuf fields that
+ * decode_raw_outputs reads (crates/kata_nn/src/output_postprocess.rs:29-112)
+ * and the MiscNNInputParams / board / rules facts that postprocess_output
+ * reads (:140-330).  24 bytes, no padding. */
+typedef struct kb_row_params {
+  int32_t symmetry;          /* 0..7, the symmetry the row was evaluated under */
+  float policy_optimism;     /* [0, 1] (NNResultBuf::policy_optimism as f32, :66) */
+  float policy_temperature;  /* nn_policy_temperature, clamped to [1e-6, 1e6] (:150) */
+  int32_t board_x, board_y;  /* board size, 1..19: ownership outside it reads 0 (:316-320) */
+  uint8_t include_owner_map; /* 0: ownership not decoded (zeros) */
+  uint8_t next_player_white; /* 1: white to move (:282) */
+  uint8_t passing_hacks;     /* enable_passing_hacks (:170-184) */
+  uint8_t no_result_off;     /* ko_rule != Simple and scoring_rule != Territory (:228-242) */
+} kb_row_params;
+
+/* ModelPostProcessParams (crates/kata_nn/src/desc.rs:671-695) and the model
+ * version.  64 bytes. */
+typedef struct kb_postprocess_params {
+  int32_t model_version;
+  float output_scale_multiplier;
+  double td_score_multiplier, score_mean_multiplier, score_stdev_multiplier, lead_multiplier,
+      variance_time_multiplier, shortterm_value_error_multiplier, shortterm_score_error_multiplier;
+} kb_postprocess_params;
+
+/* Decode n rows of raw heads (the packed kb_forward_device output, head-major:
+ * policy [n, 6, 362] | value [n, 3] | misc [n, 10] | moremisc [n, 8] |
+ * ownership [n, 361]) into d_decoded, head-major: policy [n, 362] | value
+ * [n, 3] | misc [n, 4] (score_mean, score_mean_sq, lead, var_time_left) |
+ * moremisc [n, 2] (shortterm_winloss_error, shortterm_score_error) | ownership
+ * [n, 361].  All pointers are device memory except pp (host, NULL = the
+ * reference defaults with model version 17); enqueued on `stream`.
+ * d_legal NULL: decode_raw_outputs only (output_postprocess.rs:29-112: the
+ * symmetry reversed, channels 0 and 5 blended by the optimism, exact).
+ * d_legal [n, 362] bytes (nonzero = legal, pass last): postprocess_output
+ * (:140-330) applied too, as the evaluator does per row (eval.rs:675-690).
+ * Replaces: the host decode in CudaBackend::finish_output (cuda.rs:2510-2600)
+ * and SharedState::postprocess_output (eval.rs:675). */
+KB_API int kb_decode_device(int n, const float* d_raw, const kb_row_params* d_rows, const uint8_t* d_legal,
+                            const kb_postprocess_params* pp, float* d_decoded, uintptr_t stream);
+
+/* Post-processing parameters that kb_submit_rows applies (default: the
+ * reference defaults with model version 17). */
+KB_API int kb_set_postprocess(kb_handle* handle, const kb_postprocess_params* pp);
+
+/* kb_submit with per-row decoding: each row is evaluated under rows[i].symmetry,
+ * then decoded on the device as kb_decode_device does (legal NULL: decode only;
+ * else host [n, 362] legality bytes and post-processing too); only the
+ * decoded outputs are copied back.  Replaces: submit_output + finish_output's
+ * decode (cuda.rs:2196-2600) and, with legal, postprocess_output. */
+KB_API int kb_submit_rows(kb_handle* handle, int n, const float* spatial, const float* global,
+                          const kb_row_params* rows, const uint8_t* legal, uint64_t* token);
+
+/* Wait for a kb_submit_rows token and copy its decoded outputs: policy [n, 362],
+ * value [n, 3], misc [n, 4], moremisc [n, 2], ownership [n, 361] (any may be
+ * NULL); status as in kb_finish (outputs withheld on a status flag). */
+KB_API int kb_finish_rows(kb_handle* handle, uint64_t token, float* policy, float* value, float* misc,
+                          float* moremisc, float* ownership, uint32_t status[2]);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,6 +66,10 @@ SIGNATURES: dict[str, tuple] = {
     "kb_forward_device": (I, [P, I, P, P, P, I]),
     "kb_read_status": (I, [P, ctypes.POINTER(ctypes.c_uint32)]),
     "kb_forward_trace": (I, [P, I, P, P, P, P]),
+    "kb_decode_device": (I, [I, P, P, P, P, P, STREAM]),
+    "kb_set_postprocess": (I, [P, P]),
+    "kb_submit_rows": (I, [P, I, P, P, P, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "kb_finish_rows": (I, [P, ctypes.c_uint64, P, P, P, P, P, ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 
@@ -74,6 +78,29 @@ class ModelDesc(ctypes.Structure):
 
     _fields_ = [("trunk_channels", ctypes.c_int), ("num_blocks", ctypes.c_int), ("num_heads", ctypes.c_int),
                 ("head_dim", ctypes.c_int), ("ffn_channels", ctypes.c_int), ("precision", ctypes.c_int)]
+
+class PostProcessParams(ctypes.Structure):
+    """kb_postprocess_params (ModelPostProcessParams, crates/kata_nn/src/desc.rs:671-695,
+    and the model version); defaults are the reference's, version 17."""
+
+    _fields_ = [("model_version", ctypes.c_int32), ("output_scale_multiplier", ctypes.c_float),
+                ("td_score_multiplier", ctypes.c_double), ("score_mean_multiplier", ctypes.c_double),
+                ("score_stdev_multiplier", ctypes.c_double), ("lead_multiplier", ctypes.c_double),
+                ("variance_time_multiplier", ctypes.c_double), ("shortterm_value_error_multiplier", ctypes.c_double),
+                ("shortterm_score_error_multiplier", ctypes.c_double)]
+
+    DEFAULTS = dict(model_version=17, output_scale_multiplier=1.0, td_score_multiplier=20.0,
+                    score_mean_multiplier=20.0, score_stdev_multiplier=20.0, lead_multiplier=20.0,
+                    variance_time_multiplier=40.0, shortterm_value_error_multiplier=0.25,
+                    shortterm_score_error_multiplier=30.0)
+
+    @classmethod
+    def make(cls, **kw) -> "PostProcessParams":
+        unknown = set(kw) - set(cls.DEFAULTS)
+        if unknown:
+            raise TypeError(f"unknown post-processing parameters: {sorted(unknown)}")
+        return cls(**dict(cls.DEFAULTS, **kw))
+
 
 # Constants mirrored from include/katab200.h.
 KB_OK, KB_E_INVALID, KB_E_CUDA, KB_E_STATE, KB_E_NONFINITE, KB_E_UNSUPPORTED = range(6)

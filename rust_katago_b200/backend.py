@@ -13,10 +13,16 @@ reference                                    here (C ABI underneath)
 ``query_output_done``                        :meth:`ComputeHandle.query_output_done`
 ``finish_output`` (cuda.rs:2510)             :meth:`ComputeHandle.finish_output`
 ``get_output``                               :meth:`ComputeHandle.get_output`
+``decode_raw_outputs`` (output_postprocess   :meth:`ComputeHandle.submit_rows` /
+.rs:29-112, in finish_output)                :meth:`ComputeHandle.finish_rows`, :func:`decode_device`
+``postprocess_output`` (output_postprocess   the same, with a legal-move mask
+.rs:140-330, eval.rs:675)
 ===========================================  ===========================================
 
-Outputs are the raw heads (no final activation, backend.rs:279-280): policy
-[n, 6, 362], value [n, 3], misc [n, 10], moremisc [n, 8], ownership [n, 361].
+``submit_output`` / ``finish_output`` return the raw heads (no final
+activation, backend.rs:279-280): policy [n, 6, 362], value [n, 3], misc [n, 10],
+moremisc [n, 8], ownership [n, 361].  ``submit_rows`` / ``finish_rows`` return
+them decoded on the device (:class:`DecodedOutputs`).
 """
 
 from __future__ import annotations
@@ -31,6 +37,62 @@ from ._capi import call, load
 from .synthetic import Topology
 
 OUT_PER_POS = 6 * 362 + 3 + 10 + 8 + 361
+DEC_PER_POS = 362 + 3 + 4 + 2 + 361
+
+# kb_row_params: one row's decoding parameters (24 bytes, the C struct's layout).
+ROW_PARAMS_DTYPE = np.dtype([("symmetry", "<i4"), ("policy_optimism", "<f4"), ("policy_temperature", "<f4"),
+                             ("board_x", "<i4"), ("board_y", "<i4"), ("include_owner_map", "u1"),
+                             ("next_player_white", "u1"), ("passing_hacks", "u1"), ("no_result_off", "u1")])
+assert ROW_PARAMS_DTYPE.itemsize == 24
+
+
+def row_params(n: int, symmetry=0, policy_optimism=0.0, policy_temperature=1.0, board_x=19, board_y=19,
+               include_owner_map=1, next_player_white=1, passing_hacks=0, no_result_off=0) -> np.ndarray:
+    """kb_row_params for n rows; each field a scalar or an [n] array.
+    symmetry / policy_optimism / include_owner_map are NNResultBuf's fields
+    (backend.rs); policy_temperature and passing_hacks MiscNNInputParams'
+    nn_policy_temperature / enable_passing_hacks; no_result_off is
+    ko_rule != Simple and scoring_rule != Territory (output_postprocess.rs:228)."""
+    rows = np.zeros(n, ROW_PARAMS_DTYPE)
+    for name, v in (("symmetry", symmetry), ("policy_optimism", policy_optimism),
+                    ("policy_temperature", policy_temperature), ("board_x", board_x), ("board_y", board_y),
+                    ("include_owner_map", include_owner_map), ("next_player_white", next_player_white),
+                    ("passing_hacks", passing_hacks), ("no_result_off", no_result_off)):
+        rows[name] = v
+    return rows
+
+
+@dataclass
+class DecodedOutputs:
+    """The NNOutput fields per row: policy [n, 362] (policy_probs), value [n, 3]
+    (white win / loss / no-result), misc [n, 4] (score_mean, score_mean_sq,
+    lead, var_time_left), moremisc [n, 2] (shortterm winloss / score error),
+    ownership [n, 361] (white_owner_map; zeros where not requested)."""
+
+    policy: np.ndarray
+    value: np.ndarray
+    misc: np.ndarray
+    moremisc: np.ndarray
+    ownership: np.ndarray
+
+
+def unpack_decoded(flat: np.ndarray, n: int) -> DecodedOutputs:
+    """Split the packed decoded output [policy | value | misc | moremisc | ownership]."""
+    parts, o = [], 0
+    for w in (362, 3, 4, 2, 361):
+        parts.append(flat[o:o + n * w].reshape(n, w))
+        o += n * w
+    return DecodedOutputs(*parts)
+
+
+def decode_device(n: int, d_raw, d_rows, d_legal, d_out, stream: int, **pp) -> None:
+    """kb_decode_device on torch device tensors: d_raw the packed raw heads of
+    n rows, d_rows n kb_row_params (uint8 [n, 24]), d_legal uint8 [n, 362] or
+    None (decode only), d_out float32 [n * DEC_PER_POS]; keyword arguments
+    override the post-processing defaults (_capi.PostProcessParams)."""
+    params = _capi.PostProcessParams.make(**pp)
+    call("kb_decode_device", n, int(d_raw.data_ptr()), int(d_rows.data_ptr()),
+         None if d_legal is None else int(d_legal.data_ptr()), ctypes.byref(params), int(d_out.data_ptr()), stream)
 
 
 @dataclass
@@ -140,6 +202,45 @@ class ComputeHandle:
                         np.zeros((n, 10), np.float32), np.zeros((n, 8), np.float32), np.zeros((n, 361), np.float32))
         status = (ctypes.c_uint32 * 2)()
         call("kb_finish", self._h, token, out.policy.ctypes.data, out.value.ctypes.data, out.misc.ctypes.data,
+             out.moremisc.ctypes.data, out.ownership.ctypes.data, status)
+        return out
+
+    def set_postprocess(self, **pp) -> None:
+        """Post-processing parameters for submit_rows (ModelPostProcessParams and
+        the model version; unspecified fields keep the reference defaults)."""
+        params = _capi.PostProcessParams.make(**pp)
+        call("kb_set_postprocess", self._h, ctypes.byref(params))
+
+    def submit_rows(self, spatial: np.ndarray, glob: np.ndarray, rows: np.ndarray, legal=None) -> int:
+        """Enqueue n positions evaluated under rows['symmetry'] and decoded on
+        the device (decode_raw_outputs); with legal ([n, 362] booleans, pass
+        last) post-processed too (postprocess_output)."""
+        spatial = np.ascontiguousarray(spatial, dtype=np.float32)
+        glob = np.ascontiguousarray(glob, dtype=np.float32)
+        n = spatial.shape[0]
+        rows = np.ascontiguousarray(rows, dtype=ROW_PARAMS_DTYPE)
+        if rows.shape != (n,):
+            raise ValueError("rows must hold one kb_row_params per position")
+        legal_ptr = None
+        if legal is not None:
+            legal = np.ascontiguousarray(legal, dtype=np.uint8)
+            if legal.shape != (n, 362):
+                raise ValueError("legal must be [n, 362]")
+            legal_ptr = legal.ctypes.data
+        tok = ctypes.c_uint64()
+        call("kb_submit_rows", self._h, n, spatial.ctypes.data, glob.ctypes.data, rows.ctypes.data, legal_ptr,
+             ctypes.byref(tok))
+        self._pending = getattr(self, "_pending", {})
+        self._pending[tok.value] = n
+        return tok.value
+
+    def finish_rows(self, token: int) -> DecodedOutputs:
+        n = self._pending.pop(token)
+        out = DecodedOutputs(np.zeros((n, 362), np.float32), np.zeros((n, 3), np.float32),
+                             np.zeros((n, 4), np.float32), np.zeros((n, 2), np.float32),
+                             np.zeros((n, 361), np.float32))
+        status = (ctypes.c_uint32 * 2)()
+        call("kb_finish_rows", self._h, token, out.policy.ctypes.data, out.value.ctypes.data, out.misc.ctypes.data,
              out.moremisc.ctypes.data, out.ownership.ctypes.data, status)
         return out
 

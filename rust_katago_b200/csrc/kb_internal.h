@@ -8,6 +8,7 @@
 
 #include <string>
 
+#include "../../include/katab200.h"
 #include "kb_status.h"
 
 namespace kb {
@@ -109,6 +110,13 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long d
 // Columns per N tile chosen for a given N (the SwiGLU dual-weight packing
 // depends on it).
 int gemm_pick_bn(int kind, int epi, int n);
+
+// Output decoding (decode.cu): decode n rows of packed raw heads into the
+// decoded layout, post-processed when `legal` is non-null.
+kb_postprocess_params default_postprocess_params();
+int check_row_params(const kb_row_params* h_rows, int n);
+int decode_rows_launch(int n, const float* raw, const kb_row_params* rows, const uint8_t* legal,
+                       const kb_postprocess_params& pp, float* out, cudaStream_t s);
 
 }  // namespace kb
 

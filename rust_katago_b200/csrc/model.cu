@@ -154,13 +154,23 @@ struct Slot {
   float* d_global = nullptr;
   float* d_out = nullptr;
   unsigned* h_status = nullptr;  // pinned copy of the status word
+  // kb_submit_rows: [row params n x 24 B | legality n x 362 B], and the decoded outputs.
+  uint8_t* h_post = nullptr;
+  uint8_t* d_post = nullptr;
+  float* h_dec = nullptr;
+  float* d_dec = nullptr;
   cudaEvent_t done = nullptr;
   int n = 0;
   bool busy = false;
+  bool decoded = false;
   uint64_t token = 0;
 };
 
 constexpr int kOutPerPos = 6 * 362 + 3 + 10 + 8 + 361;
+constexpr int kDecPerPos = 362 + 3 + 4 + 2 + 361;
+constexpr int kPostPerPos = static_cast<int>(sizeof(kb_row_params)) + 362;
+static_assert(sizeof(kb_row_params) == 24, "kb_row_params is 24 bytes");
+static_assert(sizeof(kb_postprocess_params) == 64, "kb_postprocess_params is 64 bytes");
 
 }  // namespace
 
@@ -183,6 +193,7 @@ struct kb_handle {
   uint32_t* row_amax = nullptr; // [M] |bits| maximum of the FFN hidden rows
   float* hp = nullptr;          // [M, 384] fp32
   unsigned* status = nullptr;   // [2]
+  kb_postprocess_params pp = kb::default_postprocess_params();
   Slot slots[2];
   uint64_t next_token = 1;
   // Graphs bake in buffer addresses: one per (batch size, input, symmetry and output buffers).
@@ -484,6 +495,10 @@ void destroy_handle(kb_handle* h) {
     cudaFree(sl.d_spatial);
     cudaFree(sl.d_global);
     cudaFree(sl.d_out);
+    cudaFreeHost(sl.h_post);
+    cudaFreeHost(sl.h_dec);
+    cudaFree(sl.d_post);
+    cudaFree(sl.d_dec);
     if (sl.done) cudaEventDestroy(sl.done);
   }
   cudaFree(h->stem_a);
@@ -713,6 +728,11 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
     if (!rc) rc = dev_alloc(&sl.d_spatial, ns, "device input");
     if (!rc) rc = dev_alloc(&sl.d_global, ng, "device input");
     if (!rc) rc = dev_alloc(&sl.d_out, no, "device output");
+    const size_t np = static_cast<size_t>(max_batch) * kPostPerPos, nd = static_cast<size_t>(max_batch) * kDecPerPos;
+    if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_post, np), "pinned row parameters");
+    if (!rc) rc = check_cuda(cudaMallocHost(&sl.h_dec, nd * sizeof(float)), "pinned decoded output");
+    if (!rc) rc = dev_alloc(&sl.d_post, np, "device row parameters");
+    if (!rc) rc = dev_alloc(&sl.d_dec, nd, "device decoded output");
     if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming), "event");
   }
   if (rc) {
@@ -774,18 +794,29 @@ int kb_read_status(kb_handle* h, uint32_t status[2]) {
   return rc;
 }
 
-int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, const int* symmetry,
-              uint64_t* token) {
+}  // extern "C"
+
+namespace {
+
+// kb_submit and kb_submit_rows: rows == nullptr returns the raw heads, else
+// each row's symmetry comes from rows and the outputs are decoded on the
+// device (post-processed when legal != nullptr) before the copy back.
+int submit_impl(kb_handle* h, int n, const float* spatial, const float* global, const int* symmetry,
+                const kb_row_params* rows, const uint8_t* legal, uint64_t* token) {
   if (!h || !spatial || !global || !token || n <= 0 || n > h->max_batch) {
-    set_error("kb_submit: need 1 <= n <= max_batch, host inputs and a token");
+    set_error("submit: need 1 <= n <= max_batch, host inputs and a token");
     return KB_E_INVALID;
   }
-  if (symmetry)
+  if (rows) {
+    const int rc = check_row_params(rows, n);
+    if (rc) return rc;
+  } else if (symmetry) {
     for (int i = 0; i < n; ++i)
       if (symmetry[i] < 0 || symmetry[i] > 7) {
         set_error("kb_submit: symmetry must be in 0..7");
         return KB_E_INVALID;
       }
+  }
   std::lock_guard<std::mutex> lock(h->mu);
   int rc = check_cuda(cudaSetDevice(h->device), "cudaSetDevice");
   if (rc) return rc;
@@ -804,7 +835,9 @@ int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, co
   memcpy(sl->h_global, global, ng * sizeof(float));
   // The symmetries ride behind the global features: one copy carries both.
   int* h_sym = reinterpret_cast<int*>(sl->h_global + ng);
-  if (symmetry)
+  if (rows)
+    for (int i = 0; i < n; ++i) h_sym[i] = rows[i].symmetry;
+  else if (symmetry)
     memcpy(h_sym, symmetry, static_cast<size_t>(n) * sizeof(int));
   else
     memset(h_sym, 0, static_cast<size_t>(n) * sizeof(int));
@@ -814,18 +847,107 @@ int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, co
   if (!rc)
     rc = check_cuda(cudaMemcpyAsync(sl->d_global, sl->h_global, (ng + n) * sizeof(float), cudaMemcpyHostToDevice, s),
                     "H2D");
+  const size_t row_bytes = static_cast<size_t>(n) * sizeof(kb_row_params);
+  if (!rc && rows) {
+    // Row parameters, then the legality bytes: one copy.
+    memcpy(sl->h_post, rows, row_bytes);
+    if (legal) memcpy(sl->h_post + row_bytes, legal, static_cast<size_t>(n) * 362);
+    rc = check_cuda(cudaMemcpyAsync(sl->d_post, sl->h_post, row_bytes + (legal ? static_cast<size_t>(n) * 362 : 0),
+                                    cudaMemcpyHostToDevice, s), "H2D");
+  }
   if (!rc) rc = run_forward(h, n, sl->d_spatial, sl->d_global, d_sym, sl->d_out, true);
-  if (!rc)
+  if (rows) {
+    if (!rc)
+      rc = decode_rows_launch(n, sl->d_out, reinterpret_cast<const kb_row_params*>(sl->d_post),
+                              legal ? sl->d_post + row_bytes : nullptr, h->pp, sl->d_dec, s);
+    if (!rc)
+      rc = check_cuda(cudaMemcpyAsync(sl->h_dec, sl->d_dec, static_cast<size_t>(n) * kDecPerPos * sizeof(float),
+                                      cudaMemcpyDeviceToHost, s), "D2H");
+  } else if (!rc) {
     rc = check_cuda(cudaMemcpyAsync(sl->h_out, sl->d_out, static_cast<size_t>(n) * kOutPerPos * sizeof(float),
                                     cudaMemcpyDeviceToHost, s), "D2H");
+  }
   if (!rc)
     rc = check_cuda(cudaMemcpyAsync(sl->h_status, h->status, 2 * sizeof(unsigned), cudaMemcpyDeviceToHost, s), "D2H");
   if (!rc) rc = check_cuda(cudaEventRecord(sl->done, s), "event record");
   if (rc) return rc;
   sl->busy = true;
+  sl->decoded = rows != nullptr;
   sl->n = n;
   sl->token = h->next_token++;
   *token = sl->token;
+  return KB_OK;
+}
+
+// Wait for a token's slot and check its status word; on success *out is the
+// slot (released) with its pinned outputs readable.
+int finish_wait(kb_handle* h, uint64_t token, bool decoded, uint32_t status[2], Slot** out) {
+  if (!h) {
+    set_error("null handle");
+    return KB_E_INVALID;
+  }
+  Slot* sl = nullptr;
+  for (auto& cand : h->slots)
+    if (cand.busy && cand.token == token) sl = &cand;
+  if (!sl) {
+    set_error("unknown or already finished token");
+    return KB_E_STATE;
+  }
+  if (sl->decoded != decoded) {
+    set_error(decoded ? "token was submitted by kb_submit: finish it with kb_finish"
+                      : "token was submitted by kb_submit_rows: finish it with kb_finish_rows");
+    return KB_E_STATE;
+  }
+  int rc = check_cuda(cudaEventSynchronize(sl->done), "event wait");
+  sl->busy = false;
+  if (rc) return rc;
+  if (status) {
+    status[0] = sl->h_status[0];
+    status[1] = sl->h_status[1];
+  }
+  if (sl->h_status[0] != 0) {
+    set_error("forward reported status flags " + std::to_string(sl->h_status[0]) + " at layer " +
+              std::to_string(static_cast<int>(sl->h_status[1])) + "; outputs withheld");
+    return KB_E_NONFINITE;
+  }
+  *out = sl;
+  return KB_OK;
+}
+
+// Copy head-major blocks of `widths[i]` floats per row out of `src`.
+void copy_heads(const float* src, int n, const int (&widths)[5], float* const (&dst)[5]) {
+  for (int i = 0; i < 5; ++i) {
+    const size_t cnt = static_cast<size_t>(n) * widths[i];
+    if (dst[i]) memcpy(dst[i], src, cnt * sizeof(float));
+    src += cnt;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int kb_submit(kb_handle* h, int n, const float* spatial, const float* global, const int* symmetry,
+              uint64_t* token) {
+  return submit_impl(h, n, spatial, global, symmetry, nullptr, nullptr, token);
+}
+
+int kb_submit_rows(kb_handle* h, int n, const float* spatial, const float* global, const kb_row_params* rows,
+                   const uint8_t* legal, uint64_t* token) {
+  if (!rows) {
+    set_error("kb_submit_rows: row parameters required");
+    return KB_E_INVALID;
+  }
+  return submit_impl(h, n, spatial, global, nullptr, rows, legal, token);
+}
+
+int kb_set_postprocess(kb_handle* h, const kb_postprocess_params* pp) {
+  if (!h || !pp) {
+    set_error("kb_set_postprocess: null argument");
+    return KB_E_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->pp = *pp;
   return KB_OK;
 }
 
@@ -848,41 +970,19 @@ int kb_query(kb_handle* h, uint64_t token) {
 
 int kb_finish(kb_handle* h, uint64_t token, float* policy, float* value, float* misc, float* moremisc,
               float* ownership, uint32_t status[2]) {
-  if (!h) {
-    set_error("null handle");
-    return KB_E_INVALID;
-  }
   Slot* sl = nullptr;
-  for (auto& cand : h->slots)
-    if (cand.busy && cand.token == token) sl = &cand;
-  if (!sl) {
-    set_error("unknown or already finished token");
-    return KB_E_STATE;
-  }
-  int rc = check_cuda(cudaEventSynchronize(sl->done), "event wait");
-  sl->busy = false;
+  const int rc = finish_wait(h, token, false, status, &sl);
   if (rc) return rc;
-  const int n = sl->n;
-  if (status) {
-    status[0] = sl->h_status[0];
-    status[1] = sl->h_status[1];
-  }
-  if (sl->h_status[0] != 0) {
-    set_error("forward reported status flags " + std::to_string(sl->h_status[0]) + " at layer " +
-              std::to_string(static_cast<int>(sl->h_status[1])) + "; outputs withheld");
-    return KB_E_NONFINITE;
-  }
-  const float* src = sl->h_out;
-  const size_t np = static_cast<size_t>(n) * 6 * 362;
-  if (policy) memcpy(policy, src, np * sizeof(float));
-  src += np;
-  if (value) memcpy(value, src, static_cast<size_t>(n) * 3 * sizeof(float));
-  src += static_cast<size_t>(n) * 3;
-  if (misc) memcpy(misc, src, static_cast<size_t>(n) * 10 * sizeof(float));
-  src += static_cast<size_t>(n) * 10;
-  if (moremisc) memcpy(moremisc, src, static_cast<size_t>(n) * 8 * sizeof(float));
-  src += static_cast<size_t>(n) * 8;
-  if (ownership) memcpy(ownership, src, static_cast<size_t>(n) * kSeq * sizeof(float));
+  copy_heads(sl->h_out, sl->n, {6 * 362, 3, 10, 8, kSeq}, {policy, value, misc, moremisc, ownership});
+  return KB_OK;
+}
+
+int kb_finish_rows(kb_handle* h, uint64_t token, float* policy, float* value, float* misc, float* moremisc,
+                   float* ownership, uint32_t status[2]) {
+  Slot* sl = nullptr;
+  const int rc = finish_wait(h, token, true, status, &sl);
+  if (rc) return rc;
+  copy_heads(sl->h_dec, sl->n, {362, 3, 4, 2, kSeq}, {policy, value, misc, moremisc, ownership});
   return KB_OK;
 }
 
