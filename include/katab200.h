@@ -313,6 +313,18 @@ KB_API int kb_mxfp8_project(const kb_mxfp8_weight* w, const void* x, int dtype, 
 #define KB_PREC_INT8 0  /* W8A8: every trunk linear INT8 x INT8 -> INT32 */
 #define KB_PREC_MXFP8 1 /* every trunk linear E4M3 x E4M3 with UE8M0 scales per 32 K, fp32 accumulate */
 
+/* Per-projection precision (the reference's LayerPrecision of a precision
+ * recipe, crates/kata_nn/src/quantization_plan.rs:36-80): */
+#define KB_PROJ_FOLLOW 0 /* the model's `precision` */
+#define KB_PROJ_INT8 1   /* W8A8, per-token / per-channel absmax scales, int32 accumulate */
+#define KB_PROJ_MXFP8 2  /* block-32 E4M3 + UE8M0, fp32 accumulate */
+#define KB_PROJ_BF16 3   /* bf16 weights and activations, fp32 accumulate (the recipe's unquantised
+                            projection; the reference's is FP16) */
+#define KB_PROJ_QKV 0
+#define KB_PROJ_OUT 1
+#define KB_PROJ_FFN_UP 2
+#define KB_PROJ_FFN_DOWN 3
+
 /* Trunk shape (BASELINE b11c768: C=768, 11 blocks, 12 heads x 64, F=3072). */
 typedef struct kb_model_desc {
   int trunk_channels; /* C; multiple of 64, <= 4096 */
@@ -321,6 +333,13 @@ typedef struct kb_model_desc {
   int head_dim;       /* 32 or 64 */
   int ffn_channels;   /* F; multiple of 64, <= 4096 */
   int precision;      /* KB_PREC_INT8 or KB_PREC_MXFP8 */
+  /* KB_PROJ_* per projection, indexed by KB_PROJ_QKV .. KB_PROJ_FFN_DOWN; all
+   * zero = every projection in `precision` (a zero-initialised descriptor). */
+  int proj_precision[4];
+  /* cudaInt8MinFfnWidth (crates/kata_nn/src/backends/int8.rs:73-83): FFN
+   * projections that resolve to INT8 run in bf16 when ffn_channels is below
+   * this width; 0 = no threshold; a multiple of 8, <= 8192. */
+  int int8_min_ffn_width;
 } kb_model_desc;
 
 /* Weight blob: fp32, out-first [N, K] row-major matrices, in this order:

@@ -153,12 +153,40 @@ def _mx_linear(xv, wdec):
     return (xdec @ wdec.T).astype(np.float32)
 
 
+def _project(kind, src, wmat, bias=None, gamma=None):
+    """fp32 result (bias included) of one trunk projection of bf16 rows `src`
+    in precision `kind` ("int8", "mxfp8" or "bf16"), with the pre-norm RMSNorm
+    fused when `gamma` is given — the single-precision branches of forward()
+    per projection: INT8 quantises the (normalised) 16-bit rows per token and
+    dequantises exactly, MXFP8 quantises them block-32, bf16 multiplies the
+    16-bit values by the bf16-rounded weight in float64 (the tensor core's fp32
+    order is not reproduced) and rounds to fp32."""
+    if kind == "int8":
+        qw, qs = quantize_weights(wmat)
+        if gamma is not None:
+            q, sa, _ = rms_quantize(src, gamma, EPS, False, kp=qw.shape[1])
+        else:
+            q, sa = quantize_rows(src, kp=qw.shape[1])
+        dots = igemm(q, qw)
+        return dequant(dots, sa, qs) if bias is None else dequant_bias(dots, sa, qs, bias)
+    xv = rms_quantize(src, gamma, EPS, False)[2] if gamma is not None else src
+    if kind == "mxfp8":
+        acc = _mx_linear(xv, _mx_weight(wmat))
+    elif kind == "bf16":
+        acc = (np.asarray(xv, np.float64) @ bf(wmat).astype(np.float64).T).astype(np.float32)
+    else:
+        raise ValueError(f"unknown projection precision {kind!r}")
+    return acc if bias is None else (acc + bias[None, :]).astype(np.float32)
+
+
 def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
     """Returns dict(policy [n,6,362], value [n,3], misc [n,10], moremisc [n,8],
     ownership [n,361], residual [n*361, C]).
 
     precision "mxfp8" runs every trunk projection as the MXFP8 path does
-    (block-32 E4M3 activations and weights, UE8M0 scales, fp32 accumulation).
+    (block-32 E4M3 activations and weights, UE8M0 scales, fp32 accumulation);
+    a 4-tuple of "int8" / "mxfp8" / "bf16" gives each projection (qkv, out,
+    ffn_up, ffn_down) its own precision, as a precision recipe does.
 
     teacher: optional (stem [n*361, C], [attention [n*361, C] per block]) float
     arrays that replace the oracle's own stem GEMM and attention results — the
@@ -176,6 +204,17 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
 
     for i in range(nb):
         cs, sn = rope_tables(w[f"{i}.rope"])
+        if isinstance(precision, (tuple, list)):
+            pq, po, pu, pd = precision
+            qkv = rope_qkv(_project(pq, x, w[f"{i}.qkv"], gamma=w[f"{i}.rms1"]), cs, sn, n, nh, hd)
+            att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None
+                   else np.asarray(teacher[1][i], np.float32))
+            x = bf((x + _project(po, att, w[f"{i}.out"])).astype(np.float32))
+            v = _project(pu, x, w[f"{i}.up"], bias=w[f"{i}.up_b"], gamma=w[f"{i}.rms2"])
+            hidden = bf(act(v, 1))
+            d = _project(pd, hidden, w[f"{i}.down"], bias=w[f"{i}.down_b"])
+            x = bf((x + d).astype(np.float32))
+            continue
         if precision == "mxfp8":
             wq, wo, wu, wd = (_mx_weight(w[f"{i}.{nm}"]) for nm in ("qkv", "out", "up", "down"))
             _, _, normed = rms_quantize(x, w[f"{i}.rms1"], EPS, False)

@@ -77,7 +77,8 @@ class ModelDesc(ctypes.Structure):
     """kb_model_desc."""
 
     _fields_ = [("trunk_channels", ctypes.c_int), ("num_blocks", ctypes.c_int), ("num_heads", ctypes.c_int),
-                ("head_dim", ctypes.c_int), ("ffn_channels", ctypes.c_int), ("precision", ctypes.c_int)]
+                ("head_dim", ctypes.c_int), ("ffn_channels", ctypes.c_int), ("precision", ctypes.c_int),
+                ("proj_precision", ctypes.c_int * 4), ("int8_min_ffn_width", ctypes.c_int)]
 
 class PostProcessParams(ctypes.Structure):
     """kb_postprocess_params (ModelPostProcessParams, crates/kata_nn/src/desc.rs:671-695,
@@ -104,6 +105,7 @@ class PostProcessParams(ctypes.Structure):
 
 # Constants mirrored from include/katab200.h.
 KB_OK, KB_E_INVALID, KB_E_CUDA, KB_E_STATE, KB_E_NONFINITE, KB_E_UNSUPPORTED = range(6)
+PROJ_FOLLOW, PROJ_INT8, PROJ_MXFP8, PROJ_BF16 = range(4)
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 EPI_I32, EPI_F16, EPI_RES_F32, EPI_16, EPI_RES16, EPI_SWIGLU16, EPI_F32 = range(7)
 ACT_NONE, ACT_GELU, ACT_SILU = 0, 1, 2

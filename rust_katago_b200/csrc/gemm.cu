@@ -172,19 +172,6 @@ __device__ __forceinline__ float2 unpack16x2(uint32_t w, bool f16) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
-// Running max(|acc|, |v|) per 16-bit lane of a packed pair: the magnitude is
-// exact, NaN propagates as the canonical NaN, the sign bit is an xor (callers
-// mask it).
-template <bool F16>
-__device__ __forceinline__ uint32_t hmax_abs2(uint32_t acc, uint32_t v) {
-  uint32_t r;
-  if constexpr (F16)
-    asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(v));
-  else
-    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(v));
-  return r;
-}
-
 // 32-bit float bits of the larger |half| held in a packed pair of |16-bit| values.
 __device__ __forceinline__ uint32_t amax16_to_f32bits(uint32_t m2, bool f16) {
   const uint32_t m = max(m2 & 0xffffu, m2 >> 16);
@@ -716,16 +703,17 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
               if constexpr (EPI == kEpiRope16) {
                 rope = col0 < g.rope_cols;  // warp-uniform
                 if (rope && row_ok) {
-                  // [token][head][pair]: the pairs of Q or K column cc (even)
-                  // start at token * rope_cols / 4 + cc / 2
+                  // [head * pairs + pair][token]: pair q of Q or K column cc
+                  // (even) is entry cc / 2 + q; the warp's 32 rows are
+                  // consecutive tokens, so each load reads one contiguous run.
                   const int half_cols = g.rope_cols / 2;
                   const int cc = c0 < half_cols ? c0 : c0 - half_cols;
-                  // (32-byte aligned: token * rope_cols / 4 and cc / 2 are multiples of 8)
-                  const size_t off = static_cast<size_t>(token) * (g.rope_cols / 4) + cc / 2;
+                  const float* pc = g.rope_cos + static_cast<size_t>(cc / 2) * g.rope_seq + token;
+                  const float* ps = g.rope_sin + static_cast<size_t>(cc / 2) * g.rope_seq + token;
 #pragma unroll
-                  for (int i = 0; i < kSub / 16; ++i) {
-                    ldg256(g.rope_cos + off + 8 * i, rc + 8 * i);
-                    ldg256(g.rope_sin + off + 8 * i, rs + 8 * i);
+                  for (int i = 0; i < kSub / 2; ++i) {
+                    rc[i] = __ldg(pc + static_cast<size_t>(i) * g.rope_seq);
+                    rs[i] = __ldg(ps + static_cast<size_t>(i) * g.rope_seq);
                   }
                 } else {
 #pragma unroll
@@ -1074,8 +1062,8 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
   if (epi == kEpiRope16 &&
       (g.rope_cos == nullptr || g.rope_sin == nullptr || g.rope_seq <= 0 || g.rope_heads <= 0 ||
        (g.rope_hd != 32 && g.rope_hd != 64) || g.rope_cols != 2 * g.rope_heads * g.rope_hd || g.rope_cols > g.n ||
-       (reinterpret_cast<uintptr_t>(g.rope_cos) & 31) || (reinterpret_cast<uintptr_t>(g.rope_sin) & 31))) {
-    set_error("rotary epilogue: needs 32-byte aligned tables, head_dim 32 or 64, rope_cols = 2 * heads * head_dim <= N");
+       (reinterpret_cast<uintptr_t>(g.rope_cos) & 3) || (reinterpret_cast<uintptr_t>(g.rope_sin) & 3))) {
+    set_error("rotary epilogue: needs fp32 tables, head_dim 32 or 64, rope_cols = 2 * heads * head_dim <= N");
     return KB_E_INVALID;
   }
   if (epi == kEpiRope16 && g.bias != nullptr) {

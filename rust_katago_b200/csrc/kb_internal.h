@@ -56,8 +56,8 @@ struct GemmArgs {
   // stored as [rows_padded/128][k/128][32 rows][4 row groups][4 K blocks].
   const uint8_t* sfa = nullptr;
   const uint8_t* sfb = nullptr;
-  // kEpiRope16: rotary tables [rope_seq, rope_heads, rope_hd / 2] (cos, sin of
-  // each pair (2p, 2p+1) of a head); the row's token is row % rope_seq, columns
+  // kEpiRope16: rotary tables [rope_heads * rope_hd / 2, rope_seq] (cos, sin of
+  // each pair (2p, 2p+1) of a head, token fastest); the row's token is row % rope_seq, columns
   // [0, rope_cols) hold Q then K, rope_cols / 2 = rope_heads * rope_hd wide each.
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
@@ -82,6 +82,10 @@ int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width
 int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t* row_amax, int rows, int width,
                               int kp, int8_t* q, float* scales, unsigned* status, unsigned layer,
                               cudaStream_t stream);
+// RMSNorm of 16-bit rows to 16-bit rows (the bf16 projection's input):
+// out = T16((x * rstd) * gamma), bound_f16 selecting the output type.
+int rms16_rows_launch(const void* x, int dtype, long ldx, int rows, int width, const float* gamma, float eps,
+                      int bound_f16, uint16_t* out, long ldo, unsigned* status, unsigned layer, cudaStream_t s);
 
 // MXFP8 (mxfp8.cu).  Largest K the block-scaled path accepts (the reference's
 // MAX_K, crates/kata_nn/src/backends/mxfp8.rs:31).

@@ -20,6 +20,19 @@ namespace kb {
 // records KB_STATUS_TIMEOUT and returns instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Running max(|acc|, |v|) per 16-bit lane of a packed pair: the magnitude is
+// exact, NaN propagates as the canonical NaN, the sign bit is an xor (callers
+// mask it).
+template <bool F16>
+__device__ __forceinline__ uint32_t hmax_abs2(uint32_t acc, uint32_t v) {
+  uint32_t r;
+  if constexpr (F16)
+    asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(v));
+  else
+    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(v));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

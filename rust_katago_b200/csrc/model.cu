@@ -88,7 +88,32 @@ int validate_desc(const kb_model_desc* d) {
               "F % 64 == 0 (<= 4096), 1..64 blocks, precision KB_PREC_INT8 or KB_PREC_MXFP8");
     return KB_E_INVALID;
   }
+  for (int i = 0; i < 4; ++i)
+    if (d->proj_precision[i] < KB_PROJ_FOLLOW || d->proj_precision[i] > KB_PROJ_BF16) {
+      set_error("model descriptor: proj_precision entries must be KB_PROJ_FOLLOW, _INT8, _MXFP8 or _BF16");
+      return KB_E_INVALID;
+    }
+  // parse_min_ffn_width (crates/kata_nn/src/backends/int8.rs:75-83)
+  if (d->int8_min_ffn_width < 0 || d->int8_min_ffn_width > 8192 || d->int8_min_ffn_width % 8 != 0) {
+    set_error("model descriptor: int8_min_ffn_width must be 8-aligned and in 0..=8192");
+    return KB_E_INVALID;
+  }
   return KB_OK;
+}
+
+// Each projection's precision (KB_PROJ_INT8 / _MXFP8 / _BF16) for qkv, out,
+// ffn_up, ffn_down: the recipe's entry, else the model's precision; an INT8
+// FFN projection narrower than int8_min_ffn_width stays unquantised, as the
+// reference's selective INT8 load keeps it in FP16 (cuda_exec.rs:631-690).
+void resolve_precision(const kb_model_desc& d, int (&out)[4]) {
+  const int base = d.precision == KB_PREC_MXFP8 ? KB_PROJ_MXFP8 : KB_PROJ_INT8;
+  for (int i = 0; i < 4; ++i) {
+    int p = d.proj_precision[i] ? d.proj_precision[i] : base;
+    if (i >= KB_PROJ_FFN_UP && p == KB_PROJ_INT8 && d.int8_min_ffn_width > 0 &&
+        d.ffn_channels < d.int8_min_ffn_width)
+      p = KB_PROJ_BF16;
+    out[i] = p;
+  }
 }
 
 template <typename T>
@@ -123,6 +148,11 @@ struct Block {
   kb_mxfp8_weight* mout = nullptr;
   kb_mxfp8_weight* mup = nullptr;
   kb_mxfp8_weight* mdown = nullptr;
+  // KB_PROJ_BF16 projections: bf16-rounded weights [N, K].
+  uint16_t* bqkv = nullptr;
+  uint16_t* bout = nullptr;
+  uint16_t* bup = nullptr;
+  uint16_t* bdown = nullptr;
   float* up_b = nullptr;
   float* down_b = nullptr;
   float* rope_cos = nullptr;  // [361, heads, head_dim/2]
@@ -133,6 +163,8 @@ struct Block {
 
 struct kb_model {
   kb_model_desc desc{};
+  int prec[4] = {};    // resolved KB_PROJ_* of qkv, out, ffn_up, ffn_down
+  bool mixed = false;  // not every projection in the model's `precision`
   int device = 0;
   uint16_t* stem_w = nullptr;  // bf16 [C, 224]
   std::vector<Block> blocks;
@@ -219,6 +251,10 @@ void destroy_model(kb_model* m) {
     kb_mxfp8_weight_destroy(b.mout);
     kb_mxfp8_weight_destroy(b.mup);
     kb_mxfp8_weight_destroy(b.mdown);
+    cudaFree(b.bqkv);
+    cudaFree(b.bout);
+    cudaFree(b.bup);
+    cudaFree(b.bdown);
     cudaFree(b.up_b);
     cudaFree(b.down_b);
     cudaFree(b.rope_cos);
@@ -303,6 +339,109 @@ int mxfp8_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale
   return rc;
 }
 
+// ---- Mixed per-projection precision (a precision recipe) ----------------
+
+int gemm_kind_of(int prec) {
+  return prec == KB_PROJ_INT8 ? kGemmI8 : prec == KB_PROJ_MXFP8 ? kGemmMXF8 : kGemmBF16;
+}
+
+// The A operand of a projection of precision `prec` from bf16 rows src [M, k]:
+// INT8 -> h->q + h->scales, MXFP8 -> h->q + h->mx_scales (with the RMSNorm
+// fused when gamma is set), BF16 -> the rows themselves, or their RMSNorm in
+// h->att.  The same quantisers as the single-precision blocks.
+int mixed_operand(kb_handle* h, int prec, const uint16_t* src, int M, int k, int kp, const float* gamma,
+                  unsigned layer, const void** a) {
+  cudaStream_t s = h->stream;
+  uint8_t* q8 = reinterpret_cast<uint8_t*>(h->q);
+  if (prec == KB_PROJ_INT8) {
+    *a = h->q;
+    return quantize_rows_launch(src, KB_DT_BF16, k, M, k, kp, gamma != nullptr, gamma, kRmsEps, 0, h->q, h->scales,
+                                h->status, layer, s);
+  }
+  if (prec == KB_PROJ_MXFP8) {
+    *a = q8;
+    if (gamma) return rms_mxfp8_launch(src, KB_DT_BF16, k, M, k, gamma, kRmsEps, 0, q8, h->mx_scales, h->status, layer, s);
+    size_t sb = 0;
+    int rc = mxfp8_dims(M, k, nullptr, nullptr, nullptr, &sb);
+    if (!rc) rc = mxfp8_quantize_launch(src, KB_DT_BF16, k, M, k, q8, h->mx_scales, sb, false, h->status, layer, s);
+    return rc;
+  }
+  if (!gamma) {
+    *a = src;
+    return KB_OK;
+  }
+  *a = h->att;
+  return rms16_rows_launch(src, KB_DT_BF16, k, M, k, gamma, kRmsEps, 0, h->att, k, h->status, layer, s);
+}
+
+// One projection out[M, n] of the mixed block in its precision.
+int mixed_gemm(kb_handle* h, int prec, const void* a, const kb_int8_weight* wi, const kb_mxfp8_weight* wm,
+               const uint16_t* wb, int M, int n, int k, int epi, void* out, const float* bias, int act, unsigned layer,
+               const Block* rope_block) {
+  GemmArgs g;
+  const void* bw = nullptr;
+  if (prec == KB_PROJ_MXFP8) {
+    g = mx_args(h, wm, M, out, bias, act, layer);
+    bw = wm->q;
+  } else {
+    g.m = M;
+    g.n = n;
+    g.out = out;
+    g.ldo = n;
+    g.bias = bias;
+    g.act = act;
+    g.out_f16 = 0;
+    g.status = h->status;
+    g.layer = layer;
+    if (prec == KB_PROJ_INT8) {
+      g.k = wi->kp;
+      g.row_scale = h->scales;
+      g.col_scale = wi->scales;
+      bw = wi->q;
+    } else {
+      g.k = k;
+      bw = wb;
+    }
+  }
+  if (rope_block) set_rope(g, *rope_block, h->model->desc);
+  return gemm_launch(gemm_kind_of(prec), epi, a, bw, g, h->stream);
+}
+
+// One transformer block whose four projections each run in their own
+// precision (kb_model::prec): the single-precision blocks' sequence, with each
+// projection's input quantised (or not) for its own precision.
+int mixed_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale, uint16_t* trace_att) {
+  const kb_model* m = h->model;
+  const kb_model_desc& d = m->desc;
+  const int c = d.trunk_channels, f = d.ffn_channels, M = n * kSeq;
+  const int kpc = (c + 15) / 16 * 16, kpf = (f + 15) / 16 * 16;
+  cudaStream_t s = h->stream;
+  const void* a = nullptr;
+  int rc = mixed_operand(h, m->prec[KB_PROJ_QKV], h->x, M, c, kpc, b.rms1, layer, &a);
+  if (!rc)
+    rc = mixed_gemm(h, m->prec[KB_PROJ_QKV], a, b.qkv, b.mqkv, b.bqkv, M, 3 * c, c, kEpiRope16, h->qkv, nullptr, 0,
+                    layer, &b);
+  if (!rc)
+    rc = attention_launch(h->qkv, nullptr, nullptr, h->att, n, kSeq, d.num_heads, d.head_dim, scale, 0, s, nullptr,
+                          h->status);
+  if (!rc && trace_att)
+    rc = check_cuda(cudaMemcpyAsync(trace_att, h->att, static_cast<size_t>(M) * c * 2, cudaMemcpyDeviceToDevice, s),
+                    "trace copy");
+  if (!rc) rc = mixed_operand(h, m->prec[KB_PROJ_OUT], h->att, M, c, kpc, nullptr, layer, &a);
+  if (!rc)
+    rc = mixed_gemm(h, m->prec[KB_PROJ_OUT], a, b.out, b.mout, b.bout, M, c, c, kEpiRes16, h->x, nullptr, 0, layer,
+                    nullptr);
+  if (!rc) rc = mixed_operand(h, m->prec[KB_PROJ_FFN_UP], h->x, M, c, kpc, b.rms2, layer, &a);
+  if (!rc)
+    rc = mixed_gemm(h, m->prec[KB_PROJ_FFN_UP], a, b.up, b.mup, b.bup, M, f, c, kEpi16, h->hidden, b.up_b,
+                    KB_ACT_GELU, layer, nullptr);
+  if (!rc) rc = mixed_operand(h, m->prec[KB_PROJ_FFN_DOWN], h->hidden, M, f, kpf, nullptr, layer, &a);
+  if (!rc)
+    rc = mixed_gemm(h, m->prec[KB_PROJ_FFN_DOWN], a, b.down, b.mdown, b.bdown, M, c, f, kEpiRes16, h->x, b.down_b, 0,
+                    layer, nullptr);
+  return rc;
+}
+
 // One forward pass of n positions on device buffers, enqueued on `s`.  When
 // `trace` is non-null it receives bf16 [(num_blocks + 2), n*361, C]: the stem
 // output, each block's attention output, and the final residual stream.
@@ -337,6 +476,11 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
   for (int bi = 0; bi < d.num_blocks; ++bi) {
     const Block& b = m->blocks[bi];
     const unsigned layer = static_cast<unsigned>(bi);
+    if (m->mixed) {
+      rc = mixed_block(h, b, layer, n, scale, trace ? trace + (1 + bi) * plane : nullptr);
+      if (rc) return rc;
+      continue;
+    }
     if (d.precision == KB_PREC_MXFP8) {
       rc = mxfp8_block(h, b, layer, n, scale, trace ? trace + (1 + bi) * plane : nullptr);
       if (rc) return rc;
@@ -561,6 +705,11 @@ int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, in
   m->desc = *desc;
   m->device = device;
   const kb_model_desc& d = *desc;
+  resolve_precision(d, m->prec);
+  {
+    const int base = d.precision == KB_PREC_MXFP8 ? KB_PROJ_MXFP8 : KB_PROJ_INT8;
+    for (int i = 0; i < 4; ++i) m->mixed = m->mixed || m->prec[i] != base;
+  }
   const int c = d.trunk_channels, f = d.ffn_channels, nh = d.num_heads, hd = d.head_dim;
   BlobCursor cur{blob, count};
   // stem [C, 217] -> bf16 [C, 224]
@@ -585,22 +734,29 @@ int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, in
     const float* freqs = cur.take(static_cast<size_t>(nh) * (hd / 2) * 2);
     rc = upload(&b.rms1, rms1, c, "upload rms");
     if (!rc) rc = upload(&b.rms2, rms2, c, "upload rms");
-    if (d.precision == KB_PREC_MXFP8) {
-      if (!rc) rc = kb_mxfp8_weight_upload(qkv, 3 * c, c, c, &b.mqkv);
-      if (!rc) rc = kb_mxfp8_weight_upload(ow, c, c, c, &b.mout);
-      if (!rc) rc = kb_mxfp8_weight_upload(up, f, c, c, &b.mup);
-      if (!rc) rc = kb_mxfp8_weight_upload(dn, c, f, f, &b.mdown);
-    } else {
-      if (!rc) rc = kb_int8_weight_upload(qkv, 3 * c, c, KB_LAYOUT_PLAIN, &b.qkv);
-      if (!rc) rc = kb_int8_weight_upload(ow, c, c, KB_LAYOUT_PLAIN, &b.out);
-      if (!rc) rc = kb_int8_weight_upload(up, f, c, KB_LAYOUT_PLAIN, &b.up);
-      if (!rc) rc = kb_int8_weight_upload(dn, c, f, KB_LAYOUT_PLAIN, &b.down);
+    // Each projection in its resolved precision.
+    const float* srcs[4] = {qkv, ow, up, dn};
+    const int ns[4] = {3 * c, c, f, c}, ks[4] = {c, c, c, f};
+    kb_int8_weight** i8[4] = {&b.qkv, &b.out, &b.up, &b.down};
+    kb_mxfp8_weight** mx[4] = {&b.mqkv, &b.mout, &b.mup, &b.mdown};
+    uint16_t** b16[4] = {&b.bqkv, &b.bout, &b.bup, &b.bdown};
+    for (int pi = 0; pi < 4 && !rc; ++pi) {
+      if (m->prec[pi] == KB_PROJ_INT8) {
+        rc = kb_int8_weight_upload(srcs[pi], ns[pi], ks[pi], KB_LAYOUT_PLAIN, i8[pi]);
+      } else if (m->prec[pi] == KB_PROJ_MXFP8) {
+        rc = kb_mxfp8_weight_upload(srcs[pi], ns[pi], ks[pi], ks[pi], mx[pi]);
+      } else {
+        std::vector<uint16_t> wb(static_cast<size_t>(ns[pi]) * ks[pi]);
+        for (size_t e = 0; e < wb.size(); ++e) wb[e] = bf16_bits(srcs[pi][e]);
+        rc = upload(b16[pi], wb.data(), wb.size(), "upload bf16 projection");
+      }
     }
     if (!rc) rc = upload(&b.up_b, up_b, f, "upload bias");
     if (!rc) rc = upload(&b.down_b, dn_b, c, "upload bias");
     if (!rc) {
       // Learned 2-D RoPE tables: angle = x*f0 + y*f1 in fp32, cosf/sinf
-      // (native_model.rs:200-228), laid out [token, head, pair].
+      // (native_model.rs:200-228), laid out [head * pairs + pair, token] so that
+      // the QKV epilogue's 32 consecutive rows read one contiguous run.
       const int pairs = hd / 2;
       std::vector<float> cs(static_cast<size_t>(kSeq) * nh * pairs), sn(cs.size());
       for (int y = 0; y < kSide; ++y)
@@ -609,7 +765,7 @@ int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, in
             for (int p = 0; p < pairs; ++p) {
               const int fi = (hh * pairs + p) * 2;
               const float angle = static_cast<float>(x) * freqs[fi] + static_cast<float>(y) * freqs[fi + 1];
-              const size_t idx = ((static_cast<size_t>(y) * kSide + x) * nh + hh) * pairs + p;
+              const size_t idx = (static_cast<size_t>(hh) * pairs + p) * kSeq + (y * kSide + x);
               cs[idx] = cosf(angle);
               sn[idx] = sinf(angle);
             }
@@ -707,7 +863,9 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
   if (!rc) rc = dev_alloc(&h->hidden, M * f, "workspace");
   if (!rc) rc = dev_alloc(&h->q, M * kq, "workspace");
   if (!rc) rc = dev_alloc(&h->scales, M, "workspace");
-  if (!rc && d.precision == KB_PREC_MXFP8) {
+  bool any_mxfp8 = false;
+  for (int i = 0; i < 4; ++i) any_mxfp8 = any_mxfp8 || model->prec[i] == KB_PROJ_MXFP8;
+  if (!rc && any_mxfp8) {
     rc = mxfp8_dims(static_cast<long>(M), static_cast<long>(c > f ? c : f), nullptr, nullptr, nullptr,
                     &h->mx_scale_bytes);
     if (!rc) rc = dev_alloc(&h->mx_scales, h->mx_scale_bytes, "workspace");

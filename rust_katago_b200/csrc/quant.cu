@@ -419,9 +419,84 @@ __global__ void __launch_bounds__(256, G <= 4 ? 3 : 1) rms_rows16_kernel(
   }
 }
 
+// Rows of exactly 256*G columns (kp == width, rows and gamma 16-byte aligned),
+// INT8 output: rms_rows16_kernel without any per-group bounds check, the
+// output type a template parameter, and the row's absolute maximum a packed
+// max(|a|, |b|) per pair (one instruction; NaN still wins, so a non-finite
+// row is classified as before).  Same arithmetic in the same order, so the
+// bytes and scales are identical to the generic kernel's.
+template <bool F16IN, bool F16OUT, int G>
+__global__ void __launch_bounds__(256, 3) rms_rows16_full_kernel(
+    const uint16_t* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows,
+    int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
+  constexpr int kW = 256 * G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int step = gridDim.x * 8;
+  int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;  // warp-uniform
+  uint4 raw[G];
+#pragma unroll
+  for (int j = 0; j < G; ++j)
+    raw[j] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx + 8 * (lane + 32 * j)));
+  for (; row < rows; row += step) {
+    float v[G][8];
+    raw16_to_float<F16IN, G>(raw, v);
+    if (row + step < rows) {
+      const uint16_t* nxt = x + static_cast<size_t>(row + step) * ldx;
+#pragma unroll
+      for (int j = 0; j < G; ++j) raw[j] = __ldg(reinterpret_cast<const uint4*>(nxt + 8 * (lane + 32 * j)));
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < G; ++j)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sum = __fmaf_rn(v[j][t], v[j][t], sum);
+    sum = warp_sum_xor(sum);
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(kW)), eps)));
+    uint32_t nw[G][4];
+    uint32_t amax2 = 0;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const float4* gp = reinterpret_cast<const float4*>(gamma + 8 * (lane + 32 * j));
+      const float4 ga = __ldg(gp), gb = __ldg(gp + 1);
+      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 n2 = mul2(mul2(make_float2(v[j][2 * t], v[j][2 * t + 1]), make_float2(rstd, rstd)),
+                               make_float2(gm[2 * t], gm[2 * t + 1]));
+        nw[j][t] = pack16x2(n2, F16OUT);
+        amax2 = hmax_abs2<F16OUT>(amax2, nw[j][t]);
+      }
+    }
+    quantize_packed_row<F16OUT, G>(nw, amax2 & 0x7fff7fffu, kW, lane, q + static_cast<size_t>(row) * kW,
+                                   scales + row, status, layer);
+  }
+}
+
+template <int G>
+int launch_rms16_full(bool f16in, bool f16out, const uint16_t* x, long ldx, const float* gamma, float eps, int rows,
+                      int8_t* q, float* scales, unsigned* status, unsigned layer, cudaStream_t s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto k = f16in ? (f16out ? rms_rows16_full_kernel<true, true, G> : rms_rows16_full_kernel<true, false, G>)
+                       : (f16out ? rms_rows16_full_kernel<false, true, G> : rms_rows16_full_kernel<false, false, G>);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+  const int want = (rows + 7) / 8, cap = per_sm * num_sms(dev);
+  k<<<want < cap ? want : cap, 256, 0, s>>>(x, ldx, gamma, eps, rows, q, scales, status, layer);
+  return check_cuda(cudaGetLastError(), "rms quantiser launch");
+}
+
 template <bool MX, int G>
 int launch_rms16(int dtype, const void* x, long ldx, const float* gamma, float eps, int rows, int width, int kp,
                  int blocks4, int bound_f16, void* q, void* scales, unsigned* status, unsigned layer, cudaStream_t s) {
+  if constexpr (!MX && G <= 4) {
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx & 7) == 0 &&
+                         (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0;
+    if (width == 256 * G && kp == width && aligned)
+      return launch_rms16_full<G>(dtype == kInF16, bound_f16 != 0, static_cast<const uint16_t*>(x), ldx, gamma, eps,
+                                  rows, static_cast<int8_t*>(q), static_cast<float*>(scales), status, layer, s);
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   // Persistent: as many CTAs as stay resident together, no second wave.
@@ -627,6 +702,43 @@ int launch_amax(const void* x, long ldx, const uint32_t* row_amax, int rows, int
 
 }  // namespace
 
+// RMSNorm of 16-bit rows to 16-bit rows, the input of an unquantised (bf16)
+// projection: out = T16((x * rstd) * gamma), the same values the fused RMS
+// quantisers quantise (rms_normalize); a non-finite row sets the status word
+// as the quantisers do.  Persistent warp per row.
+template <bool F16IN, int G>
+__global__ void __launch_bounds__(256) rms_rows16_out16_kernel(
+    const uint16_t* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows, int width,
+    int bound_f16, uint16_t* __restrict__ out, long ldo, unsigned* status, unsigned layer) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = (width + 7) / 8;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    uint4 raw[G];
+    load_raw16<G>(x + static_cast<size_t>(row) * ldx, width, lane, raw);
+    float v[G][8];
+    raw16_to_float<F16IN, G>(raw, v);
+    uint32_t nw[G][4];
+    uint32_t amax2;
+    rms_normalize<G>(v, gamma, eps, width, lane, bound_f16 != 0, nw, amax2);
+    const uint32_t m16 = warp_max_u32(max(amax2 & 0xffffu, amax2 >> 16));
+    const uint32_t inf16 = bound_f16 ? 0x7c00u : 0x7f80u;
+    if (lane == 0 && m16 >= inf16) record_status(status, m16 > inf16 ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+    uint16_t* dst = out + static_cast<size_t>(row) * ldo;
+    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j, c0 = 8 * g;
+      if (g >= groups) continue;
+      if (vec && c0 + 8 <= width) {
+        *reinterpret_cast<uint4*>(dst + c0) = make_uint4(nw[j][0], nw[j][1], nw[j][2], nw[j][3]);
+      } else {
+        for (int t = 0; t < 8 && c0 + t < width; ++t)
+          dst[c0 + t] = static_cast<uint16_t>((t & 1) ? nw[j][t / 2] >> 16 : nw[j][t / 2] & 0xffffu);
+      }
+    }
+  }
+}
+
 // Fused RMSNorm -> 16-bit -> MXFP8 over rows of `width` (<= 4096) columns.
 int rms_mxfp8_launch(const void* x, int dtype, long ldx, int rows, int width, const float* gamma, float eps,
                      int bound_f16, uint8_t* q, uint8_t* scales, unsigned* status, unsigned layer,
@@ -726,6 +838,35 @@ int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width
                                                 scales, status, layer, stream);
   }
   set_error("unknown activation dtype");
+  return KB_E_INVALID;
+}
+
+
+int rms16_rows_launch(const void* x, int dtype, long ldx, int rows, int width, const float* gamma, float eps,
+                      int bound_f16, uint16_t* out, long ldo, unsigned* status, unsigned layer, cudaStream_t s) {
+  if ((dtype != kInF16 && dtype != kInBF16) || width <= 0 || width > 4096 || ldx < width || ldo < width ||
+      gamma == nullptr || !(eps > 0.0f)) {
+    set_error("RMS to 16-bit rows: 16-bit input, width <= 4096, strides >= width, gamma, eps > 0");
+    return KB_E_INVALID;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int want = (rows + 7) / 8, cap = 8 * num_sms(dev);
+  const int grid = want < cap ? want : cap;
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  const int need = (width + 255) / 256;
+#define KB_R16(GG)                                                                                          \
+  if (need <= GG) {                                                                                         \
+    if (dtype == kInF16)                                                                                    \
+      rms_rows16_out16_kernel<true, GG><<<grid, 256, 0, s>>>(xs, ldx, gamma, eps, rows, width, bound_f16, out, \
+                                                             ldo, status, layer);                             \
+    else                                                                                                    \
+      rms_rows16_out16_kernel<false, GG><<<grid, 256, 0, s>>>(xs, ldx, gamma, eps, rows, width, bound_f16, out, \
+                                                              ldo, status, layer);                            \
+    return check_cuda(cudaGetLastError(), "rms 16-bit launch");                                             \
+  }
+  KB_R16(1) KB_R16(2) KB_R16(3) KB_R16(4) KB_R16(6) KB_R16(8) KB_R16(12) KB_R16(16)
+#undef KB_R16
   return KB_E_INVALID;
 }
 

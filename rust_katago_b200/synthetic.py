@@ -28,12 +28,28 @@ class Topology:
     head_dim: int = 64
     ffn_channels: int = 3072
     precision: int = 0  # KB_PREC_INT8 (0) or KB_PREC_MXFP8 (1)
+    # KB_PROJ_* per projection (qkv, out, ffn_up, ffn_down); 0 = follow `precision`
+    proj_precision: tuple = (0, 0, 0, 0)
+    int8_min_ffn_width: int = 0
 
     def desc(self):
         from ._capi import ModelDesc
 
         return ModelDesc(self.trunk_channels, self.num_blocks, self.num_heads, self.head_dim, self.ffn_channels,
-                         self.precision)
+                         self.precision, (ctypes.c_int * 4)(*self.proj_precision), self.int8_min_ffn_width)
+
+    def resolved_precision(self) -> tuple:
+        """Each projection's precision as the model loader resolves it: "int8",
+        "mxfp8" or "bf16" for (qkv, out, ffn_up, ffn_down)."""
+        names = {1: "int8", 2: "mxfp8", 3: "bf16"}
+        base = 2 if self.precision == 1 else 1
+        out = []
+        for i, p in enumerate(self.proj_precision):
+            p = p or base
+            if i >= 2 and p == 1 and self.int8_min_ffn_width and self.ffn_channels < self.int8_min_ffn_width:
+                p = 3
+            out.append(names[p])
+        return tuple(out)
 
 
 B11C768 = Topology()

@@ -130,6 +130,32 @@ def test_rms_quantize_bit_exact(cuda, oracle, rows, mid, boundary, nonfinite):
     assert same_f32(host(s), os_)
 
 
+@pytest.mark.parametrize("mid,stride", [(256, 256), (512, 512), (768, 768), (1024, 1024), (768, 776), (384, 384)])
+@pytest.mark.parametrize("dtype", [_capi.DT_BF16, _capi.DT_F16])
+@pytest.mark.parametrize("boundary", [_capi.DT_F16, _capi.DT_BF16])
+def test_rms_quantize_16bit_input_bit_exact(cuda, oracle, mid, stride, dtype, boundary):
+    """16-bit residual rows (the trunk's case): full rows of 256*G columns take
+    the kernel without bounds checks, other widths and strides the generic one;
+    both against the oracle, with zero, tiny, huge and non-finite rows."""
+    torch = cuda
+    rows = 3001
+    x = np.zeros((rows, stride), np.float32)
+    x[:, :mid] = rms_input(rows, mid)
+    x[0, 0], x[1, 3], x[2, mid - 1] = np.inf, np.nan, -np.inf
+    f16 = dtype == _capi.DT_F16
+    xb = oracle.f16_encode(x) if f16 else oracle.bf16_encode(x)
+    xv = oracle.decode16(xb, f16)
+    gamma = ((np.arange(mid) % 101).astype(np.float32) / np.float32(37.0) - 1).astype(np.float32)
+    kp = (mid + 15) // 16 * 16
+    q = torch.full((rows, kp), 77, dtype=torch.int8, device="cuda")
+    s = torch.zeros(rows, device="cuda")
+    int8.rms_quantize(dev(torch, xb), dtype, rows, mid, stride, dev(torch, gamma), 1e-5, boundary, kp, q, s)
+    torch.cuda.synchronize()
+    oq, os_, _ = oracle.rms_quantize(np.ascontiguousarray(xv[:, :mid]), gamma, 1e-5, boundary == _capi.DT_F16, kp=kp)
+    assert (host(q) == oq).all()
+    assert same_f32(host(s), os_)
+
+
 @pytest.mark.parametrize("dtype", [_capi.DT_F16, _capi.DT_BF16, _capi.DT_F32])
 @pytest.mark.parametrize("rows,width,stride", [(1, 8, 8), (3, 24, 32), (1025, 472, 480), (2000, 3072, 3072), (7, 1160, 1163)])
 def test_quantize_rows_bit_exact(cuda, oracle, dtype, rows, width, stride):
