@@ -37,12 +37,15 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle row of K per stage
 // Epilogue warps: 16 (four per TMEM lane quarter) for the arithmetic-heavy
-// 16-bit epilogues of short-K projections (bias + activation, rotary), 8 for
-// the others (residual adds, fp32 / int32 outputs), whose cost is memory.
-template <int EPI>
-constexpr int epi_warps() { return (EPI == 3 /* kEpi16 */ || EPI == 7 /* kEpiRope16 */) ? 16 : 8; }
-template <int EPI>
-constexpr int gemm_threads() { return 64 + 32 * epi_warps<EPI>(); }
+// 16-bit epilogues (bias + activation, rotary) and for the residual add of
+// short-K projections, where draining the epilogue bounds the tile; 8 for the
+// others (long-K residual adds keep the deeper operand ring; fp32 / int32
+// outputs).
+template <int EPI, int DEEP>
+constexpr int epi_warps() {
+  return (EPI == 3 /* kEpi16 */ || EPI == 7 /* kEpiRope16 */ || (EPI == 4 /* kEpiRes16 */ && DEEP)) ? 16 : 8;
+}
+constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
 constexpr int kStageTile = 32 * 64;  // one 32x32 16-bit staging tile (2 KiB)
 constexpr int kSmemLimit = 227 * 1024;
 
@@ -298,11 +301,11 @@ __device__ __forceinline__ float2 acc_bias_pairn(const uint32_t (&v)[N], int i, 
   }
 }
 
-template <int KIND, int BN, int EPI, int ACT, int SB>
-__global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
+template <int KIND, int BN, int EPI, int ACT, int SB, int EW>
+__global__ void __launch_bounds__(gemm_threads(EW), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g, const int use_tma_out) {
-  constexpr int kEpiWarps = epi_warps<EPI>();
+  constexpr int kEpiWarps = EW;
   constexpr int kParts = kEpiWarps / 4;  // epilogue warps per TMEM lane quarter
   // Columns per accumulator read: 16 with 16 epilogue warps (register budget), else 32.
   constexpr int kSub = kEpiWarps == 16 ? 16 : 32;
@@ -533,40 +536,48 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
               issue_load();
             }
             uint8_t* buf = stage + (sq % SB) * kStageTile;
-            uint32_t v[32];
-            tmem_ldn<32>(taddr + j * 32, v);
-            float sw[32], bias[32];
-            if (g.cols_vec) {  // warp-uniform
-              if constexpr (KIND == kGemmI8) load_vec_aligned<32>(g.col_scale + col0, sw);
-              if (with_bias) load_vec_aligned<32>(g.bias + col0, bias);
-            } else {
-              if constexpr (KIND == kGemmI8) load_vecn<32>(g.col_scale, col0, g.n, sw);
-              if (with_bias) load_vecn<32>(g.bias, col0, g.n, bias);
-            }
-            tmem_ld_wait();
-            if (!__all_sync(0xffffffffu, mbar_wait(&rbar[sq % SB], (sq / SB) & 1, abort_flag))) {
-              ok = false;
-              break;
-            }
             const int swz = (lane >> 1) & 3;
             uint32_t amax2 = 0;
+            // The chunk's 32 columns in kHalves pieces of kSub (16 with 16
+            // epilogue warps: the register budget of a 576-thread CTA).
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint4* cell = reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ swz) << 4));
-              const uint4 r4 = *cell;
-              const uint32_t rw[4] = {r4.x, r4.y, r4.z, r4.w};
-              uint32_t ow[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int i = 4 * c + q;
-                const float2 x =
-                    with_bias ? acc_bias_pairn<KIND, 32>(v, i, sa, sw, bias) : acc_pairn<KIND, 32>(v, i, sa, sw);
-                const float2 r = unpack16x2(rw[q], f16);
-                ow[q] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
-                if constexpr (KIND == kGemmMXF8) amax2 = __vmaxu2(amax2, ow[q] & 0x7fff7fffu);
+            for (int hh = 0; hh < kHalves; ++hh) {
+              const int c0 = col0 + hh * kSub;
+              uint32_t v[kSub];
+              tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, v);
+              float sw[kSub], bias[kSub];
+              if (g.cols_vec) {  // warp-uniform
+                if constexpr (KIND == kGemmI8) load_vec_aligned<kSub>(g.col_scale + c0, sw);
+                if (with_bias) load_vec_aligned<kSub>(g.bias + c0, bias);
+              } else {
+                if constexpr (KIND == kGemmI8) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
+                if (with_bias) load_vecn<kSub>(g.bias, c0, g.n, bias);
               }
-              *cell = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+              tmem_ld_wait();
+              if (hh == 0 && !__all_sync(0xffffffffu, mbar_wait(&rbar[sq % SB], (sq / SB) & 1, abort_flag))) {
+                ok = false;
+                break;
+              }
+#pragma unroll
+              for (int c = 0; c < kSub / 8; ++c) {
+                const int cc = hh * (kSub / 8) + c;  // 16-byte cell of the 32-column chunk
+                uint4* cell = reinterpret_cast<uint4*>(buf + lane * 64 + ((cc ^ swz) << 4));
+                const uint4 r4 = *cell;
+                const uint32_t rw[4] = {r4.x, r4.y, r4.z, r4.w};
+                uint32_t ow[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const int i = 4 * c + q;
+                  const float2 x = with_bias ? acc_bias_pairn<KIND, kSub>(v, i, sa, sw, bias)
+                                             : acc_pairn<KIND, kSub>(v, i, sa, sw);
+                  const float2 r = unpack16x2(rw[q], f16);
+                  ow[q] = pack16x2(make_float2(__fadd_rn(r.x, x.x), __fadd_rn(r.y, x.y)), f16);
+                  if constexpr (KIND == kGemmMXF8) amax2 = __vmaxu2(amax2, ow[q] & 0x7fff7fffu);
+                }
+                *cell = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+              }
             }
+            if (!ok) break;
             if constexpr (KIND == kGemmMXF8)
               nonfinite |= row_ok && max(amax2 & 0xffffu, amax2 >> 16) >= (f16 ? 0x7c00u : 0x7f80u);
             fence_proxy_async_smem();
@@ -922,10 +933,10 @@ bool epi_16bit(int epi) {
 template <int KIND, int BN, int EPI, int ACT, int DEEP>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int use_tma_out,
                const GemmArgs& g, cudaStream_t stream) {
-  constexpr int EW = epi_warps<EPI>();
+  constexpr int EW = epi_warps<EPI, DEEP>();
   constexpr int SB = DEEP ? (EW == 16 ? 2 : 4) : (EW == 16 ? 1 : 2);
   using Cfg = GemmCfg<KIND, BN, SB, EW>;
-  auto kern = gemm_kernel<KIND, BN, EPI, ACT, SB>;
+  auto kern = gemm_kernel<KIND, BN, EPI, ACT, SB, EW>;
   int dev = 0;
   cudaGetDevice(&dev);
   // Function attributes live in each device's context: set once per device.
@@ -938,7 +949,7 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   }
   const int tiles = ((g.m + kBM - 1) / kBM) * ((g.n + BN - 1) / BN);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kern<<<grid, gemm_threads<EPI>(), Cfg::kSmemBytes, stream>>>(ma, mb, mo, g, use_tma_out);
+  kern<<<grid, gemm_threads(EW), Cfg::kSmemBytes, stream>>>(ma, mb, mo, g, use_tma_out);
   return check_cuda(cudaGetLastError(), "gemm launch");
 }
 

@@ -192,6 +192,7 @@ struct Slot {
   float* h_dec = nullptr;
   float* d_dec = nullptr;
   cudaEvent_t done = nullptr;
+  cudaEvent_t inputs_ready = nullptr;  // this slot's host-to-device copies landed
   int n = 0;
   bool busy = false;
   bool decoded = false;
@@ -212,6 +213,9 @@ struct kb_handle {
   int max_batch = 0;
   int nhwc = 0;
   cudaStream_t stream = nullptr;
+  // Host-to-device input copies of kb_submit / kb_submit_rows: a second
+  // submission's copies overlap the forward of the one in flight.
+  cudaStream_t copy_stream = nullptr;
   // workspace
   uint16_t* stem_a = nullptr;   // [M, 224] bf16
   uint16_t* x = nullptr;        // [M, C] residual
@@ -644,6 +648,7 @@ void destroy_handle(kb_handle* h) {
     cudaFree(sl.d_post);
     cudaFree(sl.d_dec);
     if (sl.done) cudaEventDestroy(sl.done);
+    if (sl.inputs_ready) cudaEventDestroy(sl.inputs_ready);
   }
   cudaFree(h->stem_a);
   cudaFree(h->x);
@@ -657,6 +662,7 @@ void destroy_handle(kb_handle* h) {
   cudaFree(h->hp);
   cudaFree(h->status);
   if (h->stream) cudaStreamDestroy(h->stream);
+  if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
   delete h;
 }
 
@@ -856,6 +862,7 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
   size_t kq = c > f ? c : f;
   kq = (kq + 15) / 16 * 16;
   rc = check_cuda(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking), "stream create");
+  if (!rc) rc = check_cuda(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking), "stream create");
   if (!rc) rc = dev_alloc(&h->stem_a, M * kStemK, "workspace");
   if (!rc) rc = dev_alloc(&h->x, M * c, "workspace");
   if (!rc) rc = dev_alloc(&h->qkv, M * 3 * c, "workspace");
@@ -892,6 +899,7 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
     if (!rc) rc = dev_alloc(&sl.d_post, np, "device row parameters");
     if (!rc) rc = dev_alloc(&sl.d_dec, nd, "device decoded output");
     if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming), "event");
+    if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&sl.inputs_ready, cudaEventDisableTiming), "event");
   }
   if (rc) {
     destroy_handle(h);
@@ -904,6 +912,7 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
 void kb_handle_destroy(kb_handle* h) {
   if (!h) return;
   cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->copy_stream);
   cudaStreamSynchronize(h->stream);
   destroy_handle(h);
 }
@@ -1000,10 +1009,13 @@ int submit_impl(kb_handle* h, int n, const float* spatial, const float* global, 
   else
     memset(h_sym, 0, static_cast<size_t>(n) * sizeof(int));
   const int* d_sym = reinterpret_cast<const int*>(sl->d_global + ng);
-  cudaStream_t s = h->stream;
-  rc = check_cuda(cudaMemcpyAsync(sl->d_spatial, sl->h_spatial, ns * sizeof(float), cudaMemcpyHostToDevice, s), "H2D");
+  cudaStream_t s = h->stream, cs = h->copy_stream;
+  // The slot is free, so the forward that last read its device inputs has
+  // completed (its `done` event was waited for): the copies may run now,
+  // beside the other slot's forward, and the forward waits for them.
+  rc = check_cuda(cudaMemcpyAsync(sl->d_spatial, sl->h_spatial, ns * sizeof(float), cudaMemcpyHostToDevice, cs), "H2D");
   if (!rc)
-    rc = check_cuda(cudaMemcpyAsync(sl->d_global, sl->h_global, (ng + n) * sizeof(float), cudaMemcpyHostToDevice, s),
+    rc = check_cuda(cudaMemcpyAsync(sl->d_global, sl->h_global, (ng + n) * sizeof(float), cudaMemcpyHostToDevice, cs),
                     "H2D");
   const size_t row_bytes = static_cast<size_t>(n) * sizeof(kb_row_params);
   if (!rc && rows) {
@@ -1011,8 +1023,10 @@ int submit_impl(kb_handle* h, int n, const float* spatial, const float* global, 
     memcpy(sl->h_post, rows, row_bytes);
     if (legal) memcpy(sl->h_post + row_bytes, legal, static_cast<size_t>(n) * 362);
     rc = check_cuda(cudaMemcpyAsync(sl->d_post, sl->h_post, row_bytes + (legal ? static_cast<size_t>(n) * 362 : 0),
-                                    cudaMemcpyHostToDevice, s), "H2D");
+                                    cudaMemcpyHostToDevice, cs), "H2D");
   }
+  if (!rc) rc = check_cuda(cudaEventRecord(sl->inputs_ready, cs), "event record");
+  if (!rc) rc = check_cuda(cudaStreamWaitEvent(s, sl->inputs_ready, 0), "stream wait");
   if (!rc) rc = run_forward(h, n, sl->d_spatial, sl->d_global, d_sym, sl->d_out, true);
   if (rows) {
     if (!rc)

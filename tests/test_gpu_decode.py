@@ -171,3 +171,34 @@ def test_submit_rows_matches_raw_submit_and_oracle(cuda):
     bad["policy_optimism"][0] = 1.5
     with pytest.raises(_capi.KbError, match="policy_optimism"):
         h.submit_rows(spatial, glob, bad)
+
+
+def test_two_submissions_in_flight(cuda):
+    """Both pipeline slots in use: the second submission's input copies run on
+    the copy stream while the first forward runs; each result equals the one
+    computed alone, bit for bit, for the raw and the decoding entry points."""
+    topo = synthetic.Topology(256, 2, 4, 64, 1024)
+    blob = synthetic.make_blob(topo, 5)
+    n = 5
+    sa, ga = synthetic.make_positions(n, 51)
+    sb, gb = synthetic.make_positions(n, 52)
+    rows = random_rows(np.random.default_rng(9), n)
+    model = backend.CudaBackend.load_model(topo, blob)
+    h = backend.CudaBackend.create_compute_handle(model, n)
+    alone_a, alone_b = h.finish_rows(h.submit_rows(sa, ga, rows)), h.finish_rows(h.submit_rows(sb, gb, rows))
+    raw_a, raw_b = h.get_output(sa, ga), h.get_output(sb, gb)
+    for _ in range(3):
+        ta, tb = h.submit_rows(sa, ga, rows), h.submit_rows(sb, gb, rows)
+        got_a, got_b = h.finish_rows(ta), h.finish_rows(tb)
+        for got, ref in ((got_a, alone_a), (got_b, alone_b)):
+            for f in FIELDS:
+                assert np.array_equal(getattr(got, f), getattr(ref, f)), f
+        ta, tb = h.submit_output(sa, ga), h.submit_output(sb, gb)
+        # finished in the other order
+        got_b, got_a = h.finish_output(tb), h.finish_output(ta)
+        for got, ref in ((got_a, raw_a), (got_b, raw_b)):
+            assert np.array_equal(got.policy, ref.policy) and np.array_equal(got.ownership, ref.ownership)
+    with pytest.raises(_capi.KbError, match="slots"):
+        h.submit_output(sa, ga)
+        h.submit_output(sb, gb)
+        h.submit_output(sa, ga)
