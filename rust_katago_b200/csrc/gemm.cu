@@ -790,6 +790,40 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
                 nonfinite |= row_ok && max(amax2 & 0xffffu, amax2 >> 16) >= (f16 ? 0x7c00u : 0x7f80u);
             }
             emit16<SB>(o, g, hw, row, row0q, col0, lane, row_ok, valid);
+          } else if (EPI == kEpiF32 && o.map != nullptr) {
+            // fp32 results through the staging tiles: 16 columns (64 bytes) of
+            // the warp's 32 rows per TMA store (the tensor map clips the
+            // tile's edges), the same arithmetic as the plain-store path.
+#pragma unroll
+            for (int hh = 0; hh < kHalves; ++hh) {
+              const int c0 = col0 + hh * kSub;
+              uint32_t v[kSub];
+              tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, v);
+              float sw[kSub], bias[kSub];
+              if constexpr (KIND == kGemmI8) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
+              load_vecn<kSub>(g.bias, c0, g.n, bias);
+              tmem_ld_wait();
+              uint32_t w[kSub];
+#pragma unroll
+              for (int i = 0; i < kSub; ++i) {
+                float x;
+                if (g.bias && KIND == kGemmI8)
+                  x = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[i])), sa), sw[i], bias[i]);
+                else if (g.bias)
+                  x = __fadd_rn(acc_value<KIND>(v[i], sa, 1.0f), bias[i]);
+                else
+                  x = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
+                if constexpr (KIND == kGemmMXF8) nonfinite |= row_ok && c0 + i < g.n && !isfinite(x);
+                w[i] = __float_as_uint(x);
+              }
+#pragma unroll
+              for (int q = 0; q < kSub / 16; ++q) {
+                uint32_t piece[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) piece[i] = w[16 * q + i];
+                emit16<SB>(o, g, piece, row, row0q, c0 + 16 * q, lane, row_ok, 0);
+              }
+            }
           } else {
 #pragma unroll
             for (int hh = 0; hh < kHalves; ++hh) {
@@ -1106,6 +1140,15 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
       (reinterpret_cast<uintptr_t>(g.out) & 15) == 0) {
     const long cols = epi == kEpiSwiGLU16 ? g.n_out : g.n;
     rc = encode_2d(&mo, CU_TENSOR_MAP_DATA_TYPE_UINT16, g.out, cols, g.m, g.ldo * 2, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+    tma_out = 1;
+  }
+  // fp32 outputs (no residual) leave through the staging tiles too: 16
+  // fp32 columns are 64 bytes, the same box as 32 16-bit columns.
+  if (!direct_store && epi == kEpiF32 && g.residual == nullptr && (g.ldo * 4) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(g.out) & 15) == 0) {
+    rc = encode_2d(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.out, g.n, g.m, g.ldo * 4, 16, 32,
                    CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
     tma_out = 1;
