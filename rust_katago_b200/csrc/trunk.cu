@@ -99,31 +99,42 @@ __global__ void stem_gather_kernel(const float* __restrict__ spatial, const floa
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // g = bf16(silu(x * gamma + beta)) over [rows, c] bf16, c a multiple of 8:
-// each thread converts 8 consecutive values (one 16-byte load and store).
+// each thread converts 8 consecutive values (one 16-byte load and store) per
+// vector, two vectors per loop trip with both loads issued first (more bytes
+// in flight per thread: the kernel streams 2 bytes in and out per value).
+__device__ __forceinline__ uint4 tip8(uint4 raw, const float* __restrict__ gamma, const float* __restrict__ beta,
+                                      int col) {
+  const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + col));
+  const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + col) + 1);
+  const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta + col));
+  const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta + col) + 1);
+  const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const float bt[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float lo = from_bf16(static_cast<uint16_t>(w[j] & 0xffffu));
+    const float hi = from_bf16(static_cast<uint16_t>(w[j] >> 16));
+    const float v0 = __fadd_rn(__fmul_rn(lo, gm[2 * j]), bt[2 * j]);
+    const float v1 = __fadd_rn(__fmul_rn(hi, gm[2 * j + 1]), bt[2 * j + 1]);
+    o[j] = static_cast<uint32_t>(bits_bf16(silu_fast(v0))) | (static_cast<uint32_t>(bits_bf16(silu_fast(v1))) << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __global__ void trunk_tip_kernel(const uint16_t* __restrict__ x, const float* __restrict__ gamma,
                                  const float* __restrict__ beta, uint16_t* __restrict__ g, long total8, int c8) {
-  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total8;
-       i += static_cast<long>(gridDim.x) * blockDim.x) {
-    const int col = static_cast<int>(i % c8) * 8;
-    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x) + i);
-    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + col));
-    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + col) + 1);
-    const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta + col));
-    const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta + col) + 1);
-    const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    const float bt[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float lo = from_bf16(static_cast<uint16_t>(w[j] & 0xffffu));
-      const float hi = from_bf16(static_cast<uint16_t>(w[j] >> 16));
-      const float v0 = __fadd_rn(__fmul_rn(lo, gm[2 * j]), bt[2 * j]);
-      const float v1 = __fadd_rn(__fmul_rn(hi, gm[2 * j + 1]), bt[2 * j + 1]);
-      o[j] = static_cast<uint32_t>(bits_bf16(silu_fast(v0))) | (static_cast<uint32_t>(bits_bf16(silu_fast(v1))) << 16);
-    }
-    reinterpret_cast<uint4*>(g)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  const uint4* x4 = reinterpret_cast<const uint4*>(x);
+  uint4* g4 = reinterpret_cast<uint4*>(g);
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + stride < total8; i += 2 * stride) {
+    const uint4 r0 = __ldg(x4 + i), r1 = __ldg(x4 + i + stride);
+    g4[i] = tip8(r0, gamma, beta, static_cast<int>(i % c8) * 8);
+    g4[i + stride] = tip8(r1, gamma, beta, static_cast<int>((i + stride) % c8) * 8);
   }
+  if (i < total8) g4[i] = tip8(__ldg(x4 + i), gamma, beta, static_cast<int>(i % c8) * 8);
 }
 
 struct HeadWeights {
