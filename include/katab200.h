@@ -194,15 +194,23 @@ KB_API int kb_int8_ffn_gelu_rms(kb_int8_workspace* ws, uintptr_t stream, const f
  * allocates nothing: its scratch is one static 8 MiB device array per device
  * (reserved when the library is loaded, held until exit), so `rows` is limited
  * to what fits (about 900 tokens, 2 positions, for C=768, F=3072); larger
- * calls fail with KB_E_INVALID and say the limit.  The first call on each
- * device looks the array's address up (cudaGetSymbolAddress) and should come
- * before any stream capture.  All calls on a device share the array: calls
+ * calls fail with KB_E_INVALID and say the limit.  The weights must live on
+ * the current device (KB_E_STATE otherwise).  The first call on each device
+ * (or kb_int8_noalloc_prepare) looks the array's address up
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All calls on a device share the array: calls
  * that overlap on the GPU race; nothing in it needs clearing between calls.
  * No counterpart in the reference. */
 KB_API int kb_int8_ffn_gelu_rms_noalloc(uintptr_t stream, const float* gamma, float eps,
                                         const kb_int8_weight* up, const float* up_bias,
                                         const kb_int8_weight* down, const float* down_bias,
                                         uint16_t* residual, int rows);
+
+/* Looks up the current device's no-alloc scratch address now, so that a caller
+ * that captures kb_int8_ffn_gelu_rms_noalloc into a CUDA graph can do the
+ * lookup before the capture begins.  Allocates nothing.  Optional: the first
+ * kb_int8_ffn_gelu_rms_noalloc call on a device does the same.
+ * No counterpart in the reference. */
+KB_API int kb_int8_noalloc_prepare(void);
 
 /* ------------------------------------------------------------------ bf16 GEMM */
 
@@ -307,6 +315,25 @@ KB_API int kb_mxfp8_gemm(const uint8_t* a_q, const uint8_t* a_scales, int rows, 
 KB_API int kb_mxfp8_project(const kb_mxfp8_weight* w, const void* x, int dtype, int rows, int stride,
                             uint8_t* q_scratch, uint8_t* scale_scratch, size_t scale_capacity, int out_kind,
                             void* out, long ldo, uint32_t* status, uint32_t layer, uintptr_t stream);
+
+/* ------------------------------------------------------------------ tests of the abort path */
+
+/* Test entry points for the bounded device waits (no reference counterpart;
+ * the reference's kernels do not wait on one another).  Every wait inside this
+ * library's kernels gives up after two seconds, records KB_STATUS_TIMEOUT in
+ * the status word, lets the copies and MMAs it has issued finish, frees its
+ * tensor memory and returns, so a fault never hangs the GPU. */
+
+/* One CTA waits `limit_ns` (1 ns .. 1 s) on a barrier that nothing arrives at,
+ * then records KB_STATUS_TIMEOUT in status[2]. */
+KB_API int kb_test_wait_timeout(unsigned long long limit_ns, uint32_t* status, uintptr_t stream);
+
+/* kb_int8_gemm_i32 with the limit of its waits on work shortened to
+ * wait_limit_ns (1 ns .. 2 s): with a limit shorter than the GEMM the kernel
+ * aborts, records KB_STATUS_TIMEOUT in status[2] and returns (dots are then
+ * partial); the stream and the device stay usable. */
+KB_API int kb_test_int8_gemm_i32_wait_limit(const int8_t* a, const int8_t* w, int32_t* dots, int m, int n, int kp,
+                                            unsigned long long wait_limit_ns, uint32_t* status, uintptr_t stream);
 
 /* ------------------------------------------------------------------ model and evaluator */
 

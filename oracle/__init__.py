@@ -76,6 +76,8 @@ def lib() -> ctypes.CDLL:
             "or_dequant_bias": (None, [P, P, P, P, I, I, P]),
             "or_w8a8_project_half": (None, [P, I, I, P, P, I, I, P]),
             "or_max_threads": (I, []),
+            "or_set_threads": (I, [I]),
+            "or_attention_tc": (None, [P, I, I, I, I, F, I, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -209,6 +211,11 @@ def w8a8_project_half(x16: np.ndarray, wq: np.ndarray, sw: np.ndarray, threads: 
 
 def max_threads() -> int:
     return int(lib().or_max_threads())
+
+
+def set_threads(threads: int) -> int:
+    """OpenMP threads of the oracle's parallel loops; returns the count in effect."""
+    return int(lib().or_set_threads(int(threads)))
 
 
 # ------------------------------------------------------------------ composed FFN blocks

@@ -319,10 +319,171 @@ void or_w8a8_project_half(const uint16_t* x16, int m, int k, const int8_t* wq, c
   }
 }
 
+/* Sets the OpenMP thread count for the oracle's parallel loops (the launcher
+ * of a multi-process run may have set OMP_NUM_THREADS=1); returns the count
+ * now in effect. */
+int or_set_threads(int threads) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+  return omp_get_max_threads();
+#else
+  (void)threads;
+  return 1;
+#endif
+}
+
 int or_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();
 #else
   return 1;
 #endif
+}
+
+/* ------------------------------------------------------------------ attention softmax */
+
+/* The special-function unit's 2^x with flush to zero, restated as the
+ * correctly rounded 2^x with subnormal results flushed: the hardware
+ * approximation differs from it by a couple of ulps at most, far below the
+ * 16-bit rounding of P that follows. */
+static float ex2_ftz(float x) {
+  float r = (float)exp2((double)x);
+  if (r < FLT_MIN) r = 0.0f;
+  return r;
+}
+
+/* 2^x on the FMA pipe, the attention kernel's own definition (attention_tc.cu
+ * exp2_poly2): x clamped to -126, n = rint(x) by the 1.5*2^23 magic add,
+ * f = x - n, a degree-3 polynomial in f, n added to the exponent field. */
+static float exp2_poly(float x) {
+  const float magic = 12582912.0f;
+  x = fmaxf(x, -126.0f);
+  const float j = x + magic;
+  const float n = j - magic;
+  const float f = fmaf(n, -1.0f, x);
+  float p = fmaf(0x1.c2ccd4p-5f, f, 0x1.f02456p-3f);
+  p = fmaf(p, f, 0x1.62f21p-1f);
+  p = fmaf(p, f, 0x1.fff9ap-1f);
+  uint32_t pb, jb;
+  memcpy(&pb, &p, 4);
+  memcpy(&jb, &j, 4);
+  pb += jb << 23;
+  memcpy(&p, &pb, 4);
+  return p;
+}
+
+/* Softmax attention over one board per (position, head) with the arithmetic
+ * of the tcgen05 attention kernel, which computes the reference's
+ * softmax(q.k * scale) . v (cuda-kernels/attention_fa2_q64.cu:82-390;
+ * tests/debug_exec_units.rs:161-242) with these definitional choices:
+ *   - the keys form two halves, [0, 192) and [192, 368), each with its own
+ *     maximum m (max of fp32 scores over the half's keys below seq);
+ *   - P = 2^(fma(s, c, -(m*c))) with c = fp32(scale * log2 e), in slices of 48
+ *     keys (the last slice of the second half has 32): in a full slice the
+ *     pairs of keys alternate between the polynomial (even pair) and the
+ *     special-function unit (odd pair); a slice with keys past seq uses the
+ *     special-function unit for its valid keys and 0 for the rest;
+ *   - the row sum l of each slice sums the unrounded P pairwise into four
+ *     partial sums (pair i into i % 4), combined as (l0 + l1) + (l2 + l3);
+ *     a half's l combines its four slices the same way;
+ *   - the P.V product takes P rounded to the 16-bit type (f16 or bf16);
+ *   - out = 16-bit((O_A fa) inv + ... ) as fa = 2^((m_A - m) c) (1 if m_A is
+ *     the maximum), inv = 1 / (l_A fa + l_B fb), out = O_A (fa inv) + O_B (fb inv),
+ *     each operation rounded on its own.
+ * What the CPU cannot reproduce: the tensor cores' fp32 summation order of the
+ * scores q.k and of P.V (here: exact sums rounded once to fp32), and the
+ * hardware 2^x (ex2_ftz).  qkv: 16-bit bits [n*seq, 3*heads*hd] with Q and K
+ * already rotated; out: 16-bit bits [n*seq, heads*hd]. */
+void or_attention_tc(const uint16_t* qkv, int n, int seq, int heads, int hd, float scale, int f16,
+                     uint16_t* out) {
+  const int c = heads * hd;
+  const size_t ld = 3 * (size_t)c;
+  const float sl = scale * 1.4426950408889634f;
+  const int kpad = 368, half_a = 192;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(dynamic)
+#endif
+  for (int bh = 0; bh < n * heads; ++bh) {
+    const int b = bh / heads, h = bh % heads;
+    double* kf = (double*)malloc(sizeof(double) * (size_t)seq * hd);
+    double* vf = (double*)malloc(sizeof(double) * (size_t)seq * hd);
+    float* s = (float*)malloc(sizeof(float) * kpad);
+    double* p16 = (double*)malloc(sizeof(double) * kpad);
+    const uint16_t* base = qkv + (size_t)b * seq * ld;
+    for (int j = 0; j < seq; ++j)
+      for (int d = 0; d < hd; ++d) {
+        kf[(size_t)j * hd + d] = f16 ? or_f16_decode(base[j * ld + c + h * hd + d])
+                                     : or_bf16_decode(base[j * ld + c + h * hd + d]);
+        vf[(size_t)j * hd + d] = f16 ? or_f16_decode(base[j * ld + 2 * c + h * hd + d])
+                                     : or_bf16_decode(base[j * ld + 2 * c + h * hd + d]);
+      }
+    for (int qi = 0; qi < seq; ++qi) {
+      double q[64];
+      for (int d = 0; d < hd; ++d)
+        q[d] = f16 ? or_f16_decode(base[qi * ld + h * hd + d]) : or_bf16_decode(base[qi * ld + h * hd + d]);
+      for (int j = 0; j < kpad; ++j) {
+        if (j < seq) {
+          double acc = 0.0;
+          for (int d = 0; d < hd; ++d) acc += q[d] * kf[(size_t)j * hd + d];
+          s[j] = (float)acc;
+        } else {
+          s[j] = 0.0f;
+        }
+      }
+      float m_h[2], l_h[2];
+      for (int hf = 0; hf < 2; ++hf) {
+        const int k0 = hf ? half_a : 0, k1 = hf ? kpad : half_a;
+        float m = -INFINITY;
+        for (int j = k0; j < k1 && j < seq; ++j) m = fmaxf(m, s[j]);
+        const float mc = m * sl;
+        float ls[4];
+        for (int sub = 0; sub < 4; ++sub) {
+          const int s0 = k0 + 48 * sub;
+          const int nk = (hf && sub == 3) ? 32 : 48;
+          const int valid = seq - s0 < nk ? seq - s0 : nk;
+          float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (int i = 0; i < nk / 2; ++i) {
+            const int j0 = s0 + 2 * i, j1 = j0 + 1;
+            float p0, p1;
+            if (valid >= nk) {
+              const float x0 = fmaf(s[j0], sl, -mc), x1 = fmaf(s[j1], sl, -mc);
+              if (i & 1) {
+                p0 = ex2_ftz(x0);
+                p1 = ex2_ftz(x1);
+              } else {
+                p0 = exp2_poly(x0);
+                p1 = exp2_poly(x1);
+              }
+            } else {
+              p0 = 2 * i < valid ? ex2_ftz(fmaf(s[j0], sl, -mc)) : 0.0f;
+              p1 = 2 * i + 1 < valid ? ex2_ftz(fmaf(s[j1], sl, -mc)) : 0.0f;
+            }
+            lp[i & 3] = lp[i & 3] + (p0 + p1);
+            p16[j0] = round16(p0, f16);
+            p16[j1] = round16(p1, f16);
+          }
+          ls[sub] = (lp[0] + lp[1]) + (lp[2] + lp[3]);
+        }
+        m_h[hf] = m;
+        l_h[hf] = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      }
+      const float mx = fmaxf(m_h[0], m_h[1]);
+      const float fa = m_h[0] == mx ? 1.0f : ex2_ftz((m_h[0] - mx) * sl);
+      const float fb = m_h[1] == mx ? 1.0f : ex2_ftz((m_h[1] - mx) * sl);
+      const float inv = 1.0f / (l_h[0] * fa + l_h[1] * fb);
+      const float wa = fa * inv, wb = fb * inv;
+      uint16_t* o = out + ((size_t)b * seq + qi) * c + h * hd;
+      for (int d = 0; d < hd; ++d) {
+        double oa = 0.0, ob = 0.0;
+        for (int j = 0; j < half_a && j < seq; ++j) oa += p16[j] * vf[(size_t)j * hd + d];
+        for (int j = half_a; j < seq; ++j) ob += p16[j] * vf[(size_t)j * hd + d];
+        const float x = (float)oa * wa + (float)ob * wb;
+        o[d] = f16 ? or_f16_encode(x) : or_bf16_encode(x);
+      }
+    }
+    free(kf);
+    free(vf);
+    free(s);
+    free(p16);
+  }
 }

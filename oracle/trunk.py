@@ -10,8 +10,10 @@ FFN hidden, bf16-rounded stem and head weights.
 
 What cannot be reproduced bit for bit, and is therefore compared with a
 tolerance: the fp32 accumulation order of the bf16 tensor-core GEMMs (stem,
-head linears) and of the attention kernel (which also rounds P to bf16 for
-the P.V product); the oracle accumulates those in float64.
+head linears) and of the attention kernel's q.k and P.V products; the oracle
+sums those exactly and rounds once.  The attention softmax itself follows the
+kernel's definition (two key halves with their own maxima, P rounded to bf16
+for P.V, the kernel's 2^x; kb_oracle.c or_attention_tc).
 
 The weight blob is parsed here independently of the product's parser, from
 the layout documented in include/katab200.h (kb_model_blob_floats).
@@ -114,18 +116,40 @@ def rope_qkv(qkv32, cs, sn, n, nh, hd):
     return bf(x.reshape(n * SEQ, 3 * c))
 
 
-def attention(qkv, cs, sn, n, nh, hd, rotate=True):
+def attention_scale(hd):
+    """The trunk's softmax scale, fp32(1 / fp32(sqrt(hd)))."""
+    return float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+
+
+def attention(qkv, cs, sn, n, nh, hd, rotate=True, exact=False, scale=None):
     """Softmax attention per (position, head) (debug_exec_units.rs:161-242).
     rotate: apply RoPE to the 16-bit Q and K here and round to bf16 (the
-    attention kernel's own rotation); False when Q and K arrive rotated."""
+    attention kernel's own rotation); False when Q and K arrive rotated.
+
+    exact=False (default): the attention kernel's own definition of the
+    softmax, restated in C (kb_oracle.c or_attention_tc: two key halves with
+    their own maxima, P rounded to bf16 for P.V, row sums of the unrounded P,
+    the kernel's 2^x), so that only fp32 summation order separates it from
+    the kernel.  exact=True: softmax in float64 with P unrounded (the
+    mathematical definition; the reference kernel keeps P in fp16)."""
     c = nh * hd
-    x = qkv.reshape(n, SEQ, 3, nh, hd)
+    x = np.asarray(qkv, np.float32).reshape(n, SEQ, 3, nh, hd)
     q, k, v = x[:, :, 0], x[:, :, 1], x[:, :, 2]
     if rotate:
         q, k = bf(rot(q, cs, sn)), bf(rot(k, cs, sn))
+    if scale is None:
+        scale = attention_scale(hd)
+    if not exact:
+        from . import bf16_encode, lib
+
+        packed = np.ascontiguousarray(np.stack([q, k, v], axis=2).reshape(n * SEQ, 3 * c), np.float32)
+        bits = np.ascontiguousarray(bf16_encode(packed))
+        out = np.empty((n * SEQ, c), np.uint16)
+        lib().or_attention_tc(bits.ctypes.data, n, SEQ, nh, hd, np.float32(scale), 0, out.ctypes.data)
+        return decode16(out, False)
     q, k = q.astype(np.float64), k.astype(np.float64)
     v = v.astype(np.float64)
-    s = np.einsum("bqhd,bkhd->bhqk", q, k) / math.sqrt(hd)
+    s = np.einsum("bqhd,bkhd->bhqk", q, k) * float(scale)
     s -= s.max(axis=-1, keepdims=True)
     p = np.exp(s)
     p /= p.sum(axis=-1, keepdims=True)
@@ -191,7 +215,8 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
     teacher: optional (stem [n*361, C], [attention [n*361, C] per block]) float
     arrays that replace the oracle's own stem GEMM and attention results — the
     two steps whose fp32 accumulation order cannot be reproduced on the CPU —
-    so that every other step can be compared bit for bit."""
+    so that every other step can be compared bit for bit.  With None in place
+    of the attention list only the stem is replaced."""
     c, nb, nh, hd, f = topo
     w = parse(blob, c, nb, nh, hd, f)
     n = spatial.shape[0]
@@ -207,7 +232,7 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
         if isinstance(precision, (tuple, list)):
             pq, po, pu, pd = precision
             qkv = rope_qkv(_project(pq, x, w[f"{i}.qkv"], gamma=w[f"{i}.rms1"]), cs, sn, n, nh, hd)
-            att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None
+            att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None or teacher[1] is None
                    else np.asarray(teacher[1][i], np.float32))
             x = bf((x + _project(po, att, w[f"{i}.out"])).astype(np.float32))
             v = _project(pu, x, w[f"{i}.up"], bias=w[f"{i}.up_b"], gamma=w[f"{i}.rms2"])
@@ -219,7 +244,7 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
             wq, wo, wu, wd = (_mx_weight(w[f"{i}.{nm}"]) for nm in ("qkv", "out", "up", "down"))
             _, _, normed = rms_quantize(x, w[f"{i}.rms1"], EPS, False)
             qkv = rope_qkv(_mx_linear(normed, wq), cs, sn, n, nh, hd)
-            att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None
+            att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None or teacher[1] is None
                    else np.asarray(teacher[1][i], np.float32))
             x = bf((x + _mx_linear(att, wo)).astype(np.float32))
             _, _, normed = rms_quantize(x, w[f"{i}.rms2"], EPS, False)
@@ -234,7 +259,7 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
         dw, ds = quantize_weights(w[f"{i}.down"])
         q, sa, _ = rms_quantize(x, w[f"{i}.rms1"], EPS, False, kp=qw.shape[1])
         qkv = rope_qkv(dequant(igemm(q, qw), sa, qs), cs, sn, n, nh, hd)
-        att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None
+        att = (attention(qkv, cs, sn, n, nh, hd, rotate=False) if teacher is None or teacher[1] is None
                else np.asarray(teacher[1][i], np.float32))
         q2, s2 = quantize_rows(att, kp=ow.shape[1])
         x = bf((x + dequant(igemm(q2, ow), s2, os_)).astype(np.float32))
@@ -278,3 +303,25 @@ def heads(hp, w, n):
     more = hid @ w["moremisc"].T.astype(np.float64) + w["moremisc_b"]
     own = va @ w["own"].astype(np.float64)
     return {"policy": policy, "value": value, "misc": misc, "moremisc": more, "ownership": own}
+
+
+def stem_output(blob, topo, spatial, glob):
+    """The oracle's stem result (bf16 values [n*361, C]), as forward computes it."""
+    w = parse(blob, *topo)
+    a = bf(stem_inputs(spatial, glob)).astype(np.float64)
+    return bf((a @ bf(w["stem"]).astype(np.float64).T).astype(np.float32))
+
+
+def perturbed_stem_forward(blob, topo, spatial, glob, fraction=1e-4, seed=0, precision="int8"):
+    """forward() with the stem output perturbed by one bf16 ulp (last mantissa
+    bit flipped) on a seeded `fraction` of its elements: the smallest
+    difference two correct implementations can have.  How far the outputs
+    move measures the trunk's own sensitivity to last-bit differences."""
+    from . import bf16_encode
+
+    stem = stem_output(blob, topo, spatial, glob)
+    bits = bf16_encode(stem)
+    mask = np.random.default_rng(seed).random(bits.shape) < fraction
+    bits = bits.copy()
+    bits[mask] ^= 1
+    return forward(blob, topo, spatial, glob, teacher=(decode16(bits, False), None), precision=precision)

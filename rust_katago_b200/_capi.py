@@ -42,6 +42,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_int8_ffn_rms": (I, [P, STREAM, P, F, P, P, P, I]),
     "kb_int8_ffn_gelu_rms": (I, [P, STREAM, P, F, P, P, P, P, P, I]),
     "kb_int8_ffn_gelu_rms_noalloc": (I, [STREAM, P, F, P, P, P, P, P, I]),
+    "kb_int8_noalloc_prepare": (I, []),
     "kb_bf16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
     "kb_attention": (I, [P, P, P, P, I, I, I, F, I, STREAM]),
     "kb_status_reset": (I, [P, STREAM]),
@@ -60,6 +61,8 @@ SIGNATURES: dict[str, tuple] = {
     "kb_handle_destroy": (None, [P]),
     "kb_handle_stream": (I, [P, ctypes.POINTER(ctypes.c_size_t)]),
     "kb_warmup": (I, [P, ctypes.POINTER(ctypes.c_int), I]),
+    "kb_test_wait_timeout": (I, [ctypes.c_ulonglong, P, STREAM]),
+    "kb_test_int8_gemm_i32_wait_limit": (I, [P, P, P, I, I, I, ctypes.c_ulonglong, P, STREAM]),
     "kb_submit": (I, [P, I, P, P, P, ctypes.POINTER(ctypes.c_uint64)]),
     "kb_query": (I, [P, ctypes.c_uint64]),
     "kb_finish": (I, [P, ctypes.c_uint64, P, P, P, P, P, ctypes.POINTER(ctypes.c_uint32)]),

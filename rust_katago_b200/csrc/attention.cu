@@ -27,8 +27,8 @@ namespace kb {
 
 bool attention_tc_supported(int seq, int head_dim);
 int attention_tc_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out, int batch,
-                        int seq, int heads, float scale, int f16, cudaStream_t stream, uint32_t* row_amax,
-                        unsigned* status);
+                        int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
+                        uint32_t* row_amax, unsigned* status);
 
 namespace {
 
@@ -315,15 +315,16 @@ int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* ro
     set_error("attention: qkv/tables must be 16-byte aligned");
     return KB_E_INVALID;
   }
-  // The board (seq 361, head_dim 64) runs on the tcgen05 kernel; other shapes
-  // (head_dim 32, short sequences) on the mma.sync kernel above.  Tactic
+  // The board (seq 361, head_dim 64 or 32) runs on the tcgen05 kernel; short
+  // sequences on the mma.sync kernel above.  Tactic
   // switch KB_ATTENTION_MMA_SYNC=1 forces the latter (for A/B timing).
   static const bool force_sync = [] {
     const char* v = getenv("KB_ATTENTION_MMA_SYNC");
     return v != nullptr && v[0] == '1';
   }();
   if (!force_sync && attention_tc_supported(seq, head_dim))
-    return attention_tc_launch(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, f16, stream, row_amax, status);
+    return attention_tc_launch(qkv, rope_cos, rope_sin, out, batch, seq, heads, head_dim, scale, f16, stream, row_amax,
+                               status);
   if (head_dim == 64)
     return f16 ? launch_attention<64, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream)
                : launch_attention<64, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, stream);

@@ -1,5 +1,5 @@
 // Self-attention over the 361 board tokens on the tcgen05 tensor cores, fused
-// with RoPE (head_dim 64).
+// with RoPE (head_dim 64 or 32).
 //
 // Replaces the reference's q64 flash attention (crates/kata_nn/cuda-kernels/
 // attention_fa2_q64.cu:82-390; launcher src/backends/cuda_exec.rs:3442) with the
@@ -10,12 +10,14 @@
 //
 // Persistent: one CTA per SM walks (position, head) pairs.  All 361 keys fit
 // on chip, so nothing streams inside a pair:
-//   shared memory  K and V of two pairs (double buffer, 368 keys x 128 B each,
-//                  keys padded to a multiple of 16) and one 128-query Q tile,
-//                  all in the UMMA 128-byte-swizzled layout, loaded by TMA
-//                  (or by three staging warps that rotate on the way in);
+//   shared memory  K and V of two pairs (double buffer, 368 keys x 2D bytes
+//                  each, keys padded to a multiple of 16) and one 128-query Q
+//                  tile, all in the UMMA swizzled layout (rows of 128 bytes
+//                  with the 128-byte swizzle for D = 64, rows of 64 bytes with
+//                  the 64-byte swizzle for D = 32), loaded by TMA (or by three
+//                  staging warps that rotate on the way in);
 //   TMEM (512 col) S_A = Q K[0:192]^T (192 columns), S_B = Q K[192:368]^T (176),
-//                  O_A = P_A V[0:192] and O_B = P_B V[192:368] (64 each), and
+//                  O_A = P_A V[0:192] and O_B = P_B V[192:368] (D each), and
 //                  the 16 row sums of two tiles (16).
 // The two key halves keep their own maxima (no rescaling: the epilogue
 // combines them), so they form a two-stage pipeline.  All 16 softmax warps
@@ -28,7 +30,7 @@
 // 16-bit pairs over their own, already read S columns (the A operand of the
 // P.V MMA, read from TMEM).  Between the halves the softmax warps finish the
 // previous tile: O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) /
-// (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), each warp writing 16 of the 64 dims
+// (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), each warp writing D/4 of the D dims
 // by TMA, plus the row |max| for the next quantiser.  Every wait is bounded.
 #include <stdint.h>
 #include <string.h>
@@ -42,14 +44,9 @@
 namespace kb {
 namespace {
 
-constexpr int kD = 64;
 constexpr int kKeysPad = 368;             // >= 361, multiple of 16
 constexpr int kHalfA = 192, kHalfB = kKeysPad - kHalfA;  // 176
 constexpr int kTileQ = 128;
-constexpr int kRowBytes = kD * 2;         // 128 B: one swizzle row
-constexpr int kKBytes = kKeysPad * kRowBytes;
-constexpr int kKVBytes = 2 * kKBytes;     // K then V of one pair
-constexpr int kQBytes = kTileQ * kRowBytes;
 constexpr int kSoftWarps = 16;
 constexpr int kMmaWarp = kSoftWarps;
 // Loader warps: two issuing TMA copies (K/V and Q; Q and K arrive rotated),
@@ -61,17 +58,33 @@ template <bool ROPE>
 constexpr int fa_threads() { return 32 * (kSoftWarps + 1 + load_warps<ROPE>()); }  // 640 / 608
 constexpr int kKvBox = 184;               // rows per K/V TMA box (2 boxes = 368 rows)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSB = kHalfA, kOA = kHalfA + kHalfB, kOB = kOA + kD;  // TMEM columns
-// Row sums l of the 8 key slices of a tile (4 per half), double-buffered by
-// tile parity, in the 16 TMEM columns left over: 496..511.
-constexpr uint32_t kLCol = kOB + kD;
+constexpr uint32_t kSB = kHalfA, kOA = kHalfA + kHalfB;  // TMEM columns
 constexpr int kBarBytes = 256;
 // Slice maxima exchanged between the 4 warps of a TMEM lane quarter:
 // [tile parity][half][slice][row] floats.
 constexpr int kMlBytes = 2 * 2 * 4 * kTileQ * 4;
-// K/V double buffer, one Q tile (loaded as soon as the previous tile's S MMAs
-// are done, several microseconds before it is needed), one output tile.
-constexpr int kSmemBytes = 2 * kKVBytes + 2 * kQBytes + kBarBytes + kMlBytes + 1024 /*alignment*/;
+
+// Geometry for head_dim D (64 or 32).
+template <int D>
+struct Geo {
+  static_assert(D == 64 || D == 32, "head_dim 64 or 32");
+  static constexpr int kRowBytes = D * 2;  // one Q/K/V row: 128 B (D 64) or 64 B (D 32)
+  static constexpr int kChunks = D / 8;    // 16-byte chunks per row
+  static constexpr int kKBytes = kKeysPad * kRowBytes;
+  static constexpr int kKVBytes = 2 * kKBytes;  // K then V of one pair
+  static constexpr int kQBytes = kTileQ * kRowBytes;
+  static constexpr int kDimsW = D / 4;          // output dims per softmax warp (4 warps per lane quarter)
+  static constexpr int kPieceBytes = 32 * kDimsW * 2;  // one warp's output piece: 32 rows x kDimsW dims
+  static constexpr uint32_t kOB = kOA + D;
+  // Row sums l of the 8 key slices of a tile (4 per half), double-buffered by
+  // tile parity, in 16 TMEM columns after O_B.
+  static constexpr uint32_t kLCol = kOB + D;
+  static_assert(kLCol + 16 <= kTmemCols, "TMEM budget");
+  // K/V double buffer, one Q tile (loaded as soon as the previous tile's S MMAs
+  // are done, several microseconds before it is needed), the output pieces.
+  static constexpr int kSmemBytes =
+      2 * kKVBytes + kQBytes + kSoftWarps * kPieceBytes + kBarBytes + kMlBytes + 1024 /*alignment*/;
+};
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
   if (f16) {
@@ -121,9 +134,20 @@ __device__ __forceinline__ uint32_t rope2(uint32_t w, float c, float s, bool f16
   return pack2(__fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s)), __fadd_rn(__fmul_rn(x, s), __fmul_rn(y, c)), f16);
 }
 
-// Byte offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
-__device__ __forceinline__ uint32_t sw128(int r, int c) {
-  return static_cast<uint32_t>(r * kRowBytes + ((c ^ (r & 7)) << 4));
+// Byte offset of 16-byte chunk `c` of row `r` in a swizzled tile: 128-byte
+// rows with the 128-byte swizzle (chunk ^ row % 8) for D = 64, 64-byte rows
+// with the 64-byte swizzle (chunk ^ (row / 2) % 4) for D = 32.
+template <int D>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  if constexpr (D == 64) return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+  else return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+
+// UMMA shared-memory descriptor of a Q, K or V tile in that layout.
+template <int D>
+__device__ __forceinline__ uint64_t tile_desc(uint32_t saddr) {
+  if constexpr (D == 64) return sw128_desc(saddr);
+  else return sw64_desc(saddr);
 }
 
 // Rows [r0, r0 + nrows) of Q, K or V (part = 0, 1, 2) of head h of one position
@@ -132,25 +156,26 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 // issued before any is used, so the copy is not bound by one load's latency.
 constexpr int kBatch = 3;
 
-template <bool F16>
+template <int D, bool F16>
 __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, size_t row_stride, int part, int h,
                                            int heads, const float* cos_t, const float* sin_t, int r0, int nrows,
                                            int seq, int tid, int nthreads, bool rotate) {
-  const int c = heads * kD;
-  const int total = nrows * 8;
+  constexpr int kCh = Geo<D>::kChunks;
+  const int c = heads * D;
+  const int total = nrows * kCh;
   for (int t0 = tid; t0 < total; t0 += kBatch * nthreads) {
     uint4 raw[kBatch];
     float4 co[kBatch], si[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       const int t = t0 + u * nthreads;
-      const int r = t >> 3, ch = t & 7;
+      const int r = t / kCh, ch = t % kCh;
       const int tok = r0 + r;
       raw[u] = make_uint4(0, 0, 0, 0);
       if (t < total && tok < seq) {
-        raw[u] = __ldg(reinterpret_cast<const uint4*>(base + tok * row_stride + part * c + h * kD + ch * 8));
+        raw[u] = __ldg(reinterpret_cast<const uint4*>(base + tok * row_stride + part * c + h * D + ch * 8));
         if (rotate) {
-          const size_t ro = (static_cast<size_t>(tok) * heads + h) * (kD / 2) + ch * 4;
+          const size_t ro = (static_cast<size_t>(tok) * heads + h) * (D / 2) + ch * 4;
           co[u] = __ldg(reinterpret_cast<const float4*>(cos_t + ro));
           si[u] = __ldg(reinterpret_cast<const float4*>(sin_t + ro));
         }
@@ -160,12 +185,12 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
     for (int u = 0; u < kBatch; ++u) {
       const int t = t0 + u * nthreads;
       if (t >= total) break;
-      const int r = t >> 3, ch = t & 7;
+      const int r = t / kCh, ch = t % kCh;
       uint4 v = raw[u];
       if (rotate && r0 + r < seq)
         v = make_uint4(rope2(raw[u].x, co[u].x, si[u].x, F16), rope2(raw[u].y, co[u].y, si[u].y, F16),
                        rope2(raw[u].z, co[u].z, si[u].z, F16), rope2(raw[u].w, co[u].w, si[u].w, F16));
-      *reinterpret_cast<uint4*>(dst + sw128(r, ch)) = v;
+      *reinterpret_cast<uint4*>(dst + swz<D>(r, ch)) = v;
     }
   }
 }
@@ -211,7 +236,7 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
   if (!__all_sync(0xffffffffu, mbar_wait(mx_bar, parity, abort_flag))) return false;
   m = fmaxf(fmaxf(mx[row], mx[kTileQ + row]), fmaxf(mx[2 * kTileQ + row], mx[3 * kTileQ + row]));
   m_out = m;
-  const float mc = m * scale_log2;
+  const float mc = __fmul_rn(m, scale_log2);
   float lp[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // partial sums (short chains)
   uint32_t pk[NK / 2];
   if (valid >= NK) {
@@ -225,7 +250,7 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
         p = make_float2(ex2(x.x), ex2(x.y));
       else
         p = exp2_poly2(x.x, x.y);
-      lp[i & 3] += p.x + p.y;
+      lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p.x, p.y));
       pk[i] = pack2(p.x, p.y, F16);
     }
   } else {
@@ -233,19 +258,19 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
     for (int i = 0; i < NK / 2; ++i) {
       const float p0 = 2 * i < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
       const float p1 = 2 * i + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
-      lp[i & 3] += p0 + p1;
+      lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p0, p1));
       pk[i] = pack2(p0, p1, F16);
     }
   }
   tmem_st16(lane_base + col, *reinterpret_cast<const uint32_t(*)[16]>(pk));
   if constexpr (NK == 48) tmem_st8(lane_base + col + 16, *reinterpret_cast<const uint32_t(*)[8]>(pk + 16));
-  tmem_st1(lane_base + lcol, __float_as_uint((lp[0] + lp[1]) + (lp[2] + lp[3])));
+  tmem_st1(lane_base + lcol, __float_as_uint(__fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3]))));
   tmem_st_wait();
   tc_fence_before();
   return true;
 }
 
-template <bool F16, bool ROPE>
+template <int D, bool F16, bool ROPE>
 __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     const __grid_constant__ CUtensorMap map_kv, const __grid_constant__ CUtensorMap map_q,
     const __grid_constant__ CUtensorMap map_out,
@@ -253,12 +278,15 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     uint16_t* __restrict__ out, int pairs, int seq, int heads, float scale_log2, uint32_t* __restrict__ row_amax,
     unsigned* status) {
   constexpr int kLoadThreads = 32 * load_warps<ROPE>();
+  using G = Geo<D>;
+  constexpr int kRowBytes = G::kRowBytes, kKBytes = G::kKBytes, kKVBytes = G::kKVBytes, kQBytes = G::kQBytes;
+  constexpr uint32_t kOB = G::kOB, kLCol = G::kLCol;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kv_buf = smem;                    // [2][K | V]
   uint8_t* q_buf = smem + 2 * kKVBytes;      // Q tile
-  uint8_t* o_buf = q_buf + kQBytes;          // output pieces: 1 KB per softmax warp (32 rows x 16 dims)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(o_buf + kQBytes);
+  uint8_t* o_buf = q_buf + kQBytes;          // output pieces: one per softmax warp (32 rows x D/4 dims)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(o_buf + kSoftWarps * G::kPieceBytes);
   uint64_t* kv_full = bars + 0;   // [2] loaders staged K/V           (128 arrivals)
   uint64_t* kv_empty = bars + 2;  // [2] MMAs done with K/V            (commit)
   uint64_t* q_full = bars + 4;    // loaders staged the Q tile          (tx bytes, or 96 arrivals)
@@ -278,7 +306,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   float* mx_ex = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][2][4][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = heads * kD;
+  const int c = heads * D;
   const size_t row_stride = 3 * static_cast<size_t>(c);
   const int tiles = (seq + kTileQ - 1) / kTileQ;
 
@@ -329,19 +357,20 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         uint8_t* ks = kv_buf + kb * kKVBytes;
         if (lane == 0) {
           mbar_arrive_expect_tx(&kv_tma[kb], 2 * kKBytes);
-          tma_load_2d(ks, &map_kv, &kv_tma[kb], c + h * kD, b * seq);
-          tma_load_2d(ks + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], c + h * kD, b * seq + kKvBox);
-          tma_load_2d(ks + kKBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD, b * seq);
-          tma_load_2d(ks + kKBytes + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], 2 * c + h * kD,
+          tma_load_2d(ks, &map_kv, &kv_tma[kb], c + h * D, b * seq);
+          tma_load_2d(ks + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], c + h * D, b * seq + kKvBox);
+          tma_load_2d(ks + kKBytes, &map_kv, &kv_tma[kb], 2 * c + h * D, b * seq);
+          tma_load_2d(ks + kKBytes + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], 2 * c + h * D,
                       b * seq + kKvBox);
           // the pair's Q tiles into L2, so each later Q load is an L2 hit
-          for (int t = 0; t < tiles; ++t) tma_prefetch_2d(&map_q, h * kD, b * seq + t * kTileQ);
+          for (int t = 0; t < tiles; ++t) tma_prefetch_2d(&map_q, h * D, b * seq + t * kTileQ);
         }
         // V rows [seq, 368) hold the next position's values (or TMA zeros):
         // clear them, their P is zero but 0 * Inf would not be.
         if (!__all_sync(0xffffffffu, mbar_wait(&kv_tma[kb], (it >> 1) & 1, abort_flag))) break;
-        for (int i = lane; i < (kKeysPad - seq) * 8; i += 32)
-          *reinterpret_cast<uint4*>(ks + kKBytes + sw128(seq + (i >> 3), i & 7)) = make_uint4(0, 0, 0, 0);
+        for (int i = lane; i < (kKeysPad - seq) * G::kChunks; i += 32)
+          *reinterpret_cast<uint4*>(ks + kKBytes + swz<D>(seq + i / G::kChunks, i % G::kChunks)) =
+              make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
         mbar_arrive(&kv_full[kb]);
       } else {
@@ -353,7 +382,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           }
           if (lane == 0) {
             mbar_arrive_expect_tx(q_full, kQBytes);
-            tma_load_2d(q_buf, &map_q, q_full, h * kD, b * seq + t * kTileQ);
+            tma_load_2d(q_buf, &map_q, q_full, h * D, b * seq + t * kTileQ);
           }
         }
         if (!ok) break;
@@ -369,10 +398,10 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       const uint16_t* base = qkv + static_cast<size_t>(b) * seq * row_stride;
       if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
       uint8_t* ks = kv_buf + kb * kKVBytes;
-      stage_rows<F16>(ks, base, row_stride, 1, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid, kLoadThreads,
-                      true);
-      stage_rows<F16>(ks + kKBytes, base, row_stride, 2, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid,
-                      kLoadThreads, false);
+      stage_rows<D, F16>(ks, base, row_stride, 1, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid,
+                         kLoadThreads, true);
+      stage_rows<D, F16>(ks + kKBytes, base, row_stride, 2, h, heads, rope_cos, rope_sin, 0, kKeysPad, seq, tid,
+                         kLoadThreads, false);
       fence_proxy_async_smem();
       mbar_arrive(&kv_full[kb]);
       bool ok = true;
@@ -381,8 +410,8 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           ok = false;
           break;
         }
-        stage_rows<F16>(q_buf, base, row_stride, 0, h, heads, rope_cos, rope_sin, t * kTileQ, kTileQ, seq, tid,
-                        kLoadThreads, true);
+        stage_rows<D, F16>(q_buf, base, row_stride, 0, h, heads, rope_cos, rope_sin, t * kTileQ, kTileQ, seq, tid,
+                           kLoadThreads, true);
         fence_proxy_async_smem();
         mbar_arrive(q_full);
       }
@@ -400,7 +429,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       const uint32_t id_common = (1u << 4) | (kFmt << 7) | (kFmt << 10) | (static_cast<uint32_t>(128 >> 4) << 24);
       const uint32_t id_sa = id_common | (static_cast<uint32_t>(kHalfA >> 3) << 17);
       const uint32_t id_sb = id_common | (static_cast<uint32_t>(kHalfB >> 3) << 17);
-      const uint32_t id_pv = id_common | (1u << 16) /* B MN-major */ | (static_cast<uint32_t>(kD >> 3) << 17);
+      const uint32_t id_pv = id_common | (1u << 16) /* B MN-major */ | (static_cast<uint32_t>(D >> 3) << 17);
       constexpr uint64_t kHalfOff = (kHalfA * kRowBytes) >> 4;  // 192 rows, descriptor units
       constexpr uint64_t kStep16 = (16 * kRowBytes) >> 4;       // 16 keys of V along K
       const int my_pairs = blockIdx.x < pairs ? (pairs - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
@@ -410,20 +439,20 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         if (t == 0 && !mbar_wait(&kv_full[kb], (it >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait(q_full, g & 1, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t kdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes));
-        const uint64_t qdesc = sw128_desc(smem_u32(q_buf));
+        const uint64_t kdesc = tile_desc<D>(smem_u32(kv_buf + kb * kKVBytes));
+        const uint64_t qdesc = tile_desc<D>(smem_u32(q_buf));
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
+        for (int kk = 0; kk < D / 16; ++kk)
           mma_issue<kKindBF16>(tmem, qdesc + 2 * kk, kdesc + 2 * kk, id_sa, kk != 0, 0, 0);
         tc_commit(sa_full);
         return true;
       };
       auto issue_sb = [&](int g) {
         const int kb = (g / tiles) & 1;
-        const uint64_t kdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes));
-        const uint64_t qdesc = sw128_desc(smem_u32(q_buf));
+        const uint64_t kdesc = tile_desc<D>(smem_u32(kv_buf + kb * kKVBytes));
+        const uint64_t qdesc = tile_desc<D>(smem_u32(q_buf));
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
+        for (int kk = 0; kk < D / 16; ++kk)
           mma_issue<kKindBF16>(tmem + kSB, qdesc + 2 * kk, kdesc + kHalfOff + 2 * kk, id_sb, kk != 0, 0, 0);
         tc_commit(sb_full);
         tc_commit(q_empty);
@@ -432,7 +461,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       if (ok && n > 0) issue_sb(0);
       for (int g = 0; g < n && ok; ++g) {
         const int kb = (g / tiles) & 1;
-        const uint64_t vdesc = sw128_desc(smem_u32(kv_buf + kb * kKVBytes + kKBytes));
+        const uint64_t vdesc = tile_desc<D>(smem_u32(kv_buf + kb * kKVBytes + kKBytes));
         if (!mbar_wait(pa_full, g & 1, abort_flag) || (g > 0 && !mbar_wait(o_free, (g - 1) & 1, abort_flag))) break;
         tc_fence_after();
         // P of keys 16i..16i+15 of a half: softmax warp i/3 holds 48 keys at
@@ -469,49 +498,64 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     int pb = 0, ph = 0, pt = 0, pg = -1;
     float pma = 0.0f, pmb = 0.0f;
     // The epilogue of tile pg: O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) /
-    // (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), 16 of the 64 dims per warp.
+    // (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), D/4 of the D dims per warp.
     auto epilogue = [&]() -> bool {
+      constexpr int kDW = G::kDimsW;
       if (!__all_sync(0xffffffffu, mbar_wait(o_full, pg & 1, abort_flag))) return false;
       tc_fence_after();
-      uint32_t lv[8], oa[16], ob[16], w[8];
-      const int dim0 = sub * 16;
+      uint32_t lv[8], oa[kDW], ob[kDW], w[kDW / 2];
+      const int dim0 = sub * kDW;
       tmem_ld8(lane_base + kLCol + (pg & 1) * 8, lv);
-      tmem_ld16(lane_base + kOA + dim0, oa);
-      tmem_ld16(lane_base + kOB + dim0, ob);
+      if constexpr (kDW == 16) {
+        tmem_ld16(lane_base + kOA + dim0, oa);
+        tmem_ld16(lane_base + kOB + dim0, ob);
+      } else {
+        tmem_ld8(lane_base + kOA + dim0, oa);
+        tmem_ld8(lane_base + kOB + dim0, ob);
+      }
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(o_free);
-      const float la = (__uint_as_float(lv[0]) + __uint_as_float(lv[1])) +
-                       (__uint_as_float(lv[2]) + __uint_as_float(lv[3]));
-      const float lb = (__uint_as_float(lv[4]) + __uint_as_float(lv[5])) +
-                       (__uint_as_float(lv[6]) + __uint_as_float(lv[7]));
+      const float la = __fadd_rn(__fadd_rn(__uint_as_float(lv[0]), __uint_as_float(lv[1])),
+                                 __fadd_rn(__uint_as_float(lv[2]), __uint_as_float(lv[3])));
+      const float lb = __fadd_rn(__fadd_rn(__uint_as_float(lv[4]), __uint_as_float(lv[5])),
+                                 __fadd_rn(__uint_as_float(lv[6]), __uint_as_float(lv[7])));
       const float mx = fmaxf(pma, pmb);
       const float fa = pma == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(pma, mx), scale_log2));
       const float fb = pmb == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(pmb, mx), scale_log2));
-      const float inv = 1.0f / (la * fa + lb * fb);
-      const float wa = fa * inv, wb = fb * inv;
+      // Every operation rounded on its own (no contraction), so the CPU
+      // restatement of this combination reproduces it exactly.
+      const float inv = __fdiv_rn(1.0f, __fadd_rn(__fmul_rn(la, fa), __fmul_rn(lb, fb)));
+      const float wa = __fmul_rn(fa, inv), wb = __fmul_rn(fb, inv);
       uint32_t am = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float x0 = __uint_as_float(oa[2 * i]) * wa + __uint_as_float(ob[2 * i]) * wb;
-        const float x1 = __uint_as_float(oa[2 * i + 1]) * wa + __uint_as_float(ob[2 * i + 1]) * wb;
+      for (int i = 0; i < kDW / 2; ++i) {
+        const float x0 = __fadd_rn(__fmul_rn(__uint_as_float(oa[2 * i]), wa), __fmul_rn(__uint_as_float(ob[2 * i]), wb));
+        const float x1 =
+            __fadd_rn(__fmul_rn(__uint_as_float(oa[2 * i + 1]), wa), __fmul_rn(__uint_as_float(ob[2 * i + 1]), wb));
         w[i] = pack2(x0, x1, F16);
         am = __vmaxu2(am, w[i] & 0x7fff7fffu);
       }
-      // Each warp's 32 rows x 16 dims leave by one TMA store of its own 1 KB
-      // piece (rows past `seq` are clipped by the tensor map): wait until the
-      // warp's previous store has read the piece, write it, store it.
-      uint8_t* piece = o_buf + warp * 1024;
+      // Each warp's 32 rows x D/4 dims leave by one TMA store of its own piece
+      // (rows past `seq` are clipped by the tensor map): wait until the warp's
+      // previous store has read the piece, write it, store it.
+      uint8_t* piece = o_buf + warp * G::kPieceBytes;
       if (lane == 0) bulk_wait_read<0>();
       __syncwarp();
-      *reinterpret_cast<uint4*>(piece + lane * 32 + (((0 ^ (lane >> 2)) & 1) << 4)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
-      *reinterpret_cast<uint4*>(piece + lane * 32 + (((1 ^ (lane >> 2)) & 1) << 4)) =
-          make_uint4(w[4], w[5], w[6], w[7]);
+      if constexpr (kDW == 16) {
+        // 32-byte rows with the 32-byte swizzle
+        *reinterpret_cast<uint4*>(piece + lane * 32 + (((0 ^ (lane >> 2)) & 1) << 4)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(piece + lane * 32 + (((1 ^ (lane >> 2)) & 1) << 4)) =
+            make_uint4(w[4], w[5], w[6], w[7]);
+      } else {
+        // 16-byte rows, no swizzle
+        *reinterpret_cast<uint4*>(piece + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_3d(&map_out, piece, ph * kD + dim0, pt * kTileQ + quarter * 32, pb);
+        tma_store_3d(&map_out, piece, ph * D + dim0, pt * kTileQ + quarter * 32, pb);
         bulk_commit();
       }
       const int query = pt * kTileQ + row;
@@ -577,10 +621,11 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
-template <bool F16, bool ROPE>
+template <int D, bool F16, bool ROPE>
 int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint16_t* out, int batch, int seq,
               int heads, float scale, uint32_t* row_amax, unsigned* status, cudaStream_t stream) {
-  auto kern = attention_fa_kernel<F16, ROPE>;
+  auto kern = attention_fa_kernel<D, F16, ROPE>;
+  constexpr int kSmemBytes = Geo<D>::kSmemBytes;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> configured{0};
@@ -593,18 +638,19 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
   CUtensorMap map_kv, map_q, map_out;
   memset(&map_kv, 0, sizeof(map_kv));
   memset(&map_q, 0, sizeof(map_q));
-  // out [batch, seq, C]: boxes of 16 dims x 32 tokens of one position, 32-byte swizzle
-  int rc0 = encode_3d(&map_out, CU_TENSOR_MAP_DATA_TYPE_UINT16, out, static_cast<long>(heads) * kD, seq, batch,
-                      static_cast<long>(heads) * kD * 2, static_cast<long>(seq) * heads * kD * 2, 16, 32, 1,
-                      CU_TENSOR_MAP_SWIZZLE_32B);
+  // out [batch, seq, C]: boxes of D/4 dims x 32 tokens of one position (32-byte
+  // rows with the 32-byte swizzle for D = 64, 16-byte rows for D = 32)
+  const long c = static_cast<long>(heads) * D;
+  int rc0 = encode_3d(&map_out, CU_TENSOR_MAP_DATA_TYPE_UINT16, out, c, seq, batch, c * 2,
+                      static_cast<long>(seq) * c * 2, D / 4, 32, 1,
+                      D == 64 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc0) return rc0;
   if (!ROPE) {
-    // [batch * seq rows, 3C columns] 16-bit; boxes of 64 columns (one head) x rows
-    const long cols = 3L * heads * kD, rows = static_cast<long>(batch) * seq;
-    int rc = encode_2d(&map_kv, CU_TENSOR_MAP_DATA_TYPE_UINT16, qkv, cols, rows, cols * 2, kD, kKvBox,
-                       CU_TENSOR_MAP_SWIZZLE_128B);
-    if (!rc) rc = encode_2d(&map_q, CU_TENSOR_MAP_DATA_TYPE_UINT16, qkv, cols, rows, cols * 2, kD, kTileQ,
-                            CU_TENSOR_MAP_SWIZZLE_128B);
+    // [batch * seq rows, 3C columns] 16-bit; boxes of D columns (one head) x rows
+    const long cols = 3 * c, rows = static_cast<long>(batch) * seq;
+    const CUtensorMapSwizzle swz_mode = D == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    int rc = encode_2d(&map_kv, CU_TENSOR_MAP_DATA_TYPE_UINT16, qkv, cols, rows, cols * 2, D, kKvBox, swz_mode);
+    if (!rc) rc = encode_2d(&map_q, CU_TENSOR_MAP_DATA_TYPE_UINT16, qkv, cols, rows, cols * 2, D, kTileQ, swz_mode);
     if (rc) return rc;
   }
   const float scale_log2 = scale * 1.4426950408889634f;
@@ -617,18 +663,35 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
 
 }  // namespace
 
-// head_dim 64 and 192 < seq <= 368 (the 361-token board): tcgen05 kernel.
-bool attention_tc_supported(int seq, int head_dim) { return head_dim == kD && seq > kHalfA && seq <= kKeysPad; }
+// head_dim 64 or 32 and 192 < seq <= 368 (the 361-token board): tcgen05 kernel.
+bool attention_tc_supported(int seq, int head_dim) {
+  return (head_dim == 64 || head_dim == 32) && seq > kHalfA && seq <= kKeysPad;
+}
 
-int attention_tc_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out, int batch,
-                        int seq, int heads, float scale, int f16, cudaStream_t stream, uint32_t* row_amax,
-                        unsigned* status) {
+template <int D>
+int attention_tc_dispatch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out, int batch,
+                          int seq, int heads, float scale, int f16, cudaStream_t stream, uint32_t* row_amax,
+                          unsigned* status) {
   // Null tables: Q and K arrive already rotated (by the QKV projection's epilogue).
   if (rope_cos == nullptr)
-    return f16 ? launch_tc<true, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream)
-               : launch_tc<false, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream);
-  return f16 ? launch_tc<true, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream)
-             : launch_tc<false, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status, stream);
+    return f16 ? launch_tc<D, true, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status,
+                                           stream)
+               : launch_tc<D, false, false>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status,
+                                            stream);
+  return f16 ? launch_tc<D, true, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status,
+                                        stream)
+             : launch_tc<D, false, true>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, row_amax, status,
+                                         stream);
+}
+
+int attention_tc_launch(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out, int batch,
+                        int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
+                        uint32_t* row_amax, unsigned* status) {
+  if (head_dim == 64)
+    return attention_tc_dispatch<64>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, f16, stream, row_amax,
+                                     status);
+  return attention_tc_dispatch<32>(qkv, rope_cos, rope_sin, out, batch, seq, heads, scale, f16, stream, row_amax,
+                                   status);
 }
 
 }  // namespace kb

@@ -212,6 +212,24 @@ int kb_int8_gemm_i32(const int8_t* a, const int8_t* w, int32_t* dots, int m, int
   return gemm_launch(kGemmI8, kEpiI32, a, w, g, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int kb_test_int8_gemm_i32_wait_limit(const int8_t* a, const int8_t* w, int32_t* dots, int m, int n, int kp,
+                                     unsigned long long wait_limit_ns, uint32_t* status, uintptr_t stream) {
+  if (!a || !w || !dots || !status || m <= 0 || n <= 0 || kp <= 0 || kp % 16 != 0 || wait_limit_ns == 0 ||
+      wait_limit_ns > 2000000000ull) {
+    set_error("kb_test_int8_gemm_i32_wait_limit: invalid arguments");
+    return KB_E_INVALID;
+  }
+  GemmArgs g;
+  g.m = m;
+  g.n = n;
+  g.k = kp;
+  g.out = dots;
+  g.ldo = n;
+  g.status = status;
+  g.wait_limit_ns = wait_limit_ns;
+  return gemm_launch(kGemmI8, kEpiI32, a, w, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int kb_int8_linear(const int8_t* a, const float* sa, const int8_t* w, const float* sw,
                    const float* bias, int m, int n, int kp, int epilogue, int act, int out_dtype,
                    void* out, int ldo, int n_out, uint32_t* row_amax, uintptr_t stream) {

@@ -13,8 +13,10 @@
 //   * the array is kNoAllocScratchBytes (8 MiB) on every device that loads the
 //     library, held until process exit; calls that need more are rejected;
 //   * its device address is looked up with cudaGetSymbolAddress once per
-//     device, on the first call made with that device current: make that first
-//     call before any stream capture begins;
+//     device, on the first call made with that device current (or by
+//     kb_int8_noalloc_prepare): make that first call before any stream capture
+//     begins.  The address is kept per device together with the CUDA context it
+//     belongs to; after a device reset the new context triggers a new lookup;
 //   * every call on a device shares the one array and it keeps the previous
 //     call's contents: nothing in it needs to start at zero (every byte the
 //     block reads is written earlier in the same call), and calls that overlap
@@ -45,9 +47,32 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
+// Per device: the CUDA context the address was looked up in, and the address.
+// A device reset (cudaDeviceReset) gives the device a new primary context, in
+// which the array lives at a new address: the lookup is then repeated.
+struct ScratchSlot {
+  CUcontext ctx = nullptr;
+  void* ptr = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
 
-// Device address of this device's scratch array; looked up once per device.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+// Device address of the current device's scratch array; looked up once per
+// device (and again only if the device's context has changed).
 int scratch_address(void** out) {
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
@@ -56,14 +81,26 @@ int scratch_address(void** out) {
     set_error("device index out of range for the no-alloc scratch table");
     return KB_E_INVALID;
   }
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  if (get_ctx == nullptr) {
+    set_error("no-alloc scratch: cuCtxGetCurrent is not available");
+    return KB_E_CUDA;
+  }
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  ScratchSlot& slot = g_scratch[dev];
+  if (slot.ptr == nullptr || ctx == nullptr || slot.ctx != ctx) {
+    // The lookup binds the device's primary context to this thread if none is
+    // current yet; the context is read again afterwards.
     void* p = nullptr;
     rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
     if (rc) return rc;
-    g_scratch_ptr[dev] = p;
+    if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    slot.ctx = ctx;
+    slot.ptr = p;
   }
-  *out = g_scratch_ptr[dev];
+  *out = slot.ptr;
   return KB_OK;
 }
 
@@ -88,6 +125,13 @@ extern "C" int kb_int8_ffn_gelu_rms_noalloc(uintptr_t stream, const float* gamma
     set_error("INT8 rows must be positive");
     return KB_E_INVALID;
   }
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (up->device != dev || down->device != dev) {
+    set_error("INT8 weight belongs to another device");
+    return KB_E_STATE;
+  }
   const int c = up->k, f = up->n;
   const int kq = up->kp > down->kp ? up->kp : down->kp;
   // Layout: hidden 16-bit [rows, f] | int8 [rows, kq] | scales f32 [rows].
@@ -102,7 +146,7 @@ extern "C" int kb_int8_ffn_gelu_rms_noalloc(uintptr_t stream, const float* gamma
     return KB_E_INVALID;
   }
   void* base = nullptr;
-  int rc = scratch_address(&base);
+  rc = scratch_address(&base);
   if (rc) return rc;
   uint8_t* p = static_cast<uint8_t*>(base);
   uint16_t* hidden = reinterpret_cast<uint16_t*>(p);
@@ -140,4 +184,9 @@ extern "C" int kb_int8_ffn_gelu_rms_noalloc(uintptr_t stream, const float* gamma
   d.bias = down_bias;
   d.out_f16 = 0;
   return gemm_launch(kGemmI8, kEpiRes16, q, down->q, d, s);
+}
+
+extern "C" int kb_int8_noalloc_prepare(void) {
+  void* base = nullptr;
+  return scratch_address(&base);
 }

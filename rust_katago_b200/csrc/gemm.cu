@@ -336,6 +336,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
   const int tiles_m = (g.m + kBM - 1) / kBM;
   const int tiles_n = (g.n + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
+  const uint64_t wlim = g.wait_limit_ns ? g.wait_limit_ns : kWaitLimitNs;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -375,7 +376,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int mb = tile / tiles_n, nb = tile % tiles_n;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, wlim)) {
             ok = false;
             break;
           }
@@ -418,12 +419,17 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       int acc = 0;
       uint32_t aph = 0;
       bool ok = true;
+      int last_s = -1;  // ring slot and phase of the last MMA commit
+      uint32_t last_ph = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) break;
+        if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, wlim)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag)) {
+          if (!mbar_wait(&full[s], ph, abort_flag, wlim)) {
             ok = false;
             break;
           }
@@ -453,6 +459,8 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
             }
           }
           tc_commit(&empty[s]);
+          last_s = s;
+          last_ph = ph;
           if (++s == kStages) {
             s = 0;
             ph ^= 1;
@@ -462,6 +470,13 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
         tc_commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) aph ^= 1;
+      }
+      if (!ok && last_s >= 0) {
+        // Aborted: the MMAs already issued must finish before the TMEM is
+        // freed.  The last commit (to empty[last_s], phase last_ph) tracks
+        // every MMA this thread issued before it.
+        int local_abort = 0;
+        mbar_wait(&empty[last_s], last_ph, &local_abort);
       }
     }
   } else {
@@ -516,7 +531,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
           const bool row_ok = row < g.m;
           float sa = 1.0f;
           if constexpr (KIND == kGemmI8) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
-          if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag))) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag, wlim))) {
             ok = false;
             break;
           }
@@ -554,7 +569,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
                 if (with_bias) load_vecn<kSub>(g.bias, c0, g.n, bias);
               }
               tmem_ld_wait();
-              if (hh == 0 && !__all_sync(0xffffffffu, mbar_wait(&rbar[sq % SB], (sq / SB) & 1, abort_flag))) {
+              if (hh == 0 && !__all_sync(0xffffffffu, mbar_wait(&rbar[sq % SB], (sq / SB) & 1, abort_flag, wlim))) {
                 ok = false;
                 break;
               }
@@ -618,7 +633,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       // the row scale is loaded while the accumulator is still being computed
       float sa = 1.0f;
       if constexpr (KIND == kGemmI8 && EPI != kEpiI32) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag, wlim))) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);

@@ -52,6 +52,10 @@ struct GemmArgs {
   int n_out = 0;                     // SwiGLU: logical output columns (hidden)
   unsigned* status = nullptr;        // sticky status word (timeouts)
   unsigned layer = KB_NO_LAYER;
+  // Limit of the kernel's bounded waits on work (0 = the default two
+  // seconds); only the abort-path test sets it.  Waits that drain copies or
+  // MMAs already issued keep the default.
+  unsigned long long wait_limit_ns = 0;
   // MXFP8 only: block-scale factors, 1 byte per (row, 32-element K block),
   // stored as [rows_padded/128][k/128][32 rows][4 row groups][4 K blocks].
   const uint8_t* sfa = nullptr;

@@ -79,14 +79,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait for the phase with the given parity to complete.  Returns false when
 // the CTA-wide abort flag is raised (by this thread on timeout, or by another
 // role that timed out); the caller must then leave its loop.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// `limit_ns` shortens the limit (tests of the abort path); waits that drain
+// copies already issued always keep the full kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((n & 63) == 0) {
+    // the clock is read every 64 tries, or on every try under a shortened limit
+    if ((n & 63) == 0 || limit_ns != kWaitLimitNs) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort_flag = 1;
         return false;
       }
@@ -230,6 +234,19 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   d |= static_cast<uint64_t>(1024 >> 4) << 32;            // stride offset between 8-row groups
   d |= static_cast<uint64_t>(1) << 46;                    // descriptor version for sm_100
   d |= static_cast<uint64_t>(2) << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+// The same for 64-byte rows with the 64-byte swizzle, 8-row core groups 512
+// bytes apart (a TMA SWIZZLE_64B load of a {64 B, rows} box); also the
+// MN-major layout of a [K rows, 32 x 16-bit] operand (one swizzle atom wide).
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                    // leading offset (unused: one atom wide)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;             // stride offset between 8-row groups
+  d |= static_cast<uint64_t>(1) << 46;                    // descriptor version for sm_100
+  d |= static_cast<uint64_t>(4) << 61;                    // SWIZZLE_64B
   return d;
 }
 

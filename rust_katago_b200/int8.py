@@ -140,6 +140,12 @@ def ffn_gelu_rms_noalloc(gamma, eps: float, up: Int8Weight, up_bias, down: Int8W
          _ptr(down_bias), _ptr(residual_bf16), rows)
 
 
+def noalloc_prepare():
+    """Look up the current device's no-alloc scratch address now (before a
+    stream capture); the first ffn_gelu_rms_noalloc call does it otherwise."""
+    call("kb_int8_noalloc_prepare")
+
+
 # ------------------------------------------------------------------ kernel-level calls
 def gemm_i32(a, w, dots, m: int, n: int, kp: int, stream=None):
     call("kb_int8_gemm_i32", _ptr(a), _ptr(w), _ptr(dots), m, n, kp, _stream(stream))

