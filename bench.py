@@ -370,7 +370,8 @@ def run_reference(args):
     import oracle
 
     oracle.build()
-    threads = max(1, os.cpu_count() or 1)
+    # explicit: torchrun sets OMP_NUM_THREADS=1 in every rank's environment
+    threads = oracle.set_threads(max(1, os.cpu_count() or 1))
     wl = WORKLOADS[args.workload](args.batch, None, seed=1234, build_device=False)
     positions = args.ref_positions
     for _ in range(min(args.warmup, 1)):
@@ -389,21 +390,203 @@ def run_reference(args):
                                    "the Rust reference cannot be built in this image)"},
         "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.workload == "trunk":
+        line["cpu_baseline"]["gemm_config1"] = config1_gemm_record(None, None, threads, gpu=False)
     print(json.dumps(line), flush=True)
     return 0
 
 
 def time_launches(torch, stream, fn, flush, n):
-    """Mean device time (ms) of fn() over n launches, CUDA events on `stream`,
-    with an L2 flush before each launch outside the events."""
+    """Device times (ms) of fn() over n launches, CUDA events on `stream`,
+    with an L2 flush (on the same stream) before each launch outside the events."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
     for s, e in evs:
-        flush.fill_(1)
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
         s.record(stream)
         fn()
         e.record(stream)
     torch.cuda.synchronize()
     return [s.elapsed_time(e) for s, e in evs]
+
+
+# ------------------------------------------------------------------ sub-records of the default run
+def config1_gemm_record(torch, flush, threads_all, gpu=True):
+    """BASELINE config 1 (the reference's CPU W8A8 projection, int8_kernels.rs:273-301,
+    bench_lowprec.rs:689-704): A N(0,1) [2888, 768] per-token absmax int8, W N(0,0.02)
+    [3072, 768] per-channel int8, int32 dot, dequant to a 16-bit output, in GOP/s:
+    the CPU oracle single-threaded and on all host threads (bounded row samples),
+    and the same projection on this GPU (kb_int8_project_half)."""
+    import oracle
+
+    m, n, k = 2888, 3072, 768
+    seed = 0x123456789ABCDEF0 ^ (m * 131 + n * 7 + k)
+    rng = np.random.default_rng(seed & 0xFFFFFFFFFFFFFFFF)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+    a16 = oracle.f16_encode(a)
+    wq, ws = oracle.quantize_weights(w)
+    rec = {"shape": [m, n, k], "ops_per_row": 2 * n * k}
+    for label, threads, rows in (("cpu_1_thread", 1, 96), ("cpu_all_threads", threads_all, m)):
+        oracle.w8a8_project_half(a16[:8], wq, ws, threads=threads)  # warm
+        t0 = time.perf_counter()
+        oracle.w8a8_project_half(a16[:rows], wq, ws, threads=threads)
+        sec = time.perf_counter() - t0
+        rec[label] = {"gops": 2.0 * rows * n * k / sec / 1e9, "threads": threads, "rows_sampled": rows}
+    if not gpu:
+        return rec
+    from rust_katago_b200 import int8
+
+    wt = int8.Int8Weight(w)
+    wsp = int8.Int8Workspace(m, k, n)
+    x = torch.from_numpy(a16.view(np.int16)).cuda()
+    out = torch.empty((m, n), dtype=torch.int16, device="cuda")
+    stream = torch.cuda.current_stream()  # the workspace's stream
+
+    def launch():
+        wsp.project_half(x, k, wt, out, m)
+
+    for _ in range(3):
+        launch()
+    ms = statistics.mean(time_launches(torch, stream, launch, flush, 10))
+    rec["gpu"] = {"gops": 2.0 * m * n * k / (ms / 1e3) / 1e9, "ms": ms,
+                  "how": "kb_int8_project_half: quantise fp16 rows, tcgen05 INT8 GEMM, fp16 dequant epilogue"}
+    rec["gpu_over_cpu_all_threads"] = rec["gpu"]["gops"] / rec["cpu_all_threads"]["gops"]
+    return rec
+
+
+def handle_forward_ms(torch, handle, batch, d_sp, d_gl, d_out, flush, steps):
+    """Device ms per forward (the handle's CUDA graph for `batch`), L2 flushed between."""
+    stream = torch.cuda.ExternalStream(handle.stream)
+    fwd = lambda: handle.forward_device(batch, d_sp, d_gl, d_out, use_graph=True)  # noqa: E731
+    for _ in range(3):
+        fwd()
+    torch.cuda.synchronize()
+    return time_launches(torch, stream, fwd, flush, steps)
+
+
+def pipelined_rows(handle, spatial, glob, rows, steps):
+    """`steps` batches through submit_rows / finish_rows with both pipeline slots in use."""
+    tok = handle.submit_rows(spatial, glob, rows)
+    for _ in range(steps - 1):
+        nxt = handle.submit_rows(spatial, glob, rows)
+        handle.finish_rows(tok)
+        tok = nxt
+    handle.finish_rows(tok)
+
+
+def trunk_sub_records(wl, torch, flush, steps, world, rank, max_over_ranks, barrier):
+    """config5 (1024 positions per GPU) and latency (B = 1, 16) on every rank, max over ranks."""
+    from rust_katago_b200 import backend, synthetic
+
+    out = {}
+    b5 = 1024
+    sp, gl = synthetic.make_positions(b5, 4321 + 7919 * rank)
+    h5 = backend.CudaBackend.create_compute_handle(wl.model, b5)
+    h5.warmup([b5])
+    d_sp, d_gl = torch.from_numpy(sp).cuda(), torch.from_numpy(gl).cuda()
+    d_out = torch.zeros(b5 * backend.OUT_PER_POS, device="cuda")
+    k5 = max(3, min(steps, 10))
+    ms = max_over_ranks(sum(handle_forward_ms(torch, h5, b5, d_sp, d_gl, d_out, flush, k5)))
+    rows = backend.row_params(b5, symmetry=np.random.default_rng(rank).integers(0, 8, b5))
+    pipelined_rows(h5, sp, gl, rows, 2)
+    barrier()
+    t0 = time.perf_counter()
+    pipelined_rows(h5, sp, gl, rows, k5)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    out["config5"] = {
+        "workload": "config5: b11c768 W8A8 trunk, 1024 positions per GPU, batch-sharded, weights replicated",
+        "batch_per_gpu": b5, "steps": k5, "ms_per_step": ms / k5,
+        "value": b5 * world * k5 / (ms / 1e3), "unit": "positions/s",
+        "e2e": {"value": b5 * world * k5 / e2e_s, "unit": "positions/s",
+                "how": "kb_submit_rows / kb_finish_rows, two batches in flight, host clock, max over ranks"}}
+    del h5, d_sp, d_gl, d_out
+    torch.cuda.empty_cache()
+
+    lat = {}
+    hl = backend.CudaBackend.create_compute_handle(wl.model, 16)
+    hl.warmup([1, 16])
+    for b in (1, 16):
+        spb, glb = synthetic.make_positions(max(b, 4), 99 + rank)
+        spb, glb = spb[:b], glb[:b]
+        d_sp, d_gl = torch.from_numpy(spb).cuda(), torch.from_numpy(glb).cuda()
+        d_out = torch.zeros(b * backend.OUT_PER_POS, device="cuda")
+        dev = handle_forward_ms(torch, hl, b, d_sp, d_gl, d_out, flush, 20)
+        rowsb = backend.row_params(b)
+        for _ in range(3):
+            hl.finish_rows(hl.submit_rows(spb, glb, rowsb))
+        rt = []
+        for _ in range(30):
+            t0 = time.perf_counter()
+            hl.finish_rows(hl.submit_rows(spb, glb, rowsb))
+            rt.append(time.perf_counter() - t0)
+        barrier()
+        t0 = time.perf_counter()
+        pipelined_rows(hl, spb, glb, rowsb, 30)
+        two_s = max_over_ranks(time.perf_counter() - t0)
+        lat[f"B{b}"] = {"forward_ms": max_over_ranks(statistics.median(dev)),
+                        "e2e_round_trip_ms": max_over_ranks(statistics.median(rt) * 1e3),
+                        "e2e_two_in_flight_positions_per_s": b * world * 30 / two_s}
+    lat["how"] = ("forward_ms: device time of one graph-launched forward (CUDA events, L2 flushed before); "
+                  "e2e_round_trip_ms: host clock of kb_submit_rows -> kb_finish_rows for one batch (median of 30); "
+                  "two_in_flight: 30 batches with both pipeline slots in use")
+    out["latency"] = lat
+    del hl
+    return out
+
+
+def sharded_record(torch, wl, world, steps):
+    """One process, one host thread and one compute handle per GPU (the
+    reference's evaluator shape, eval.rs:245-330; rust_katago_b200.sharding),
+    1024 positions per GPU, decoded rows through kb_submit_rows / kb_finish_rows
+    with both pipeline slots in use; host clock around all threads.  Run on
+    devices [0] and then [0 .. world-1]."""
+    from rust_katago_b200 import backend, sharding, synthetic
+
+    per = 1024
+    res = {}
+    for devs in ([0], list(range(world))) if world > 1 else ([0],):
+        ev = sharding.ShardedEvaluator(wl.topo, wl.blob, devs, per)
+        n = per * len(devs)
+        sp, gl = synthetic.make_positions(n, 2468)
+        rows = backend.row_params(per, symmetry=np.random.default_rng(5).integers(0, 8, per))
+        shards = sharding.split_batch(sp, gl, len(devs))
+        for i, h in enumerate(ev.handles):
+            with torch.cuda.device(devs[i]):
+                h.warmup([per])
+        k = max(3, min(steps, 10))
+
+        def run(nsteps):
+            errs = []
+
+            def work(i):
+                try:
+                    with torch.cuda.device(devs[i]):
+                        _, _, s_i, g_i = shards[i]
+                        pipelined_rows(ev.handles[i], s_i, g_i, rows, nsteps)
+                except Exception as e:  # surfaced after join
+                    errs.append(e)
+
+            ts = [threading.Thread(target=work, args=(i,)) for i in range(len(devs))]
+            t0 = time.perf_counter()
+            for t in ts:
+                t.start()
+            for t in ts:
+                t.join()
+            if errs:
+                raise errs[0]
+            return time.perf_counter() - t0
+
+        run(2)
+        sec = run(k)
+        res[len(devs)] = n * k / sec
+        del ev
+    value = res[max(res)]
+    return {"value": value, "unit": "positions/s", "devices": max(res), "positions_per_gpu": per,
+            "single_device_value": res[1], "efficiency_vs_n_x_single": value / (max(res) * res[1]),
+            "how": "one process, ShardedEvaluator (one handle and host thread per GPU), kb_submit_rows / "
+                   "kb_finish_rows with two batches in flight per GPU, pinned staging and H2D/D2H included, "
+                   "host clock around all threads"}
 
 
 def main():
@@ -416,6 +599,7 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="positions per GPU (trunk / trunk_mxfp8 256, ffn 64)")
     ap.add_argument("--ref-positions", type=int, default=1, help="positions per CPU reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config5 / latency / sharded sub-records")
     args = ap.parse_args()
     if args.batch is None:
         args.batch = 64 if args.workload == "ffn" else 256
@@ -504,18 +688,38 @@ def main():
                 "int8_gemm_frac_of_peak": tot_ops / (tot_ms / 1e3) / 1e12 / int8_peak,
                 "int8_gemm_share_of_step": tot_ms / ms_per_step}
 
+    # sub-records of the default workload (config 5 and latency on every rank)
+    extras = {}
+    if args.workload == "trunk" and not args.no_extras:
+        extras.update(trunk_sub_records(wl, torch, flush, args.steps, world, rank, max_over_ranks, barrier))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
+        import oracle
+
+        threads = oracle.set_threads(os.cpu_count() or 1)
         positions = 1
         sec = statistics.mean(wl.cpu_reference(positions, threads) for _ in range(2))
         cpu = {"value": positions / sec, "unit": "positions/s", "cores": threads, "kind": "port",
                "sample": f"{positions} position ({positions * 361} tokens) of the same workload through the CPU "
-                         "oracle (restatement of the reference's W8A8 CPU arithmetic), mean of 2 runs"}
+                         "oracle (restatement of the reference's W8A8 CPU arithmetic), mean of 2 runs",
+               "gemm_config1": config1_gemm_record(torch, flush, threads)}
 
     if world > 1:
+        # The one-process sharded run uses every rank's GPU from rank 0; the
+        # other ranks wait on a host-side (gloo) barrier, so no collective
+        # kernel occupies their GPUs meanwhile.
+        from datetime import timedelta
+
+        host_group = dist.new_group(backend="gloo", timeout=timedelta(seconds=900))
+        dist.barrier(group=host_group)
+        if rank == 0 and args.workload == "trunk" and not args.no_extras:
+            extras["sharded_e2e"] = sharded_record(torch, wl, world, args.steps)
+        dist.barrier(group=host_group)
         dist.barrier()
         dist.destroy_process_group()
+    elif args.workload == "trunk" and not args.no_extras:
+        extras["sharded_e2e"] = sharded_record(torch, wl, world, args.steps)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world, "steps": args.steps,
@@ -532,6 +736,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
     return 0
 

@@ -221,6 +221,13 @@ KB_API int kb_int8_noalloc_prepare(void);
 KB_API int kb_bf16_linear(const uint16_t* a, const uint16_t* w, const float* bias, int m, int n, int k,
                    int epilogue, int act, int out_dtype, void* out, int ldo, uintptr_t stream);
 
+/* The same GEMM with binary16 operands (f16 x f16, fp32 accumulation): the
+ * nested trunk's outer linears and unquantised projections.
+ * Replaces: the FP16 hgemm / hgemm_residual linears of the outer trunk
+ * (cuda_exec.rs:1170-1240, gemm_v2.cu:397-1153). */
+KB_API int kb_f16_linear(const uint16_t* a, const uint16_t* w, const float* bias, int m, int n, int k,
+                         int epilogue, int act, int out_dtype, void* out, int ldo, uintptr_t stream);
+
 /* ------------------------------------------------------------------ attention */
 
 /* Multi-head attention over the 361 board tokens with RoPE on Q and K:
@@ -345,14 +352,25 @@ KB_API int kb_test_int8_gemm_i32_wait_limit(const int8_t* a, const int8_t* w, in
 #define KB_PROJ_FOLLOW 0 /* the model's `precision` */
 #define KB_PROJ_INT8 1   /* W8A8, per-token / per-channel absmax scales, int32 accumulate */
 #define KB_PROJ_MXFP8 2  /* block-32 E4M3 + UE8M0, fp32 accumulate */
-#define KB_PROJ_BF16 3   /* bf16 weights and activations, fp32 accumulate (the recipe's unquantised
-                            projection; the reference's is FP16) */
+#define KB_PROJ_BF16 3   /* unquantised 16-bit projection, fp32 accumulate: bf16 weights and activations
+                            in the flat topology, binary16 (the reference's FP16) in the nested one */
 #define KB_PROJ_QKV 0
 #define KB_PROJ_OUT 1
 #define KB_PROJ_FFN_UP 2
 #define KB_PROJ_FFN_DOWN 3
 
-/* Trunk shape (BASELINE b11c768: C=768, 11 blocks, 12 heads x 64, F=3072). */
+/* Trunk topologies. */
+#define KB_TOPO_FLAT 0   /* BASELINE: num_blocks x [RMSNorm, attention, RMSNorm, GELU FFN] on a bf16
+                            residual stream of width C (below) */
+#define KB_TOPO_NESTED 1 /* the reference's TF3 nested bottleneck (native_model.rs:79-124): per outer
+                            block, gate-SiLU of the fp32 raw trunk, C -> mid linear, pairs_per_block x
+                            [RMSNorm, attention (head_dim 32), RMSNorm, SwiGLU FFN mid -> 2H -> mid] on an
+                            fp32 stream of width mid, gate-SiLU, mid -> C linear added to the raw trunk;
+                            binary16 at every 16-bit boundary, INT8 FFN */
+
+/* Trunk shape (BASELINE b11c768: C=768, 11 blocks, 12 heads x 64, F=3072;
+ * the reference's TF3 b11c768: nested, C=768, mid 384, 11 blocks of 3 pairs,
+ * 12 heads x 32, F = SwiGLU hidden 1152). */
 typedef struct kb_model_desc {
   int trunk_channels; /* C; multiple of 64, <= 4096 */
   int num_blocks;     /* 1..64 */
@@ -367,6 +385,12 @@ typedef struct kb_model_desc {
    * projections that resolve to INT8 run in bf16 when ffn_channels is below
    * this width; 0 = no threshold; a multiple of 8, <= 8192. */
   int int8_min_ffn_width;
+  /* Appended fields (all zero = the flat topology with epsilon 1e-6). */
+  int topology;        /* KB_TOPO_FLAT or KB_TOPO_NESTED */
+  int mid_channels;    /* nested: inner width; num_heads * head_dim == mid_channels, multiple of 32,
+                          < trunk_channels */
+  int pairs_per_block; /* nested: attention / FFN pairs per outer block, 1..8 */
+  float norm_eps;      /* RMSNorm epsilon (RmsNormLayer::eps), 0 = 1e-6 */
 } kb_model_desc;
 
 /* Weight blob: fp32, out-first [N, K] row-major matrices, in this order:
@@ -381,6 +405,16 @@ typedef struct kb_model_desc {
  *          bias2 [96], conv2p [6, 96], v2 [192, 576], v2_bias [192], value [3, 192],
  *          value_bias [3], misc [10, 192], misc_bias [10], moremisc [8, 192],
  *          moremisc_bias [8], ownership [192].
+ * KB_TOPO_NESTED (the reference's lowered TF3 graph, native_model.rs:79-165;
+ * M = mid_channels, H = ffn_channels, all matrices [out, in]):
+ *   stem [C, 217] as above;
+ *   per outer block: pre_gate_scale [C], pre_gate_bias [C] (the block's
+ *     pre_bn, applied to the raw trunk), pre_conv [M, C];
+ *     per pair: rms1 [M], qkv [3M, M] ([Q; K; V]), out [M, M],
+ *       rope_freqs [heads, 16, 2], rms2 [M], ffn_gate [H, M] (linear1: the
+ *       SiLU branch), ffn_up [H, M] (linear_gate), ffn_down [M, H];
+ *     post_gate_scale [M], post_gate_bias [M] (post_bn), post_conv [C, M];
+ *   trunk tip and heads as above.
  * Same roles as the reference's LayerGraph layers (src/native_model.rs:21-165,
  * tests/debug_exec_units.rs:101-380). */
 KB_API int kb_model_blob_floats(const kb_model_desc* desc, size_t* count);
@@ -439,9 +473,13 @@ KB_API int kb_forward_device(kb_handle* handle, int n, const float* d_spatial, c
                              float* d_out, int use_graph);
 
 /* kb_forward_device without a graph that also copies intermediates into
- * d_trace, bf16 [(num_blocks + 2), n*361, C]: the stem output, each block's
- * attention output, the final residual stream (for parity tests and debugging;
- * plays the role of the reference's per-layer debug runs, tests/debug_exec_units.rs). */
+ * d_trace, 16-bit [(num_blocks + 2), n*361, C]: flat topology (bf16): the stem
+ * output, each block's attention output, the final residual stream; nested
+ * topology (binary16): the gated stem output (block 0's pre_bn), after each
+ * outer block the gated raw trunk that follows it (the next block's pre_bn,
+ * or the trunk tip after the last), then the trunk tip again.  For parity
+ * tests and debugging; plays the role of the reference's per-layer debug runs
+ * (tests/debug_exec_units.rs). */
 KB_API int kb_forward_trace(kb_handle* handle, int n, const float* d_spatial, const float* d_global,
                             float* d_out, uint16_t* d_trace);
 

@@ -78,6 +78,8 @@ def lib() -> ctypes.CDLL:
             "or_max_threads": (I, []),
             "or_set_threads": (I, [I]),
             "or_attention_tc": (None, [P, I, I, I, I, F, I, P]),
+            "or_tc_gemm16": (None, [P, P, I, I, I, I, P]),
+            "or_rope_tables": (None, [P, I, I, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -206,6 +208,19 @@ def w8a8_project_half(x16: np.ndarray, wq: np.ndarray, sw: np.ndarray, threads: 
     n = wq.shape[0]
     out = np.zeros((m, n), np.uint16)
     lib().or_w8a8_project_half(_p(x16), m, k, _p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sw, np.float32)), n, threads, _p(out))
+    return out
+
+
+def tc_gemm16(a_bits: np.ndarray, w_bits: np.ndarray, f16: bool = False) -> np.ndarray:
+    """fp32 [m, n] = a[m, k] . w[n, k]^T with the tensor cores' accumulation
+    (kb_oracle.c or_tc_gemm16) from 16-bit operand bits."""
+    a_bits = np.ascontiguousarray(a_bits, np.uint16)
+    w_bits = np.ascontiguousarray(w_bits, np.uint16)
+    m, k = a_bits.shape
+    n = w_bits.shape[0]
+    assert w_bits.shape[1] == k
+    out = np.empty((m, n), np.float32)
+    lib().or_tc_gemm16(_p(a_bits), _p(w_bits), m, n, k, 1 if f16 else 0, _p(out))
     return out
 
 

@@ -8,12 +8,15 @@ restatements of the reference's W8A8 arithmetic) and the same 16-bit rounding
 points as the product: bf16 residual stream, bf16 QKV / attention output /
 FFN hidden, bf16-rounded stem and head weights.
 
-What cannot be reproduced bit for bit, and is therefore compared with a
-tolerance: the fp32 accumulation order of the bf16 tensor-core GEMMs (stem,
-head linears) and of the attention kernel's q.k and P.V products; the oracle
-sums those exactly and rounds once.  The attention softmax itself follows the
-kernel's definition (two key halves with their own maxima, P rounded to bf16
-for P.V, the kernel's 2^x; kb_oracle.c or_attention_tc).
+The 16-bit tensor-core GEMMs (stem, head linears, bf16 projections) and the
+attention kernel's q.k and P.V products follow the tensor cores' own fp32
+accumulation (kb_oracle.c tc_block16: blocks of 16 products aligned to the
+largest exponent, truncated, rounded toward zero), and the attention softmax
+the kernel's definition (two key halves with their own maxima, P rounded to
+bf16 for P.V, the kernel's polynomial 2^x; kb_oracle.c or_attention_tc), so
+the residual stream is reproduced bit for bit.  The policy/value heads after
+the head linears are computed in float64 (their fp32 order is not restated)
+and compared with a tolerance.
 
 The weight blob is parsed here independently of the product's parser, from
 the layout documented in include/katab200.h (kb_model_blob_floats).
@@ -25,7 +28,8 @@ import math
 
 import numpy as np
 
-from . import bf16_encode, decode16, dequant, dequant_bias, igemm, quantize_rows, quantize_weights, rms_quantize, round16
+from . import (bf16_encode, decode16, dequant, dequant_bias, igemm, quantize_rows, quantize_weights, rms_quantize,
+               round16, tc_gemm16)
 
 SEQ, SIDE = 361, 19
 EPS = 1e-6
@@ -79,17 +83,16 @@ def stem_inputs(spatial, glob):
 
 
 def rope_tables(freqs):
-    """cos/sin [361, heads, pairs]: angle = x*f0 + y*f1 in float32 (native_model.rs:200-228)."""
+    """cos/sin [361, heads, pairs]: angle = x*f0 + y*f1 in float32, then the C
+    library's cosf / sinf, as the reference's f32::cos / f32::sin compute them
+    (native_model.rs:200-228; kb_oracle.c or_rope_tables)."""
+    from . import lib
+
+    freqs = np.ascontiguousarray(freqs, np.float32)
     nh, pairs, _ = freqs.shape
     cs = np.zeros((SEQ, nh, pairs), np.float32)
     sn = np.zeros_like(cs)
-    for y in range(SIDE):
-        for x in range(SIDE):
-            ang = (np.float32(x) * freqs[:, :, 0]).astype(np.float32) + (np.float32(y) * freqs[:, :, 1]).astype(np.float32)
-            ang = ang.astype(np.float32)
-            t = y * SIDE + x
-            cs[t] = np.cos(ang.astype(np.float64)).astype(np.float32)
-            sn[t] = np.sin(ang.astype(np.float64)).astype(np.float32)
+    lib().or_rope_tables(freqs.ctypes.data, nh, pairs, cs.ctypes.data, sn.ctypes.data)
     return cs, sn
 
 
@@ -121,7 +124,7 @@ def attention_scale(hd):
     return float(np.float32(1.0) / np.sqrt(np.float32(hd)))
 
 
-def attention(qkv, cs, sn, n, nh, hd, rotate=True, exact=False, scale=None):
+def attention(qkv, cs, sn, n, nh, hd, rotate=True, exact=False, scale=None, f16=False):
     """Softmax attention per (position, head) (debug_exec_units.rs:161-242).
     rotate: apply RoPE to the 16-bit Q and K here and round to bf16 (the
     attention kernel's own rotation); False when Q and K arrive rotated.
@@ -131,7 +134,8 @@ def attention(qkv, cs, sn, n, nh, hd, rotate=True, exact=False, scale=None):
     their own maxima, P rounded to bf16 for P.V, row sums of the unrounded P,
     the kernel's 2^x), so that only fp32 summation order separates it from
     the kernel.  exact=True: softmax in float64 with P unrounded (the
-    mathematical definition; the reference kernel keeps P in fp16)."""
+    mathematical definition; the reference kernel keeps P in fp16).  f16: the
+    16-bit type is binary16 (qkv values on its grid), else bfloat16."""
     c = nh * hd
     x = np.asarray(qkv, np.float32).reshape(n, SEQ, 3, nh, hd)
     q, k, v = x[:, :, 0], x[:, :, 1], x[:, :, 2]
@@ -140,13 +144,13 @@ def attention(qkv, cs, sn, n, nh, hd, rotate=True, exact=False, scale=None):
     if scale is None:
         scale = attention_scale(hd)
     if not exact:
-        from . import bf16_encode, lib
+        from . import f16_encode, lib
 
         packed = np.ascontiguousarray(np.stack([q, k, v], axis=2).reshape(n * SEQ, 3 * c), np.float32)
-        bits = np.ascontiguousarray(bf16_encode(packed))
+        bits = np.ascontiguousarray(f16_encode(packed) if f16 else bf16_encode(packed))
         out = np.empty((n * SEQ, c), np.uint16)
-        lib().or_attention_tc(bits.ctypes.data, n, SEQ, nh, hd, np.float32(scale), 0, out.ctypes.data)
-        return decode16(out, False)
+        lib().or_attention_tc(bits.ctypes.data, n, SEQ, nh, hd, np.float32(scale), 1 if f16 else 0, out.ctypes.data)
+        return decode16(out, f16)
     q, k = q.astype(np.float64), k.astype(np.float64)
     v = v.astype(np.float64)
     s = np.einsum("bqhd,bkhd->bhqk", q, k) * float(scale)
@@ -154,7 +158,7 @@ def attention(qkv, cs, sn, n, nh, hd, rotate=True, exact=False, scale=None):
     p = np.exp(s)
     p /= p.sum(axis=-1, keepdims=True)
     o = np.einsum("bhqk,bkhd->bqhd", p, v)
-    return bf(o.reshape(n * SEQ, c).astype(np.float32))
+    return round16(o.reshape(n * SEQ, c).astype(np.float32), f16)
 
 
 def _mx_weight(w):
@@ -183,8 +187,8 @@ def _project(kind, src, wmat, bias=None, gamma=None):
     fused when `gamma` is given — the single-precision branches of forward()
     per projection: INT8 quantises the (normalised) 16-bit rows per token and
     dequantises exactly, MXFP8 quantises them block-32, bf16 multiplies the
-    16-bit values by the bf16-rounded weight in float64 (the tensor core's fp32
-    order is not reproduced) and rounds to fp32."""
+    16-bit values by the bf16-rounded weight with the tensor cores' fp32
+    accumulation (tc_gemm16)."""
     if kind == "int8":
         qw, qs = quantize_weights(wmat)
         if gamma is not None:
@@ -197,7 +201,7 @@ def _project(kind, src, wmat, bias=None, gamma=None):
     if kind == "mxfp8":
         acc = _mx_linear(xv, _mx_weight(wmat))
     elif kind == "bf16":
-        acc = (np.asarray(xv, np.float64) @ bf(wmat).astype(np.float64).T).astype(np.float32)
+        acc = tc_gemm16(bf16_encode(xv), bf16_encode(wmat))
     else:
         raise ValueError(f"unknown projection precision {kind!r}")
     return acc if bias is None else (acc + bias[None, :]).astype(np.float32)
@@ -223,8 +227,7 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
     if teacher is not None:
         x = np.asarray(teacher[0], np.float32)
     else:
-        a = bf(stem_inputs(spatial, glob)).astype(np.float64)
-        x = bf((a @ bf(w["stem"]).astype(np.float64).T).astype(np.float32))
+        x = stem_output(blob, topo, spatial, glob)
     from . import act
 
     for i in range(nb):
@@ -271,11 +274,7 @@ def forward(blob, topo, spatial, glob, teacher=None, precision="int8"):
         x = bf((x + d).astype(np.float32))
     # trunk tip: silu(x*gamma + beta) (debug_exec_units.rs:272-282)
     g = bf(act(((x * w["tip_g"][None, :]).astype(np.float32) + w["tip_b"][None, :]).astype(np.float32), 2))
-    g64 = g.astype(np.float64)
-    hp = np.concatenate([g64 @ bf(w["p1"]).astype(np.float64).T,
-                         g64 @ bf(w["g1"]).astype(np.float64).T + w["g1_b"],
-                         g64 @ bf(w["v1"]).astype(np.float64).T + w["v1_b"]], axis=1).reshape(n, SEQ, 384)
-    out = heads(hp, w, n)
+    out = heads(head_linears(g, w).reshape(n, SEQ, 384).astype(np.float64), w, n)
     out["residual"] = x
     return out
 
@@ -306,10 +305,18 @@ def heads(hp, w, n):
 
 
 def stem_output(blob, topo, spatial, glob):
-    """The oracle's stem result (bf16 values [n*361, C]), as forward computes it."""
+    """The stem (3x3 conv + global linear as one bf16 GEMM on the tensor
+    cores): bf16 values [n*361, C]."""
     w = parse(blob, *topo)
-    a = bf(stem_inputs(spatial, glob)).astype(np.float64)
-    return bf((a @ bf(w["stem"]).astype(np.float64).T).astype(np.float32))
+    return bf(tc_gemm16(bf16_encode(stem_inputs(spatial, glob)), bf16_encode(w["stem"])))
+
+
+def head_linears(g, w):
+    """fp32 [rows, 384] = g . [p1 | g1 | v1]^T on the tensor cores (bf16
+    operands) + [0 | g1_b | v1_b], the biases added in fp32."""
+    wm = np.concatenate([w["p1"], w["g1"], w["v1"]], axis=0)
+    bias = np.concatenate([np.zeros(96, np.float32), w["g1_b"], w["v1_b"]]).astype(np.float32)
+    return (tc_gemm16(bf16_encode(g), bf16_encode(wm)) + bias[None, :]).astype(np.float32)
 
 
 def perturbed_stem_forward(blob, topo, spatial, glob, fraction=1e-4, seed=0, precision="int8"):

@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_int8_ffn_gelu_rms_noalloc": (I, [STREAM, P, F, P, P, P, P, P, I]),
     "kb_int8_noalloc_prepare": (I, []),
     "kb_bf16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
+    "kb_f16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
     "kb_attention": (I, [P, P, P, P, I, I, I, F, I, STREAM]),
     "kb_status_reset": (I, [P, STREAM]),
     "kb_mxfp8_dimensions": (I, [I, I, IP, IP, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
@@ -81,7 +82,9 @@ class ModelDesc(ctypes.Structure):
 
     _fields_ = [("trunk_channels", ctypes.c_int), ("num_blocks", ctypes.c_int), ("num_heads", ctypes.c_int),
                 ("head_dim", ctypes.c_int), ("ffn_channels", ctypes.c_int), ("precision", ctypes.c_int),
-                ("proj_precision", ctypes.c_int * 4), ("int8_min_ffn_width", ctypes.c_int)]
+                ("proj_precision", ctypes.c_int * 4), ("int8_min_ffn_width", ctypes.c_int),
+                ("topology", ctypes.c_int), ("mid_channels", ctypes.c_int), ("pairs_per_block", ctypes.c_int),
+                ("norm_eps", ctypes.c_float)]
 
 class PostProcessParams(ctypes.Structure):
     """kb_postprocess_params (ModelPostProcessParams, crates/kata_nn/src/desc.rs:671-695,
@@ -114,6 +117,7 @@ EPI_I32, EPI_F16, EPI_RES_F32, EPI_16, EPI_RES16, EPI_SWIGLU16, EPI_F32 = range(
 ACT_NONE, ACT_GELU, ACT_SILU = 0, 1, 2
 LAYOUT_PLAIN, LAYOUT_SWIGLU_DUAL = 0, 1
 PREC_INT8, PREC_MXFP8 = 0, 1
+TOPO_FLAT, TOPO_NESTED = 0, 1
 MX_OUT_HALF, MX_OUT_FLOAT, MX_OUT_FLOAT_RESIDUAL, MX_OUT_BF16, MX_OUT_BF16_RESIDUAL = range(5)
 STATUS_NAN, STATUS_INF, STATUS_OUTPUT_NONFINITE, STATUS_WEIGHT_OVERFLOW = 1, 2, 4, 8
 STATUS_UNSUPPORTED_ARCH, STATUS_TIMEOUT = 16, 32

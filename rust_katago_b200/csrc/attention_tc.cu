@@ -31,7 +31,9 @@
 // P.V MMA, read from TMEM).  Between the halves the softmax warps finish the
 // previous tile: O = (O_A 2^((m_A-m)c) + O_B 2^((m_B-m)c)) /
 // (l_A 2^((m_A-m)c) + l_B 2^((m_B-m)c)), each warp writing D/4 of the D dims
-// by TMA, plus the row |max| for the next quantiser.  Every wait is bounded.
+// by TMA, plus the row |max| for the next quantiser.  Every exponential is the
+// same FMA-pipe polynomial (exp2_poly2), so the softmax is a fixed sequence of
+// IEEE operations that the CPU oracle restates exactly.  Every wait is bounded.
 #include <stdint.h>
 #include <string.h>
 
@@ -95,14 +97,10 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x for a pair of x <= 0 on the FMA pipe, relieving the special-function
-// unit (which takes the other half of the exponentials): x clamped to -126,
+// 2^x for a pair of x <= 0 on the FMA pipe, the kernel's one definition of
+// the exponential (a fixed sequence of IEEE operations, so the CPU oracle
+// reproduces every P bit for bit; the special-function unit's approximation
+// would not be reproducible): x clamped to -126,
 // n = rint(x) by the 1.5 * 2^23 magic add, f = x - n in [-0.5, 0.5], 2^f by a
 // degree-3 polynomial (least-squares Chebyshev fit of 2^f on [-0.5, 0.5],
 // relative error 1.4e-4: below the 16-bit rounding of P), and 2^n added to
@@ -242,22 +240,19 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
   if (valid >= NK) {
 #pragma unroll
     for (int i = 0; i < NK / 2; ++i) {
-      // half the exponentials on the special-function unit, half on the FMA pipe
       const float2 x = fma2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
                             make_float2(scale_log2, scale_log2), make_float2(-mc, -mc));
-      float2 p;
-      if (i & 1)
-        p = make_float2(ex2(x.x), ex2(x.y));
-      else
-        p = exp2_poly2(x.x, x.y);
+      const float2 p = exp2_poly2(x.x, x.y);
       lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p.x, p.y));
       pk[i] = pack2(p.x, p.y, F16);
     }
   } else {
 #pragma unroll
     for (int i = 0; i < NK / 2; ++i) {
-      const float p0 = 2 * i < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc)) : 0.0f;
-      const float p1 = 2 * i + 1 < valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc)) : 0.0f;
+      const float2 e = exp2_poly2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -mc),
+                                  __fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc));
+      const float p0 = 2 * i < valid ? e.x : 0.0f;
+      const float p1 = 2 * i + 1 < valid ? e.y : 0.0f;
       lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p0, p1));
       pk[i] = pack2(p0, p1, F16);
     }
@@ -521,8 +516,9 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       const float lb = __fadd_rn(__fadd_rn(__uint_as_float(lv[4]), __uint_as_float(lv[5])),
                                  __fadd_rn(__uint_as_float(lv[6]), __uint_as_float(lv[7])));
       const float mx = fmaxf(pma, pmb);
-      const float fa = pma == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(pma, mx), scale_log2));
-      const float fb = pmb == mx ? 1.0f : ex2(__fmul_rn(__fsub_rn(pmb, mx), scale_log2));
+      const float2 fab = exp2_poly2(__fmul_rn(__fsub_rn(pma, mx), scale_log2), __fmul_rn(__fsub_rn(pmb, mx), scale_log2));
+      const float fa = pma == mx ? 1.0f : fab.x;
+      const float fb = pmb == mx ? 1.0f : fab.y;
       // Every operation rounded on its own (no contraction), so the CPU
       // restatement of this combination reproduces it exactly.
       const float inv = __fdiv_rn(1.0f, __fadd_rn(__fmul_rn(la, fa), __fmul_rn(lb, fb)));

@@ -545,4 +545,25 @@ int kb_bf16_linear(const uint16_t* a, const uint16_t* w, const float* bias, int 
   return gemm_launch(kGemmBF16, epilogue, a, w, g, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int kb_f16_linear(const uint16_t* a, const uint16_t* w, const float* bias, int m, int n, int k, int epilogue,
+                  int act, int out_dtype, void* out, int ldo, uintptr_t stream) {
+  if (!a || !w || !out || m <= 0 || n <= 0 || k <= 0 || k % 8 != 0 || ldo < n ||
+      (epilogue != KB_EPI_16 && epilogue != KB_EPI_RES16 && epilogue != KB_EPI_F32) || act < 0 ||
+      act > KB_ACT_SILU) {
+    set_error("kb_f16_linear: invalid arguments (k must be a multiple of 8)");
+    return KB_E_INVALID;
+  }
+  GemmArgs g;
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.out = out;
+  g.ldo = ldo;
+  g.bias = bias;
+  g.act = act;
+  g.out_f16 = out_dtype == KB_DT_F16;
+  g.ab_f16 = 1;
+  return gemm_launch(kGemmBF16, epilogue, a, w, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -160,15 +160,6 @@ __device__ __forceinline__ void load_vec32(const float* p, int col0, int n, floa
   }
 }
 
-// Round a pair to the 16-bit output type; element 0 in the low half.
-__device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
-  if (f16) {
-    const __half2 h = __floats2half2_rn(v.x, v.y);
-    return *reinterpret_cast<const uint32_t*>(&h);
-  }
-  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 __device__ __forceinline__ float2 unpack16x2(uint32_t w, bool f16) {
   if (f16) return make_float2(from_f16(static_cast<uint16_t>(w & 0xffffu)), from_f16(static_cast<uint16_t>(w >> 16)));
@@ -413,7 +404,10 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc<KIND>(BN);
+      // kGemmBF16 with ab_f16: both operands binary16 (format 0) instead of
+      // bfloat16 (format 1); A and B always share one type.
+      const uint32_t idesc =
+          make_idesc<KIND>(BN) & ~(KIND == kGemmBF16 && g.ab_f16 ? ((7u << 7) | (7u << 10)) : 0u);
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;

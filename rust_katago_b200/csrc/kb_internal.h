@@ -52,6 +52,9 @@ struct GemmArgs {
   int n_out = 0;                     // SwiGLU: logical output columns (hidden)
   unsigned* status = nullptr;        // sticky status word (timeouts)
   unsigned layer = KB_NO_LAYER;
+  // kGemmBF16 only: the 16-bit operands are binary16 (f16 x f16 -> f32)
+  // instead of bfloat16.
+  int ab_f16 = 0;
   // Limit of the kernel's bounded waits on work (0 = the default two
   // seconds); only the abort-path test sets it.  Waits that drain copies or
   // MMAs already issued keep the default.

@@ -43,6 +43,17 @@ __device__ __forceinline__ float kb_expf(float x) {
   return x != x ? x : y;
 }
 
+// Round a pair to the 16-bit type (binary16 or bfloat16, round to nearest
+// even); element 0 in the low half.
+__device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
+  if (f16) {
+    const __half2 h = __floats2half2_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // SiLU exactly as the reference writes it inside its SwiGLU: g / (1 + e^-g)
 // (cuda-kernels/int8_ops.cu:111-113), with kb_expf in place of expf.
 __device__ __forceinline__ float kb_silu(float g) {

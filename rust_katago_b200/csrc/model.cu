@@ -12,11 +12,19 @@
 //                          sticky status check before outputs are published
 //   kb_forward_device    ~ CudaModel::apply (cuda_exec.rs:913) on device buffers
 //
-// The trunk (BASELINE b11c768 topology): stem (3x3 conv 22->C + global linear,
-// one bf16 GEMM) -> num_blocks x [RMSNorm -> INT8 QKV GEMM -> RoPE attention ->
-// INT8 out-proj + residual -> RMSNorm -> INT8 up GEMM + GELU -> INT8 down GEMM +
-// residual] on a bf16 residual stream -> trunk tip (BN affine + SiLU) -> one
-// bf16 GEMM for all per-token head linears -> policy/value heads.
+// The flat trunk (BASELINE b11c768 topology): stem (3x3 conv 22->C + global
+// linear, one bf16 GEMM) -> num_blocks x [RMSNorm -> INT8 QKV GEMM -> RoPE
+// attention -> INT8 out-proj + residual -> RMSNorm -> INT8 up GEMM + GELU ->
+// INT8 down GEMM + residual] on a bf16 residual stream -> trunk tip (BN affine +
+// SiLU) -> one bf16 GEMM for all per-token head linears -> policy/value heads.
+//
+// The nested trunk (the reference's TF3 graph, native_model.rs:79-124, run as
+// cuda_exec.rs:1136-1700 runs it): stem as one binary16 GEMM into an fp32 raw
+// trunk -> per outer block [gate-SiLU (pre_bn) -> binary16 C->mid linear into
+// an fp32 inner stream -> pairs x (RMSNorm -> QKV (INT8 or binary16, RoPE in
+// the epilogue) -> attention D32 -> out-proj + fp32 residual -> RMSNorm -> INT8
+// SwiGLU FFN + fp32 residual) -> gate-SiLU (post_bn) -> binary16 mid->C linear
+// added to the raw trunk] -> trunk tip -> heads.
 #include <math.h>
 #include <string.h>
 
@@ -36,7 +44,9 @@ int attention_launch(const uint16_t* qkv, const float* rope_cos, const float* ro
                      int batch, int seq, int heads, int head_dim, float scale, int f16, cudaStream_t stream,
                      uint32_t* row_amax = nullptr, unsigned* status = nullptr);
 int stem_gather_launch(const float* spatial, const float* global, const int* sym, uint16_t* a, int batch,
-                       int nhwc, cudaStream_t s);
+                       int nhwc, cudaStream_t s, int f16 = 0);
+int gate_silu_launch(const float* x, long ldx, const float* scale, const float* bias, uint16_t* out, long ldo,
+                     long rows, int w, int f16, cudaStream_t s);
 int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, uint16_t* g, long rows, int c,
                      cudaStream_t s);
 int heads_launch(const float* hp, const float* const* wts, float* policy, float* value, float* misc,
@@ -53,6 +63,7 @@ constexpr int kInC = 22, kInG = 19;
 constexpr int kStemK = 224, kStemKUsed = 217;
 constexpr int kHeadN = 384;  // p1 96 | g1 96 | v1 192
 constexpr float kRmsEps = 1e-6f;
+constexpr int kNestedHeadDim = 32;  // native_model.rs:15 (DIM)
 
 // Host-side view of the fp32 weight blob (layout documented in katab200.h).
 struct BlobCursor {
@@ -70,7 +81,13 @@ struct BlobCursor {
 size_t blob_floats(const kb_model_desc& d) {
   const size_t c = d.trunk_channels, f = d.ffn_channels, h = d.num_heads, hd = d.head_dim;
   size_t n = c * kStemKUsed;
-  n += d.num_blocks * (c + 3 * c * c + c * c + c + f * c + f + c * f + c + h * (hd / 2) * 2);
+  if (d.topology == KB_TOPO_NESTED) {
+    const size_t m = d.mid_channels;
+    const size_t pair = m + 3 * m * m + m * m + h * (hd / 2) * 2 + m + 2 * f * m + m * f;
+    n += d.num_blocks * (2 * c + m * c + d.pairs_per_block * pair + 2 * m + c * m);
+  } else {
+    n += d.num_blocks * (c + 3 * c * c + c * c + c + f * c + f + c * f + c + h * (hd / 2) * 2);
+  }
   n += 2 * c;
   n += 96 * c + 96 * c + 96 + 192 * c + 192;
   n += 96 * 288 + 96 * 288 + 96 + 6 * 96 + 96 + 6 * 96;
@@ -78,7 +95,49 @@ size_t blob_floats(const kb_model_desc& d) {
   return n;
 }
 
+int validate_nested(const kb_model_desc* d) {
+  const int m = d->mid_channels, h = d->ffn_channels;
+  // native_model.rs:31-60, :91-104 (D = 32, SwiGLU hidden <= 3*mid, 8-aligned),
+  // plus this build's GEMM tiling (C % 64, mid % 32).
+  if (d->trunk_channels <= 0 || d->trunk_channels % 64 != 0 || d->trunk_channels > 4096 || m < 32 ||
+      m % 32 != 0 || m >= d->trunk_channels || m > 2048 || d->num_blocks <= 0 || d->num_blocks > 64 ||
+      d->pairs_per_block < 1 || d->pairs_per_block > 8 || d->head_dim != kNestedHeadDim ||
+      d->num_heads * kNestedHeadDim != m || h <= 0 || h % 8 != 0 || h > 3 * m ||
+      !(d->norm_eps >= 0.0f) || !std::isfinite(d->norm_eps)) {
+    set_error("nested model descriptor: need C % 64 == 0 (<= 4096), 32 <= mid < C with mid % 32 == 0, "
+              "heads * 32 == mid (head_dim 32), SwiGLU hidden 8-aligned and <= 3*mid, 1..64 outer blocks of "
+              "1..8 pairs, a finite epsilon >= 0");
+    return KB_E_INVALID;
+  }
+  if (d->precision != KB_PREC_INT8) {
+    set_error("nested model descriptor: precision must be KB_PREC_INT8 (INT8 SwiGLU FFN)");
+    return KB_E_INVALID;
+  }
+  for (int i = 0; i < 4; ++i) {
+    const int p = d->proj_precision[i];
+    const bool ok = i < KB_PROJ_FFN_UP ? (p == KB_PROJ_FOLLOW || p == KB_PROJ_INT8 || p == KB_PROJ_BF16)
+                                       : (p == KB_PROJ_FOLLOW || p == KB_PROJ_INT8);
+    if (!ok) {
+      set_error("nested model descriptor: qkv / out projections INT8 or 16-bit (KB_PROJ_BF16 = binary16 here), "
+                "the SwiGLU FFN INT8");
+      return KB_E_INVALID;
+    }
+  }
+  if (d->int8_min_ffn_width < 0 || d->int8_min_ffn_width > 8192 || d->int8_min_ffn_width % 8 != 0 ||
+      (d->int8_min_ffn_width > 0 && h < d->int8_min_ffn_width)) {
+    set_error("nested model descriptor: int8_min_ffn_width would leave the SwiGLU FFN unquantised, which the "
+              "nested path does not run");
+    return KB_E_INVALID;
+  }
+  return KB_OK;
+}
+
 int validate_desc(const kb_model_desc* d) {
+  if (d && d->topology == KB_TOPO_NESTED) return validate_nested(d);
+  if (d && (d->topology != KB_TOPO_FLAT || !(d->norm_eps >= 0.0f) || !std::isfinite(d->norm_eps))) {
+    set_error("model descriptor: topology must be KB_TOPO_FLAT or KB_TOPO_NESTED, norm_eps finite and >= 0");
+    return KB_E_INVALID;
+  }
   if (!d || d->trunk_channels <= 0 || d->trunk_channels % 64 != 0 || d->trunk_channels > 4096 ||
       d->num_blocks <= 0 || d->num_blocks > 64 || d->num_heads <= 0 ||
       (d->head_dim != 32 && d->head_dim != 64) || d->num_heads * d->head_dim != d->trunk_channels ||
@@ -136,6 +195,65 @@ uint16_t bf16_bits(float v) {
   return static_cast<uint16_t>(b >> 16);
 }
 
+// IEEE binary16 round-to-nearest-even of a finite float (host).
+uint16_t f16_bits(float v) {
+  uint32_t b;
+  memcpy(&b, &v, 4);
+  const uint16_t sign = static_cast<uint16_t>((b >> 16) & 0x8000u);
+  const int e = static_cast<int>((b >> 23) & 255u) - 127 + 15;
+  uint32_t mant = b & 0x7fffffu;
+  if (e >= 31) return static_cast<uint16_t>(sign | 0x7c00u);
+  if (e <= 0) {
+    if (e < -10) return sign;
+    mant |= 0x800000u;
+    const uint32_t shift = static_cast<uint32_t>(14 - e);
+    uint32_t r = mant >> shift;
+    const uint32_t rem = mant & ((1u << shift) - 1u), half = 1u << (shift - 1);
+    if (rem > half || (rem == half && (r & 1u))) ++r;
+    return static_cast<uint16_t>(sign | r);
+  }
+  uint32_t r = mant >> 13;
+  const uint32_t rem = mant & 0x1fffu;
+  uint32_t ex = static_cast<uint32_t>(e);
+  if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) {
+    if (++r == 0x400u) {
+      r = 0;
+      if (++ex >= 31) return static_cast<uint16_t>(sign | 0x7c00u);
+    }
+  }
+  return static_cast<uint16_t>(sign | (ex << 10) | r);
+}
+
+uint16_t bits16(float v, bool f16) { return f16 ? f16_bits(v) : bf16_bits(v); }
+
+// Rotary tables of one attention layer: angle = x*f0 + y*f1 in fp32, cosf /
+// sinf (native_model.rs:200-228), laid out [head * pairs + pair, token] so the
+// QKV epilogue's 32 consecutive rows (tokens) read one contiguous run.
+int upload_rope(const float* freqs, int nh, int hd, float** cos_d, float** sin_d) {
+  const int pairs = hd / 2;
+  std::vector<float> cs(static_cast<size_t>(kSeq) * nh * pairs), sn(cs.size());
+  for (int y = 0; y < kSide; ++y)
+    for (int x = 0; x < kSide; ++x)
+      for (int hh = 0; hh < nh; ++hh)
+        for (int p = 0; p < pairs; ++p) {
+          const int fi = (hh * pairs + p) * 2;
+          const float angle = static_cast<float>(x) * freqs[fi] + static_cast<float>(y) * freqs[fi + 1];
+          const size_t idx = (static_cast<size_t>(hh) * pairs + p) * kSeq + (y * kSide + x);
+          cs[idx] = cosf(angle);
+          sn[idx] = sinf(angle);
+        }
+  int rc = upload(cos_d, cs.data(), cs.size(), "upload rope");
+  if (!rc) rc = upload(sin_d, sn.data(), sn.size(), "upload rope");
+  return rc;
+}
+
+// A weight [n, k] as binary16 on the device.
+int upload_f16(uint16_t** dst, const float* w, size_t count) {
+  std::vector<uint16_t> hw(count);
+  for (size_t i = 0; i < count; ++i) hw[i] = f16_bits(w[i]);
+  return upload(dst, hw.data(), hw.size(), "upload binary16 weight");
+}
+
 struct Block {
   float* rms1 = nullptr;
   float* rms2 = nullptr;
@@ -159,10 +277,36 @@ struct Block {
   float* rope_sin = nullptr;
 };
 
+// One attention / FFN pair of a nested outer block.
+struct NestedPair {
+  float* rms1 = nullptr;
+  float* rms2 = nullptr;
+  kb_int8_weight* qkv = nullptr;  // INT8 projections, or
+  kb_int8_weight* out = nullptr;
+  uint16_t* hqkv = nullptr;       // binary16 [3M, M] / [M, M]
+  uint16_t* hout = nullptr;
+  kb_int8_weight* dual = nullptr;  // SwiGLU [gate; up] [2H, M], tile-interleaved
+  kb_int8_weight* down = nullptr;  // [M, H]
+  float* rope_cos = nullptr;       // [heads * 16 + pair, token]
+  float* rope_sin = nullptr;
+};
+
+struct NestedBlock {
+  float* pre_s = nullptr;  // pre_bn scale / bias [C]
+  float* pre_b = nullptr;
+  uint16_t* pre_w = nullptr;  // binary16 [M, C]
+  std::vector<NestedPair> pairs;
+  float* post_s = nullptr;  // post_bn scale / bias [M]
+  float* post_b = nullptr;
+  uint16_t* post_w = nullptr;  // binary16 [C, M]
+};
+
 }  // namespace
 
 struct kb_model {
   kb_model_desc desc{};
+  float eps = kRmsEps;  // RMSNorm epsilon
+  std::vector<NestedBlock> nblocks;  // KB_TOPO_NESTED
   int prec[4] = {};    // resolved KB_PROJ_* of qkv, out, ffn_up, ffn_down
   bool mixed = false;  // not every projection in the model's `precision`
   int device = 0;
@@ -228,6 +372,8 @@ struct kb_handle {
   size_t mx_scale_bytes = 0;
   uint32_t* row_amax = nullptr; // [M] |bits| maximum of the FFN hidden rows
   float* hp = nullptr;          // [M, 384] fp32
+  float* x32 = nullptr;         // nested: raw trunk [M, C] fp32
+  float* mid32 = nullptr;       // nested: inner stream [M, mid] fp32
   unsigned* status = nullptr;   // [2]
   kb_postprocess_params pp = kb::default_postprocess_params();
   Slot slots[2];
@@ -263,6 +409,26 @@ void destroy_model(kb_model* m) {
     cudaFree(b.down_b);
     cudaFree(b.rope_cos);
     cudaFree(b.rope_sin);
+  }
+  for (auto& nb : m->nblocks) {
+    cudaFree(nb.pre_s);
+    cudaFree(nb.pre_b);
+    cudaFree(nb.pre_w);
+    cudaFree(nb.post_s);
+    cudaFree(nb.post_b);
+    cudaFree(nb.post_w);
+    for (auto& pr : nb.pairs) {
+      cudaFree(pr.rms1);
+      cudaFree(pr.rms2);
+      kb_int8_weight_destroy(pr.qkv);
+      kb_int8_weight_destroy(pr.out);
+      cudaFree(pr.hqkv);
+      cudaFree(pr.hout);
+      kb_int8_weight_destroy(pr.dual);
+      kb_int8_weight_destroy(pr.down);
+      cudaFree(pr.rope_cos);
+      cudaFree(pr.rope_sin);
+    }
   }
   cudaFree(m->tip_gamma);
   cudaFree(m->tip_beta);
@@ -314,7 +480,7 @@ int mxfp8_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale
   const int c = d.trunk_channels, f = d.ffn_channels, M = n * kSeq;
   cudaStream_t s = h->stream;
   uint8_t* q = reinterpret_cast<uint8_t*>(h->q);
-  int rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms1, kRmsEps, 0, q, h->mx_scales, h->status, layer, s);
+  int rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms1, h->model->eps, 0, q, h->mx_scales, h->status, layer, s);
   if (!rc) {
     GemmArgs gq = mx_args(h, b.mqkv, M, h->qkv, nullptr, 0, layer);
     set_rope(gq, b, d);
@@ -333,7 +499,7 @@ int mxfp8_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale
   if (!rc)
     rc = mxfp8_quantize_launch(h->att, KB_DT_BF16, c, M, c, q, h->mx_scales, sb_c, false, h->status, layer, s);
   if (!rc) rc = gemm_launch(kGemmMXF8, kEpiRes16, q, b.mout->q, mx_args(h, b.mout, M, h->x, nullptr, 0, layer), s);
-  if (!rc) rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms2, kRmsEps, 0, q, h->mx_scales, h->status, layer, s);
+  if (!rc) rc = rms_mxfp8_launch(h->x, KB_DT_BF16, c, M, c, b.rms2, h->model->eps, 0, q, h->mx_scales, h->status, layer, s);
   if (!rc)
     rc = gemm_launch(kGemmMXF8, kEpi16, q, b.mup->q, mx_args(h, b.mup, M, h->hidden, b.up_b, KB_ACT_GELU, layer), s);
   if (!rc)
@@ -359,12 +525,15 @@ int mixed_operand(kb_handle* h, int prec, const uint16_t* src, int M, int k, int
   uint8_t* q8 = reinterpret_cast<uint8_t*>(h->q);
   if (prec == KB_PROJ_INT8) {
     *a = h->q;
-    return quantize_rows_launch(src, KB_DT_BF16, k, M, k, kp, gamma != nullptr, gamma, kRmsEps, 0, h->q, h->scales,
+    return quantize_rows_launch(src, KB_DT_BF16, k, M, k, kp, gamma != nullptr, gamma, h->model->eps, 0, h->q,
+                                h->scales,
                                 h->status, layer, s);
   }
   if (prec == KB_PROJ_MXFP8) {
     *a = q8;
-    if (gamma) return rms_mxfp8_launch(src, KB_DT_BF16, k, M, k, gamma, kRmsEps, 0, q8, h->mx_scales, h->status, layer, s);
+    if (gamma)
+      return rms_mxfp8_launch(src, KB_DT_BF16, k, M, k, gamma, h->model->eps, 0, q8, h->mx_scales, h->status, layer,
+                              s);
     size_t sb = 0;
     int rc = mxfp8_dims(M, k, nullptr, nullptr, nullptr, &sb);
     if (!rc) rc = mxfp8_quantize_launch(src, KB_DT_BF16, k, M, k, q8, h->mx_scales, sb, false, h->status, layer, s);
@@ -375,7 +544,7 @@ int mixed_operand(kb_handle* h, int prec, const uint16_t* src, int M, int k, int
     return KB_OK;
   }
   *a = h->att;
-  return rms16_rows_launch(src, KB_DT_BF16, k, M, k, gamma, kRmsEps, 0, h->att, k, h->status, layer, s);
+  return rms16_rows_launch(src, KB_DT_BF16, k, M, k, gamma, h->model->eps, 0, h->att, k, h->status, layer, s);
 }
 
 // One projection out[M, n] of the mixed block in its precision.
@@ -446,6 +615,186 @@ int mixed_block(kb_handle* h, const Block& b, unsigned layer, int n, float scale
   return rc;
 }
 
+// ---- nested (TF3) trunk --------------------------------------------------
+
+// The attention scale of the lowered TF3 graph: qk_scale = 1 / sqrt(sqrt(32))
+// applied to both q and k (native_model.rs:195), i.e. qk_scale^2 on q.k
+// (cuda_exec.rs:1294), each step rounded to fp32.
+float nested_attention_scale() {
+  const float qk = 1.0f / sqrtf(sqrtf(static_cast<float>(kNestedHeadDim)));
+  return qk * qk;
+}
+
+// A binary16 tensor-core GEMM with an fp32 result: out[M, n] = a . w^T, plus
+// the fp32 `residual` (may alias out) when given.
+int f16_gemm_f32(kb_handle* h, const uint16_t* a, const uint16_t* w, int M, int n, int k, float* out,
+                 const float* residual) {
+  GemmArgs g;
+  g.m = M;
+  g.n = n;
+  g.k = k;
+  g.out = out;
+  g.ldo = n;
+  g.residual = const_cast<float*>(residual);
+  g.ldr = n;
+  g.ab_f16 = 1;
+  g.status = h->status;
+  return gemm_launch(kGemmBF16, kEpiF32, a, w, g, h->stream);
+}
+
+// One attention / FFN pair on the fp32 inner stream h->mid32 [M, mid]:
+// RMSNorm -> QKV (INT8 with the fused RMS quantiser, or binary16 on the
+// RMSNorm's binary16 rows) with RoPE in the epilogue -> attention (binary16
+// P) -> out-proj added to the fp32 stream (INT8 dequant-residual, or binary16
+// GEMM + residual) -> RMSNorm -> INT8 dual GEMM + SwiGLU (fp16 boundaries) ->
+// requant -> INT8 down GEMM added to the fp32 stream: the reference's
+// Int8Workspace::ffn_rms (int8.rs:1135-1172).
+int nested_pair(kb_handle* h, const NestedPair& p, unsigned layer, int n, float scale) {
+  const kb_model* m = h->model;
+  const kb_model_desc& d = m->desc;
+  const int mid = d.mid_channels, hid = d.ffn_channels, M = n * kSeq;
+  cudaStream_t s = h->stream;
+  int rc;
+  GemmArgs g;
+  g.m = M;
+  g.n = 3 * mid;
+  g.out = h->qkv;
+  g.ldo = 3 * mid;
+  g.out_f16 = 1;
+  g.status = h->status;
+  g.layer = layer;
+  g.rope_cos = p.rope_cos;
+  g.rope_sin = p.rope_sin;
+  g.rope_cols = 2 * mid;
+  g.rope_heads = d.num_heads;
+  g.rope_hd = kNestedHeadDim;
+  g.rope_seq = kSeq;
+  if (p.qkv) {
+    rc = quantize_rows_launch(h->mid32, KB_DT_F32, mid, M, mid, p.qkv->kp, true, p.rms1, m->eps, 1, h->q, h->scales,
+                              h->status, layer, s);
+    if (rc) return rc;
+    g.k = p.qkv->kp;
+    g.row_scale = h->scales;
+    g.col_scale = p.qkv->scales;
+    rc = gemm_launch(kGemmI8, kEpiRope16, h->q, p.qkv->q, g, s);
+  } else {
+    rc = rms16_rows_launch(h->mid32, KB_DT_F32, mid, M, mid, p.rms1, m->eps, 1, h->att, mid, h->status, layer, s);
+    if (rc) return rc;
+    g.k = mid;
+    g.ab_f16 = 1;
+    rc = gemm_launch(kGemmBF16, kEpiRope16, h->att, p.hqkv, g, s);
+  }
+  if (rc) return rc;
+  if (p.out) {
+    rc = check_cuda(cudaMemsetAsync(h->row_amax, 0, static_cast<size_t>(M) * sizeof(uint32_t), s), "amax reset");
+    if (rc) return rc;
+  }
+  rc = attention_launch(h->qkv, nullptr, nullptr, h->att, n, kSeq, d.num_heads, kNestedHeadDim, scale, 1, s,
+                        p.out ? h->row_amax : nullptr, h->status);
+  if (rc) return rc;
+  if (p.out) {
+    rc = quantize_rows_amax_launch(h->att, KB_DT_F16, mid, h->row_amax, M, mid, p.out->kp, h->q, h->scales, h->status,
+                                   layer, s);
+    if (rc) return rc;
+    GemmArgs o;
+    o.m = M;
+    o.n = mid;
+    o.k = p.out->kp;
+    o.out = h->mid32;
+    o.ldo = mid;
+    o.row_scale = h->scales;
+    o.col_scale = p.out->scales;
+    o.status = h->status;
+    o.layer = layer;
+    rc = gemm_launch(kGemmI8, kEpiResF32, h->q, p.out->q, o, s);
+  } else {
+    rc = f16_gemm_f32(h, h->att, p.hout, M, mid, mid, h->mid32, h->mid32);
+  }
+  if (rc) return rc;
+  // SwiGLU FFN: RMSNorm -> fp16 boundary -> INT8 -> dual GEMM + SwiGLU -> requant -> down + fp32 residual
+  rc = quantize_rows_launch(h->mid32, KB_DT_F32, mid, M, mid, p.dual->kp, true, p.rms2, m->eps, 1, h->q, h->scales,
+                            h->status, layer, s);
+  if (rc) return rc;
+  GemmArgs u;
+  u.m = M;
+  u.n = p.dual->n_stored;
+  u.k = p.dual->kp;
+  u.out = h->hidden;
+  u.ldo = hid;
+  u.row_scale = h->scales;
+  u.col_scale = p.dual->scales;
+  u.out_f16 = 1;
+  u.n_out = hid;
+  u.status = h->status;
+  u.layer = layer;
+  rc = gemm_launch(kGemmI8, kEpiSwiGLU16, h->q, p.dual->q, u, s, 256);
+  if (rc) return rc;
+  rc = quantize_rows_launch(h->hidden, KB_DT_F16, hid, M, hid, p.down->kp, false, nullptr, 0.0f, 0, h->q, h->scales,
+                            h->status, layer, s);
+  if (rc) return rc;
+  GemmArgs dn;
+  dn.m = M;
+  dn.n = mid;
+  dn.k = p.down->kp;
+  dn.out = h->mid32;
+  dn.ldo = mid;
+  dn.row_scale = h->scales;
+  dn.col_scale = p.down->scales;
+  dn.status = h->status;
+  dn.layer = layer;
+  return gemm_launch(kGemmI8, kEpiResF32, h->q, p.down->q, dn, s);
+}
+
+// The nested forward; `trace` as documented for kb_forward_trace.
+int forward_nested(kb_handle* h, int n, const float* d_spatial, const float* d_global, const int* d_sym, float* d_out,
+                   uint16_t* trace) {
+  kb_model* m = h->model;
+  const kb_model_desc& d = m->desc;
+  const int c = d.trunk_channels, mid = d.mid_channels, M = n * kSeq;
+  cudaStream_t s = h->stream;
+  const size_t plane = static_cast<size_t>(M) * c;
+  const float scale = nested_attention_scale();
+  int rc = stem_gather_launch(d_spatial, d_global, d_sym, h->stem_a, n, h->nhwc, s, 1);
+  if (!rc) rc = f16_gemm_f32(h, h->stem_a, m->stem_w, M, c, kStemK, h->x32, nullptr);
+  for (int bi = 0; bi < d.num_blocks && !rc; ++bi) {
+    const NestedBlock& b = m->nblocks[bi];
+    // pre_bn gate of the raw trunk (the stem's conv_bias_gate for block 0)
+    rc = gate_silu_launch(h->x32, c, b.pre_s, b.pre_b, h->x, c, M, c, 1, s);
+    if (!rc && trace)
+      rc = check_cuda(cudaMemcpyAsync(trace + bi * plane, h->x, plane * 2, cudaMemcpyDeviceToDevice, s), "trace");
+    if (!rc) rc = f16_gemm_f32(h, h->x, b.pre_w, M, mid, c, h->mid32, nullptr);
+    for (size_t pi = 0; pi < b.pairs.size() && !rc; ++pi)
+      rc = nested_pair(h, b.pairs[pi], static_cast<unsigned>(bi * d.pairs_per_block + pi), n, scale);
+    // post_bn gate of the inner stream, then the mid -> C linear into the raw trunk
+    if (!rc) rc = gate_silu_launch(h->mid32, mid, b.post_s, b.post_b, h->att, mid, M, mid, 1, s);
+    if (!rc) rc = f16_gemm_f32(h, h->att, b.post_w, M, c, mid, h->x32, h->x32);
+  }
+  if (rc) return rc;
+  rc = gate_silu_launch(h->x32, c, m->tip_gamma, m->tip_beta, h->att, c, M, c, 1, s);
+  if (!rc && trace)
+    for (int i = d.num_blocks; i < d.num_blocks + 2 && !rc; ++i)
+      rc = check_cuda(cudaMemcpyAsync(trace + i * plane, h->att, plane * 2, cudaMemcpyDeviceToDevice, s), "trace");
+  if (rc) return rc;
+  {
+    GemmArgs g;
+    g.m = M;
+    g.n = kHeadN;
+    g.k = c;
+    g.out = h->hp;
+    g.ldo = kHeadN;
+    g.bias = m->head_b;
+    g.ab_f16 = 1;
+    rc = gemm_launch(kGemmBF16, kEpiF32, h->att, m->head_w, g, s);
+    if (rc) return rc;
+  }
+  float* pol = d_out;
+  float* val = pol + static_cast<size_t>(n) * 6 * 362;
+  float* misc = val + static_cast<size_t>(n) * 3;
+  float* more = misc + static_cast<size_t>(n) * 10;
+  float* own = more + static_cast<size_t>(n) * 8;
+  return heads_launch(h->hp, m->head_ptrs, pol, val, misc, more, own, n, h->status, s);
+}
+
 // One forward pass of n positions on device buffers, enqueued on `s`.  When
 // `trace` is non-null it receives bf16 [(num_blocks + 2), n*361, C]: the stem
 // output, each block's attention output, and the final residual stream.
@@ -458,6 +807,7 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
   int rc = check_cuda(cudaMemsetAsync(h->status, 0, sizeof(unsigned), s), "status reset");
   if (!rc) rc = check_cuda(cudaMemsetAsync(h->status + 1, 0xff, sizeof(unsigned), s), "status reset");
   if (rc) return rc;
+  if (d.topology == KB_TOPO_NESTED) return forward_nested(h, n, d_spatial, d_global, d_sym, d_out, trace);
   rc = stem_gather_launch(d_spatial, d_global, d_sym, h->stem_a, n, h->nhwc, s);
   if (rc) return rc;
   {
@@ -491,7 +841,7 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
       continue;
     }
     // attention
-    rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.qkv->kp, true, b.rms1, kRmsEps, 0, h->q, h->scales,
+    rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.qkv->kp, true, b.rms1, m->eps, 0, h->q, h->scales,
                               h->status, layer, s);
     if (rc) return rc;
     GemmArgs g;
@@ -536,7 +886,7 @@ int forward(kb_handle* h, int n, const float* d_spatial, const float* d_global, 
     rc = gemm_launch(kGemmI8, kEpiRes16, h->q, b.out->q, o, s);
     if (rc) return rc;
     // FFN
-    rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.up->kp, true, b.rms2, kRmsEps, 0, h->q, h->scales,
+    rc = quantize_rows_launch(h->x, KB_DT_BF16, c, M, c, b.up->kp, true, b.rms2, m->eps, 0, h->q, h->scales,
                               h->status, layer, s);
     if (rc) return rc;
     rc = check_cuda(cudaMemsetAsync(h->row_amax, 0, static_cast<size_t>(M) * sizeof(uint32_t), s), "amax reset");
@@ -660,10 +1010,68 @@ void destroy_handle(kb_handle* h) {
   cudaFree(h->mx_scales);
   cudaFree(h->row_amax);
   cudaFree(h->hp);
+  cudaFree(h->x32);
+  cudaFree(h->mid32);
   cudaFree(h->status);
   if (h->stream) cudaStreamDestroy(h->stream);
   if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
   delete h;
+}
+
+// The nested blocks of the weight blob (layout in katab200.h): 16-bit weights
+// as binary16, the SwiGLU FFN and the projections resolved to INT8 quantised
+// per output channel (QuantizedWeights::new, int8.rs:171-211), the dual FFN
+// weight [gate; up] tile-interleaved as kb_int8_weight_upload packs it.
+int load_nested(kb_model* m, BlobCursor& cur) {
+  const kb_model_desc& d = m->desc;
+  const int c = d.trunk_channels, mid = d.mid_channels, hid = d.ffn_channels, nh = d.num_heads;
+  m->nblocks.resize(d.num_blocks);
+  int rc = KB_OK;
+  for (int bi = 0; bi < d.num_blocks && !rc; ++bi) {
+    NestedBlock& b = m->nblocks[bi];
+    const float* pre_s = cur.take(c);
+    const float* pre_b = cur.take(c);
+    const float* pre_w = cur.take(static_cast<size_t>(mid) * c);
+    rc = upload(&b.pre_s, pre_s, c, "upload gate");
+    if (!rc) rc = upload(&b.pre_b, pre_b, c, "upload gate");
+    if (!rc) rc = upload_f16(&b.pre_w, pre_w, static_cast<size_t>(mid) * c);
+    b.pairs.resize(d.pairs_per_block);
+    for (int pi = 0; pi < d.pairs_per_block && !rc; ++pi) {
+      NestedPair& p = b.pairs[pi];
+      const float* rms1 = cur.take(mid);
+      const float* qkv = cur.take(3ull * mid * mid);
+      const float* ow = cur.take(1ull * mid * mid);
+      const float* freqs = cur.take(static_cast<size_t>(nh) * (kNestedHeadDim / 2) * 2);
+      const float* rms2 = cur.take(mid);
+      const float* gate = cur.take(1ull * hid * mid);
+      const float* up = cur.take(1ull * hid * mid);
+      const float* down = cur.take(1ull * mid * hid);
+      rc = upload(&p.rms1, rms1, mid, "upload rms");
+      if (!rc) rc = upload(&p.rms2, rms2, mid, "upload rms");
+      if (!rc)
+        rc = m->prec[KB_PROJ_QKV] == KB_PROJ_INT8 ? kb_int8_weight_upload(qkv, 3 * mid, mid, KB_LAYOUT_PLAIN, &p.qkv)
+                                                  : upload_f16(&p.hqkv, qkv, 3ull * mid * mid);
+      if (!rc)
+        rc = m->prec[KB_PROJ_OUT] == KB_PROJ_INT8 ? kb_int8_weight_upload(ow, mid, mid, KB_LAYOUT_PLAIN, &p.out)
+                                                  : upload_f16(&p.hout, ow, 1ull * mid * mid);
+      if (!rc) {
+        std::vector<float> dual(2ull * hid * mid);
+        memcpy(dual.data(), gate, sizeof(float) * hid * mid);
+        memcpy(dual.data() + static_cast<size_t>(hid) * mid, up, sizeof(float) * hid * mid);
+        rc = kb_int8_weight_upload(dual.data(), 2 * hid, mid, KB_LAYOUT_SWIGLU_DUAL, &p.dual);
+      }
+      if (!rc) rc = kb_int8_weight_upload(down, mid, hid, KB_LAYOUT_PLAIN, &p.down);
+      if (!rc) rc = upload_rope(freqs, nh, kNestedHeadDim, &p.rope_cos, &p.rope_sin);
+    }
+    if (rc) break;
+    const float* post_s = cur.take(mid);
+    const float* post_b = cur.take(mid);
+    const float* post_w = cur.take(static_cast<size_t>(c) * mid);
+    rc = upload(&b.post_s, post_s, mid, "upload gate");
+    if (!rc) rc = upload(&b.post_b, post_b, mid, "upload gate");
+    if (!rc) rc = upload_f16(&b.post_w, post_w, static_cast<size_t>(c) * mid);
+  }
+  return rc;
 }
 
 }  // namespace
@@ -718,16 +1126,20 @@ int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, in
   }
   const int c = d.trunk_channels, f = d.ffn_channels, nh = d.num_heads, hd = d.head_dim;
   BlobCursor cur{blob, count};
-  // stem [C, 217] -> bf16 [C, 224]
+  const bool nested = d.topology == KB_TOPO_NESTED;
+  if (d.norm_eps > 0.0f) m->eps = d.norm_eps;
+  // stem [C, 217] -> 16-bit [C, 224] (bf16 flat, binary16 nested)
   {
     const float* w = cur.take(static_cast<size_t>(c) * kStemKUsed);
     std::vector<uint16_t> wb(static_cast<size_t>(c) * kStemK, 0);
     for (int r = 0; r < c; ++r)
-      for (int k = 0; k < kStemKUsed; ++k) wb[static_cast<size_t>(r) * kStemK + k] = bf16_bits(w[r * kStemKUsed + k]);
+      for (int k = 0; k < kStemKUsed; ++k)
+        wb[static_cast<size_t>(r) * kStemK + k] = bits16(w[r * kStemKUsed + k], nested);
     rc = upload(&m->stem_w, wb.data(), wb.size(), "upload stem");
   }
-  m->blocks.resize(d.num_blocks);
-  for (int bi = 0; bi < d.num_blocks && !rc; ++bi) {
+  if (nested && !rc) rc = load_nested(m, cur);
+  m->blocks.resize(nested ? 0 : d.num_blocks);
+  for (int bi = 0; bi < static_cast<int>(m->blocks.size()) && !rc; ++bi) {
     Block& b = m->blocks[bi];
     const float* rms1 = cur.take(c);
     const float* qkv = cur.take(3ull * c * c);
@@ -759,25 +1171,7 @@ int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, in
     }
     if (!rc) rc = upload(&b.up_b, up_b, f, "upload bias");
     if (!rc) rc = upload(&b.down_b, dn_b, c, "upload bias");
-    if (!rc) {
-      // Learned 2-D RoPE tables: angle = x*f0 + y*f1 in fp32, cosf/sinf
-      // (native_model.rs:200-228), laid out [head * pairs + pair, token] so that
-      // the QKV epilogue's 32 consecutive rows read one contiguous run.
-      const int pairs = hd / 2;
-      std::vector<float> cs(static_cast<size_t>(kSeq) * nh * pairs), sn(cs.size());
-      for (int y = 0; y < kSide; ++y)
-        for (int x = 0; x < kSide; ++x)
-          for (int hh = 0; hh < nh; ++hh)
-            for (int p = 0; p < pairs; ++p) {
-              const int fi = (hh * pairs + p) * 2;
-              const float angle = static_cast<float>(x) * freqs[fi] + static_cast<float>(y) * freqs[fi + 1];
-              const size_t idx = (static_cast<size_t>(hh) * pairs + p) * kSeq + (y * kSide + x);
-              cs[idx] = cosf(angle);
-              sn[idx] = sinf(angle);
-            }
-      rc = upload(&b.rope_cos, cs.data(), cs.size(), "upload rope");
-      if (!rc) rc = upload(&b.rope_sin, sn.data(), sn.size(), "upload rope");
-    }
+    if (!rc) rc = upload_rope(freqs, nh, hd, &b.rope_cos, &b.rope_sin);
   }
   if (!rc) {
     const float* tg = cur.take(c);
@@ -794,10 +1188,10 @@ int kb_model_load(const kb_model_desc* desc, const float* blob, size_t count, in
     std::vector<uint16_t> hw(static_cast<size_t>(kHeadN) * c);
     std::vector<float> hb(kHeadN, 0.0f);
     for (size_t i = 0; i < 96ull * c; ++i) {
-      hw[i] = bf16_bits(p1[i]);
-      hw[96ull * c + i] = bf16_bits(g1[i]);
+      hw[i] = bits16(p1[i], nested);
+      hw[96ull * c + i] = bits16(g1[i], nested);
     }
-    for (size_t i = 0; i < 192ull * c; ++i) hw[192ull * c + i] = bf16_bits(v1[i]);
+    for (size_t i = 0; i < 192ull * c; ++i) hw[192ull * c + i] = bits16(v1[i], nested);
     for (int i = 0; i < 96; ++i) hb[96 + i] = g1b[i];
     for (int i = 0; i < 192; ++i) hb[192 + i] = v1b[i];
     rc = upload(&m->head_w, hw.data(), hw.size(), "upload head linears");
@@ -882,6 +1276,10 @@ int kb_handle_create(kb_model* model, int max_batch, int inputs_nhwc, kb_handle*
   }
   if (!rc) rc = dev_alloc(&h->row_amax, M, "workspace");
   if (!rc) rc = dev_alloc(&h->hp, M * kHeadN, "workspace");
+  if (!rc && d.topology == KB_TOPO_NESTED) {
+    rc = dev_alloc(&h->x32, M * c, "workspace");
+    if (!rc) rc = dev_alloc(&h->mid32, M * static_cast<size_t>(d.mid_channels), "workspace");
+  }
   if (!rc) rc = dev_alloc(&h->status, 2, "status word");
   for (auto& sl : h->slots) {
     const size_t ns = static_cast<size_t>(max_batch) * kInC * kSeq, ng = static_cast<size_t>(max_batch) * (kInG + 1),

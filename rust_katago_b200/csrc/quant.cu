@@ -147,14 +147,6 @@ __device__ __forceinline__ uint2 quant_group_fast(const uint32_t (&w)[4], float 
   return make_uint2(pack4_magic(m[0], m[1], m[2], m[3]), pack4_magic(m[4], m[5], m[6], m[7]));
 }
 
-__device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
-  if (f16) {
-    const __half2 h = __floats2half2_rn(v.x, v.y);
-    return *reinterpret_cast<const uint32_t*>(&h);
-  }
-  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 // Quantise a warp-held row of packed 16-bit values (lane l holds groups
 // l, l+32, ...; amax2 = this lane's packed |bits| maximum).
@@ -739,6 +731,50 @@ __global__ void __launch_bounds__(256) rms_rows16_out16_kernel(
   }
 }
 
+// The same for fp32 rows (the nested trunk's fp32 inner stream, the input of
+// an unquantised attention projection).
+template <int G>
+__global__ void __launch_bounds__(256) rms_rows32_out16_kernel(
+    const float* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows, int width,
+    int bound_f16, uint16_t* __restrict__ out, long ldo, unsigned* status, unsigned layer) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = (width + 7) / 8;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    const float* src = x + static_cast<size_t>(row) * ldx;
+    const bool vin = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+    float v[G][8];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j;
+      if (g < groups) {
+        load_group<kInF32>(src, g, width, vin, v[j]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[j][t] = 0.0f;
+      }
+    }
+    uint32_t nw[G][4];
+    uint32_t amax2;
+    rms_normalize<G>(v, gamma, eps, width, lane, bound_f16 != 0, nw, amax2);
+    const uint32_t m16 = warp_max_u32(max(amax2 & 0xffffu, amax2 >> 16));
+    const uint32_t inf16 = bound_f16 ? 0x7c00u : 0x7f80u;
+    if (lane == 0 && m16 >= inf16) record_status(status, m16 > inf16 ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+    uint16_t* dst = out + static_cast<size_t>(row) * ldo;
+    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int g = lane + 32 * j, c0 = 8 * g;
+      if (g >= groups) continue;
+      if (vec && c0 + 8 <= width) {
+        *reinterpret_cast<uint4*>(dst + c0) = make_uint4(nw[j][0], nw[j][1], nw[j][2], nw[j][3]);
+      } else {
+        for (int t = 0; t < 8 && c0 + t < width; ++t)
+          dst[c0 + t] = static_cast<uint16_t>((t & 1) ? nw[j][t / 2] >> 16 : nw[j][t / 2] & 0xffffu);
+      }
+    }
+  }
+}
+
 // Fused RMSNorm -> 16-bit -> MXFP8 over rows of `width` (<= 4096) columns.
 int rms_mxfp8_launch(const void* x, int dtype, long ldx, int rows, int width, const float* gamma, float eps,
                      int bound_f16, uint8_t* q, uint8_t* scales, unsigned* status, unsigned layer,
@@ -844,9 +880,9 @@ int quantize_rows_launch(const void* x, int dtype, long ldx, int rows, int width
 
 int rms16_rows_launch(const void* x, int dtype, long ldx, int rows, int width, const float* gamma, float eps,
                       int bound_f16, uint16_t* out, long ldo, unsigned* status, unsigned layer, cudaStream_t s) {
-  if ((dtype != kInF16 && dtype != kInBF16) || width <= 0 || width > 4096 || ldx < width || ldo < width ||
-      gamma == nullptr || !(eps > 0.0f)) {
-    set_error("RMS to 16-bit rows: 16-bit input, width <= 4096, strides >= width, gamma, eps > 0");
+  if ((dtype != kInF16 && dtype != kInBF16 && dtype != kInF32) || width <= 0 || width > 4096 || ldx < width ||
+      ldo < width || gamma == nullptr || !(eps > 0.0f)) {
+    set_error("RMS to 16-bit rows: fp32 or 16-bit input, width <= 4096, strides >= width, gamma, eps > 0");
     return KB_E_INVALID;
   }
   int dev = 0;
@@ -855,6 +891,16 @@ int rms16_rows_launch(const void* x, int dtype, long ldx, int rows, int width, c
   const int grid = want < cap ? want : cap;
   const uint16_t* xs = static_cast<const uint16_t*>(x);
   const int need = (width + 255) / 256;
+  if (dtype == kInF32) {
+#define KB_R32(GG)                                                                                            \
+  if (need <= GG) {                                                                                           \
+    rms_rows32_out16_kernel<GG><<<grid, 256, 0, s>>>(static_cast<const float*>(x), ldx, gamma, eps, rows, width, \
+                                                     bound_f16, out, ldo, status, layer);                       \
+    return check_cuda(cudaGetLastError(), "rms fp32 to 16-bit launch");                                       \
+  }
+    KB_R32(1) KB_R32(2) KB_R32(4) KB_R32(8) KB_R32(16)
+#undef KB_R32
+  }
 #define KB_R16(GG)                                                                                          \
   if (need <= GG) {                                                                                         \
     if (dtype == kInF16)                                                                                    \

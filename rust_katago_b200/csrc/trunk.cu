@@ -52,7 +52,8 @@ __device__ __forceinline__ int sym_source(int sym, int r, int c) {
 // 16-byte store; the tap index (ic, ky, kx) advances incrementally.
 constexpr int kStemGroups = kStemK / 8;  // 28
 __global__ void stem_gather_kernel(const float* __restrict__ spatial, const float* __restrict__ global,
-                                   const int* __restrict__ sym, uint16_t* __restrict__ a, int batch, int nhwc) {
+                                   const int* __restrict__ sym, uint16_t* __restrict__ a, int batch, int nhwc,
+                                   int f16) {
   const long total = static_cast<long>(batch) * kSeq * kStemGroups;
   for (long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += static_cast<long>(gridDim.x) * blockDim.x) {
@@ -85,10 +86,7 @@ __global__ void stem_gather_kernel(const float* __restrict__ spatial, const floa
     }
     uint32_t w[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
-      w[q] = *reinterpret_cast<const uint32_t*>(&p);
-    }
+    for (int q = 0; q < 4; ++q) w[q] = pack16x2(make_float2(v[2 * q], v[2 * q + 1]), f16 != 0);
     reinterpret_cast<uint4*>(a)[idx] = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
@@ -135,6 +133,37 @@ __global__ void trunk_tip_kernel(const uint16_t* __restrict__ x, const float* __
     g4[i + stride] = tip8(r1, gamma, beta, static_cast<int>((i + stride) % c8) * 8);
   }
   if (i < total8) g4[i] = tip8(__ldg(x4 + i), gamma, beta, static_cast<int>(i % c8) * 8);
+}
+
+// The nested trunk's gates (BN affine folded to scale/bias, then SiLU):
+// out16 = T16(silu(x * scale + bias)) from fp32 rows x [rows, w] (row stride
+// ldx), into 16-bit rows (stride ldo), w a multiple of 8.  The affine is two
+// rounded operations and the SiLU kb_silu, so the CPU oracle reproduces every
+// value; 8 columns per thread (two 16-byte loads, one 16-byte store).
+__global__ void gate_silu_kernel(const float* __restrict__ x, long ldx, const float* __restrict__ scale,
+                                 const float* __restrict__ bias, uint16_t* __restrict__ out, long ldo, long rows,
+                                 int w8, int f16) {
+  const long total = rows * w8;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long r = i / w8;
+    const int c = static_cast<int>(i - r * w8) * 8;
+    const float4* src = reinterpret_cast<const float4*>(x + r * ldx + c);
+    const float4 a = __ldg(src), b = __ldg(src + 1);
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + c)), s1 = __ldg(reinterpret_cast<const float4*>(scale + c) + 1);
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + c)), b1 = __ldg(reinterpret_cast<const float4*>(bias + c) + 1);
+    const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float v0 = kb_silu(__fadd_rn(__fmul_rn(xv[2 * q], sv[2 * q]), bv[2 * q]));
+      const float v1 = kb_silu(__fadd_rn(__fmul_rn(xv[2 * q + 1], sv[2 * q + 1]), bv[2 * q + 1]));
+      o[q] = pack16x2(make_float2(v0, v1), f16 != 0);
+    }
+    *reinterpret_cast<uint4*>(out + r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 struct HeadWeights {
@@ -361,7 +390,7 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
 }  // namespace
 
 int stem_gather_launch(const float* spatial, const float* global, const int* sym, uint16_t* a, int batch,
-                       int nhwc, cudaStream_t s) {
+                       int nhwc, cudaStream_t s, int f16) {
   if (reinterpret_cast<uintptr_t>(a) & 15) {
     set_error("stem gather: the operand must be 16-byte aligned");
     return KB_E_INVALID;
@@ -371,7 +400,7 @@ int stem_gather_launch(const float* spatial, const float* global, const int* sym
   cudaGetDevice(&dev);
   const long want = (total + 255) / 256, cap = 16L * num_sms(dev);
   stem_gather_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(spatial, global, sym, a, batch,
-                                                                                     nhwc);
+                                                                                     nhwc, f16);
   return check_cuda(cudaGetLastError(), "stem gather launch");
 }
 
@@ -388,6 +417,23 @@ int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, u
   const long want = (total8 + 255) / 256, cap = 8L * num_sms(dev);
   trunk_tip_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(x, gamma, beta, g, total8, c / 8);
   return check_cuda(cudaGetLastError(), "trunk tip launch");
+}
+
+int gate_silu_launch(const float* x, long ldx, const float* scale, const float* bias, uint16_t* out, long ldo,
+                     long rows, int w, int f16, cudaStream_t s) {
+  if (w % 8 != 0 || ldx % 4 != 0 || ldo % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(scale) & 15) ||
+      (reinterpret_cast<uintptr_t>(bias) & 15)) {
+    set_error("gate: width a multiple of 8, 16-byte aligned rows and vectors");
+    return KB_E_INVALID;
+  }
+  const long total = rows * (w / 8);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long want = (total + 255) / 256, cap = 8L * num_sms(dev);
+  gate_silu_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(x, ldx, scale, bias, out, ldo, rows,
+                                                                                   w / 8, f16);
+  return check_cuda(cudaGetLastError(), "gate launch");
 }
 
 int heads_launch(const float* hp, const float* const* wts, float* policy, float* value, float* misc,

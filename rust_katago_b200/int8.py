@@ -174,3 +174,9 @@ def rms_quantize(x, dtype, rows, width, stride, gamma, eps, boundary_dtype, kp, 
 def bf16_linear(a, w, bias, m, n, k, epilogue, out, ldo, act=0, out_dtype=_capi.DT_BF16, stream=None):
     call("kb_bf16_linear", _ptr(a), _ptr(w), _ptr(bias), m, n, k, epilogue, act, out_dtype, _ptr(out), ldo,
          _stream(stream))
+
+
+def f16_linear(a, w, bias, m, n, k, epilogue, out, ldo, act=0, out_dtype=_capi.DT_F16, stream=None):
+    """kb_f16_linear: binary16 operands, fp32 accumulation, the same epilogues."""
+    call("kb_f16_linear", _ptr(a), _ptr(w), _ptr(bias), m, n, k, epilogue, act, out_dtype, _ptr(out), ldo,
+         _stream(stream))
