@@ -80,6 +80,7 @@ def lib() -> ctypes.CDLL:
             "or_attention_tc": (None, [P, I, I, I, I, F, I, P]),
             "or_tc_gemm16": (None, [P, P, I, I, I, I, P]),
             "or_rope_tables": (None, [P, I, I, P, P]),
+            "or_tc_gemm_mxf8": (None, [P, P, P, P, I, I, I, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -221,6 +222,20 @@ def tc_gemm16(a_bits: np.ndarray, w_bits: np.ndarray, f16: bool = False) -> np.n
     assert w_bits.shape[1] == k
     out = np.empty((m, n), np.float32)
     lib().or_tc_gemm16(_p(a_bits), _p(w_bits), m, n, k, 1 if f16 else 0, _p(out))
+    return out
+
+
+def tc_gemm_mxf8(a, w) -> np.ndarray:
+    """fp32 [m, n] accumulator of the block-scaled tensor-core GEMM of two
+    MXFP8 operands (oracle.mxfp8.Packed: E4M3 codes and unpacked UE8M0 scales),
+    with the tensor cores' accumulation (kb_oracle.c or_tc_gemm_mxf8)."""
+    assert a.kp == w.kp
+    ac = np.ascontiguousarray(a.values, np.uint8)
+    wc = np.ascontiguousarray(w.values, np.uint8)
+    asc = np.ascontiguousarray(a.logical_scales, np.uint8)
+    wsc = np.ascontiguousarray(w.logical_scales, np.uint8)
+    out = np.empty((a.rows, w.rows), np.float32)
+    lib().or_tc_gemm_mxf8(_p(ac), _p(asc), _p(wc), _p(wsc), a.rows, w.rows, a.kp, _p(out))
     return out
 
 

@@ -8,9 +8,9 @@ restatements of the reference's W8A8 arithmetic) and the same 16-bit rounding
 points as the product: bf16 residual stream, bf16 QKV / attention output /
 FFN hidden, bf16-rounded stem and head weights.
 
-The 16-bit tensor-core GEMMs (stem, head linears, bf16 projections) and the
-attention kernel's q.k and P.V products follow the tensor cores' own fp32
-accumulation (kb_oracle.c tc_block16: blocks of 16 products aligned to the
+The 16-bit and MXFP8 tensor-core GEMMs (stem, head linears, bf16 and
+block-scaled projections) and the attention kernel's q.k and P.V products
+follow the tensor cores' own fp32 accumulation (kb_oracle.c tc_block16: blocks of 16 products aligned to the
 largest exponent, truncated, rounded toward zero), and the attention softmax
 the kernel's definition (two key halves with their own maxima, P rounded to
 bf16 for P.V, the kernel's polynomial 2^x; kb_oracle.c or_attention_tc), so
@@ -162,23 +162,21 @@ def attention(qkv, cs, sn, n, nh, hd, rotate=True, exact=False, scale=None, f16=
 
 
 def _mx_weight(w):
-    """Decoded float64 [n, k] of an MXFP8 weight quantised from the original fp32."""
+    """An MXFP8 weight (E4M3 codes + UE8M0 scales) quantised from the original fp32."""
     from . import mxfp8 as mx
 
     n, k = w.shape
-    return mx.quantize(w, n, k, k, check_weight=True).decoded()
+    return mx.quantize(w, n, k, k, check_weight=True)
 
 
-def _mx_linear(xv, wdec):
+def _mx_linear(xv, wq):
     """fp32 accumulator of an MXFP8 projection: the activation's 16-bit values
-    quantised block-32 (mxfp8.cu:36-79), the product of decoded operands summed
-    exactly in float64, rounded once to fp32 (the tensor core accumulates in
-    fp32 in an order not reproduced here)."""
-    from . import mxfp8 as mx
+    quantised block-32 (mxfp8.cu:36-79), then the block-scaled GEMM with the
+    tensor cores' accumulation (kb_oracle.c or_tc_gemm_mxf8)."""
+    from . import mxfp8 as mx, tc_gemm_mxf8
 
     rows, k = xv.shape
-    xdec = mx.quantize(np.ascontiguousarray(xv, np.float32), rows, k, k).decoded()
-    return (xdec @ wdec.T).astype(np.float32)
+    return tc_gemm_mxf8(mx.quantize(np.ascontiguousarray(xv, np.float32), rows, k, k), wq)
 
 
 def _project(kind, src, wmat, bias=None, gamma=None):

@@ -198,6 +198,16 @@ def gemm_case(kb, rows, n, k, mode, exact, seed):
     bits = _bits(out, 0 if mode == m.OUT_HALF else 1, rows * n)
     mx.check_output(bits, mode == m.OUT_HALF, k, exact_v, sum_abs, exact)
     check_weight(w, w_ref)
+    # bit for bit against the tensor cores' block-scaled accumulation as the
+    # oracle restates it (kb_oracle.c or_tc_gemm_mxf8)
+    import oracle
+
+    acc = oracle.tc_gemm_mxf8(x_ref, w_ref).ravel()
+    if mode == m.OUT_HALF:
+        assert np.array_equal(bits, mx.half_encode(acc)), "half output differs from the accumulation model"
+    else:
+        want = acc if residual is None else (residual + acc).astype(np.float32)
+        assert np.array_equal(bits.view(np.uint32), want.view(np.uint32)), "fp32 output differs from the model"
     return bits
 
 

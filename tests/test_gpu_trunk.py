@@ -109,51 +109,62 @@ def check_outputs(got, ref, tol_policy=1e-2, tol_own=2e-2, tol_pooled=1e-2):
     return errs, top1
 
 
-# north_star's bound: <= 1e-2 relative L2 on the policy logits (ownership 2e-2).
-@pytest.mark.parametrize("topo,tol_policy,tol_own", [(SMALL, 1e-2, 2e-2), (SMALL32, 1e-2, 2e-2)],
-                         ids=["c256h64", "c384h32"])
-def test_small_trunk_matches_oracle(cuda, oracle, topo, tol_policy, tol_own):
+def trace_forward(torch, topo, blob, spatial, glob, precision="int8"):
+    """GPU forward with the trace (stem, attention per block, final residual)
+    and the oracle's free-running forward on the same inputs."""
+    n = spatial.shape[0]
+    model = backend.CudaBackend.load_model(topo, blob)
+    h = backend.CudaBackend.create_compute_handle(model, n)
+    dsp, dgl = torch.from_numpy(spatial).cuda(), torch.from_numpy(glob).cuda()
+    dout = torch.zeros(n * backend.OUT_PER_POS, device="cuda")
+    trace = torch.zeros((topo.num_blocks + 2, n * 361, topo.trunk_channels), dtype=torch.bfloat16, device="cuda")
+    h.forward_trace(n, dsp, dgl, dout, trace)
+    torch.cuda.synchronize()
+    ref = otrunk.forward(blob, (topo.trunk_channels, topo.num_blocks, topo.num_heads, topo.head_dim,
+                                topo.ffn_channels), spatial, glob, precision=precision)
+    return trace.float().cpu().numpy(), backend.unpack_outputs(dout.cpu().numpy(), n), ref, h
+
+
+def assert_free_running_bit_exact(tr, got, ref):
+    """The final residual stream equal bit for bit; the heads (fp32 on the GPU
+    after the trunk tip's fast SiLU, float64 in the oracle) within 1e-4
+    relative L2, far inside north_star's bounds."""
+    same = float(np.mean(tr[-1] == ref["residual"]))
+    assert same == 1.0, f"final residual: {same:.6f} identical"
+    errs, top1 = check_outputs(got, ref, tol_policy=1e-4, tol_own=1e-4, tol_pooled=1e-4)
+    assert top1 == 1.0
+
+
+# north_star's bound is <= 1e-2 relative L2 on the policy logits; the oracle
+# restates every step, so the trunk is compared bit for bit.
+@pytest.mark.parametrize("topo", [SMALL, SMALL32], ids=["c256h64", "c384h32"])
+def test_small_trunk_matches_oracle(cuda, oracle, topo):
     blob = synthetic.make_blob(topo, 5)
     spatial, glob = synthetic.make_positions(3, 7)
-    got, _, _ = run_trunk(topo, blob, spatial, glob)
-    ref = otrunk.forward(blob, (topo.trunk_channels, topo.num_blocks, topo.num_heads, topo.head_dim,
-                                topo.ffn_channels), spatial, glob)
-    check_outputs(got, ref, tol_policy, tol_own)
+    tr, got, ref, _ = trace_forward(cuda, topo, blob, spatial, glob)
+    assert_free_running_bit_exact(tr, got, ref)
 
 
 def test_b11c768_trunk_matches_oracle(cuda, oracle):
-    """Free-running b11c768 forward (BASELINE config 3's model) vs the oracle.
+    """Free-running b11c768 forward (BASELINE config 3's model), bit for bit.
 
-    Eleven blocks of INT8 requantisation make this trunk's outputs sensitive to
-    any last-bit difference upstream: flipping the last bit of 0.01% of the
-    oracle's own stem outputs (about 100 of 1.1 million values) moves its policy
-    by ~2.7e-2 and its ownership by ~6e-2 relative L2, the INT8 rounding noise
-    level, once the roundings downstream decorrelate.  The GPU and the oracle
-    differ only in such bits (the tensor cores' fp32 summation order in the stem
-    and attention; every INT8 step is bit-exact under teacher forcing, below).
-    So the free-running bound is the oracle's own spread under that minimal
-    perturbation (x1.25), or north_star's 1e-2 / 2e-2 where the spread is
-    smaller; pooled heads stay within 1e-2 and the best move of every position
-    agrees."""
+    This bar is the meaningful one: eleven blocks of INT8 requantisation make
+    the trunk's outputs sensitive to any last-bit difference upstream
+    (flipping the last bit of 0.01% of the stem outputs moves the policy by
+    ~2.7e-2 relative L2), so anything short of reproducing every rounding
+    would land at that level."""
     topo = synthetic.B11C768
-    t = (768, 11, 12, 64, 3072)
     blob = synthetic.make_blob(topo, 1234)
     spatial, glob = synthetic.make_positions(4, 11)
-    got, _, _ = run_trunk(topo, blob, spatial, glob)
-    ref = otrunk.forward(blob, t, spatial, glob)
-    moved = otrunk.perturbed_stem_forward(blob, t, spatial, glob, fraction=1e-4, seed=1)
-    spread = {k: rel_l2(moved[k], ref[k]) for k in ("policy", "ownership")}
-    print("oracle's own spread under a one-ulp perturbation of 0.01% of the stem:",
-          {k: round(v, 5) for k, v in spread.items()})
-    _, top1 = check_outputs(got, ref, tol_policy=max(1e-2, 1.25 * spread["policy"]),
-                            tol_own=max(2e-2, 1.25 * spread["ownership"]))
-    assert top1 == 1.0
+    tr, got, ref, _ = trace_forward(cuda, topo, blob, spatial, glob)
+    assert_free_running_bit_exact(tr, got, ref)
 
 
 @pytest.mark.parametrize("topo,n", [(SMALL32, 3), (synthetic.B11C768, 2)], ids=["c384h32", "b11c768"])
 def test_trunk_teacher_forced_bit_exact(cuda, oracle, topo, n):
     """With the GPU's stem output and per-block attention outputs fed to the
-    oracle (the two steps with unreproducible fp32 accumulation order), every
+    oracle (the steps whose fp32 accumulation the oracle restates from the
+    tensor cores' measured behaviour), every
     other step — RMSNorm quantisers, INT8 GEMMs, dequant, GELU, requantisers,
     residual adds — matches bit for bit: the final residual stream is identical,
     and the heads (fp32 accumulation again) agree to 1e-4."""
