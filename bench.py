@@ -532,6 +532,26 @@ def trunk_sub_records(wl, torch, flush, steps, world, rank, max_over_ranks, barr
                   "two_in_flight: 30 batches with both pipeline slots in use")
     out["latency"] = lat
     del hl
+
+    # The reference's own TF3 b11c768 topology (nested bottleneck, 11 x 3
+    # attention / SwiGLU pairs at width 384, 12 x 32 heads), same batch, both
+    # its INT8 recipes: every projection INT8, and the default FFN scope
+    # (attention projections binary16).
+    tf3 = {}
+    sp, gl = synthetic.make_positions(wl.batch, 77 + rank)
+    d_sp, d_gl = torch.from_numpy(sp).cuda(), torch.from_numpy(gl).cuda()
+    d_out = torch.zeros(wl.batch * backend.OUT_PER_POS, device="cuda")
+    for label, topo in (("int8", synthetic.TF3_B11C768), ("ffn_scope", synthetic.TF3_B11C768_FFN)):
+        model = backend.CudaBackend.load_model(topo, synthetic.make_blob(topo, 1234), torch.cuda.current_device())
+        ht = backend.CudaBackend.create_compute_handle(model, wl.batch)
+        ht.warmup([wl.batch])
+        kt = max(3, min(steps, 10))
+        ms = max_over_ranks(sum(handle_forward_ms(torch, ht, wl.batch, d_sp, d_gl, d_out, flush, kt)))
+        tf3[label] = {"ms_per_step": ms / kt, "value": wl.batch * world * kt / (ms / 1e3), "unit": "positions/s"}
+        del ht, model
+    tf3["workload"] = ("the reference's TF3 b11c768 (nested: C 768, mid 384, 11 x 3 pairs, 12 x 32 heads, SwiGLU "
+                       f"1152), batch {wl.batch} per GPU, device time per graph-launched forward")
+    out["tf3_b11c768"] = tf3
     return out
 
 

@@ -429,6 +429,7 @@ KB_API int kb_model_load(const kb_model_desc* desc, const float* blob, size_t co
                          kb_model** out);
 KB_API void kb_model_destroy(kb_model* model);
 
+
 /* A compute handle: one stream, a workspace for max_batch positions, two
  * pipeline slots with pinned staging.  Not thread-safe: one thread per handle.
  * Replaces: CudaBackend::create_compute_handle (src/backends/cuda.rs:2926). */
@@ -532,6 +533,31 @@ KB_API int kb_decode_device(int n, const float* d_raw, const kb_row_params* d_ro
 /* Post-processing parameters that kb_submit_rows applies (default: the
  * reference defaults with model version 17). */
 KB_API int kb_set_postprocess(kb_handle* handle, const kb_postprocess_params* pp);
+
+/* ---- Model files ------------------------------------------------------- */
+
+/* Parse a native KataGo model file of the reference's TF3 family (.bin.gz,
+ * .bin, .txt.gz or .txt: text tokens with "@BIN@" little-endian fp32 weight
+ * arrays) into the nested topology's descriptor and weight blob: model
+ * version 17, nested bottleneck blocks of attention (12 x 32 heads at mid
+ * 384 in the shipped b11c768) / SwiGLU FFN pairs, SiLU, standard trunk-tip
+ * BN, unit BN scales in the heads; anything else fails with the reason.  BN
+ * layers are folded to scale / bias in fp32, matrices transposed to
+ * out-first, head channels remapped as the reference lowers them.  blob may
+ * be NULL (size query: *count receives the float count); the descriptor's
+ * precision fields are INT8.  pp (nullable) receives the file's
+ * post-processing multipliers and model version.
+ * Replaces: model_parser.rs load_model_file / parse_model (:1002-1160) and
+ * native_model.rs lower_model (:21-165). */
+KB_API int kb_model_file_parse(const char* path, kb_model_desc* desc, float* blob, size_t capacity, size_t* count,
+                               kb_postprocess_params* pp);
+
+/* kb_model_file_parse then kb_model_load on `device`; the precision fields
+ * (precision, proj_precision, int8_min_ffn_width) come from `recipe`
+ * (NULL = every projection INT8).
+ * Replaces: Backend::load_model_file (backend.rs:206-410, cuda.rs:2618-2680). */
+KB_API int kb_model_load_file(const char* path, const kb_model_desc* recipe, int device, kb_model** out,
+                              kb_postprocess_params* pp);
 
 /* kb_submit with per-row decoding: each row is evaluated under rows[i].symmetry,
  * then decoded on the device as kb_decode_device does (legal NULL: decode only;

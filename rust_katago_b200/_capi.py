@@ -58,6 +58,8 @@ SIGNATURES: dict[str, tuple] = {
     "kb_model_blob_floats": (I, [P, ctypes.POINTER(ctypes.c_size_t)]),
     "kb_model_load": (I, [P, P, ctypes.c_size_t, I, PP]),
     "kb_model_destroy": (None, [P]),
+    "kb_model_file_parse": (I, [ctypes.c_char_p, P, P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), P]),
+    "kb_model_load_file": (I, [ctypes.c_char_p, P, I, PP, P]),
     "kb_handle_create": (I, [P, I, I, PP]),
     "kb_handle_destroy": (None, [P]),
     "kb_handle_stream": (I, [P, ctypes.POINTER(ctypes.c_size_t)]),

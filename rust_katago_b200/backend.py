@@ -6,7 +6,8 @@ implemented by `CudaBackend` (src/backends/cuda.rs:2610-3105), maps to:
 ===========================================  ===========================================
 reference                                    here (C ABI underneath)
 ===========================================  ===========================================
-``load_model_file`` (cuda.rs:2618)           :meth:`CudaBackend.load_model`
+``load_model_file`` (cuda.rs:2618)           :meth:`CudaBackend.load_model_file` (a native TF3
+                                             file), :meth:`CudaBackend.load_model` (a blob)
 ``create_compute_handle`` (cuda.rs:2926)     :meth:`CudaBackend.create_compute_handle`
 ``warmup_batches``                           :meth:`ComputeHandle.warmup`
 ``submit_output`` (cuda.rs:2196)             :meth:`ComputeHandle.submit_output`
@@ -120,6 +121,30 @@ def unpack_outputs(flat: np.ndarray, n: int) -> NNOutputs:
 
 
 class Model:
+    @classmethod
+    def from_file(cls, path: str, recipe: Topology | None = None, device: int = 0) -> "Model":
+        """kb_model_load_file: a native model file of the reference's TF3 family;
+        the precision fields come from `recipe` (None = every projection INT8).
+        The parsed shape is in .topology, the file's post-processing
+        parameters in .postprocess."""
+        self = cls.__new__(cls)
+        desc = _capi.ModelDesc()
+        count = ctypes.c_size_t()
+        call("kb_model_file_parse", str(path).encode(), ctypes.byref(desc), None, 0, ctypes.byref(count), None)
+        self.topology = Topology(desc.trunk_channels, desc.num_blocks, desc.num_heads, desc.head_dim,
+                                 desc.ffn_channels, recipe.precision if recipe else 0,
+                                 tuple(recipe.proj_precision) if recipe else (0, 0, 0, 0),
+                                 recipe.int8_min_ffn_width if recipe else 0, desc.topology, desc.mid_channels,
+                                 desc.pairs_per_block, float(desc.norm_eps))
+        self.device = device
+        self.postprocess = _capi.PostProcessParams()
+        h = ctypes.c_void_p()
+        rdesc = recipe.desc() if recipe else None
+        call("kb_model_load_file", str(path).encode(), ctypes.byref(rdesc) if rdesc else None, device,
+             ctypes.byref(h), ctypes.byref(self.postprocess))
+        self._h = h
+        return self
+
     def __init__(self, topology: Topology, blob: np.ndarray, device: int = 0):
         blob = np.ascontiguousarray(blob, dtype=np.float32)
         self.topology = topology
@@ -269,6 +294,11 @@ class CudaBackend:
     @staticmethod
     def load_model(topology: Topology, blob: np.ndarray, device: int = 0) -> Model:
         return Model(topology, blob, device)
+
+    @staticmethod
+    def load_model_file(path: str, recipe: Topology | None = None, device: int = 0) -> Model:
+        """Backend::load_model_file (backend.rs:206-410) for the TF3 family."""
+        return Model.from_file(path, recipe, device)
 
     @staticmethod
     def create_compute_handle(model: Model, max_batch: int, inputs_nhwc: bool = False) -> ComputeHandle:

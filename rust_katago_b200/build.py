@@ -33,6 +33,10 @@ NVCC_FLAGS = [
     "-fvisibility=hidden",
     "-Xptxas",
     "-warn-spills",
+    # host code rounds every multiply and add on its own (the model-file
+    # loader folds batch norms with the reference's f32 arithmetic)
+    "-Xcompiler",
+    "-ffp-contract=off",
 ]
 
 
@@ -69,7 +73,7 @@ def build(verbose: bool = False) -> Path:
         objs = list(ex.map(lambda s: _compile(s, verbose), sources))
     if LIB.exists() and LIB.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
         return LIB
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart_static", "-lrt", "-ldl", "-lpthread"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart_static", "-lz", "-lrt", "-ldl", "-lpthread"]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)
