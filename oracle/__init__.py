@@ -64,7 +64,7 @@ def lib() -> ctypes.CDLL:
             "or_bf16_decode": (F, [ctypes.c_uint16]),
             "or_encode16": (None, [P, Z, I, P]),
             "or_decode16": (None, [P, Z, I, P]),
-            "or_expf": (F, [F]),
+            "or_silu_exp": (F, [F]),
             "or_silu": (F, [F]),
             "or_gelu": (F, [F]),
             "or_act": (None, [P, Z, I, P]),

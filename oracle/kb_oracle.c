@@ -101,21 +101,18 @@ void or_decode16(const uint16_t* x, size_t n, int f16, float* out) {
 
 /* ------------------------------------------------------------------ elementwise math */
 
-static float pow2i(int k) {
-  uint32_t bits = (uint32_t)(k + 127) << 23;
-  float f;
-  memcpy(&f, &bits, 4);
-  return f;
-}
-
-/* exp(x) by Cody-Waite reduction with the Cephes ln2 split and the degree-7
- * Taylor polynomial; the same operation sequence as the GPU kernels. */
-float or_expf(float x) {
-  if (x != x) return x;
-  if (x > 0x1.62e42ep+6f) return INFINITY;
-  if (x < -0x1.9fe36ap+6f) return 0.0f;
-  const float n = rintf(x * 0x1.715476p+0f);
-  float r = fmaf(-n, 0x1.63p-1f, x);
+/* e^x for the SiLU denominator 1 + e^x (x = -g), the same operation sequence
+ * as silu_exp in the kernels (rust_katago_b200/csrc/kb_numeric.cuh): x clamped
+ * to [-20, 89] (which leaves 1 + e^x unchanged: below -17.4 it rounds to 1,
+ * above ln(FLT_MAX) the arithmetic overflows as the true value does);
+ * n = x*log2(e) rounded to the nearest integer by one fused multiply-add with
+ * the shifter 1.5 * 2^23; Cody-Waite reduction with the Cephes ln2 split; the
+ * degree-7 Taylor polynomial; the scaling (p * 2^(n-1)) * 2. */
+float or_silu_exp(float x) {
+  const float xc = fminf(fmaxf(x, -20.0f), 89.0f);
+  const float k = fmaf(xc, 0x1.715476p+0f, 0x1.8p+23f);
+  const float n = k - 0x1.8p+23f;
+  float r = fmaf(-n, 0x1.63p-1f, xc);
   r = fmaf(n, 0x1.bd0106p-13f, r);
   float p = 0x1.a01a02p-13f;
   p = fmaf(p, r, 0x1.6c16c2p-10f);
@@ -125,14 +122,14 @@ float or_expf(float x) {
   p = fmaf(p, r, 0.5f);
   p = fmaf(p, r, 1.0f);
   p = fmaf(p, r, 1.0f);
-  const int ni = (int)n;
-  const int n1 = ni / 2;
-  const int n2 = ni - n1;
-  return (p * pow2i(n1)) * pow2i(n2);
+  const uint32_t bits = ((uint32_t)((int)n + 126)) << 23; /* 2^(n-1) */
+  float s;
+  memcpy(&s, &bits, 4);
+  return (p * s) * 2.0f;
 }
 
 /* g / (1 + e^-g): the SiLU inside the reference's SwiGLU (int8_ops.cu:111-113). */
-float or_silu(float g) { return g / (1.0f + or_expf(-g)); }
+float or_silu(float g) { return g / (1.0f + or_silu_exp(-g)); }
 
 /* GELU(x) = x * Phi(x): s = min(RN(x*x)*0.125 - 1 (fused), 1), P = the degree-10
  * polynomial of rust_katago_b200/gelu_fit.py in s (Horner, fused),

@@ -37,13 +37,16 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle row of K per stage
 // Epilogue warps: 16 (four per TMEM lane quarter) for the arithmetic-heavy
-// 16-bit epilogues (bias + activation, rotary) and for the residual add of
-// short-K projections, where draining the epilogue bounds the tile; 8 for the
-// others (long-K residual adds keep the deeper operand ring; fp32 / int32
-// outputs).
+// 16-bit epilogues (bias + activation, rotary, SwiGLU) and for the residual
+// adds of short-K projections, where draining the epilogue bounds the tile; 8
+// for the others (long-K residual adds keep the deeper operand ring; plain
+// fp32 / int32 outputs).
 template <int EPI, int DEEP>
 constexpr int epi_warps() {
-  return (EPI == 3 /* kEpi16 */ || EPI == 7 /* kEpiRope16 */ || (EPI == 4 /* kEpiRes16 */ && DEEP)) ? 16 : 8;
+  return (EPI == 3 /* kEpi16 */ || EPI == 7 /* kEpiRope16 */ || EPI == 5 /* kEpiSwiGLU16 */ ||
+          ((EPI == 4 /* kEpiRes16 */ || EPI == 2 /* kEpiResF32 */) && DEEP))
+             ? 16
+             : 8;
 }
 constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
 constexpr int kStageTile = 32 * 64;  // one 32x32 16-bit staging tile (2 KiB)
@@ -318,7 +321,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* res_bar = tempty + 3;  // [epilogue warp][SB]: residual tiles landed (Res16 through TMA)
+  uint64_t* res_bar = tempty + 3;  // [epilogue warp][SB]: residual tiles landed (residuals through TMA)
   static_assert((2 * kStages + 5 + kEpiWarps * SB) * 8 <= 512, "barrier area exceeded");
 
   const int warp = threadIdx.x >> 5;
@@ -338,7 +341,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], kEpiWarps);
     }
-    if constexpr (EPI == kEpiRes16)
+    if constexpr (EPI == kEpiRes16 || EPI == kEpiResF32 || EPI == kEpiF32)
       for (int i = 0; i < kEpiWarps * SB; ++i) mbar_init(&res_bar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -484,23 +487,28 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     int acc = 0;
     uint32_t aph = 0;
     bool handled = false;
-    if constexpr (EPI == kEpiRes16) {
-      if (use_tma_out) {
+    if constexpr (EPI == kEpiRes16 || EPI == kEpiResF32 || EPI == kEpiF32) {
+      // (kEpiF32 takes this path only with a residual, which the host has
+      // checked is the output itself)
+      if (use_tma_out && (EPI != kEpiF32 || g.residual != nullptr)) {
         handled = true;
         // ---- residual through shared memory.  Each warp walks a stream of
-        // 32x32 chunks (its columns of each tile, tile after tile); the 16-bit
-        // residual of a chunk is TMA-loaded into a staging tile kLook chunks
-        // ahead (the stream runs across tiles, so the next tile's first
-        // residuals are in flight while this one finishes), the dequantised
-        // accumulator is added in place and the tile is TMA-stored back with
-        // the same tensor map (64-byte swizzle, out-of-range rows and columns
-        // read as zero and are clipped on the store).
+        // chunks of 32 rows x 64 bytes (32 16-bit or 16 fp32 columns; its
+        // columns of each tile, tile after tile); the residual of a chunk is
+        // TMA-loaded into a staging tile kLook chunks ahead (the stream runs
+        // across tiles, so the next tile's first residuals are in flight while
+        // this one finishes), the dequantised accumulator is added in place and
+        // the tile is TMA-stored back with the same tensor map (64-byte
+        // swizzle, out-of-range rows and columns read as zero and are clipped
+        // on the store).
+        constexpr bool kF32 = EPI != kEpiRes16;
+        constexpr int kCC = kF32 ? 16 : 32;  // columns per chunk
         constexpr int kLook = SB >= 4 ? 2 : 1;
         static_assert(SB - kLook - 1 >= 0, "residual staging needs SB > kLook");
-        constexpr int kChunksR = BN / 32 / kParts;
+        constexpr int kChunksR = BN / kCC / kParts;
         uint8_t* stage = staging + e * SB * kStageTile;
         uint64_t* rbar = res_bar + e * SB;
-        auto chunk_col = [&](int t, int jj) { return (t % tiles_n) * BN + (part * kChunksR + jj) * 32; };
+        auto chunk_col = [&](int t, int jj) { return (t % tiles_n) * BN + (part * kChunksR + jj) * kCC; };
         int ld_tile = blockIdx.x, ld_jj = 0, ld_n = 0;  // next chunk to load; loads issued
         auto issue_load = [&]() {  // lane 0
           while (ld_tile < num_tiles && chunk_col(ld_tile, ld_jj) >= g.n)
@@ -547,6 +555,47 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
             uint8_t* buf = stage + (sq % SB) * kStageTile;
             const int swz = (lane >> 1) & 3;
             uint32_t amax2 = 0;
+            if constexpr (kF32) {
+              // 16 fp32 columns: four 16-byte cells of four values.  The same
+              // arithmetic as the direct-store fp32 epilogues.
+              uint32_t v[16];
+              tmem_ldn<16>(taddr + j * kCC, v);
+              float sw[16], bias[16];
+              const bool add_bias = EPI == kEpiF32 && with_bias;  // warp-uniform
+              if (g.cols_vec) {  // warp-uniform
+                if constexpr (KIND == kGemmI8) load_vec_aligned<16>(g.col_scale + col0, sw);
+                if (add_bias) load_vec_aligned<16>(g.bias + col0, bias);
+              } else {
+                if constexpr (KIND == kGemmI8) load_vecn<16>(g.col_scale, col0, g.n, sw);
+                if (add_bias) load_vecn<16>(g.bias, col0, g.n, bias);
+              }
+              tmem_ld_wait();
+              if (!__all_sync(0xffffffffu, mbar_wait(&rbar[sq % SB], (sq / SB) & 1, abort_flag, wlim))) {
+                ok = false;
+                break;
+              }
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float4* cell = reinterpret_cast<float4*>(buf + lane * 64 + ((c ^ swz) << 4));
+                const float4 r4 = *cell;
+                const float r[4] = {r4.x, r4.y, r4.z, r4.w};
+                float y[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const int i = 4 * c + q;
+                  float x;
+                  if (EPI == kEpiResF32 || !add_bias)
+                    x = acc_value<KIND>(v[i], sa, KIND == kGemmI8 ? sw[i] : 1.0f);
+                  else if (KIND == kGemmI8)
+                    x = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[i])), sa), sw[i], bias[i]);
+                  else
+                    x = __fadd_rn(acc_value<KIND>(v[i], sa, 1.0f), bias[i]);
+                  y[q] = __fadd_rn(r[q], x);
+                  if constexpr (KIND == kGemmMXF8) nonfinite |= row_ok && col0 + i < g.n && !isfinite(y[q]);
+                }
+                *cell = make_float4(y[0], y[1], y[2], y[3]);
+              }
+            } else {
             // The chunk's 32 columns in kHalves pieces of kSub (16 with 16
             // epilogue warps: the register budget of a 576-thread CTA).
 #pragma unroll
@@ -585,6 +634,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
                 }
                 *cell = make_uint4(ow[0], ow[1], ow[2], ow[3]);
               }
+            }
             }
             if (!ok) break;
             if constexpr (KIND == kGemmMXF8)
@@ -650,26 +700,37 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
             uint32_t vg[kSub], vu[kSub];
             tmem_ldn<kSub>(taddr + j * 32 + hh * kSub, vg);
             tmem_ldn<kSub>(taddr + BN / 2 + j * 32 + hh * kSub, vu);
-            tmem_ld_wait();
             float swg[kSub], swu[kSub];
             if constexpr (KIND == kGemmI8) {
-              load_vecn<kSub>(g.col_scale, gcol0 + hh * kSub, g.n, swg);
-              load_vecn<kSub>(g.col_scale, gcol0 + BN / 2 + hh * kSub, g.n, swu);
+              if (g.cols_vec) {  // warp-uniform
+                load_vec_aligned<kSub>(g.col_scale + gcol0 + hh * kSub, swg);
+                load_vec_aligned<kSub>(g.col_scale + gcol0 + BN / 2 + hh * kSub, swu);
+              } else {
+                load_vecn<kSub>(g.col_scale, gcol0 + hh * kSub, g.n, swg);
+                load_vecn<kSub>(g.col_scale, gcol0 + BN / 2 + hh * kSub, g.n, swu);
+              }
             }
+            tmem_ld_wait();
+            // Pairs of columns: gate and up dequantised and rounded to binary16
+            // (the reference's fp16 boundary), SiLU of the gate, the product
+            // rounded to binary16.  The output is always binary16.
 #pragma unroll
             for (int i = 0; i < kSub / 2; ++i) {
-              uint32_t pair = 0;
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int c = 2 * i + h;
-                const float gv = from16(bits16(acc_value<KIND>(vg[c], sa, KIND == kGemmI8 ? swg[c] : 1.0f), f16), f16);
-                const float uv = from16(bits16(acc_value<KIND>(vu[c], sa, KIND == kGemmI8 ? swu[c] : 1.0f), f16), f16);
-                const uint16_t b = bits16(__fmul_rn(uv, kb_silu(gv)), f16);
-                if (hh * kSub + c < valid) amax = max(amax, abs_bits(from16(b, f16)));
-                pair |= static_cast<uint32_t>(b) << (16 * h);
-              }
-              hw[hh * (kSub / 2) + i] = pair;
+              const float2 gq = acc_pairn<KIND, kSub>(vg, i, sa, swg);
+              const float2 uq = acc_pairn<KIND, kSub>(vu, i, sa, swu);
+              const float2 gv = unpack16x2(pack16x2(gq, true), true);
+              const float2 uv = unpack16x2(pack16x2(uq, true), true);
+              hw[hh * (kSub / 2) + i] = pack16x2(mul2(uv, kb_silu2(gv)), true);
             }
+          }
+          if (g.row_amax != nullptr) {  // warp-uniform
+            uint32_t amax2 = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const uint32_t mask = 2 * i + 1 < valid ? 0x7fff7fffu : (2 * i < valid ? 0x00007fffu : 0u);
+              amax2 = __vmaxu2(amax2, hw[i] & mask);
+            }
+            amax = max(amax, amax16_to_f32bits(amax2, true));
           }
           emit16<SB>(o, g, hw, row, row0q, ocol0, lane, row_ok, valid);
         }
@@ -1120,6 +1181,10 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     set_error("rotary epilogue: needs fp32 tables, head_dim 32 or 64, rope_cols = 2 * heads * head_dim <= N");
     return KB_E_INVALID;
   }
+  if (epi == kEpiSwiGLU16 && !g.out_f16) {
+    set_error("SwiGLU epilogue: the output is binary16 (out_f16 = 1)");
+    return KB_E_INVALID;
+  }
   if (epi == kEpiRope16 && g.bias != nullptr) {
     set_error("rotary epilogue: the QKV projection takes no bias");
     return KB_E_INVALID;
@@ -1130,7 +1195,8 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
   }
   // MXFP8 keeps BN = 128: two 128-column accumulators plus the per-stage
   // scale-factor columns fill the 512 TMEM columns.
-  const int bn = kind == kGemmMXF8 ? 128 : bn_hint ? bn_hint : gemm_pick_bn(kind, epi, g.n);
+  // The SwiGLU tile is 128 gate + 128 up columns: BN = 256 always.
+  const int bn = kind == kGemmMXF8 ? 128 : epi == kEpiSwiGLU16 ? 256 : bn_hint ? bn_hint : gemm_pick_bn(kind, epi, g.n);
   CUtensorMap ma, mb, mo;
   memset(&mo, 0, sizeof(mo));
   int rc = make_operand_map(&ma, a, kind, g.m, g.k, kBM);
@@ -1153,10 +1219,13 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
     if (rc) return rc;
     tma_out = 1;
   }
-  // fp32 outputs (no residual) leave through the staging tiles too: 16
-  // fp32 columns are 64 bytes, the same box as 32 16-bit columns.
-  if (!direct_store && epi == kEpiF32 && g.residual == nullptr && (g.ldo * 4) % 16 == 0 &&
-      (reinterpret_cast<uintptr_t>(g.out) & 15) == 0) {
+  // fp32 outputs leave through the staging tiles too (16 fp32 columns are 64
+  // bytes, the same box as 32 16-bit columns), and an fp32 residual that is
+  // the output itself (kEpiResF32 always; kEpiF32 when residual == out) comes
+  // in through them.
+  const bool f32_in_place = epi == kEpiResF32 ||
+                            (epi == kEpiF32 && (g.residual == nullptr || (g.residual == g.out && g.ldr == g.ldo)));
+  if (!direct_store && f32_in_place && (g.ldo * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15) == 0) {
     rc = encode_2d(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.out, g.n, g.m, g.ldo * 4, 16, 32,
                    CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;

@@ -11,38 +11,6 @@
 
 namespace kb {
 
-// 2^k for -126 <= k <= 127, built from its exponent bits.
-__device__ __forceinline__ float pow2i(int k) { return __int_as_float((k + 127) << 23); }
-
-// exp(x): Cody-Waite range reduction x = n*ln2 + r with ln2 split as
-// 0.693359375 - 2.12194440e-4 (the two-constant split used by Cephes expf),
-// then the degree-7 Taylor polynomial sum r^i/i! on |r| <= ~0.35 in Horner
-// form with fused multiply-adds, then an exact two-step scaling by 2^n.
-// Truncation error of the polynomial is below 6e-9 relative.
-// Branch-free: the input is clamped into the finite range for the arithmetic
-// and the out-of-range results (inf, 0, NaN) are selected at the end.
-__device__ __forceinline__ float kb_expf(float x) {
-  const float xc = fminf(fmaxf(x, -0x1.9fe36ap+6f), 0x1.62e42ep+6f);
-  const float n = rintf(__fmul_rn(xc, 0x1.715476p+0f /* log2(e) */));
-  float r = __fmaf_rn(-n, 0x1.63p-1f /* 0.693359375 */, xc);
-  r = __fmaf_rn(n, 0x1.bd0106p-13f /* 2.12194440e-4 */, r);
-  float p = 0x1.a01a02p-13f /* 1/5040 */;
-  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f /* 1/720 */);
-  p = __fmaf_rn(p, r, 0x1.111112p-7f /* 1/120 */);
-  p = __fmaf_rn(p, r, 0x1.555556p-5f /* 1/24 */);
-  p = __fmaf_rn(p, r, 0x1.555556p-3f /* 1/6 */);
-  p = __fmaf_rn(p, r, 0.5f);
-  p = __fmaf_rn(p, r, 1.0f);
-  p = __fmaf_rn(p, r, 1.0f);
-  const int ni = static_cast<int>(n);
-  const int n1 = ni / 2;
-  const int n2 = ni - n1;
-  float y = __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(n2));
-  y = x > 0x1.62e42ep+6f ? __int_as_float(0x7f800000) : y;
-  y = x < -0x1.9fe36ap+6f ? 0.0f : y;
-  return x != x ? x : y;
-}
-
 // Round a pair to the 16-bit type (binary16 or bfloat16, round to nearest
 // even); element 0 in the low half.
 __device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
@@ -54,11 +22,6 @@ __device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// SiLU exactly as the reference writes it inside its SwiGLU: g / (1 + e^-g)
-// (cuda-kernels/int8_ops.cu:111-113), with kb_expf in place of expf.
-__device__ __forceinline__ float kb_silu(float g) {
-  return __fdiv_rn(g, __fadd_rn(1.0f, kb_expf(-g)));
-}
 
 // GELU(x) = x * Phi(x) with Phi the standard normal CDF:
 //   s   = min(x^2/8 - 1, 1)                      (rounded: RN(RN(x*x)*0.125 - 1))
@@ -121,6 +84,78 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return f2unpack(r);
 }
 
+// e^x for the SiLU denominator 1 + e^x (x = -g), without conversion or
+// transcendental instructions: Cody-Waite reduction x = n*ln2 + r with ln2
+// split as 0.693359375 - 2.12194440e-4 (the two-constant split of Cephes
+// expf), the degree-7 Taylor polynomial sum r^i/i! on |r| <= ~0.35 in Horner
+// form with fused multiply-adds (truncation below 6e-9 relative), and 2^n
+// applied as (p * 2^(n-1)) * 2.  n is the exact product x*log2(e) rounded to
+// the nearest integer (ties to even) by one fused multiply-add with the
+// shifter 1.5 * 2^23, whose result also holds n in its low mantissa bits.
+// x is clamped to [-20, 89], which leaves 1 + e^x unchanged: below -17.4,
+// e^x < 2^-25 and 1 + e^x rounds to 1 for the clamped value as for the true
+// one; above ln(FLT_MAX) = 88.7228 the true e^x overflows, and so does
+// (p * 2^127) * 2 for every float x in (88.7228, 89] (p > 1 there).  A NaN
+// g reaches the division unchanged.
+constexpr float kSiluLog2e = 0x1.715476p+0f;
+constexpr float kSiluShifter = 0x1.8p+23f;  // 1.5 * 2^23
+#define KB_SILU_EXP_POLY(FMA, P, R)                       \
+  P = FMA(P, R, C2(0x1.6c16c2p-10f)); /* 1/720 */        \
+  P = FMA(P, R, C2(0x1.111112p-7f));  /* 1/120 */        \
+  P = FMA(P, R, C2(0x1.555556p-5f));  /* 1/24 */         \
+  P = FMA(P, R, C2(0x1.555556p-3f));  /* 1/6 */          \
+  P = FMA(P, R, C2(0.5f));                               \
+  P = FMA(P, R, C2(1.0f));                               \
+  P = FMA(P, R, C2(1.0f));
+
+// 2^(n-1) from the shifter sum k = 1.5 * 2^23 + n (bits 0x4B400000 + n):
+// its bits shifted left by 23 are n << 23 (mod 2^32).
+__device__ __forceinline__ float silu_exp_scale(float k) {
+  return __int_as_float((__float_as_int(k) << 23) + (126 << 23));
+}
+
+__device__ __forceinline__ float silu_exp(float x) {
+#define C2(v) (v)
+  const float xc = fminf(fmaxf(x, -20.0f), 89.0f);
+  const float k = __fmaf_rn(xc, kSiluLog2e, kSiluShifter);
+  const float n = __fadd_rn(k, -kSiluShifter);
+  float r = __fmaf_rn(-n, 0x1.63p-1f /* 0.693359375 */, xc);
+  r = __fmaf_rn(n, 0x1.bd0106p-13f /* 2.12194440e-4 */, r);
+  float p = 0x1.a01a02p-13f /* 1/5040 */;
+  KB_SILU_EXP_POLY(__fmaf_rn, p, r)
+  return __fmul_rn(__fmul_rn(p, silu_exp_scale(k)), 2.0f);
+#undef C2
+}
+
+// silu_exp on a pair, bit-identical to two scalar calls.
+__device__ __forceinline__ float2 silu_exp2(float2 x) {
+#define C2(v) make_float2(v, v)
+  const float2 xc = make_float2(fminf(fmaxf(x.x, -20.0f), 89.0f), fminf(fmaxf(x.y, -20.0f), 89.0f));
+  const float2 k = fma2(xc, C2(kSiluLog2e), C2(kSiluShifter));
+  const float2 n = add2(k, C2(-kSiluShifter));
+  float2 r = fma2(n, C2(-0x1.63p-1f), xc);
+  r = fma2(n, C2(0x1.bd0106p-13f), r);
+  float2 p = C2(0x1.a01a02p-13f);
+  KB_SILU_EXP_POLY(fma2, p, r)
+  return mul2(mul2(p, make_float2(silu_exp_scale(k.x), silu_exp_scale(k.y))), C2(2.0f));
+#undef C2
+}
+#undef KB_SILU_EXP_POLY
+
+// SiLU exactly as the reference writes it inside its SwiGLU: g / (1 + e^-g)
+// (cuda-kernels/int8_ops.cu:111-113), with silu_exp in place of expf.
+__device__ __forceinline__ float kb_silu(float g) {
+  return __fdiv_rn(g, __fadd_rn(1.0f, silu_exp(-g)));
+}
+
+// kb_silu on a pair, bit-identical to two scalar calls.  (The one packed
+// multiply that feeds a packed add, e^x's final * 2, is exact, so contracting
+// the two into a fused multiply-add leaves every result unchanged.)
+__device__ __forceinline__ float2 kb_silu2(float2 g) {
+  const float2 d = add2(make_float2(1.0f, 1.0f), silu_exp2(make_float2(-g.x, -g.y)));
+  return make_float2(__fdiv_rn(g.x, d.x), __fdiv_rn(g.y, d.y));
+}
+
 // kb_gelu on a pair, bit-identical to two scalar calls.
 __device__ __forceinline__ float2 kb_gelu2(float2 x) {
   constexpr float c[11] = {KB_GELU_COEFFS};
@@ -139,7 +174,7 @@ enum Act : int { kActNone = 0, kActGelu = 1, kActSilu = 2 };
 template <int ACT>
 __device__ __forceinline__ float2 apply_act2(float2 v) {
   if constexpr (ACT == kActGelu) return kb_gelu2(v);
-  else if constexpr (ACT == kActSilu) return make_float2(kb_silu(v.x), kb_silu(v.y));
+  else if constexpr (ACT == kActSilu) return kb_silu2(v);
   else return v;
 }
 

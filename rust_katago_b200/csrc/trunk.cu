@@ -138,29 +138,32 @@ __global__ void trunk_tip_kernel(const uint16_t* __restrict__ x, const float* __
 // The nested trunk's gates (BN affine folded to scale/bias, then SiLU):
 // out16 = T16(silu(x * scale + bias)) from fp32 rows x [rows, w] (row stride
 // ldx), into 16-bit rows (stride ldo), w a multiple of 8.  The affine is two
-// rounded operations and the SiLU kb_silu, so the CPU oracle reproduces every
-// value; 8 columns per thread (two 16-byte loads, one 16-byte store).
+// rounded operations and the SiLU kb_silu (here on pairs: kb_silu2, the same
+// bits), so the CPU oracle reproduces every value; 8 columns per thread (two
+// 16-byte loads, one 16-byte store), rows * w / 8 < 2^31 items.
 __global__ void gate_silu_kernel(const float* __restrict__ x, long ldx, const float* __restrict__ scale,
-                                 const float* __restrict__ bias, uint16_t* __restrict__ out, long ldo, long rows,
-                                 int w8, int f16) {
-  const long total = rows * w8;
-  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long>(gridDim.x) * blockDim.x) {
-    const long r = i / w8;
-    const int c = static_cast<int>(i - r * w8) * 8;
+                                 const float* __restrict__ bias, uint16_t* __restrict__ out, long ldo, uint32_t total,
+                                 FastDiv w8, int f16) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t r = w8.div(i);
+    const int c = static_cast<int>(i - r * w8.d) * 8;
     const float4* src = reinterpret_cast<const float4*>(x + r * ldx + c);
     const float4 a = __ldg(src), b = __ldg(src + 1);
     const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + c)), s1 = __ldg(reinterpret_cast<const float4*>(scale + c) + 1);
     const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + c)), b1 = __ldg(reinterpret_cast<const float4*>(bias + c) + 1);
-    const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float2 xv[4] = {make_float2(a.x, a.y), make_float2(a.z, a.w), make_float2(b.x, b.y), make_float2(b.z, b.w)};
+    const float2 sv[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w), make_float2(s1.x, s1.y),
+                          make_float2(s1.z, s1.w)};
+    const float2 bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                          make_float2(b1.z, b1.w)};
     uint32_t o[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const float v0 = kb_silu(__fadd_rn(__fmul_rn(xv[2 * q], sv[2 * q]), bv[2 * q]));
-      const float v1 = kb_silu(__fadd_rn(__fmul_rn(xv[2 * q + 1], sv[2 * q + 1]), bv[2 * q + 1]));
-      o[q] = pack16x2(make_float2(v0, v1), f16 != 0);
+      // scalar rounded affine: a packed multiply feeding a packed add may be
+      // contracted into a fused multiply-add by the assembler
+      const float2 v = make_float2(__fadd_rn(__fmul_rn(xv[q].x, sv[q].x), bv[q].x),
+                                   __fadd_rn(__fmul_rn(xv[q].y, sv[q].y), bv[q].y));
+      o[q] = pack16x2(kb_silu2(v), f16 != 0);
     }
     *reinterpret_cast<uint4*>(out + r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -428,11 +431,16 @@ int gate_silu_launch(const float* x, long ldx, const float* scale, const float* 
     return KB_E_INVALID;
   }
   const long total = rows * (w / 8);
+  if (rows < 0 || total >= (1L << 31)) {
+    set_error("gate: rows * width / 8 must be below 2^31");
+    return KB_E_INVALID;
+  }
+  if (total == 0) return KB_OK;
   int dev = 0;
   cudaGetDevice(&dev);
   const long want = (total + 255) / 256, cap = 8L * num_sms(dev);
-  gate_silu_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(x, ldx, scale, bias, out, ldo, rows,
-                                                                                   w / 8, f16);
+  gate_silu_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(
+      x, ldx, scale, bias, out, ldo, static_cast<uint32_t>(total), FastDiv(static_cast<uint32_t>(w / 8)), f16);
   return check_cuda(cudaGetLastError(), "gate launch");
 }
 

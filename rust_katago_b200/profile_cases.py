@@ -6,13 +6,18 @@ Each case runs one kernel family at the b11c768 trunk's batch-256 shapes (or
 one whole forward) twice, so `ncu -s 1 -c 1` captures a warm launch:
 
   trunk   two forwards without a graph (104 kernels each)
+  tf3     two forwards of the nested TF3 b11c768 trunk (INT8 recipe) without a graph
+  tf3ffn  the same with the FFN-scope recipe (binary16 QKV and out projections)
   up      INT8 GEMM 92416x3072x768 + bias + GELU (the FFN up projection)
   down    INT8 GEMM 92416x768x3072 + bias + bf16 residual
   attn    attention, 256 positions x 12 heads x 64 (Q and K already rotated, the trunk's path)
+  attn32  attention of the TF3 trunk: 256 positions x 12 heads x 32, binary16
   qkv     INT8 GEMM 92416x2304x768 with the rotary epilogue (the trunk's QKV projection)
   quant   streaming quantiser of the 92416x3072 bf16 FFN hidden
   rms     fused RMSNorm -> bf16 -> INT8 quantiser, 92416x768
   mxup    MXFP8 block-scaled GEMM 92416x3072x768 -> bf16 (the up projection)
+  swiglu  INT8 SwiGLU FFN of the TF3 trunk, 92416 rows, mid 384, hidden 1152: dual GEMM
+          (92416x2304x384, SwiGLU epilogue) -> requantiser -> down GEMM + fp32 residual
   mxquant MXFP8 block-32 quantiser of a 92416x768 bf16 activation
 """
 
@@ -30,8 +35,9 @@ def main(argv):
     batch = int(argv[2]) if len(argv) > 2 else 256
     m = batch * 361
     torch.cuda.set_device(0)
-    if case == "trunk":
-        topo = synthetic.B11C768
+    if case in ("trunk", "tf3", "tf3ffn"):
+        topo = {"trunk": synthetic.B11C768, "tf3": synthetic.TF3_B11C768,
+                "tf3ffn": synthetic.TF3_B11C768_FFN}[case]
         model = backend.CudaBackend.load_model(topo, synthetic.make_blob(topo, 1234))
         h = backend.CudaBackend.create_compute_handle(model, batch)
         sp, gl = synthetic.make_positions(batch, 5)
@@ -52,15 +58,14 @@ def main(argv):
         out = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
         for _ in range(2):
             int8.linear(a, sa, w, sw, b, m, n, k, epi, out, n, act=act)
-    elif case == "attn":
-        heads, d = 12, 64
-        qkv = torch.randn(m, 3 * heads * d, device="cuda").to(torch.bfloat16)
-        cs = torch.ones(361, heads, d // 2, device="cuda")
-        sn = torch.zeros_like(cs)
-        out = torch.empty(m, heads * d, dtype=torch.bfloat16, device="cuda")
+    elif case in ("attn", "attn32"):
+        heads, d = 12, 64 if case == "attn" else 32
+        dt, tdt = (_capi.DT_BF16, torch.bfloat16) if case == "attn" else (_capi.DT_F16, torch.float16)
+        qkv = torch.randn(m, 3 * heads * d, device="cuda").to(tdt)
+        out = torch.empty(m, heads * d, dtype=tdt, device="cuda")
         for _ in range(2):
             _capi.call("kb_attention", qkv.data_ptr(), 0, 0, out.data_ptr(), batch, heads,
-                       d, 0.125, _capi.DT_BF16, int(torch.cuda.current_stream().cuda_stream))
+                       d, d ** -0.5, dt, int(torch.cuda.current_stream().cuda_stream))
     elif case == "quant":
         x = torch.randn(m, 3072, device="cuda").to(torch.bfloat16).view(torch.int16)
         amax = torch.full((m,), 0x41000000, dtype=torch.int32, device="cuda")  # |x| <= 8.0 as f32 bits
@@ -75,6 +80,19 @@ def main(argv):
         s = torch.empty(m, device="cuda")
         for _ in range(2):
             int8.rms_quantize(x, _capi.DT_BF16, m, 768, 768, g, 1e-6, _capi.DT_BF16, 768, q, s)
+    elif case == "swiglu":
+        import numpy as np
+
+        mid, hid = 384, 1152
+        rng = np.random.default_rng(0)
+        dual = int8.Int8Weight((0.05 * rng.standard_normal((2 * hid, mid))).astype(np.float32),
+                               _capi.LAYOUT_SWIGLU_DUAL)
+        down = int8.Int8Weight((0.05 * rng.standard_normal((mid, hid))).astype(np.float32))
+        ws = int8.Int8Workspace(m, hid, hid)
+        x = torch.randn(m, mid, device="cuda").to(torch.float16).view(torch.int16)
+        res = torch.zeros(m, mid, device="cuda")
+        for _ in range(2):
+            ws.ffn(x, dual, down, res, m)
     elif case in ("mxup", "mxquant"):
         import numpy as np
 

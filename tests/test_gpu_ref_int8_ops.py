@@ -13,7 +13,7 @@ int8_ops.cu, compiled unmodified for sm_100a and run on the same GPU
   listed, one step at most, and each differing scale is one fp16 step of the
   row maximum apart.
 * SwiGLU requantisation: the reference computes e^-g with CUDA's expf, this
-  library with its own kb_expf (a fixed IEEE sequence the oracle restates);
+  library with its own silu_exp (a fixed IEEE sequence the oracle restates);
   the same bound and listing as for the RMS quantiser.
 """
 

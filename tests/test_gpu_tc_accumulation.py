@@ -59,3 +59,30 @@ def test_gemm16_accumulation_bit_exact(cuda, oracle, f16, k, wide):
     got = out.cpu().numpy()
     ref = oracle.tc_gemm16(ab, wb, f16=f16)
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"{np.mean(got != ref):.4%} differ"
+
+
+def test_silu_every_binary16_input(cuda, oracle):
+    """The kernels' SiLU (packed pairs, as in the SwiGLU and gate epilogues) on
+    every finite binary16 value: an identity GEMM passes each value through
+    (one nonzero product per output; -0 sums to +0 with the other products,
+    as the oracle's accumulation restates), the epilogue applies the SiLU and
+    rounds to binary16; bitwise against the oracle."""
+    torch = cuda
+    h = np.arange(1 << 16, dtype=np.uint16)
+    h = h[np.isfinite(h.view(np.float16))]
+    k = 128
+    rows = -(-h.size // k)
+    a = np.zeros(rows * k, np.uint16)
+    a[:h.size] = h
+    a = a.reshape(rows, k)
+    eye = np.eye(k, dtype=np.float32)
+    da = torch.from_numpy(a.view(np.int16)).cuda()
+    dw = torch.from_numpy(oracle.f16_encode(eye).view(np.int16)).cuda()
+    out = torch.zeros((rows, k), dtype=torch.int16, device="cuda")
+    int8.f16_linear(da, dw, None, rows, k, k, _capi.EPI_16, out, k, act=_capi.ACT_SILU, out_dtype=_capi.DT_F16)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint16)
+    passed = oracle.tc_gemm16(a, oracle.f16_encode(eye), f16=True)
+    assert np.array_equal(passed.view(np.uint32)[a != 0x8000], oracle.decode16(a, True).view(np.uint32)[a != 0x8000])
+    ref = oracle.f16_encode(oracle.act(passed, _capi.ACT_SILU))
+    assert np.array_equal(got, ref), f"{(got != ref).sum()} of {got.size} differ"

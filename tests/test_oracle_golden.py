@@ -97,20 +97,43 @@ def test_reference_cpu_projection_matches_composition(oracle):
     assert (out == g[key + "half"]).all()
 
 
-def test_expf_accuracy(oracle):
+def test_silu_exp_accuracy(oracle):
+    """The SiLU's e^x: accurate on [-20, 88.72], and 1 + e^x unchanged by its clamp."""
     lib = oracle.lib()
-    xs = np.concatenate([np.linspace(-103, 88.7, 20001), np.random.default_rng(3).uniform(-20, 20, 20000)])
+    xs = np.concatenate([np.linspace(-20, 88.72, 20001), np.random.default_rng(3).uniform(-20, 20, 20000)])
     worst = 0.0
     for x in xs.astype(np.float32):
-        got = lib.or_expf(float(x))
+        got = lib.or_silu_exp(float(x))
         ref = math.exp(float(x))
-        if ref < 1.2e-38:
-            assert abs(got - ref) <= 2.0 ** -149 * 2
-            continue
         worst = max(worst, abs(got - ref) / ref)
     assert worst < 3e-7  # about 2.5 ulp worst case, typically < 1 ulp
-    assert lib.or_expf(float("inf")) == math.inf and lib.or_expf(-1000.0) == 0.0
-    assert math.isnan(lib.or_expf(float("nan")))
+    # every float above ln(FLT_MAX) overflows, the largest below it does not
+    top = np.float32(88.72283)
+    assert math.isfinite(lib.or_silu_exp(float(np.nextafter(top, np.float32(0)))))
+    for x in (np.nextafter(np.float32(88.72284), np.float32(100)), 88.75, 89.0, 1e4, math.inf):
+        assert lib.or_silu_exp(float(x)) == math.inf
+    # below the clamp, 1 + e^x rounds to 1 as the clamped value's does
+    for x in (-17.4, -20.0, -50.0, -1e4, -math.inf):
+        assert np.float32(1) + np.float32(lib.or_silu_exp(float(x))) == np.float32(1)
+    # a NaN argument reaches the SiLU division, which returns NaN
+    assert math.isnan(lib.or_silu(float("nan")))
+    assert lib.or_silu(-1e4) == 0.0 and math.copysign(1, lib.or_silu(-1e4)) == -1
+    assert lib.or_silu(1e4) == 1e4
+
+
+def test_silu_every_binary16_input(oracle):
+    """SiLU of every finite binary16 value against float64 with the fp32
+    denominator (which overflows to inf for g < -88.72, as expf's does), to
+    2 ulp of fp32."""
+    lib = oracle.lib()
+    h = np.arange(1 << 16, dtype=np.uint16).view(np.float16)
+    h = h[np.isfinite(h)].astype(np.float32)
+    with np.errstate(over="ignore"):
+        for g in h:
+            got = np.float32(lib.or_silu(float(g)))
+            d = np.float32(1.0 + math.exp(-float(g))) if g > -700 else np.float32(np.inf)
+            ref = float(g) / float(d)
+            assert abs(got - ref) <= 2.5e-7 * abs(ref) + 1e-44, (g, got, ref)
 
 
 def test_gelu_silu_accuracy(oracle):
