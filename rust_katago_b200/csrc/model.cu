@@ -646,8 +646,9 @@ int f16_gemm_f32(kb_handle* h, const uint16_t* a, const uint16_t* w, int M, int 
 // RMSNorm -> QKV (INT8 with the fused RMS quantiser, or binary16 on the
 // RMSNorm's binary16 rows) with RoPE in the epilogue -> attention (binary16
 // P) -> out-proj added to the fp32 stream (INT8 dequant-residual, or binary16
-// GEMM + residual) -> RMSNorm -> INT8 dual GEMM + SwiGLU (fp16 boundaries) ->
-// requant -> INT8 down GEMM added to the fp32 stream: the reference's
+// GEMM + residual) -> RMSNorm -> INT8 dual GEMM + SwiGLU (fp16 boundaries,
+// row |max| from the epilogue) -> one-pass requant -> INT8 down GEMM added to
+// the fp32 stream: the reference's
 // Int8Workspace::ffn_rms (int8.rs:1135-1172).
 int nested_pair(kb_handle* h, const NestedPair& p, unsigned layer, int n, float scale) {
   const kb_model* m = h->model;
@@ -727,10 +728,14 @@ int nested_pair(kb_handle* h, const NestedPair& p, unsigned layer, int n, float 
   u.n_out = hid;
   u.status = h->status;
   u.layer = layer;
+  // the epilogue emits each row's |max| so the requantiser needs one pass
+  u.row_amax = h->row_amax;
+  rc = check_cuda(cudaMemsetAsync(h->row_amax, 0, static_cast<size_t>(M) * sizeof(uint32_t), s), "amax reset");
+  if (rc) return rc;
   rc = gemm_launch(kGemmI8, kEpiSwiGLU16, h->q, p.dual->q, u, s, 256);
   if (rc) return rc;
-  rc = quantize_rows_launch(h->hidden, KB_DT_F16, hid, M, hid, p.down->kp, false, nullptr, 0.0f, 0, h->q, h->scales,
-                            h->status, layer, s);
+  rc = quantize_rows_amax_launch(h->hidden, KB_DT_F16, hid, h->row_amax, M, hid, p.down->kp, h->q, h->scales,
+                                 h->status, layer, s);
   if (rc) return rc;
   GemmArgs dn;
   dn.m = M;
