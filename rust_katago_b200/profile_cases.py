@@ -10,6 +10,7 @@ one whole forward) twice, so `ncu -s 1 -c 1` captures a warm launch:
   tf3ffn  the same with the FFN-scope recipe (binary16 QKV and out projections)
   up      INT8 GEMM 92416x3072x768 + bias + GELU (the FFN up projection)
   down    INT8 GEMM 92416x768x3072 + bias + bf16 residual
+  out     INT8 GEMM 92416x768x768 + bias + bf16 residual (the attention out-projection)
   attn    attention, 256 positions x 12 heads x 64 (Q and K already rotated, the trunk's path)
   attn32  attention of the TF3 trunk: 256 positions x 12 heads x 32, binary16
   qkv     INT8 GEMM 92416x2304x768 with the rotary epilogue (the trunk's QKV projection)
@@ -19,6 +20,7 @@ one whole forward) twice, so `ncu -s 1 -c 1` captures a warm launch:
   swiglu  INT8 SwiGLU FFN of the TF3 trunk, 92416 rows, mid 384, hidden 1152: dual GEMM
           (92416x2304x384, SwiGLU epilogue) -> requantiser -> down GEMM + fp32 residual
   mxquant MXFP8 block-32 quantiser of a 92416x768 bf16 activation
+  decode  output decoding + post-processing of 256 positions (kb_decode_device, legality mask)
 """
 
 from __future__ import annotations
@@ -45,9 +47,10 @@ def main(argv):
         dout = torch.zeros(batch * backend.OUT_PER_POS, device="cuda")
         for _ in range(2):
             h.forward_device(batch, dsp, dgl, dout, use_graph=False)
-    elif case in ("up", "down", "qkv"):
+    elif case in ("up", "down", "qkv", "out"):
         n, k, epi, act = {"up": (3072, 768, _capi.EPI_16, _capi.ACT_GELU),
                           "down": (768, 3072, _capi.EPI_RES16, 0),
+                          "out": (768, 768, _capi.EPI_RES16, 0),
                           "qkv": (2304, 768, _capi.EPI_16, 0)}[case]
         # (the qkv case times the plain 16-bit epilogue; the trunk adds the rotary tables)
         a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda")
@@ -80,6 +83,17 @@ def main(argv):
         s = torch.empty(m, device="cuda")
         for _ in range(2):
             int8.rms_quantize(x, _capi.DT_BF16, m, 768, 768, g, 1e-6, _capi.DT_BF16, 768, q, s)
+    elif case == "decode":
+        import numpy as np
+
+        rng = np.random.default_rng(0)
+        raw = torch.from_numpy(rng.standard_normal(batch * backend.OUT_PER_POS).astype(np.float32)).cuda()
+        rows = backend.row_params(batch, symmetry=rng.integers(0, 8, batch), policy_optimism=0.3)
+        d_rows = torch.from_numpy(np.ascontiguousarray(rows).view(np.uint8).reshape(batch, 24)).cuda()
+        legal = torch.from_numpy((rng.random((batch, 362)) < 0.8).astype(np.uint8)).cuda()
+        out = torch.empty(batch * backend.DEC_PER_POS, device="cuda")
+        for _ in range(2):
+            backend.decode_device(batch, raw, d_rows, legal, out, int(torch.cuda.current_stream().cuda_stream))
     elif case == "swiglu":
         import numpy as np
 
