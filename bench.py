@@ -203,8 +203,10 @@ class FfnWorkload:
 
 
 def gemm_launcher(torch, m, n, k, epi, act):
-    """A launch of the INT8 GEMM kernel on random operands of the given shape."""
-    from rust_katago_b200 import int8
+    """A launch of the INT8 GEMM kernel on random operands of the given shape;
+    the GELU projection also emits the row |max| as the trunk's launch does
+    (the atomics feed its streaming requantiser)."""
+    from rust_katago_b200 import _capi, int8
 
     a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda")
     w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda")
@@ -212,9 +214,10 @@ def gemm_launcher(torch, m, n, k, epi, act):
     sw = torch.rand(n, device="cuda") * 0.01
     bias = torch.rand(n, device="cuda") * 0.01
     out = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+    amax = torch.zeros(m, dtype=torch.int32, device="cuda") if act == _capi.ACT_GELU else None
 
     def launch():
-        int8.linear(a, sa, w, sw, bias, m, n, k, epi, out, n, act=act)
+        int8.linear(a, sa, w, sw, bias, m, n, k, epi, out, n, act=act, row_amax=amax)
 
     return launch
 
