@@ -64,36 +64,43 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// One potentially blocking probe: the thread is suspended until the phase
+// with the given parity completes or about `suspend_ns` have passed (the
+// instruction's suspend-time hint), so a waiting warp issues nothing while it
+// waits instead of spinning beside the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
       : "memory");
   return ok != 0;
 }
 
+// Suspend-time hint of one probe: long against any legitimate wait inside a
+// kernel (microseconds), short against the two-second limit.
+constexpr uint32_t kSuspendNs = 1000000u;
+
 // Wait for the phase with the given parity to complete.  Returns false when
 // the CTA-wide abort flag is raised (by this thread on timeout, or by another
 // role that timed out); the caller must then leave its loop.
-// `limit_ns` shortens the limit (tests of the abort path); waits that drain
-// copies already issued always keep the full kWaitLimitNs.
+// `limit_ns` shortens the limit (tests of the abort path; each probe then
+// suspends for at most a quarter of it); waits that drain copies already
+// issued always keep the full kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint64_t limit_ns = kWaitLimitNs) {
-  if (mbar_try_wait(bar, parity)) return true;
+  const uint32_t hint = limit_ns >= 4ull * kSuspendNs ? kSuspendNs : static_cast<uint32_t>(limit_ns / 4 + 1);
+  if (mbar_try_wait(bar, parity, hint)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t n = 1;; ++n) {
-    if (mbar_try_wait(bar, parity)) return true;
-    // the clock is read every 64 tries, or on every try under a shortened limit
-    if ((n & 63) == 0 || limit_ns != kWaitLimitNs) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > limit_ns) {
-        *abort_flag = 1;
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait(bar, parity, hint)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > limit_ns) {
+      *abort_flag = 1;
+      return false;
     }
   }
 }
