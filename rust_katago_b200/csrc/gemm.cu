@@ -1136,7 +1136,9 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long d
 int gemm_pick_bn(int kind, int epi, int n) {
   (void)kind;
   if (epi == kEpiSwiGLU16) return 256;
-  if (n % 256 == 0 || n > 2048) return 256;
+  // Wider tiles once N is past four 256-column tiles, even with a partial
+  // last one: the short-K projections are bound by per-tile epilogue work.
+  if (n % 256 == 0 || n > 1024) return 256;
   return 128;
 }
 
