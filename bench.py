@@ -42,8 +42,8 @@ METRIC = "positions/sec b11c768 W8A8 fwd @1/2/4/8 B200; INT8 GEMM % tensor peak"
 L2_FLUSH_BYTES = 256 << 20
 
 
-# ncu summaries (profiles/*.md) of the GEMMs that can dominate the step.
-PROFILE_OF_GEMM = {"up 768->3072 + GELU": "gemm_i8_up_gelu_b256.md"}
+# ncu summaries (profiles/*.md) of the kernels that can dominate the step.
+PROFILE_OF_GEMM = {"up 768->3072 + GELU": "gemm_i8_up_gelu_b256.md", "attention": "attention_b256.md"}
 
 
 def profile_traffic(gemm_label):
@@ -319,6 +319,27 @@ class TrunkWorkload:
 
     def gemm_launcher(self, m, n, k, epi, act):
         return gemm_launcher(self.torch, m, n, k, epi, act)
+
+    def attention(self):
+        """The trunk's attention launch (Q and K already rotated by the QKV
+        epilogue, 12 heads x 64, bf16, row |max| for the next quantiser):
+        (label, launcher, launches per forward, algorithmic bytes, FLOPs)."""
+        from rust_katago_b200 import _capi
+
+        torch, t = self.torch, self.topo
+        m, c = self.batch * 361, t.trunk_channels
+        qkv = (torch.randn(m, 3 * c, device="cuda") * 1.5).to(torch.bfloat16)
+        out = torch.empty(m, c, dtype=torch.bfloat16, device="cuda")
+        amax = torch.zeros(m, dtype=torch.int32, device="cuda")
+        stream = torch.cuda.current_stream()
+
+        def launch():
+            _capi.call("kb_attention_amax", qkv.data_ptr(), out.data_ptr(), amax.data_ptr(), self.batch,
+                       t.num_heads, t.head_dim, t.head_dim ** -0.5, _capi.DT_BF16, int(stream.cuda_stream))
+
+        launch.keep = (qkv, out, amax)
+        flops = 4.0 * 361 * 361 * t.head_dim * t.num_heads * self.batch
+        return ("attention 12x64 (pre-rotated, row amax)", launch, t.num_blocks, 4 * m * c * 2, flops)
 
 
 class TrunkMxfp8Workload(TrunkWorkload):
@@ -706,10 +727,42 @@ def main():
                 "kernel_ms": dom["ms"],
                 "peak_note": f"{'FP8' if getattr(wl, 'dtype', 'int8') == 'e4m3' else 'INT8'} dense peak = "
                              f"2 x the {peaks['source']} cuBLAS bf16 burst "
-                             f"({peaks['bf16_tflops']} TFLOP/s): tcgen05 kind::i8 issues at twice kind::f16",
-                "int8_gemms": gemm_rows,
-                "int8_gemm_frac_of_peak": tot_ops / (tot_ms / 1e3) / 1e12 / int8_peak,
-                "int8_gemm_share_of_step": tot_ms / ms_per_step}
+                             f"({peaks['bf16_tflops']} TFLOP/s): tcgen05 kind::i8 issues at twice kind::f16"}
+    # The trunk's attention, timed the same way: when its share of the step is
+    # the largest, it is the dominant kernel and the roofline describes it.
+    att = None
+    if hasattr(wl, "attention"):
+        label, fn, per_step, nbytes, flops = wl.attention()
+        for _ in range(3):
+            fn()
+        ams = statistics.mean(time_launches(torch, torch.cuda.current_stream(), fn, flush, 10))
+        t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9) * 1e3
+        t_tc = flops / (peaks["bf16_tflops"] * 1e12) * 1e3
+        att = {"kernel": label, "ms": ams, "per_step": per_step, "bytes": nbytes, "flops": flops,
+               "hbm_gbs": nbytes / (ams / 1e3) / 1e9, "tflops": flops / (ams / 1e3) / 1e12,
+               "bound": "hbm" if t_hbm >= t_tc else "tensor"}
+        if ams * per_step > dom["ms"] * dom["per_step"]:
+            gemm_roofline = roofline
+            hbm = att["bound"] == "hbm"
+            roofline = {"bound": att["bound"], "achieved": att["hbm_gbs"] if hbm else att["tflops"],
+                        "peak": peaks["hbm_gbs"] if hbm else peaks["bf16_tflops"],
+                        "unit": "GB/s" if hbm else "TFLOP/s",
+                        "frac": (att["hbm_gbs"] / peaks["hbm_gbs"]) if hbm else (att["tflops"] / peaks["bf16_tflops"]),
+                        "traffic": profile_traffic("attention"),
+                        "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one launch, from the ncu "
+                                        "capture summarised in profiles/attention_b256.md (same shape)",
+                        "kernel": f"attention_fa_kernel<64> {label} (batch {wl.batch})", "kernel_ms": ams,
+                        "peak_note": f"{peaks['source']} copy bandwidth; the kernel's ideal time is "
+                                     f"{max(t_hbm, t_tc) * 1e3:.0f} us ({att['bound']}-bound: "
+                                     f"{nbytes / 1e6:.0f} MB read and written, {flops / 1e9:.1f} GFLOP); what "
+                                     "sets its pace is the softmax warps' exponentials on the FMA pipe",
+                        "dominant_gemm": gemm_roofline}
+    roofline.update({"int8_gemms": gemm_rows,
+                     "int8_gemm_frac_of_peak": tot_ops / (tot_ms / 1e3) / 1e12 / int8_peak,
+                     "int8_gemm_share_of_step": tot_ms / ms_per_step})
+    if att is not None:
+        roofline["attention"] = att
+        roofline["attention_share_of_step"] = att["ms"] * att["per_step"] / ms_per_step
 
     # sub-records of the default workload (config 5 and latency on every rank)
     extras = {}

@@ -241,6 +241,15 @@ KB_API int kb_f16_linear(const uint16_t* a, const uint16_t* w, const float* bias
 KB_API int kb_attention(const uint16_t* qkv, const float* rope_cos, const float* rope_sin, uint16_t* out,
                         int batch, int heads, int head_dim, float scale, int dtype, uintptr_t stream);
 
+/* The trunk's attention launch: Q and K already rotated, and row_amax
+ * [batch*361] (zeroed by the caller) raised with atomicMax to the fp32 bits of
+ * each output row's largest |16-bit value|, the input of
+ * kb_int8_quantize_rows_amax for the out-projection.
+ * Replaces: attention_fa2_q64_kernel (attention_fa2_q64.cu:82-390) followed by
+ * the row maximum of int8_quantize_rows_kernel (int8_ops.cu:62-89). */
+KB_API int kb_attention_amax(const uint16_t* qkv, uint16_t* out, uint32_t* row_amax, int batch, int heads,
+                             int head_dim, float scale, int dtype, uintptr_t stream);
+
 /* ------------------------------------------------------------------ MXFP8 (block-scaled E4M3) */
 
 /* Status word [flags, first_layer]: flags OR-ed, first_layer = first layer

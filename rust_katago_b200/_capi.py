@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "kb_bf16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
     "kb_f16_linear": (I, [P, P, P, I, I, I, I, I, I, P, I, STREAM]),
     "kb_attention": (I, [P, P, P, P, I, I, I, F, I, STREAM]),
+    "kb_attention_amax": (I, [P, P, P, I, I, I, F, I, STREAM]),
     "kb_status_reset": (I, [P, STREAM]),
     "kb_mxfp8_dimensions": (I, [I, I, IP, IP, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
     "kb_mxfp8_quantize": (I, [P, I, I, I, I, P, P, ctypes.c_size_t, P, ctypes.c_uint32, STREAM]),

@@ -20,6 +20,16 @@ extern "C" int kb_attention(const uint16_t* qkv, const float* rope_cos, const fl
                               dtype == KB_DT_F16, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int kb_attention_amax(const uint16_t* qkv, uint16_t* out, uint32_t* row_amax, int batch, int heads,
+                                 int head_dim, float scale, int dtype, uintptr_t stream) {
+  if ((dtype != KB_DT_BF16 && dtype != KB_DT_F16) || row_amax == nullptr) {
+    kb::set_error("kb_attention_amax: dtype must be KB_DT_BF16 or KB_DT_F16, row_amax non-null");
+    return KB_E_INVALID;
+  }
+  return kb::attention_launch(qkv, nullptr, nullptr, out, batch, 361, heads, head_dim, scale, dtype == KB_DT_F16,
+                              reinterpret_cast<cudaStream_t>(stream), row_amax);
+}
+
 namespace {
 
 // One CTA waits, with the given limit, on an mbarrier that nothing ever

@@ -86,6 +86,31 @@ def test_attention_prerotated_matches_oracle(cuda, oracle, batch, scale, hd):
     attention_agreement(got, ref, exact, f"pre-rotated d{hd} b{batch} x{scale}")
 
 
+@pytest.mark.parametrize("hd,dtype", [(64, "bf16"), (32, "f16")])
+def test_attention_amax_entry(cuda, oracle, hd, dtype):
+    """kb_attention_amax (the trunk's launch): the same output as kb_attention
+    with NULL tables, and each row's |max| as fp32 bits."""
+    torch = cuda
+    batch, heads = 2, 12
+    c = heads * hd
+    rng = np.random.default_rng(hd)
+    enc, dt, f16 = ((oracle.bf16_encode, _capi.DT_BF16, False) if dtype == "bf16"
+                    else (oracle.f16_encode, _capi.DT_F16, True))
+    qkv = enc((rng.standard_normal((batch * 361, 3 * c)) * 1.5).astype(np.float32))
+    dq = torch.from_numpy(np.ascontiguousarray(qkv.view(np.int16))).cuda()
+    a = torch.zeros((batch * 361, c), dtype=torch.int16, device="cuda")
+    b = torch.zeros_like(a)
+    amax = torch.zeros(batch * 361, dtype=torch.int32, device="cuda")
+    s = int(torch.cuda.current_stream().cuda_stream)
+    _capi.call("kb_attention", dq.data_ptr(), None, None, a.data_ptr(), batch, heads, hd, hd ** -0.5, dt, s)
+    _capi.call("kb_attention_amax", dq.data_ptr(), b.data_ptr(), amax.data_ptr(), batch, heads, hd, hd ** -0.5, dt, s)
+    torch.cuda.synchronize()
+    ga, gb = a.cpu().numpy().view(np.uint16), b.cpu().numpy().view(np.uint16)
+    assert np.array_equal(ga, gb)
+    expect = np.abs(oracle.decode16(gb, f16)).max(axis=1).astype(np.float32).view(np.uint32)
+    assert np.array_equal(amax.cpu().numpy().view(np.uint32), expect)
+
+
 def run_trunk(topo, blob, spatial, glob, max_batch=None):
     model = backend.CudaBackend.load_model(topo, blob)
     h = backend.CudaBackend.create_compute_handle(model, max_batch or spatial.shape[0])
