@@ -265,7 +265,7 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
   return true;
 }
 
-template <int D, bool F16, bool ROPE>
+template <int D, bool F16, bool ROPE, bool SPLIT>
 __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     const __grid_constant__ CUtensorMap map_kv, const __grid_constant__ CUtensorMap map_q,
     const __grid_constant__ CUtensorMap map_out,
@@ -304,6 +304,12 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   const int c = heads * D;
   const size_t row_stride = 3 * static_cast<size_t>(c);
   const int tiles = (seq + kTileQ - 1) / kTileQ;
+  // Jobs: a (position, head) pair with tpj of its query tiles, K and V loaded
+  // once per job: all tiles, or (SPLIT, when the pairs alone would leave SMs
+  // idle) one tile per job.
+  const int tpj = SPLIT ? 1 : tiles;
+  const int jpp = SPLIT ? tiles : 1;  // jobs per pair
+  const int jobs = pairs * jpp;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -344,8 +350,9 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     const bool kv_loader = warp == kMmaWarp + 1;
     if (lane == 0) tma_prefetch_desc(kv_loader ? &map_kv : &map_q);
     int g = 0;  // global Q tile counter
-    for (int it = 0, p = blockIdx.x; p < pairs; ++it, p += gridDim.x) {
+    for (int it = 0, j = blockIdx.x; j < jobs; ++it, j += gridDim.x) {
       const int kb = it & 1;
+      const int p = j / jpp, t0 = (j % jpp) * tpj;
       const int b = p / heads, h = p % heads;
       if (kv_loader) {
         if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
@@ -357,8 +364,8 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           tma_load_2d(ks + kKBytes, &map_kv, &kv_tma[kb], 2 * c + h * D, b * seq);
           tma_load_2d(ks + kKBytes + kKvBox * kRowBytes, &map_kv, &kv_tma[kb], 2 * c + h * D,
                       b * seq + kKvBox);
-          // the pair's Q tiles into L2, so each later Q load is an L2 hit
-          for (int t = 0; t < tiles; ++t) tma_prefetch_2d(&map_q, h * D, b * seq + t * kTileQ);
+          // the job's Q tiles into L2, so each later Q load is an L2 hit
+          for (int t = t0; t < t0 + tpj; ++t) tma_prefetch_2d(&map_q, h * D, b * seq + t * kTileQ);
         }
         // V rows [seq, 368) hold the next position's values (or TMA zeros):
         // clear them, their P is zero but 0 * Inf would not be.
@@ -370,7 +377,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         mbar_arrive(&kv_full[kb]);
       } else {
         bool ok = true;
-        for (int t = 0; t < tiles; ++t, ++g) {
+        for (int t = t0; t < t0 + tpj; ++t, ++g) {
           if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (g & 1) ^ 1, abort_flag))) {
             ok = false;
             break;
@@ -387,8 +394,9 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     // ------------------------------------------------------------ staging loaders (RoPE here)
     const int tid = threadIdx.x - 32 * (kMmaWarp + 1);
     int g = 0;  // global Q tile counter
-    for (int it = 0, p = blockIdx.x; p < pairs; ++it, p += gridDim.x) {
+    for (int it = 0, j = blockIdx.x; j < jobs; ++it, j += gridDim.x) {
       const int kb = it & 1;
+      const int p = j / jpp, t0 = (j % jpp) * tpj;
       const int b = p / heads, h = p % heads;
       const uint16_t* base = qkv + static_cast<size_t>(b) * seq * row_stride;
       if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[kb], ((it >> 1) & 1) ^ 1, abort_flag))) break;
@@ -400,7 +408,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       fence_proxy_async_smem();
       mbar_arrive(&kv_full[kb]);
       bool ok = true;
-      for (int t = 0; t < tiles; ++t, ++g) {
+      for (int t = t0; t < t0 + tpj; ++t, ++g) {
         if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (g & 1) ^ 1, abort_flag))) {
           ok = false;
           break;
@@ -427,10 +435,10 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       const uint32_t id_pv = id_common | (1u << 16) /* B MN-major */ | (static_cast<uint32_t>(D >> 3) << 17);
       constexpr uint64_t kHalfOff = (kHalfA * kRowBytes) >> 4;  // 192 rows, descriptor units
       constexpr uint64_t kStep16 = (16 * kRowBytes) >> 4;       // 16 keys of V along K
-      const int my_pairs = blockIdx.x < pairs ? (pairs - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
-      const int n = my_pairs * tiles;
+      const int my_jobs = blockIdx.x < jobs ? (jobs - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+      const int n = my_jobs * tpj;
       auto issue_sa = [&](int g) -> bool {
-        const int it = g / tiles, t = g % tiles, kb = it & 1;
+        const int it = g / tpj, t = g % tpj, kb = it & 1;
         if (t == 0 && !mbar_wait(&kv_full[kb], (it >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait(q_full, g & 1, abort_flag)) return false;
         tc_fence_after();
@@ -443,7 +451,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         return true;
       };
       auto issue_sb = [&](int g) {
-        const int kb = (g / tiles) & 1;
+        const int kb = (g / tpj) & 1;
         const uint64_t kdesc = tile_desc<D>(smem_u32(kv_buf + kb * kKVBytes));
         const uint64_t qdesc = tile_desc<D>(smem_u32(q_buf));
 #pragma unroll
@@ -455,7 +463,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       bool ok = n == 0 || issue_sa(0);
       if (ok && n > 0) issue_sb(0);
       for (int g = 0; g < n && ok; ++g) {
-        const int kb = (g / tiles) & 1;
+        const int kb = (g / tpj) & 1;
         const uint64_t vdesc = tile_desc<D>(smem_u32(kv_buf + kb * kKVBytes + kKBytes));
         if (!mbar_wait(pa_full, g & 1, abort_flag) || (g > 0 && !mbar_wait(o_free, (g - 1) & 1, abort_flag))) break;
         tc_fence_after();
@@ -471,7 +479,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
           mma_f16_ts(tmem + kOB, tmem + kSB + 48 * (i / 3) + 8 * (i % 3), vdesc + kHalfOff + kStep16 * i, id_pv,
                      i != 0);
         tc_commit(o_full);
-        if (g % tiles == tiles - 1) tc_commit(&kv_empty[kb]);
+        if (g % tpj == tpj - 1) tc_commit(&kv_empty[kb]);
         if (g + 1 < n) {
           if (!mbar_wait(o_full, g & 1, abort_flag)) break;
           issue_sb(g + 1);
@@ -564,9 +572,10 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
     };
     int g = 0;
     bool ok = true;
-    for (int p = blockIdx.x; p < pairs && ok; p += gridDim.x) {
+    for (int j = blockIdx.x; j < jobs && ok; j += gridDim.x) {
+      const int p = j / jpp, t0 = (j % jpp) * tpj;
       const int b = p / heads, h = p % heads;
-      for (int t = 0; t < tiles; ++t, ++g) {
+      for (int t = t0; t < t0 + tpj; ++t, ++g) {
         float* mxg = mx_ex + (g & 1) * (2 * 4 * kTileQ);
         const uint32_t lcol = kLCol + (g & 1) * 8;
         // half A
@@ -620,15 +629,18 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
 template <int D, bool F16, bool ROPE>
 int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint16_t* out, int batch, int seq,
               int heads, float scale, uint32_t* row_amax, unsigned* status, cudaStream_t stream) {
-  auto kern = attention_fa_kernel<D, F16, ROPE>;
+  auto k_pairs = attention_fa_kernel<D, F16, ROPE, false>;
+  auto k_split = attention_fa_kernel<D, F16, ROPE, true>;
   constexpr int kSmemBytes = Geo<D>::kSmemBytes;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> configured{0};
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return check_cuda(e, "attention smem attribute");
+    for (auto k : {k_pairs, k_split}) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return check_cuda(e, "attention smem attribute");
+    }
     configured.fetch_or(bit);
   }
   CUtensorMap map_kv, map_q, map_out;
@@ -651,7 +663,13 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
   }
   const float scale_log2 = scale * 1.4426950408889634f;
   const int pairs = batch * heads;
-  const int grid = pairs < num_sms(dev) ? pairs : num_sms(dev);
+  // Few pairs (small batches): one query tile per job, so the grid fills more
+  // SMs (each job loads its pair's K and V itself).
+  const int tiles = (seq + kTileQ - 1) / kTileQ;
+  const bool split = pairs < num_sms(dev);
+  const int jobs = pairs * (split ? tiles : 1);
+  auto kern = split ? k_split : k_pairs;
+  const int grid = jobs < num_sms(dev) ? jobs : num_sms(dev);
   kern<<<grid, fa_threads<ROPE>(), kSmemBytes, stream>>>(map_kv, map_q, map_out, qkv, cos_t, sin_t, out, pairs, seq,
                                                         heads, scale_log2, row_amax, status);
   return check_cuda(cudaGetLastError(), "attention launch");

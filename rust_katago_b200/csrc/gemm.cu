@@ -40,11 +40,12 @@ constexpr int kBKBytes = 128;  // one 128-byte swizzle row of K per stage
 // 16-bit epilogues (bias + activation, rotary, SwiGLU) and for the residual
 // adds of short-K projections, where draining the epilogue bounds the tile; 8
 // for the others (long-K residual adds keep the deeper operand ring; plain
-// fp32 / int32 outputs).
-template <int EPI, int DEEP>
+// fp32 / int32 outputs).  64-column tiles (small M) always take 8: one
+// 32-column chunk per warp.
+template <int EPI, int DEEP, int BN>
 constexpr int epi_warps() {
-  return (EPI == 3 /* kEpi16 */ || EPI == 7 /* kEpiRope16 */ || EPI == 5 /* kEpiSwiGLU16 */ ||
-          ((EPI == 4 /* kEpiRes16 */ || EPI == 2 /* kEpiResF32 */) && DEEP))
+  return BN > 64 && (EPI == 3 /* kEpi16 */ || EPI == 7 /* kEpiRope16 */ || EPI == 5 /* kEpiSwiGLU16 */ ||
+                     ((EPI == 4 /* kEpiRes16 */ || EPI == 2 /* kEpiResF32 */) && DEEP))
              ? 16
              : 8;
 }
@@ -1037,7 +1038,7 @@ bool epi_16bit(int epi) {
 template <int KIND, int BN, int EPI, int ACT, int DEEP>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, int use_tma_out,
                const GemmArgs& g, cudaStream_t stream) {
-  constexpr int EW = epi_warps<EPI, DEEP>();
+  constexpr int EW = epi_warps<EPI, DEEP, BN>();
   constexpr int SB = DEEP ? (EW == 16 ? 2 : 4) : (EW == 16 ? 1 : 2);
   using Cfg = GemmCfg<KIND, BN, SB, EW>;
   auto kern = gemm_kernel<KIND, BN, EPI, ACT, SB, EW>;
@@ -1133,13 +1134,18 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long d
   return KB_OK;
 }
 
-int gemm_pick_bn(int kind, int epi, int n) {
+int gemm_pick_bn(int kind, int epi, int m, int n) {
   (void)kind;
   if (epi == kEpiSwiGLU16) return 256;
   // Wider tiles once N is past four 256-column tiles, even with a partial
   // last one: the short-K projections are bound by per-tile epilogue work.
-  if (n % 256 == 0 || n > 1024) return 256;
-  return 128;
+  int bn = (n % 256 == 0 || n > 1024) ? 256 : 128;
+  // Small M (a few positions): narrower tiles while the grid leaves SMs idle.
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long mt = (m + kBM - 1) / kBM;
+  while (bn > 64 && mt * ((n + bn - 1) / bn) < num_sms(dev)) bn /= 2;
+  return bn;
 }
 
 int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs& g,
@@ -1198,7 +1204,7 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
   // MXFP8 keeps BN = 128: two 128-column accumulators plus the per-stage
   // scale-factor columns fill the 512 TMEM columns.
   // The SwiGLU tile is 128 gate + 128 up columns: BN = 256 always.
-  const int bn = kind == kGemmMXF8 ? 128 : epi == kEpiSwiGLU16 ? 256 : bn_hint ? bn_hint : gemm_pick_bn(kind, epi, g.n);
+  const int bn = kind == kGemmMXF8 ? 128 : epi == kEpiSwiGLU16 ? 256 : bn_hint ? bn_hint : gemm_pick_bn(kind, epi, g.m, g.n);
   CUtensorMap ma, mb, mo;
   memset(&mo, 0, sizeof(mo));
   int rc = make_operand_map(&ma, a, kind, g.m, g.k, kBM);
@@ -1237,12 +1243,14 @@ int gemm_launch(int kind, int epi, const void* a, const void* b, const GemmArgs&
   ga.cols_vec = g.n % 32 == 0 && (reinterpret_cast<uintptr_t>(g.col_scale) & 31) == 0 &&
                 (reinterpret_cast<uintptr_t>(g.bias) & 31) == 0;
   if (kind == kGemmI8) {
-    return bn == 256 ? dispatch_sb<kGemmI8, 256>(epi, ma, mb, mo, tma_out, ga, stream)
-                     : dispatch_sb<kGemmI8, 128>(epi, ma, mb, mo, tma_out, ga, stream);
+    return bn == 256   ? dispatch_sb<kGemmI8, 256>(epi, ma, mb, mo, tma_out, ga, stream)
+           : bn == 128 ? dispatch_sb<kGemmI8, 128>(epi, ma, mb, mo, tma_out, ga, stream)
+                       : dispatch_sb<kGemmI8, 64>(epi, ma, mb, mo, tma_out, ga, stream);
   }
   if (kind == kGemmBF16) {
-    return bn == 256 ? dispatch_sb<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, ga, stream)
-                     : dispatch_sb<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, ga, stream);
+    return bn == 256   ? dispatch_sb<kGemmBF16, 256>(epi, ma, mb, mo, tma_out, ga, stream)
+           : bn == 128 ? dispatch_sb<kGemmBF16, 128>(epi, ma, mb, mo, tma_out, ga, stream)
+                       : dispatch_sb<kGemmBF16, 64>(epi, ma, mb, mo, tma_out, ga, stream);
   }
   if (kind == kGemmMXF8) return dispatch_sb<kGemmMXF8, 128>(epi, ma, mb, mo, tma_out, ga, stream);
   set_error("GEMM kind not supported");

@@ -120,7 +120,7 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, long d
 
 // Columns per N tile chosen for a given N (the SwiGLU dual-weight packing
 // depends on it).
-int gemm_pick_bn(int kind, int epi, int n);
+int gemm_pick_bn(int kind, int epi, int m, int n);
 
 // Output decoding (decode.cu): decode n rows of packed raw heads into the
 // decoded layout, post-processed when `legal` is non-null.

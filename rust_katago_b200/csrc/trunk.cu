@@ -187,7 +187,7 @@ struct HeadWeights {
   const float* own_w;      // [192]
 };
 
-constexpr int kHeadThreads = 384;
+constexpr int kHeadThreads = 768;
 constexpr int kHeadWarps = kHeadThreads / 32;
 
 
@@ -201,21 +201,55 @@ __device__ __forceinline__ float warp_dot(const float* __restrict__ wrow, const 
   return a;
 }
 
-// One CTA (12 warps) per position.  hp: [B*361, 384] fp32 = [p1 | g1 + bias | v1 + bias].
-// Pass 1: warp w pools tokens w, w+12, ...; lane l owns float4 columns l,
-// l+32 and l+64 (< 72) of the 288 [g1 | v1] columns, so every row is read
-// coalesced; per-warp partial sums / maxima are combined in a fixed order.
-// Then the small matrix-vector products, one warp per output, and pass 2:
-// per token, lanes split the 96 p1 and 192 v1 channels and the 7 outputs
-// (6 policy moves, ownership) are warp reductions.
+// Four such dot products at once (rows w0 + r * stride, r < 4) over K floats,
+// K a multiple of 4: lane l reads the 16-byte pieces l, l + 32, ... of each
+// row, all four rows' loads in flight together (the products are
+// latency-bound, not bandwidth-bound).
+template <int K>
+__device__ __forceinline__ void warp_dot4(const float* __restrict__ w0, int stride, const float* vec, int lane,
+                                          float (&out)[4]) {
+  constexpr int kP = K / 4;             // 16-byte pieces per row
+  constexpr int kQ = (kP + 31) / 32;    // pieces per lane (the last one partial)
+  float4 wv[4][kQ];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < kQ; ++q)
+      wv[r][q] = lane + 32 * q < kP ? __ldg(reinterpret_cast<const float4*>(w0 + r * stride) + lane + 32 * q)
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    float a = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) {
+      if (lane + 32 * q >= kP) continue;
+      const float4 v = *reinterpret_cast<const float4*>(vec + 4 * (lane + 32 * q));
+      a = __fmaf_rn(wv[r][q].x, v.x, a);
+      a = __fmaf_rn(wv[r][q].y, v.y, a);
+      a = __fmaf_rn(wv[r][q].z, v.z, a);
+      a = __fmaf_rn(wv[r][q].w, v.w, a);
+    }
+    out[r] = a;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) out[r] += __shfl_xor_sync(0xffffffffu, out[r], o);
+}
+
+// One CTA of 24 warps per position.  Pass 1 pools the SiLU'd head activations
+// (two tokens per warp per step), the matrix-vector products run four outputs
+// per warp at a time, pass 2 computes each token's policy moves and ownership
+// (two tokens per warp per step): everything here is latency-bound, so the
+// work is arranged to keep many loads in flight per warp.
 __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __restrict__ hp, HeadWeights w,
                                                             float* __restrict__ policy, float* __restrict__ value,
                                                             float* __restrict__ misc, float* __restrict__ moremisc,
                                                             float* __restrict__ ownership, unsigned* status) {
   __shared__ float part_sum[kHeadWarps][288];
   __shared__ float part_max[kHeadWarps][96];
-  __shared__ float pooled_p[288];
-  __shared__ float pooled_v[576];
+  __shared__ __align__(16) float pooled_p[288];
+  __shared__ __align__(16) float pooled_v[576];
   __shared__ float gproj[96];
   __shared__ float pass1[96];
   __shared__ float vhid[192];
@@ -236,17 +270,29 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
     for (int i = 0; i < 12; ++i) sum[i] = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) mx[i] = __int_as_float(0xff800000);
-    for (int t = warp; t < kSeq; t += kHeadWarps) {
-      const float4* r4 = reinterpret_cast<const float4*>(rows + static_cast<size_t>(t) * 384 + 96);
+    for (int t0 = warp; t0 < kSeq; t0 += 2 * kHeadWarps) {
+      float4 v[2][3];
 #pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        if (q < nq) {
-          const float4 v = __ldg(r4 + lane + 32 * q);
-          const float a[4] = {silu_fast(v.x), silu_fast(v.y), silu_fast(v.z), silu_fast(v.w)};
+      for (int u = 0; u < 2; ++u) {
+        const int t = t0 + u * kHeadWarps;
+        const float4* r4 = reinterpret_cast<const float4*>(rows + static_cast<size_t>(t) * 384 + 96);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            sum[4 * q + e] += a[e];
-            if (q == 0) mx[e] = fmaxf(mx[e], a[e]);
+        for (int q = 0; q < 3; ++q)
+          v[u][q] = (t < kSeq && q < nq) ? __ldg(r4 + lane + 32 * q) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (t0 + u * kHeadWarps >= kSeq) continue;
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          if (q < nq) {
+            const float a[4] = {silu_fast(v[u][q].x), silu_fast(v[u][q].y), silu_fast(v[u][q].z),
+                                silu_fast(v[u][q].w)};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              sum[4 * q + e] += a[e];
+              if (q == 0) mx[e] = fmaxf(mx[e], a[e]);
+            }
           }
         }
       }
@@ -281,17 +327,28 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
     }
   }
   __syncthreads();
-  // ---- small matrix-vector products: outputs 0..95 gproj, 96..191 pass1, 192..383 v2
-  for (int o = warp; o < 384; o += kHeadWarps) {
-    if (o < 96) {
-      const float a = warp_dot(w.g_matmul + o * 288, pooled_p, 288, lane);
-      if (lane == 0) gproj[o] = a + w.bias2[o];
-    } else if (o < 192) {
-      const float a = warp_dot(w.pass1_w + (o - 96) * 288, pooled_p, 288, lane);
-      if (lane == 0) pass1[o - 96] = silu_fast(a + w.pass1_b[o - 96]);
+  // ---- matrix-vector products, four outputs per warp at a time: groups 0..23
+  // gproj, 24..47 pass1 (288 wide), 48..95 v2 (576 wide)
+  for (int grp = warp; grp < 96; grp += kHeadWarps) {
+    float a[4];
+    if (grp < 48) {
+      const bool gp = grp < 24;
+      const int o0 = 4 * (gp ? grp : grp - 24);
+      warp_dot4<288>((gp ? w.g_matmul : w.pass1_w) + o0 * 288, 288, pooled_p, lane, a);
+      if (lane < 4) {
+        const int o = o0 + lane;
+        const float x = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
+        if (gp) gproj[o] = x + w.bias2[o];
+        else pass1[o] = silu_fast(x + w.pass1_b[o]);
+      }
     } else {
-      const float a = warp_dot(w.v2_w + (o - 192) * 576, pooled_v, 576, lane);
-      if (lane == 0) vhid[o - 192] = silu_fast(a + w.v2_b[o - 192]);
+      const int o0 = 4 * (grp - 48);
+      warp_dot4<576>(w.v2_w + o0 * 576, 576, pooled_v, lane, a);
+      if (lane < 4) {
+        const int o = o0 + lane;
+        const float x = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
+        vhid[o] = silu_fast(x + w.v2_b[o]);
+      }
     }
   }
   __syncthreads();
@@ -324,7 +381,7 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
       }
     }
   }
-  // ---- pass 2: per token, policy moves (6) and ownership
+  // ---- pass 2: per token, policy moves (6) and ownership, two tokens per step
   {
     float gp[4], cw[6][4], ow[8];
     if (lane < 24)
@@ -339,47 +396,63 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const float* __rest
       ow[e] = ownw[4 * lane + e];
       ow[4 + e] = lane < 16 ? ownw[128 + 4 * lane + e] : 0.0f;
     }
-    for (int t = warp; t < kSeq; t += kHeadWarps) {
-      const float* r = rows + static_cast<size_t>(t) * 384;
-      float acc[7] = {0, 0, 0, 0, 0, 0, 0};
-      if (lane < 24) {
-        const float4 p = __ldg(reinterpret_cast<const float4*>(r) + lane);
-        const float pv[4] = {p.x, p.y, p.z, p.w};
+    for (int t0 = warp; t0 < kSeq; t0 += 2 * kHeadWarps) {
+      float4 pq[2], vq[2], uq[2];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float pa = silu_fast(pv[e] + gp[e]);
-#pragma unroll
-          for (int o = 0; o < 6; ++o) acc[o] = __fmaf_rn(pa, cw[o][e], acc[o]);
-        }
+      for (int u = 0; u < 2; ++u) {
+        const int t = t0 + u * kHeadWarps;
+        const float* r = rows + static_cast<size_t>(t < kSeq ? t : t0) * 384;
+        pq[u] = lane < 24 ? __ldg(reinterpret_cast<const float4*>(r) + lane) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        vq[u] = __ldg(reinterpret_cast<const float4*>(r + 192) + lane);
+        uq[u] = lane < 16 ? __ldg(reinterpret_cast<const float4*>(r + 320) + lane)
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
-      {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(r + 192) + lane);
-        acc[6] = __fmaf_rn(silu_fast(v.x), ow[0], acc[6]);
-        acc[6] = __fmaf_rn(silu_fast(v.y), ow[1], acc[6]);
-        acc[6] = __fmaf_rn(silu_fast(v.z), ow[2], acc[6]);
-        acc[6] = __fmaf_rn(silu_fast(v.w), ow[3], acc[6]);
+      float acc[2][7];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+#pragma unroll
+        for (int o = 0; o < 7; ++o) acc[u][o] = 0.0f;
+        if (lane < 24) {
+          const float pv[4] = {pq[u].x, pq[u].y, pq[u].z, pq[u].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float pa = silu_fast(pv[e] + gp[e]);
+#pragma unroll
+            for (int o = 0; o < 6; ++o) acc[u][o] = __fmaf_rn(pa, cw[o][e], acc[u][o]);
+          }
+        }
+        acc[u][6] = __fmaf_rn(silu_fast(vq[u].x), ow[0], acc[u][6]);
+        acc[u][6] = __fmaf_rn(silu_fast(vq[u].y), ow[1], acc[u][6]);
+        acc[u][6] = __fmaf_rn(silu_fast(vq[u].z), ow[2], acc[u][6]);
+        acc[u][6] = __fmaf_rn(silu_fast(vq[u].w), ow[3], acc[u][6]);
         if (lane < 16) {
-          const float4 u = __ldg(reinterpret_cast<const float4*>(r + 320) + lane);
-          acc[6] = __fmaf_rn(silu_fast(u.x), ow[4], acc[6]);
-          acc[6] = __fmaf_rn(silu_fast(u.y), ow[5], acc[6]);
-          acc[6] = __fmaf_rn(silu_fast(u.z), ow[6], acc[6]);
-          acc[6] = __fmaf_rn(silu_fast(u.w), ow[7], acc[6]);
+          acc[u][6] = __fmaf_rn(silu_fast(uq[u].x), ow[4], acc[u][6]);
+          acc[u][6] = __fmaf_rn(silu_fast(uq[u].y), ow[5], acc[u][6]);
+          acc[u][6] = __fmaf_rn(silu_fast(uq[u].z), ow[6], acc[u][6]);
+          acc[u][6] = __fmaf_rn(silu_fast(uq[u].w), ow[7], acc[u][6]);
         }
       }
 #pragma unroll
-      for (int o = 0; o < 7; ++o)
+      for (int sh = 16; sh > 0; sh >>= 1)
 #pragma unroll
-        for (int sh = 16; sh > 0; sh >>= 1) acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], sh);
-      if (lane < 6) {
-        float a = acc[0];
+        for (int u = 0; u < 2; ++u)
 #pragma unroll
-        for (int o = 1; o < 6; ++o)
-          if (lane == o) a = acc[o];
-        pol[lane * 362 + t] = a;
-        bad |= !isfinite(a);
-      } else if (lane == 6) {
-        ownership[static_cast<size_t>(b) * kSeq + t] = acc[6];
-        bad |= !isfinite(acc[6]);
+          for (int o = 0; o < 7; ++o) acc[u][o] += __shfl_xor_sync(0xffffffffu, acc[u][o], sh);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = t0 + u * kHeadWarps;
+        if (t >= kSeq) continue;
+        if (lane < 6) {
+          float a = acc[u][0];
+#pragma unroll
+          for (int o = 1; o < 6; ++o)
+            if (lane == o) a = acc[u][o];
+          pol[lane * 362 + t] = a;
+          bad |= !isfinite(a);
+        } else if (lane == 6) {
+          ownership[static_cast<size_t>(b) * kSeq + t] = acc[u][6];
+          bad |= !isfinite(acc[u][6]);
+        }
       }
     }
   }
