@@ -664,9 +664,14 @@ int launch_tc(const uint16_t* qkv, const float* cos_t, const float* sin_t, uint1
   const float scale_log2 = scale * 1.4426950408889634f;
   const int pairs = batch * heads;
   // Few pairs (small batches): one query tile per job, so the grid fills more
-  // SMs (each job loads its pair's K and V itself).
+  // SMs evenly (each job loads its pair's K and V itself).
   const int tiles = (seq + kTileQ - 1) / kTileQ;
-  const bool split = pairs < num_sms(dev);
+  // One tile per job when the pairs fill at most two rounds over the SMs and
+  // single tiles take fewer rounds than whole pairs (B = 1 and 16 with 12
+  // heads); larger batches keep one K / V load per pair.
+  const long sms = num_sms(dev);
+  const bool split = pairs < 2 * sms &&
+                     (static_cast<long>(pairs) * tiles + sms - 1) / sms < (pairs + sms - 1) / sms * tiles;
   const int jobs = pairs * (split ? tiles : 1);
   auto kern = split ? k_split : k_pairs;
   const int grid = jobs < num_sms(dev) ? jobs : num_sms(dev);
