@@ -294,3 +294,39 @@ def test_bf16_linear_matches_fp32(cuda, m, n, k):
     int8.bf16_linear(a, w, bias, m, n, k, _capi.EPI_16, out16, n, act=_capi.ACT_NONE)
     torch.cuda.synchronize()
     assert torch.equal(out16, out.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("m,n,k,ldo", [(300, 136, 64, 140), (4096, 136, 768, 144), (361, 72, 48, 76)])
+def test_f32_output_ragged_padded_rows(cuda, oracle, m, n, k, ldo):
+    """fp32 outputs through the staging tiles and TMA stores with N not a
+    multiple of 16 columns and a row stride above N: bitwise against the
+    oracle (16-bit GEMM + bias; INT8 dequant), and the padding columns of
+    every row keep their guard values."""
+    torch = cuda
+    rng = np.random.default_rng(m + n + k)
+    guard = np.float32(-7.25)
+    # 16-bit GEMM (binary16 operands) + bias
+    a = oracle.f16_encode(rng.standard_normal((m, k)).astype(np.float32))
+    w = oracle.f16_encode((0.05 * rng.standard_normal((n, k))).astype(np.float32))
+    bias = (0.1 * rng.standard_normal(n)).astype(np.float32)
+    out = torch.full((m, ldo), float(guard), device="cuda")
+    int8.f16_linear(torch.from_numpy(a.view(np.int16)).cuda(), torch.from_numpy(w.view(np.int16)).cuda(),
+                    torch.from_numpy(bias).cuda(), m, n, k, _capi.EPI_F32, out, ldo)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    ref = (oracle.tc_gemm16(a, w, f16=True) + bias[None, :]).astype(np.float32)
+    assert same_f32(got[:, :n], ref)
+    assert (got[:, n:] == guard).all()
+    # INT8 GEMM, fp32 dequant epilogue, no bias
+    kp = (k + 15) // 16 * 16
+    aq = rng.integers(-127, 128, (m, kp), dtype=np.int8)
+    wq = rng.integers(-127, 128, (n, kp), dtype=np.int8)
+    sa = (rng.random(m) * 0.01).astype(np.float32)
+    sw = (rng.random(n) * 0.01).astype(np.float32)
+    out2 = torch.full((m, ldo), float(guard), device="cuda")
+    int8.linear(dev(torch, aq), torch.from_numpy(sa).cuda(), dev(torch, wq), torch.from_numpy(sw).cuda(), None,
+                m, n, kp, _capi.EPI_F32, out2, ldo)
+    torch.cuda.synchronize()
+    got2 = out2.cpu().numpy()
+    assert same_f32(got2[:, :n], oracle.dequant(oracle.igemm(aq, wq), sa, sw))
+    assert (got2[:, n:] == guard).all()
