@@ -58,19 +58,19 @@ template <int IN, bool CHECK_WEIGHT>
 __global__ void __launch_bounds__(256)
     mxfp8_quantize_kernel(const void* __restrict__ src, long ld, int rows, int k, int kp, int blocks4,
                           int rows_pad, int vec, uint8_t* __restrict__ q, uint8_t* __restrict__ scales,
-                          unsigned* status, unsigned layer) {
-  const long per_row = static_cast<long>(blocks4) * 4;  // 8-element groups per padded row
-  const long total = static_cast<long>(rows_pad) * per_row;
+                          unsigned* status, unsigned layer, FastDiv per_row) {
+  // per_row.d = 8-element groups per padded row; rows_pad * per_row.d < 2^31
+  const uint32_t total = static_cast<uint32_t>(rows_pad) * per_row.d;
   const int lane = threadIdx.x & 31;
-  const long warp = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const long warps = (static_cast<long>(gridDim.x) * blockDim.x) >> 5;
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
   const int nblocks = kp >> 5;
   // Warp-uniform trip count: the quad shuffles below need all 32 lanes.
-  for (long base = warp * 32; base < total; base += warps * 32) {
-    const long gi = base + lane;
+  for (uint32_t base = warp * 32; base < total; base += warps * 32) {
+    const uint32_t gi = base + lane;
     const bool active = gi < total;
-    const int row = active ? static_cast<int>(gi / per_row) : 0;
-    const int grp = active ? static_cast<int>(gi - static_cast<long>(row) * per_row) : 0;
+    const int row = active ? static_cast<int>(per_row.div(gi)) : 0;
+    const int grp = active ? static_cast<int>(gi - static_cast<uint32_t>(row) * per_row.d) : 0;
     const int blk = grp >> 2;
     const int col0 = grp * 8;
     const bool live = active && row < rows && blk < nblocks;
@@ -132,16 +132,21 @@ template <int IN>
 int launch(const void* x, long ld, int rows, int k, int kp, int blocks4, int rows_pad, int vec, bool check_weight,
            uint8_t* q, uint8_t* scales, unsigned* status, unsigned layer, cudaStream_t stream) {
   const long total = static_cast<long>(rows_pad) * blocks4 * 4;
+  if (total >= (1L << 31)) {
+    set_error("mxfp8 quantiser: rows x padded width / 8 must be below 2^31");
+    return KB_E_INVALID;
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   const long want = (total + 255) / 256;
   const int grid = static_cast<int>(want < 8L * num_sms(dev) ? want : 8L * num_sms(dev));
+  const FastDiv per_row(static_cast<uint32_t>(blocks4) * 4u);
   if (check_weight)
     mxfp8_quantize_kernel<IN, true><<<grid, 256, 0, stream>>>(x, ld, rows, k, kp, blocks4, rows_pad, vec, q,
-                                                               scales, status, layer);
+                                                               scales, status, layer, per_row);
   else
     mxfp8_quantize_kernel<IN, false><<<grid, 256, 0, stream>>>(x, ld, rows, k, kp, blocks4, rows_pad, vec, q,
-                                                                scales, status, layer);
+                                                                scales, status, layer, per_row);
   return check_cuda(cudaGetLastError(), "mxfp8 quantiser launch");
 }
 
