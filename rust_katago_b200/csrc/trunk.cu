@@ -122,17 +122,21 @@ __device__ __forceinline__ uint4 tip8(uint4 raw, const float* __restrict__ gamma
 }
 
 __global__ void trunk_tip_kernel(const uint16_t* __restrict__ x, const float* __restrict__ gamma,
-                                 const float* __restrict__ beta, uint16_t* __restrict__ g, long total8, int c8) {
+                                 const float* __restrict__ beta, uint16_t* __restrict__ g, uint32_t total8,
+                                 FastDiv c8) {
+  // 32-bit vector indices (total8 < 2^31, checked on the host); the column
+  // of vector i is (i mod c8) * 8, by a multiply-shift division
   const uint4* x4 = reinterpret_cast<const uint4*>(x);
   uint4* g4 = reinterpret_cast<uint4*>(g);
-  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
-  long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  auto col = [&](uint32_t v) { return static_cast<int>(v - c8.div(v) * c8.d) * 8; };
   for (; i + stride < total8; i += 2 * stride) {
     const uint4 r0 = __ldg(x4 + i), r1 = __ldg(x4 + i + stride);
-    g4[i] = tip8(r0, gamma, beta, static_cast<int>(i % c8) * 8);
-    g4[i + stride] = tip8(r1, gamma, beta, static_cast<int>((i + stride) % c8) * 8);
+    g4[i] = tip8(r0, gamma, beta, col(i));
+    g4[i + stride] = tip8(r1, gamma, beta, col(i + stride));
   }
-  if (i < total8) g4[i] = tip8(__ldg(x4 + i), gamma, beta, static_cast<int>(i % c8) * 8);
+  if (i < total8) g4[i] = tip8(__ldg(x4 + i), gamma, beta, col(i));
 }
 
 // The nested trunk's gates (BN affine folded to scale/bias, then SiLU):
@@ -488,10 +492,16 @@ int trunk_tip_launch(const uint16_t* x, const float* gamma, const float* beta, u
     return KB_E_INVALID;
   }
   const long total8 = rows * c / 8;
+  if (total8 >= (1L << 30)) {  // i + stride stays below 2^31
+    set_error("trunk tip: rows * channels / 8 must be below 2^30");
+    return KB_E_INVALID;
+  }
+  if (total8 == 0) return KB_OK;
   int dev = 0;
   cudaGetDevice(&dev);
   const long want = (total8 + 255) / 256, cap = 8L * num_sms(dev);
-  trunk_tip_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(x, gamma, beta, g, total8, c / 8);
+  trunk_tip_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, s>>>(
+      x, gamma, beta, g, static_cast<uint32_t>(total8), FastDiv(static_cast<uint32_t>(c / 8)));
   return check_cuda(cudaGetLastError(), "trunk tip launch");
 }
 
