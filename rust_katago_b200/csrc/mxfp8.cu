@@ -23,9 +23,11 @@
 namespace kb {
 namespace {
 
+// Eight values of a row as floats; for 16-bit input also the raw packed
+// pairs (zero past k).
 template <int IN>
 __device__ __forceinline__ void load8(const void* src, long ld, int row, int col0, int k, bool vec,
-                                      float (&v)[8]) {
+                                      float (&v)[8], uint32_t (&raw)[4]) {
   if constexpr (IN == KB_DT_F32) {
     const float* p = static_cast<const float*>(src) + static_cast<size_t>(row) * ld + col0;
     if (vec) {
@@ -41,15 +43,19 @@ __device__ __forceinline__ void load8(const void* src, long ld, int row, int col
     constexpr bool f16 = IN == KB_DT_F16;
     if (vec) {
       const uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
-      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        v[2 * i] = from16(static_cast<uint16_t>(u[i] & 0xffffu), f16);
-        v[2 * i + 1] = from16(static_cast<uint16_t>(u[i] >> 16), f16);
-      }
+      raw[0] = w.x, raw[1] = w.y, raw[2] = w.z, raw[3] = w.w;
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = col0 + i < k ? from16(__ldg(p + i), f16) : 0.0f;
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = col0 + 2 * i < k ? __ldg(p + 2 * i) : 0u;
+        const uint32_t hi = col0 + 2 * i + 1 < k ? __ldg(p + 2 * i + 1) : 0u;
+        raw[i] = lo | (hi << 16);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = from16(static_cast<uint16_t>(raw[i] & 0xffffu), f16);
+      v[2 * i + 1] = from16(static_cast<uint16_t>(raw[i] >> 16), f16);
     }
   }
 }
@@ -75,22 +81,43 @@ __global__ void __launch_bounds__(256)
     const int col0 = grp * 8;
     const bool live = active && row < rows && blk < nblocks;
     float v[8];
+    uint32_t raw[4] = {0u, 0u, 0u, 0u};
     if (live && col0 < k) {
-      load8<IN>(src, ld, row, col0, k, vec != 0, v);
+      load8<IN>(src, ld, row, col0, k, vec != 0, v, raw);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = 0.0f;
     }
     unsigned bad = 0;
     float a = 0.0f;
+    // Non-finite values are flagged and zeroed; a = the largest finite |v|.
+    auto classify = [&]() {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t mag = __float_as_uint(v[i]) & 0x7fffffffu;
-      if (mag >= 0x7f800000u) {
-        bad |= mag > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF;
-        v[i] = 0.0f;
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t mag = __float_as_uint(v[i]) & 0x7fffffffu;
+        if (mag >= 0x7f800000u) {
+          bad |= mag > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF;
+          v[i] = 0.0f;
+        }
+        a = fmaxf(a, fabsf(v[i]));
       }
-      a = fmaxf(a, fabsf(v[i]));
+    };
+    if constexpr (IN == KB_DT_F32) {
+      classify();
+    } else {
+      // 16-bit input: the group's |max| from the packed pairs (one
+      // max.NaN.abs per pair; NaN wins), the per-value pass only for a
+      // group holding a NaN or an infinity.
+      constexpr bool f16 = IN == KB_DT_F16;
+      constexpr uint32_t inf16 = f16 ? 0x7c00u : 0x7f80u;
+      uint32_t m2 = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) m2 = hmax_abs2<f16>(m2, raw[i]);
+      const uint32_t m16 = max(m2 & 0x7fffu, (m2 >> 16) & 0x7fffu);
+      if (m16 >= inf16)
+        classify();
+      else
+        a = from16(static_cast<uint16_t>(m16), f16);
     }
     if (bad) record_status(status, bad, layer);
     unsigned any_bad = bad;
@@ -103,10 +130,12 @@ __global__ void __launch_bounds__(256)
     const float rcp = ue8m0_reciprocal(scale);
     uint32_t w0 = 0, w1 = 0;
     if (!zero) {
-      w0 = e4m3x2(__fmul_rn(v[0], rcp), __fmul_rn(v[1], rcp)) |
-           (e4m3x2(__fmul_rn(v[2], rcp), __fmul_rn(v[3], rcp)) << 16);
-      w1 = e4m3x2(__fmul_rn(v[4], rcp), __fmul_rn(v[5], rcp)) |
-           (e4m3x2(__fmul_rn(v[6], rcp), __fmul_rn(v[7], rcp)) << 16);
+      // (packed products feed only the conversions: nothing to contract)
+      float2 sv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sv[i] = mul2(make_float2(v[2 * i], v[2 * i + 1]), make_float2(rcp, rcp));
+      w0 = e4m3x2(sv[0].x, sv[0].y) | (e4m3x2(sv[1].x, sv[1].y) << 16);
+      w1 = e4m3x2(sv[2].x, sv[2].y) | (e4m3x2(sv[3].x, sv[3].y) << 16);
     }
     if constexpr (CHECK_WEIGHT) {
       // Static weights must decode to finite fp32 values (mxfp8.cu:62-65):
