@@ -8,8 +8,10 @@
 // to the 16-bit type, softmax of (q.k) * scale over all keys in fp32, P rounded
 // to the 16-bit type for the P.V product, output [tokens, C] heads merged.
 //
-// Persistent: one CTA per SM walks (position, head) pairs.  All 361 keys fit
-// on chip, so nothing streams inside a pair:
+// Persistent: one CTA per SM walks jobs, each a (position, head) pair with all
+// its query tiles, or, at small batch (SPLIT), one query tile of a pair, so the
+// grid fills more SMs.  All 361 keys fit on chip, so nothing streams inside a
+// job:
 //   shared memory  K and V of two pairs (double buffer, 368 keys x 2D bytes
 //                  each, keys padded to a multiple of 16) and one 128-query Q
 //                  tile, all in the UMMA swizzled layout (rows of 128 bytes
