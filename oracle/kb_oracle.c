@@ -131,17 +131,16 @@ float or_silu_exp(float x) {
 /* g / (1 + e^-g): the SiLU inside the reference's SwiGLU (int8_ops.cu:111-113). */
 float or_silu(float g) { return g / (1.0f + or_silu_exp(-g)); }
 
-/* GELU(x) = x * Phi(x): s = min(RN(x*x)*0.125 - 1 (fused), 1), P = the degree-10
- * polynomial of rust_katago_b200/gelu_fit.py in s (Horner, fused),
+/* GELU(x) = x * Phi(x): t = min(RN(x*x), 16), P = the degree-7 polynomial of
+ * rust_katago_b200/gelu_fit.py in t (Horner, fused),
  * Phi = saturate(fma(x, P, 0.5)) to [0, 1] with NaN -> 0 (the PTX .sat rule);
  * the same operation sequence as kb_gelu in the kernels. */
 float or_gelu(float x) {
-  static const float c[11] = {0x1.68585ap-3f, -0x1.5961f4p-4f, 0x1.ca3788p-5f, -0x1.2df2f6p-5f,
-                              0x1.70d728p-6f, -0x1.9ab164p-7f, 0x1.9a7b1cp-8f, -0x1.5eeeecp-9f,
-                              0x1.229b08p-10f, -0x1.31c494p-11f, 0x1.a02d8ap-13f};
-  const float s = fminf(fmaf(x * x, 0.125f, -1.0f), 1.0f);
-  float p = c[10];
-  for (int i = 9; i >= 0; --i) p = fmaf(p, s, c[i]);
+  static const float c[8] = {0x1.985bf8p-2f, -0x1.0eb09cp-4f, 0x1.3b2a38p-7f, -0x1.0fadb6p-10f,
+                             0x1.4b96f4p-14f, -0x1.0b18b6p-18f, 0x1.f68866p-24f, -0x1.9e1896p-30f};
+  const float t = fminf(x * x, 16.0f);
+  float p = c[7];
+  for (int i = 6; i >= 0; --i) p = fmaf(p, t, c[i]);
   float phi = fmaf(x, p, 0.5f);
   if (!(phi > 0.0f)) phi = 0.0f; /* negative, zero or NaN */
   if (phi > 1.0f) phi = 1.0f;

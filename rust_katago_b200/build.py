@@ -50,7 +50,8 @@ def nvcc() -> str:
 def _compile(src: Path, verbose: bool) -> Path:
     obj = BUILD / (src.stem + ".o")
     if obj.exists() and obj.stat().st_mtime >= max(
-        [src.stat().st_mtime] + [p.stat().st_mtime for p in CSRC.glob("*.h*")]
+        [src.stat().st_mtime]
+        + [p.stat().st_mtime for pat in ("*.h", "*.cuh") for p in CSRC.glob(pat)]
         + [p.stat().st_mtime for p in (PKG.parent / "include").glob("*.h")]
     ):
         return obj

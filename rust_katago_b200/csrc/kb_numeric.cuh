@@ -24,19 +24,20 @@ __device__ __forceinline__ uint32_t pack16x2(float2 v, bool f16) {
 
 
 // GELU(x) = x * Phi(x) with Phi the standard normal CDF:
-//   s   = min(x^2/8 - 1, 1)                      (rounded: RN(RN(x*x)*0.125 - 1))
-//   P   = degree-10 polynomial in s (Horner, fused multiply-adds)
+//   t   = min(x^2, 16)                           (rounded: RN(x*x))
+//   P   = degree-7 polynomial in t (Horner, fused multiply-adds)
 //   Phi = saturate(fma(x, P, 0.5)) to [0, 1]
-// P is the least-squares Chebyshev fit of 0.5*erf(sqrt(t/2))/sqrt(t) on
-// t = x^2 in [0, 16] (rust_katago_b200/gelu_fit.py).  For |x| <= 4 this is
-// 0.5 + x*P(x^2); beyond, s stays at 1 and the saturation pins Phi to 0 or 1
-// (exactly, once |x| exceeds 4 by 2e-4).  |error| <= 3.2e-5 * max(1, |x|).
-// NaN propagates (Phi = 0, x * 0 = NaN).  Only fused multiply-adds, one min
-// and a saturating FMA: no division, no exp, no compare-and-select.
-#define KB_GELU_COEFFS                                                                      \
-  0x1.68585ap-3f, -0x1.5961f4p-4f, 0x1.ca3788p-5f, -0x1.2df2f6p-5f, 0x1.70d728p-6f,        \
-      -0x1.9ab164p-7f, 0x1.9a7b1cp-8f, -0x1.5eeeecp-9f, 0x1.229b08p-10f, -0x1.31c494p-11f, \
-      0x1.a02d8ap-13f
+// P is the weighted minimax fit of 0.5*erf(sqrt(t/2))/sqrt(t) on t in
+// [0, 16], weight min(t, sqrt(t)), so that the GELU error relative to
+// max(1, |x|) is what is minimised (rust_katago_b200/gelu_fit.py).  For
+// |x| <= 4 this is 0.5 + x*P(x^2); beyond, t stays at 16 and the saturation
+// pins Phi to 0 or 1 (exactly, once |x| exceeds 4 by 2e-4).
+// |error| <= 3.2e-5 * max(1, |x|).  NaN propagates (t = 16, Phi = 0,
+// x * 0 = NaN).  Only fused multiply-adds, one min and a saturating FMA: no
+// division, no exp, no compare-and-select.
+#define KB_GELU_COEFFS                                                                       \
+  0x1.985bf8p-2f, -0x1.0eb09cp-4f, 0x1.3b2a38p-7f, -0x1.0fadb6p-10f, 0x1.4b96f4p-14f,        \
+      -0x1.0b18b6p-18f, 0x1.f68866p-24f, -0x1.9e1896p-30f
 
 __device__ __forceinline__ float fma_sat(float a, float b, float c) {
   float r;
@@ -45,11 +46,11 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
 }
 
 __device__ __forceinline__ float kb_gelu(float x) {
-  constexpr float c[11] = {KB_GELU_COEFFS};
-  const float s = fminf(__fmaf_rn(__fmul_rn(x, x), 0.125f, -1.0f), 1.0f);
-  float p = c[10];
+  constexpr float c[8] = {KB_GELU_COEFFS};
+  const float t = fminf(__fmul_rn(x, x), 16.0f);
+  float p = c[7];
 #pragma unroll
-  for (int i = 9; i >= 0; --i) p = __fmaf_rn(p, s, c[i]);
+  for (int i = 6; i >= 0; --i) p = __fmaf_rn(p, t, c[i]);
   return __fmul_rn(x, fma_sat(x, p, 0.5f));
 }
 
@@ -158,13 +159,13 @@ __device__ __forceinline__ float2 kb_silu2(float2 g) {
 
 // kb_gelu on a pair, bit-identical to two scalar calls.
 __device__ __forceinline__ float2 kb_gelu2(float2 x) {
-  constexpr float c[11] = {KB_GELU_COEFFS};
-  float2 s = fma2(mul2(x, x), make_float2(0.125f, 0.125f), make_float2(-1.0f, -1.0f));
-  s.x = fminf(s.x, 1.0f);
-  s.y = fminf(s.y, 1.0f);
-  float2 p = make_float2(c[10], c[10]);
+  constexpr float c[8] = {KB_GELU_COEFFS};
+  float2 t = mul2(x, x);
+  t.x = fminf(t.x, 16.0f);
+  t.y = fminf(t.y, 16.0f);
+  float2 p = make_float2(c[7], c[7]);
 #pragma unroll
-  for (int i = 9; i >= 0; --i) p = fma2(p, s, make_float2(c[i], c[i]));
+  for (int i = 6; i >= 0; --i) p = fma2(p, t, make_float2(c[i], c[i]));
   // (the packed FMA has no saturating form: two scalar saturating FMAs)
   return mul2(x, make_float2(fma_sat(x.x, p.x, 0.5f), fma_sat(x.y, p.y, 0.5f)));
 }
