@@ -678,6 +678,35 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       // the row scale is loaded while the accumulator is still being computed
       float sa = 1.0f;
       if constexpr (KIND == kGemmI8 && EPI != kEpiI32) sa = row_ok ? __ldg(g.row_scale + row) : 0.0f;
+      // Rotary tables (kEpiRope16) of the next kSub-column piece, loaded one
+      // piece ahead, the tile's first while the accumulator is being computed:
+      // they come from L2, and a piece of arithmetic covers most of that latency.
+      // (256-column tiles only: the narrower tiles' epilogues would spill with
+      // the second set of table registers, and load each piece's own tables.)
+      constexpr bool kRopeAhead = BN == 256;
+      float rc_n[kSub / 2], rs_n[kSub / 2];
+      auto rope_load = [&](int c0) {
+        if constexpr (EPI == kEpiRope16) {
+          if (row_ok && c0 < g.rope_cols) {
+            // [head * pairs + pair][token]: pair q of Q or K column cc (even)
+            // is entry cc / 2 + q; the warp's 32 rows are consecutive tokens,
+            // so each load reads one contiguous run.
+            const int half_cols = g.rope_cols / 2;
+            const int cc = c0 < half_cols ? c0 : c0 - half_cols;
+            const float* pc = g.rope_cos + static_cast<size_t>(cc / 2) * g.rope_seq + token;
+            const float* ps = g.rope_sin + static_cast<size_t>(cc / 2) * g.rope_seq + token;
+#pragma unroll
+            for (int i = 0; i < kSub / 2; ++i) {
+              rc_n[i] = __ldg(pc + static_cast<size_t>(i) * g.rope_seq);
+              rs_n[i] = __ldg(ps + static_cast<size_t>(i) * g.rope_seq);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < kSub / 2; ++i) rc_n[i] = 1.0f, rs_n[i] = 0.0f;
+          }
+        }
+      };
+      if constexpr (EPI == kEpiRope16 && kRopeAhead) rope_load(nb * BN + part * (BN / 32 / kParts) * 32);
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph, abort_flag, wlim))) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -779,27 +808,19 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
                 if constexpr (KIND == kGemmI8) load_vecn<kSub>(g.col_scale, c0, g.n, sw);
                 if (with_bias) load_vecn<kSub>(g.bias, c0, g.n, bias);
               }
-              // Rotary tables of these kSub / 2 pairs (kEpiRope16, Q and K columns).
+              // Rotary tables of these kSub / 2 pairs (kEpiRope16, Q and K
+              // columns; loaded one piece ahead), then the next piece's loads:
+              // the other half of this chunk, or the next chunk's first.
               float rc[kSub / 2], rs[kSub / 2];
               bool rope = false;
               if constexpr (EPI == kEpiRope16) {
                 rope = col0 < g.rope_cols;  // warp-uniform
-                if (rope && row_ok) {
-                  // [head * pairs + pair][token]: pair q of Q or K column cc
-                  // (even) is entry cc / 2 + q; the warp's 32 rows are
-                  // consecutive tokens, so each load reads one contiguous run.
-                  const int half_cols = g.rope_cols / 2;
-                  const int cc = c0 < half_cols ? c0 : c0 - half_cols;
-                  const float* pc = g.rope_cos + static_cast<size_t>(cc / 2) * g.rope_seq + token;
-                  const float* ps = g.rope_sin + static_cast<size_t>(cc / 2) * g.rope_seq + token;
+                if constexpr (!kRopeAhead) rope_load(c0);
 #pragma unroll
-                  for (int i = 0; i < kSub / 2; ++i) {
-                    rc[i] = __ldg(pc + static_cast<size_t>(i) * g.rope_seq);
-                    rs[i] = __ldg(ps + static_cast<size_t>(i) * g.rope_seq);
-                  }
-                } else {
-#pragma unroll
-                  for (int i = 0; i < kSub / 2; ++i) rc[i] = 1.0f, rs[i] = 0.0f;
+                for (int i = 0; i < kSub / 2; ++i) rc[i] = rc_n[i], rs[i] = rs_n[i];
+                if constexpr (kRopeAhead) {
+                  if (hh + 1 < kHalves) rope_load(c0 + kSub);
+                  else if (jj + 1 < kChunks) rope_load(col0 + 32);
                 }
               }
               tmem_ld_wait();
