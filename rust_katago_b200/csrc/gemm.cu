@@ -754,13 +754,18 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
             }
           }
           if (g.row_amax != nullptr) {  // warp-uniform
+            // Columns past the matrix edge (a partial chunk, warp-uniform) are
+            // zeroed first (the tensor store clips them anyway), so one
+            // max-of-|x| per pair covers every chunk; sign bits masked once.
+            if (valid < 32) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                hw[i] &= 2 * i + 1 < valid ? 0xffffffffu : (2 * i < valid ? 0x0000ffffu : 0u);
+            }
             uint32_t amax2 = 0;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const uint32_t mask = 2 * i + 1 < valid ? 0x7fff7fffu : (2 * i < valid ? 0x00007fffu : 0u);
-              amax2 = __vmaxu2(amax2, hw[i] & mask);
-            }
-            amax = max(amax, amax16_to_f32bits(amax2, true));
+            for (int i = 0; i < 16; ++i) amax2 = hmax_abs2<true>(amax2, hw[i]);
+            amax = max(amax, amax16_to_f32bits(amax2 & 0x7fff7fffu, true));
           }
           emit16<SB>(o, g, hw, row, row0q, ocol0, lane, row_ok, valid);
         }

@@ -415,41 +415,60 @@ __global__ void __launch_bounds__(256, G <= 4 ? 3 : 1) rms_rows16_kernel(
 // INT8 output: rms_rows16_kernel without any per-group bounds check, the
 // output type a template parameter, and the row's absolute maximum a packed
 // max(|a|, |b|) per pair (one instruction; NaN still wins, so a non-finite
-// row is classified as before).  Same arithmetic in the same order, so the
-// bytes and scales are identical to the generic kernel's.
+// row is classified as before).
+//
+// Two rows per warp: half-warp h = lane / 16 holds row 2w + h of warp w's
+// pair, lane l = lane % 16 the groups l + 16j (j < 2G).  The sum of squares
+// runs as the warp-per-row layout's lanes l and l + 16 run it: chain A over
+// groups l, l + 32, ... and chain B over l + 16, l + 48, ..., each in group
+// order, then A + B (the first step of the 32-lane xor butterfly, offset 16)
+// and the butterfly over offsets 8, 4, 2, 1 inside the half: the same
+// additions in the same order, so the bytes and scales are identical to the
+// generic kernel's.  The per-row work (both reductions, the correctly rounded
+// 1/sqrt, the scale and its reciprocal) is issued once for two rows.
 template <bool F16IN, bool F16OUT, int G>
-__global__ void __launch_bounds__(256, 3) rms_rows16_full_kernel(
+__global__ void __launch_bounds__(256, 2) rms_rows16_full_kernel(
     const uint16_t* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows,
     int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
   constexpr int kW = 256 * G;
+  constexpr int kJ = 2 * G;  // groups per lane
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int step = gridDim.x * 8;
-  int row = blockIdx.x * 8 + warp;
-  if (row >= rows) return;  // warp-uniform
-  uint4 raw[G];
+  const int half = lane >> 4, hl = lane & 15;
+  const int step = gridDim.x * 16;
+  int row0 = (blockIdx.x * 8 + warp) * 2;  // the pair's first row (warp-uniform)
+  if (row0 >= rows) return;
+  uint4 raw[kJ];
+  auto load = [&](int r) {
 #pragma unroll
-  for (int j = 0; j < G; ++j)
-    raw[j] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx + 8 * (lane + 32 * j)));
-  for (; row < rows; row += step) {
-    float v[G][8];
-    raw16_to_float<F16IN, G>(raw, v);
-    if (row + step < rows) {
-      const uint16_t* nxt = x + static_cast<size_t>(row + step) * ldx;
+    for (int j = 0; j < kJ; ++j)
+      raw[j] = r < rows ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * ldx + 8 * (hl + 16 * j)))
+                        : make_uint4(0, 0, 0, 0);
+  };
+  load(row0 + half);
+  for (; row0 < rows; row0 += step) {
+    const int row = row0 + half;
+    const bool ok = row < rows;
+    float v[kJ][8];
+    raw16_to_float<F16IN, kJ>(raw, v);
+    if (row0 + step < rows) load(row + step);
+    float sa = 0.0f, sb = 0.0f;
 #pragma unroll
-      for (int j = 0; j < G; ++j) raw[j] = __ldg(reinterpret_cast<const uint4*>(nxt + 8 * (lane + 32 * j)));
-    }
-    float sum = 0.0f;
+    for (int j = 0; j < kJ; j += 2)
 #pragma unroll
-    for (int j = 0; j < G; ++j)
+      for (int t = 0; t < 8; ++t) sa = __fmaf_rn(v[j][t], v[j][t], sa);
 #pragma unroll
-      for (int t = 0; t < 8; ++t) sum = __fmaf_rn(v[j][t], v[j][t], sum);
-    sum = warp_sum_xor(sum);
+    for (int j = 1; j < kJ; j += 2)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sb = __fmaf_rn(v[j][t], v[j][t], sb);
+    float sum = __fadd_rn(sa, sb);
+#pragma unroll
+    for (int o = 8; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
     const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(kW)), eps)));
-    uint32_t nw[G][4];
+    uint32_t nw[kJ][4];
     uint32_t amax2 = 0;
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const float4* gp = reinterpret_cast<const float4*>(gamma + 8 * (lane + 32 * j));
+    for (int j = 0; j < kJ; ++j) {
+      const float4* gp = reinterpret_cast<const float4*>(gamma + 8 * (hl + 16 * j));
       const float4 ga = __ldg(gp), gb = __ldg(gp + 1);
       const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
@@ -460,8 +479,31 @@ __global__ void __launch_bounds__(256, 3) rms_rows16_full_kernel(
         amax2 = hmax_abs2<F16OUT>(amax2, nw[j][t]);
       }
     }
-    quantize_packed_row<F16OUT, G>(nw, amax2 & 0x7fff7fffu, kW, lane, q + static_cast<size_t>(row) * kW,
-                                   scales + row, status, layer);
+    // The half's absolute maximum, its scale (quantize_packed_row's rule).
+    amax2 &= 0x7fff7fffu;
+    const uint32_t m16 = max(amax2 & 0xffffu, amax2 >> 16);
+    uint32_t amax = F16OUT ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16);
+#pragma unroll
+    for (int o = 8; o; o >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = int8_scale_from_amax(amax);
+    const bool bad = amax >= 0x7f800000u;
+    if (ok && hl == 0) {
+      scales[row] = scale;
+      if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+    }
+    if (!ok) continue;
+    int8_t* dst = q + static_cast<size_t>(row) * kW;
+    if (!bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u) {
+      const float r = __frcp_rn(scale);
+#pragma unroll
+      for (int j = 0; j < kJ; ++j)
+        *reinterpret_cast<uint2*>(dst + 8 * (hl + 16 * j)) = quant_group_fast<F16OUT>(nw[j], scale, r);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kJ; ++j)
+        quantize_group_slow(make_uint4(nw[j][0], nw[j][1], nw[j][2], nw[j][3]), F16OUT, scale, bad,
+                            dst + 8 * (hl + 16 * j));
+    }
   }
 }
 
@@ -474,7 +516,7 @@ int launch_rms16_full(bool f16in, bool f16out, const uint16_t* x, long ldx, cons
                        : (f16out ? rms_rows16_full_kernel<false, true, G> : rms_rows16_full_kernel<false, false, G>);
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
-  const int want = (rows + 7) / 8, cap = per_sm * num_sms(dev);
+  const int want = (rows + 15) / 16, cap = per_sm * num_sms(dev);  // two rows per warp
   k<<<want < cap ? want : cap, 256, 0, s>>>(x, ldx, gamma, eps, rows, q, scales, status, layer);
   return check_cuda(cudaGetLastError(), "rms quantiser launch");
 }
