@@ -603,9 +603,11 @@ static float exp2_poly(float x) {
  *   - P = exp2_poly(fma(s, c, -(m*c))) with c = fp32(scale * log2 e), in
  *     slices of 48 keys (the last slice of the second half has 32); keys past
  *     seq have P = 0;
- *   - the row sum l of each slice sums the unrounded P pairwise into four
- *     partial sums (pair i into i % 4), combined as (l0 + l1) + (l2 + l3);
- *     a half's l combines its four slices the same way;
+ *   - head dim 64: the row sum l of each slice sums the unrounded P pairwise
+ *     into four partial sums (pair i into i % 4), combined as
+ *     (l0 + l1) + (l2 + l3); a half's l combines its four slices the same way;
+ *     head dim 32: a half's l is P.1 on the tensor cores, the rounded P in
+ *     blocks of 16 keys (tc_block16), the accumulation O_h gets;
  *   - O_h = P.V of each half on the tensor cores, P rounded to the 16-bit type
  *     (f16 or bf16), blocks of 16 keys in key order (tc_block16);
  *   - out = 16-bit(O_A wa + O_B wb) with fa = 2^((m_A - m) c) (1 if m_A is the
@@ -619,6 +621,8 @@ void or_attention_tc(const uint16_t* qkv, int n, int seq, int heads, int hd, flo
   const size_t ld = 3 * (size_t)c;
   const float sl = scale * 1.4426950408889634f;
   const int kpad = 368, half_a = 192;
+  float ones[368]; /* the B operand of P.1 (head dim 32), read-only below */
+  for (int j = 0; j < kpad; ++j) ones[j] = 1.0f;
 #ifdef _OPENMP
 #pragma omp parallel for schedule(dynamic)
 #endif
@@ -664,7 +668,11 @@ void or_attention_tc(const uint16_t* qkv, int n, int seq, int heads, int hd, flo
           ls[sub] = (lp[0] + lp[1]) + (lp[2] + lp[3]);
         }
         m_h[hf] = m;
-        l_h[hf] = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        if (hd == 32) {
+          l_h[hf] = tc_dot(p16 + k0, ones, k1 - k0, f16);
+        } else {
+          l_h[hf] = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        }
       }
       const float mx = fmaxf(m_h[0], m_h[1]);
       const float fa = m_h[0] == mx ? 1.0f : exp2_poly((m_h[0] - mx) * sl);

@@ -20,7 +20,10 @@
 //                  staging warps that rotate on the way in);
 //   TMEM (512 col) S_A = Q K[0:192]^T (192 columns), S_B = Q K[192:368]^T (176),
 //                  O_A = P_A V[0:192] and O_B = P_B V[192:368] (D each), and
-//                  the 16 row sums of two tiles (16).
+//                  the row sums: for D = 64 the softmax's slice sums of two
+//                  tiles (16 columns); for D = 32 l_A = P_A . 1 and
+//                  l_B = P_B . 1 on the tensor cores (a 16-column MMA each
+//                  against a tile of ones: no per-score add in the softmax).
 // The two key halves keep their own maxima (no rescaling: the epilogue
 // combines them), so they form a two-stage pipeline.  All 16 softmax warps
 // (four per TMEM lane quarter, one query row per thread, 48 keys of each half
@@ -84,10 +87,19 @@ struct Geo {
   // tile parity, in 16 TMEM columns after O_B.
   static constexpr uint32_t kLCol = kOB + D;
   static_assert(kLCol + 16 <= kTmemCols, "TMEM budget");
+  // D = 32: each half's row sum comes from the tensor cores instead, P times a
+  // tile of ones (N = 16, all 16 columns equal) into LA / LB after O_B, so the
+  // softmax adds nothing per score; D = 64 has no TMEM room for the 32 columns.
+  static constexpr bool kMmaSums = D == 32;
+  static constexpr uint32_t kLA = kOB + D, kLB = kLA + 16;
+  static_assert(!kMmaSums || kLB + 16 <= kTmemCols, "TMEM budget");
+  // The ones tile: K-major without swizzle, two 8-row core matrices along N
+  // (256 bytes apart) by two along K (128 bytes apart), 512 bytes read.
+  static constexpr int kOnesBytes = kMmaSums ? 512 : 0;
   // K/V double buffer, one Q tile (loaded as soon as the previous tile's S MMAs
   // are done, several microseconds before it is needed), the output pieces.
   static constexpr int kSmemBytes =
-      2 * kKVBytes + kQBytes + kSoftWarps * kPieceBytes + kBarBytes + kMlBytes + 1024 /*alignment*/;
+      2 * kKVBytes + kQBytes + kSoftWarps * kPieceBytes + kBarBytes + kMlBytes + kOnesBytes + 1024 /*alignment*/;
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
@@ -201,9 +213,9 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint16_t* base, s
 // shared memory (mx: [slice][row] of this parity and half, barrier `mx_bar`
 // with 128 arrivals), then P = 2^((S - m) c) is written as packed 16-bit
 // pairs over columns [col, col + NK/2) (keys 2j, 2j+1 at column col + j:
-// columns this thread has already read), and the slice's row sum l to TMEM
-// column `lcol`.  Returns false if a wait gave up.
-template <int NK, bool F16>
+// columns this thread has already read), and (SUMS) the slice's row sum l to
+// TMEM column `lcol`.  Returns false if a wait gave up.
+template <int NK, bool F16, bool SUMS>
 __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, int valid, float scale_log2, float* mx,
                                               int sub, int row, uint64_t* mx_bar, uint32_t parity,
                                               volatile int* abort_flag, uint32_t lcol, float& m_out) {
@@ -245,7 +257,7 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
       const float2 x = fma2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
                             make_float2(scale_log2, scale_log2), make_float2(-mc, -mc));
       const float2 p = exp2_poly2(x.x, x.y);
-      lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p.x, p.y));
+      if constexpr (SUMS) lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p.x, p.y));
       pk[i] = pack2(p.x, p.y, F16);
     }
   } else {
@@ -255,13 +267,14 @@ __device__ __forceinline__ bool softmax_slice(uint32_t lane_base, uint32_t col, 
                                   __fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -mc));
       const float p0 = 2 * i < valid ? e.x : 0.0f;
       const float p1 = 2 * i + 1 < valid ? e.y : 0.0f;
-      lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p0, p1));
+      if constexpr (SUMS) lp[i & 3] = __fadd_rn(lp[i & 3], __fadd_rn(p0, p1));
       pk[i] = pack2(p0, p1, F16);
     }
   }
   tmem_st16(lane_base + col, *reinterpret_cast<const uint32_t(*)[16]>(pk));
   if constexpr (NK == 48) tmem_st8(lane_base + col + 16, *reinterpret_cast<const uint32_t(*)[8]>(pk + 16));
-  tmem_st1(lane_base + lcol, __float_as_uint(__fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3]))));
+  if constexpr (SUMS)
+    tmem_st1(lane_base + lcol, __float_as_uint(__fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3]))));
   tmem_st_wait();
   tc_fence_before();
   return true;
@@ -301,6 +314,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* mx_ex = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][2][4][128]
+  uint8_t* ones_buf = reinterpret_cast<uint8_t*>(bars) + kBarBytes + kMlBytes;  // D = 32: B of P . 1
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = heads * D;
@@ -336,6 +350,12 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
+  }
+  if constexpr (G::kMmaSums) {
+    const uint32_t one2 = F16 ? 0x3c003c00u : 0x3f803f80u;  // 1.0 in both 16-bit halves
+    for (int i = threadIdx.x; i < G::kOnesBytes / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(ones_buf)[i] = make_uint4(one2, one2, one2, one2);
+    fence_proxy_async_smem();  // visible to the tensor cores after the barrier
   }
   tc_fence_before();
   __syncthreads();
@@ -435,6 +455,8 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       const uint32_t id_sa = id_common | (static_cast<uint32_t>(kHalfA >> 3) << 17);
       const uint32_t id_sb = id_common | (static_cast<uint32_t>(kHalfB >> 3) << 17);
       const uint32_t id_pv = id_common | (1u << 16) /* B MN-major */ | (static_cast<uint32_t>(D >> 3) << 17);
+      // P . 1 (D = 32): B K-major, N = 16, the ones tile (built where used)
+      constexpr uint32_t kIdOnesN = static_cast<uint32_t>(16 >> 3) << 17;
       constexpr uint64_t kHalfOff = (kHalfA * kRowBytes) >> 4;  // 192 rows, descriptor units
       constexpr uint64_t kStep16 = (16 * kRowBytes) >> 4;       // 16 keys of V along K
       const int my_jobs = blockIdx.x < jobs ? (jobs - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
@@ -473,6 +495,10 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         // its own S columns 48(i/3).., two keys per column.
         for (int i = 0; i < kHalfA / 16; ++i)
           mma_f16_ts(tmem + kOA, tmem + 48 * (i / 3) + 8 * (i % 3), vdesc + kStep16 * i, id_pv, i != 0);
+        if constexpr (G::kMmaSums)  // l_A = P_A . 1, the same 16-key accumulation steps as O_A
+          for (int i = 0; i < kHalfA / 16; ++i)
+            mma_f16_ts(tmem + G::kLA, tmem + 48 * (i / 3) + 8 * (i % 3),
+                       noswizzle_desc(smem_u32(ones_buf), 128, 256), id_common | kIdOnesN, i != 0);
         tc_commit(pva_done);
         if (g + 1 < n && (!mbar_wait(pva_done, g & 1, abort_flag) || !issue_sa(g + 1))) break;
         if (!mbar_wait(pb_full, g & 1, abort_flag)) break;
@@ -480,6 +506,10 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         for (int i = 0; i < kHalfB / 16; ++i)
           mma_f16_ts(tmem + kOB, tmem + kSB + 48 * (i / 3) + 8 * (i % 3), vdesc + kHalfOff + kStep16 * i, id_pv,
                      i != 0);
+        if constexpr (G::kMmaSums)
+          for (int i = 0; i < kHalfB / 16; ++i)
+            mma_f16_ts(tmem + G::kLB, tmem + kSB + 48 * (i / 3) + 8 * (i % 3),
+                       noswizzle_desc(smem_u32(ones_buf), 128, 256), id_common | kIdOnesN, i != 0);
         tc_commit(o_full);
         if (g % tpj == tpj - 1) tc_commit(&kv_empty[kb]);
         if (g + 1 < n) {
@@ -510,7 +540,12 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       tc_fence_after();
       uint32_t lv[8], oa[kDW], ob[kDW], w[kDW / 2];
       const int dim0 = sub * kDW;
-      tmem_ld8(lane_base + kLCol + (pg & 1) * 8, lv);
+      if constexpr (G::kMmaSums) {
+        tmem_ld1(lane_base + G::kLA, lv[0]);
+        tmem_ld1(lane_base + G::kLB, lv[1]);
+      } else {
+        tmem_ld8(lane_base + kLCol + (pg & 1) * 8, lv);
+      }
       if constexpr (kDW == 16) {
         tmem_ld16(lane_base + kOA + dim0, oa);
         tmem_ld16(lane_base + kOB + dim0, ob);
@@ -521,10 +556,16 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(o_free);
-      const float la = __fadd_rn(__fadd_rn(__uint_as_float(lv[0]), __uint_as_float(lv[1])),
-                                 __fadd_rn(__uint_as_float(lv[2]), __uint_as_float(lv[3])));
-      const float lb = __fadd_rn(__fadd_rn(__uint_as_float(lv[4]), __uint_as_float(lv[5])),
-                                 __fadd_rn(__uint_as_float(lv[6]), __uint_as_float(lv[7])));
+      float la, lb;
+      if constexpr (G::kMmaSums) {
+        la = __uint_as_float(lv[0]);
+        lb = __uint_as_float(lv[1]);
+      } else {
+        la = __fadd_rn(__fadd_rn(__uint_as_float(lv[0]), __uint_as_float(lv[1])),
+                       __fadd_rn(__uint_as_float(lv[2]), __uint_as_float(lv[3])));
+        lb = __fadd_rn(__fadd_rn(__uint_as_float(lv[4]), __uint_as_float(lv[5])),
+                       __fadd_rn(__uint_as_float(lv[6]), __uint_as_float(lv[7])));
+      }
       const float mx = fmaxf(pma, pmb);
       const float2 fab = exp2_poly2(__fmul_rn(__fsub_rn(pma, mx), scale_log2), __fmul_rn(__fsub_rn(pmb, mx), scale_log2));
       const float fa = pma == mx ? 1.0f : fab.x;
@@ -587,7 +628,7 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         }
         tc_fence_after();
         float ma;
-        if (!softmax_slice<48, F16>(lane_base, col_a, valid_a, scale_log2, mxg, sub, row, &mx_full[quarter],
+        if (!softmax_slice<48, F16, !G::kMmaSums>(lane_base, col_a, valid_a, scale_log2, mxg, sub, row, &mx_full[quarter],
                                     g & 1, abort_flag, lcol + sub, ma)) {
           ok = false;
           break;
@@ -604,10 +645,10 @@ __global__ void __launch_bounds__(fa_threads<ROPE>(), 1) attention_fa_kernel(
         }
         tc_fence_after();
         float mb;
-        const bool done = sub == 3 ? softmax_slice<32, F16>(lane_base, col_b, valid_b, scale_log2, mxg + 4 * kTileQ,
+        const bool done = sub == 3 ? softmax_slice<32, F16, !G::kMmaSums>(lane_base, col_b, valid_b, scale_log2, mxg + 4 * kTileQ,
                                                             sub, row, &mx_full[4 + quarter], g & 1, abort_flag,
                                                             lcol + 4 + sub, mb)
-                                   : softmax_slice<48, F16>(lane_base, col_b, valid_b, scale_log2, mxg + 4 * kTileQ,
+                                   : softmax_slice<48, F16, !G::kMmaSums>(lane_base, col_b, valid_b, scale_log2, mxg + 4 * kTileQ,
                                                             sub, row, &mx_full[4 + quarter], g & 1, abort_flag,
                                                             lcol + 4 + sub, mb);
         if (!done) {

@@ -247,6 +247,18 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 // The same for 64-byte rows with the 64-byte swizzle, 8-row core groups 512
 // bytes apart (a TMA SWIZZLE_64B load of a {64 B, rows} box); also the
 // MN-major layout of a [K rows, 32 x 16-bit] operand (one swizzle atom wide).
+// UMMA shared-memory descriptor without swizzle (K-major core matrices of
+// 8 rows x 16 bytes; `lbo`: bytes between core matrices along K, `sbo`: along
+// M/N).
+__device__ __forceinline__ uint64_t noswizzle_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>(lbo >> 4) << 16;           // leading offset
+  d |= static_cast<uint64_t>(sbo >> 4) << 32;           // stride offset
+  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version for sm_100
+  return d;                                             // layout type 0: no swizzle
+}
+
 __device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address
@@ -358,6 +370,10 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
+}
+// One 32-bit TMEM column of 32 lanes -> one register per thread.
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t& r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
 }
 // One 32-bit TMEM column of 32 lanes <- one register per thread.
 __device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t r) {

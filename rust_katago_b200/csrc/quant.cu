@@ -630,11 +630,141 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
   }
 }
 
+// fp32 rows of exactly 128*J columns (J <= 4; kp == width; rows, stride and
+// gamma 16-byte aligned) through RMSNorm -> 16-bit boundary -> INT8: two rows
+// per warp, persistent, the next pair's rows loaded while this pair is
+// quantised.  Half-warp h = lane / 16 holds row 2w + h of warp w's pair, lane
+// l = lane % 16 the groups l + 16k (k < J), so every lane carries J groups
+// (the warp-per-row layout leaves lanes idle whenever 32 does not divide the
+// row's groups: at 384 columns lanes 16..31 hold one group, lanes 0..15 two).
+// The sum of squares is the warp-per-row layout's, bit for bit: that layout's
+// lane l holds groups l, l + 32, ... (even k here) and lane l + 16 groups
+// l + 16, l + 48, ... (odd k); each chain runs in group order, then A + B is
+// the butterfly's offset-16 step and offsets 8, 4, 2, 1 stay inside the half.
+// Normalisation, the row maximum and the quantisation are per element, the
+// scale per row, so bytes and scales equal quantize_rows_kernel's.
+template <bool F16OUT, int J>
+__global__ void __launch_bounds__(256, 2) rms_rows32_pair_kernel(
+    const float* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows,
+    int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
+  constexpr int kW = 128 * J;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, hl = lane & 15;
+  const int step = gridDim.x * 16;
+  int row0 = (blockIdx.x * 8 + warp) * 2;  // the pair's first row (warp-uniform)
+  if (row0 >= rows) return;
+  float4 raw[J][2];
+  auto load = [&](int r) {
+#pragma unroll
+    for (int k = 0; k < J; ++k) {
+      if (r < rows) {
+        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * ldx + 8 * (hl + 16 * k));
+        raw[k][0] = __ldg(src);
+        raw[k][1] = __ldg(src + 1);
+      } else {
+        raw[k][0] = raw[k][1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    }
+  };
+  load(row0 + half);
+  for (; row0 < rows; row0 += step) {
+    const int row = row0 + half;
+    const bool ok = row < rows;
+    float v[J][8];
+#pragma unroll
+    for (int k = 0; k < J; ++k) {
+      v[k][0] = raw[k][0].x, v[k][1] = raw[k][0].y, v[k][2] = raw[k][0].z, v[k][3] = raw[k][0].w;
+      v[k][4] = raw[k][1].x, v[k][5] = raw[k][1].y, v[k][6] = raw[k][1].z, v[k][7] = raw[k][1].w;
+    }
+    if (row0 + step < rows) load(row + step);
+    float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+    for (int k = 0; k < J; k += 2)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sa = __fmaf_rn(v[k][t], v[k][t], sa);
+#pragma unroll
+    for (int k = 1; k < J; k += 2)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sb = __fmaf_rn(v[k][t], v[k][t], sb);
+    float sum = __fadd_rn(sa, sb);
+#pragma unroll
+    for (int o = 8; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(kW)), eps)));
+    uint32_t nw[J][4];
+    uint32_t amax2 = 0;
+#pragma unroll
+    for (int k = 0; k < J; ++k) {
+      const float4* gp = reinterpret_cast<const float4*>(gamma + 8 * (hl + 16 * k));
+      const float4 ga = __ldg(gp), gb = __ldg(gp + 1);
+      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 n2 = mul2(mul2(make_float2(v[k][2 * t], v[k][2 * t + 1]), make_float2(rstd, rstd)),
+                               make_float2(gm[2 * t], gm[2 * t + 1]));
+        nw[k][t] = pack16x2(n2, F16OUT);
+        amax2 = hmax_abs2<F16OUT>(amax2, nw[k][t]);
+      }
+    }
+    amax2 &= 0x7fff7fffu;
+    const uint32_t m16 = max(amax2 & 0xffffu, amax2 >> 16);
+    uint32_t amax = F16OUT ? __float_as_uint(from_f16(static_cast<uint16_t>(m16))) : (m16 << 16);
+#pragma unroll
+    for (int o = 8; o; o >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = int8_scale_from_amax(amax);
+    const bool bad = amax >= 0x7f800000u;
+    if (ok && hl == 0) {
+      scales[row] = scale;
+      if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+    }
+    if (!ok) continue;
+    int8_t* dst = q + static_cast<size_t>(row) * kW;
+    if (!bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u) {
+      const float r = __frcp_rn(scale);
+#pragma unroll
+      for (int k = 0; k < J; ++k)
+        *reinterpret_cast<uint2*>(dst + 8 * (hl + 16 * k)) = quant_group_fast<F16OUT>(nw[k], scale, r);
+    } else {
+#pragma unroll
+      for (int k = 0; k < J; ++k)
+        quantize_group_slow(make_uint4(nw[k][0], nw[k][1], nw[k][2], nw[k][3]), F16OUT, scale, bad,
+                            dst + 8 * (hl + 16 * k));
+    }
+  }
+}
+
+template <int J>
+int launch_rms32_pair(bool f16out, const float* x, long ldx, const float* gamma, float eps, int rows, int8_t* q,
+                      float* scales, unsigned* status, unsigned layer, cudaStream_t s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto k = f16out ? rms_rows32_pair_kernel<true, J> : rms_rows32_pair_kernel<false, J>;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+  const int want = (rows + 15) / 16, cap = per_sm * num_sms(dev);  // two rows per warp
+  k<<<want < cap ? want : cap, 256, 0, s>>>(x, ldx, gamma, eps, rows, q, scales, status, layer);
+  return check_cuda(cudaGetLastError(), "rms quantiser launch");
+}
+
 template <int IN, bool RMS, int G>
 int launch_g(const void* x, long ldx, const float* gamma, float eps, int rows, int width, int kp,
              int bound_f16, int8_t* q, float* scales, unsigned* status, unsigned layer, cudaStream_t s) {
   if constexpr (RMS && IN != kInF32)
     return launch_rms16<false, G>(IN, x, ldx, gamma, eps, rows, width, kp, 0, bound_f16, q, scales, status, layer, s);
+  if constexpr (RMS && IN == kInF32 && G <= 2) {
+    // full fp32 rows of 128, 256, 384 or 512 columns: the two-rows-per-warp kernel
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx & 3) == 0 &&
+                         (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 7) == 0;
+    if (aligned && kp == width && width % 128 == 0) {
+      const float* xf = static_cast<const float*>(x);
+      switch (width / 128) {
+        case 1: return launch_rms32_pair<1>(bound_f16 != 0, xf, ldx, gamma, eps, rows, q, scales, status, layer, s);
+        case 2: return launch_rms32_pair<2>(bound_f16 != 0, xf, ldx, gamma, eps, rows, q, scales, status, layer, s);
+        case 3: return launch_rms32_pair<3>(bound_f16 != 0, xf, ldx, gamma, eps, rows, q, scales, status, layer, s);
+        case 4: return launch_rms32_pair<4>(bound_f16 != 0, xf, ldx, gamma, eps, rows, q, scales, status, layer, s);
+        default: break;
+      }
+    }
+  }
   quantize_rows_kernel<IN, RMS, G><<<(rows + 7) / 8, 256, 0, s>>>(x, ldx, gamma, eps, rows, width, kp,
                                                                   bound_f16, q, scales, status, layer);
   return check_cuda(cudaGetLastError(), "quantiser launch");

@@ -109,10 +109,13 @@ def rms_input(rows, mid):
     return v.astype(np.float32).reshape(rows, mid)
 
 
-@pytest.mark.parametrize("rows,mid", [(1, 384), (361, 512), (1025, 384), (2888, 512), (23104, 768)])
+@pytest.mark.parametrize("rows,mid", [(1, 384), (361, 512), (1025, 384), (2888, 512), (23104, 768), (17, 128),
+                                      (33, 256)])
 @pytest.mark.parametrize("boundary", [_capi.DT_F16, _capi.DT_BF16])
 @pytest.mark.parametrize("nonfinite", [False, True])
 def test_rms_quantize_bit_exact(cuda, oracle, rows, mid, boundary, nonfinite):
+    """fp32 rows: widths of 128..512 columns take the two-rows-per-warp kernel,
+    768 the warp-per-row one; zero, tiny, huge and non-finite rows."""
     torch = cuda
     x = rms_input(rows, mid)
     if nonfinite:
