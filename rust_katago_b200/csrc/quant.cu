@@ -426,6 +426,10 @@ __global__ void __launch_bounds__(256, G <= 4 ? 3 : 1) rms_rows16_kernel(
 // additions in the same order, so the bytes and scales are identical to the
 // generic kernel's.  The per-row work (both reductions, the correctly rounded
 // 1/sqrt, the scale and its reciprocal) is issued once for two rows.
+// Row count from which the two-rows-per-warp RMS quantisers are used (below it,
+// a few positions' rows, one row per warp keeps more warps on the short pass).
+constexpr int kPairRows = 2048;
+
 template <bool F16IN, bool F16OUT, int G>
 __global__ void __launch_bounds__(256, 2) rms_rows16_full_kernel(
     const uint16_t* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows,
@@ -507,16 +511,70 @@ __global__ void __launch_bounds__(256, 2) rms_rows16_full_kernel(
   }
 }
 
+// The same rows one per warp (lane l holds groups l, l + 32, ...), for small
+// row counts (a batch of a few positions), where two rows per warp would halve
+// the warps on the critical path; bit-identical to the pair kernel above.
+template <bool F16IN, bool F16OUT, int G>
+__global__ void __launch_bounds__(256, 3) rms_rows16_row_kernel(
+    const uint16_t* __restrict__ x, long ldx, const float* __restrict__ gamma, float eps, int rows,
+    int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
+  constexpr int kW = 256 * G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int step = gridDim.x * 8;
+  int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;  // warp-uniform
+  uint4 raw[G];
+#pragma unroll
+  for (int j = 0; j < G; ++j)
+    raw[j] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx + 8 * (lane + 32 * j)));
+  for (; row < rows; row += step) {
+    float v[G][8];
+    raw16_to_float<F16IN, G>(raw, v);
+    if (row + step < rows) {
+      const uint16_t* nxt = x + static_cast<size_t>(row + step) * ldx;
+#pragma unroll
+      for (int j = 0; j < G; ++j) raw[j] = __ldg(reinterpret_cast<const uint4*>(nxt + 8 * (lane + 32 * j)));
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < G; ++j)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sum = __fmaf_rn(v[j][t], v[j][t], sum);
+    sum = warp_sum_xor(sum);
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(kW)), eps)));
+    uint32_t nw[G][4];
+    uint32_t amax2 = 0;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const float4* gp = reinterpret_cast<const float4*>(gamma + 8 * (lane + 32 * j));
+      const float4 ga = __ldg(gp), gb = __ldg(gp + 1);
+      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 n2 = mul2(mul2(make_float2(v[j][2 * t], v[j][2 * t + 1]), make_float2(rstd, rstd)),
+                               make_float2(gm[2 * t], gm[2 * t + 1]));
+        nw[j][t] = pack16x2(n2, F16OUT);
+        amax2 = hmax_abs2<F16OUT>(amax2, nw[j][t]);
+      }
+    }
+    quantize_packed_row<F16OUT, G>(nw, amax2 & 0x7fff7fffu, kW, lane, q + static_cast<size_t>(row) * kW,
+                                   scales + row, status, layer);
+  }
+}
+
 template <int G>
 int launch_rms16_full(bool f16in, bool f16out, const uint16_t* x, long ldx, const float* gamma, float eps, int rows,
                       int8_t* q, float* scales, unsigned* status, unsigned layer, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto k = f16in ? (f16out ? rms_rows16_full_kernel<true, true, G> : rms_rows16_full_kernel<true, false, G>)
-                       : (f16out ? rms_rows16_full_kernel<false, true, G> : rms_rows16_full_kernel<false, false, G>);
+  const bool pair = rows >= kPairRows;
+  const auto k = pair ? (f16in ? (f16out ? rms_rows16_full_kernel<true, true, G> : rms_rows16_full_kernel<true, false, G>)
+                               : (f16out ? rms_rows16_full_kernel<false, true, G> : rms_rows16_full_kernel<false, false, G>))
+                      : (f16in ? (f16out ? rms_rows16_row_kernel<true, true, G> : rms_rows16_row_kernel<true, false, G>)
+                               : (f16out ? rms_rows16_row_kernel<false, true, G> : rms_rows16_row_kernel<false, false, G>));
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
-  const int want = (rows + 15) / 16, cap = per_sm * num_sms(dev);  // two rows per warp
+  const int want = pair ? (rows + 15) / 16 : (rows + 7) / 8, cap = per_sm * num_sms(dev);
   k<<<want < cap ? want : cap, 256, 0, s>>>(x, ldx, gamma, eps, rows, q, scales, status, layer);
   return check_cuda(cudaGetLastError(), "rms quantiser launch");
 }
@@ -754,7 +812,7 @@ int launch_g(const void* x, long ldx, const float* gamma, float eps, int rows, i
     // full fp32 rows of 128, 256, 384 or 512 columns: the two-rows-per-warp kernel
     const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx & 3) == 0 &&
                          (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 7) == 0;
-    if (aligned && kp == width && width % 128 == 0) {
+    if (aligned && kp == width && width % 128 == 0 && rows >= kPairRows) {
       const float* xf = static_cast<const float*>(x);
       switch (width / 128) {
         case 1: return launch_rms32_pair<1>(bound_f16 != 0, xf, ldx, gamma, eps, rows, q, scales, status, layer, s);

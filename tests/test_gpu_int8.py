@@ -136,12 +136,13 @@ def test_rms_quantize_bit_exact(cuda, oracle, rows, mid, boundary, nonfinite):
 @pytest.mark.parametrize("mid,stride", [(256, 256), (512, 512), (768, 768), (1024, 1024), (768, 776), (384, 384)])
 @pytest.mark.parametrize("dtype", [_capi.DT_BF16, _capi.DT_F16])
 @pytest.mark.parametrize("boundary", [_capi.DT_F16, _capi.DT_BF16])
-def test_rms_quantize_16bit_input_bit_exact(cuda, oracle, mid, stride, dtype, boundary):
+@pytest.mark.parametrize("rows", [3001, 361])
+def test_rms_quantize_16bit_input_bit_exact(cuda, oracle, mid, stride, dtype, boundary, rows):
     """16-bit residual rows (the trunk's case): full rows of 256*G columns take
-    the kernel without bounds checks, other widths and strides the generic one;
-    both against the oracle, with zero, tiny, huge and non-finite rows."""
+    the kernels without bounds checks (two rows per warp from 2048 rows, one
+    below), other widths and strides the generic one; all against the oracle,
+    with zero, tiny, huge and non-finite rows."""
     torch = cuda
-    rows = 3001
     x = np.zeros((rows, stride), np.float32)
     x[:, :mid] = rms_input(rows, mid)
     x[0, 0], x[1, 3], x[2, mid - 1] = np.inf, np.nan, -np.inf
