@@ -905,6 +905,67 @@ __global__ void __launch_bounds__(256) quantize_rows_amax_kernel(
   }
 }
 
+// Rows of exactly 128*J columns (J <= 3, kp == width) from kPairRows rows on,
+// two rows per warp: half-warp h holds row 2w + h, lane l = lane % 16 the
+// groups l + 16k (k < J).  At 384 columns every lane then carries three
+// groups, where one row per warp leaves lanes 16..31 with one and lanes 0..15
+// with two.  Per element the same quantisation as quantize_rows_amax_kernel,
+// the scale once per row (no reduction: the producer supplied the maximum).
+template <bool F16, int J>
+__global__ void __launch_bounds__(256) quantize_rows_amax_pair_kernel(
+    const uint16_t* __restrict__ x, long ldx, const uint32_t* __restrict__ row_amax, int rows,
+    int8_t* __restrict__ q, float* __restrict__ scales, unsigned* status, unsigned layer) {
+  constexpr int kW = 128 * J;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, hl = lane & 15;
+  const int step = gridDim.x * 16;
+  for (int row = (blockIdx.x * 8 + warp) * 2 + half; row - half < rows; row += step) {
+    if (row >= rows) continue;  // the halves never exchange data
+    const uint16_t* src = x + static_cast<size_t>(row) * ldx;
+    uint32_t w[J][4];
+#pragma unroll
+    for (int k = 0; k < J; ++k) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(src + 8 * (hl + 16 * k)));
+      w[k][0] = a.x; w[k][1] = a.y; w[k][2] = a.z; w[k][3] = a.w;
+    }
+    const uint32_t amax = __ldg(row_amax + row);
+    const float scale = int8_scale_from_amax(amax);
+    const bool bad = amax >= 0x7f800000u;
+    if (hl == 0) {
+      scales[row] = scale;
+      if (bad) record_status(status, amax > 0x7f800000u ? KB_STATUS_NAN : KB_STATUS_INF, layer);
+    }
+    int8_t* dst = q + static_cast<size_t>(row) * kW;
+    if (!bad && amax >= 0x00800000u && __float_as_uint(scale) >= 0x00800000u) {
+      const float r = __frcp_rn(scale);
+#pragma unroll
+      for (int k = 0; k < J; ++k)
+        *reinterpret_cast<uint2*>(dst + 8 * (hl + 16 * k)) = quant_group_fast<F16>(w[k], scale, r);
+    } else {
+#pragma unroll
+      for (int k = 0; k < J; ++k)
+        quantize_group_slow(make_uint4(w[k][0], w[k][1], w[k][2], w[k][3]), F16, scale, bad, dst + 8 * (hl + 16 * k));
+    }
+  }
+}
+
+template <bool F16, int J>
+int launch_amax_pair(const void* x, long ldx, const uint32_t* row_amax, int rows, int8_t* q, float* scales,
+                     unsigned* status, unsigned layer, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quantize_rows_amax_pair_kernel<F16, J>, 256, 0) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int want = (rows + 15) / 16;
+  const int cap = per_sm * num_sms(dev);
+  quantize_rows_amax_pair_kernel<F16, J><<<want < cap ? want : cap, 256, 0, stream>>>(
+      static_cast<const uint16_t*>(x), ldx, row_amax, rows, q, scales, status, layer);
+  return check_cuda(cudaGetLastError(), "amax quantiser launch");
+}
+
 template <bool F16, int G>
 int launch_amax(const void* x, long ldx, const uint32_t* row_amax, int rows, int width, int kp, int8_t* q,
                 float* scales, unsigned* status, unsigned layer, cudaStream_t stream) {
@@ -1059,6 +1120,14 @@ int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t
   }
   const int need = (kp / 8 + 31) / 32;  // 16-byte groups per lane
   const bool f16 = dtype == kInF16;
+  if (rows >= kPairRows && kp == width && width % 128 == 0 && width <= 384) {
+#define KB_AP(JJ)                                                                                              \
+  if (width == 128 * JJ)                                                                                       \
+    return f16 ? launch_amax_pair<true, JJ>(x, ldx, row_amax, rows, q, scales, status, layer, stream)          \
+               : launch_amax_pair<false, JJ>(x, ldx, row_amax, rows, q, scales, status, layer, stream);
+    KB_AP(1) KB_AP(2) KB_AP(3)
+#undef KB_AP
+  }
 #define KB_AQ(GG)                                                                                          \
   if (need <= GG)                                                                                          \
     return f16 ? launch_amax<true, GG>(x, ldx, row_amax, rows, width, kp, q, scales, status, layer, stream) \

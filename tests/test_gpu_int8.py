@@ -188,10 +188,15 @@ def test_quantize_rows_bit_exact(cuda, oracle, dtype, rows, width, stride):
     assert same_f32(host(s), os_)
 
 
-@pytest.mark.parametrize("rows,width", [(1, 8), (361, 3072), (1000, 472), (92416, 3072)])
-def test_gemm_row_amax_and_streaming_quantiser(cuda, oracle, rows, width):
-    """GEMM epilogue row_amax + streaming quantiser == full-row quantiser (bitwise)."""
+@pytest.mark.parametrize("rows,width", [(1, 8), (361, 3072), (1000, 472), (92416, 3072), (4099, 384),
+                                        (2048, 256), (2049, 128), (2047, 384)])
+@pytest.mark.parametrize("f16", [False, True])
+def test_gemm_row_amax_and_streaming_quantiser(cuda, oracle, rows, width, f16):
+    """GEMM epilogue row_amax + streaming quantiser == full-row quantiser
+    (bitwise); rows of 128..384 columns from 2048 rows take the two-rows-per-warp
+    kernel."""
     torch = cuda
+    odt = _capi.DT_F16 if f16 else _capi.DT_BF16
     rng = np.random.default_rng(rows + width)
     kp = 768
     a = torch.from_numpy(rng.integers(-127, 128, (rows, kp), dtype=np.int8)).cuda()
@@ -201,13 +206,14 @@ def test_gemm_row_amax_and_streaming_quantiser(cuda, oracle, rows, width):
     bias = torch.from_numpy((0.02 * rng.standard_normal(width)).astype(np.float32)).cuda()
     out = torch.zeros((rows, width), dtype=torch.int16, device="cuda")
     amax = torch.zeros(rows, dtype=torch.int32, device="cuda")
-    int8.linear(a, sa, w, sw, bias, rows, width, kp, _capi.EPI_16, out, width, act=_capi.ACT_GELU, row_amax=amax)
+    int8.linear(a, sa, w, sw, bias, rows, width, kp, _capi.EPI_16, out, width, act=_capi.ACT_GELU,
+                out_dtype=odt, row_amax=amax)
     kpo = (width + 15) // 16 * 16
     q = torch.full((rows, kpo), 9, dtype=torch.int8, device="cuda")
     s = torch.zeros(rows, device="cuda")
-    int8.quantize_rows_amax(out, _capi.DT_BF16, rows, width, width, kpo, amax, q, s)
+    int8.quantize_rows_amax(out, odt, rows, width, width, kpo, amax, q, s)
     torch.cuda.synchronize()
-    hid = oracle.decode16(out.cpu().numpy().view(np.uint16), False)
+    hid = oracle.decode16(out.cpu().numpy().view(np.uint16), f16)
     oq, os_ = oracle.quantize_rows(hid, kp=kpo)
     assert (q.cpu().numpy() == oq).all()
     assert same_f32(s.cpu().numpy(), os_)
