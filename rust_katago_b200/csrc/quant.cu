@@ -905,11 +905,11 @@ __global__ void __launch_bounds__(256) quantize_rows_amax_kernel(
   }
 }
 
-// Rows of exactly 128*J columns (J <= 3, kp == width) from kPairRows rows on,
-// two rows per warp: half-warp h holds row 2w + h, lane l = lane % 16 the
+// Rows of exactly 128*J columns (J <= 3 or 9, kp == width) from kPairRows rows
+// on, two rows per warp: half-warp h holds row 2w + h, lane l = lane % 16 the
 // groups l + 16k (k < J).  At 384 columns every lane then carries three
 // groups, where one row per warp leaves lanes 16..31 with one and lanes 0..15
-// with two.  Per element the same quantisation as quantize_rows_amax_kernel,
+// with two; at 1152 (the TF3 SwiGLU hidden) nine, instead of five and four.  Per element the same quantisation as quantize_rows_amax_kernel,
 // the scale once per row (no reduction: the producer supplied the maximum).
 template <bool F16, int J>
 __global__ void __launch_bounds__(256) quantize_rows_amax_pair_kernel(
@@ -1120,12 +1120,12 @@ int quantize_rows_amax_launch(const void* x, int dtype, long ldx, const uint32_t
   }
   const int need = (kp / 8 + 31) / 32;  // 16-byte groups per lane
   const bool f16 = dtype == kInF16;
-  if (rows >= kPairRows && kp == width && width % 128 == 0 && width <= 384) {
+  if (rows >= kPairRows && kp == width && width % 128 == 0 && (width <= 384 || width == 1152)) {
 #define KB_AP(JJ)                                                                                              \
   if (width == 128 * JJ)                                                                                       \
     return f16 ? launch_amax_pair<true, JJ>(x, ldx, row_amax, rows, q, scales, status, layer, stream)          \
                : launch_amax_pair<false, JJ>(x, ldx, row_amax, rows, q, scales, status, layer, stream);
-    KB_AP(1) KB_AP(2) KB_AP(3)
+    KB_AP(1) KB_AP(2) KB_AP(3) KB_AP(9)
 #undef KB_AP
   }
 #define KB_AQ(GG)                                                                                          \

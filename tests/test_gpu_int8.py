@@ -189,12 +189,12 @@ def test_quantize_rows_bit_exact(cuda, oracle, dtype, rows, width, stride):
 
 
 @pytest.mark.parametrize("rows,width", [(1, 8), (361, 3072), (1000, 472), (92416, 3072), (4099, 384),
-                                        (2048, 256), (2049, 128), (2047, 384)])
+                                        (2048, 256), (2049, 128), (2047, 384), (2049, 1152)])
 @pytest.mark.parametrize("f16", [False, True])
 def test_gemm_row_amax_and_streaming_quantiser(cuda, oracle, rows, width, f16):
     """GEMM epilogue row_amax + streaming quantiser == full-row quantiser
-    (bitwise); rows of 128..384 columns from 2048 rows take the two-rows-per-warp
-    kernel."""
+    (bitwise); rows of 128..384 or 1152 columns from 2048 rows take the
+    two-rows-per-warp kernel."""
     torch = cuda
     odt = _capi.DT_F16 if f16 else _capi.DT_BF16
     rng = np.random.default_rng(rows + width)
